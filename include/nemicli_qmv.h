@@ -1,0 +1,96 @@
+/*
+ * nemicli_qmv.h — C ABI of the B200 quantized matrix-vector path (GGUF block weights x activations).
+ *
+ * Plain pointers and sizes only.  Every pointer is a CUDA device pointer (or host memory the GPU
+ * can address) unless a comment says otherwise; `stream` is a cudaStream_t (0: the legacy default
+ * stream).  Every call only enqueues work on `stream` and returns a status: 0 = ok, else one of
+ * QMV_ERR_* (qmv_status_string explains it).  Nothing is allocated and nothing is read back on the
+ * host, so the calls can be captured in a CUDA graph.  There is no CPU fallback: a shape, format
+ * or alignment the kernels cannot take is refused with a status.
+ *
+ * Activation input (the reference's "Eingang", ggufengine/mmvq.py:825-849): for n values (n % 32 == 0)
+ *   xq  int8[n]    q  = rint(x / d),            d = max|x| / 127 per 32 values
+ *   xq2 int8[n]    q2 = rint((x - q d) / (d / 254)) clamped to +-127
+ *   xd  float[n/32] d
+ *   xs  float[n/32] sum of the 32 values of x
+ * Token t of a multi-token input starts at value t * n_in (xq, xq2) and t * n_in / 32 (xd, xs).
+ * Alignment: xq, xq2 16 bytes; xd, xs 8 bytes.
+ *
+ * Weights stay in raw GGUF block layout, row-major (n_out rows of n_in / block_values blocks).
+ * Formats (GGML type ids): Q4_0 = 2, Q8_0 = 8, Q4_K = 12, Q6_K = 14, IQ2_XXS = 16, TQ2_0 = 35.
+ * Alignment: Q4_K weights 16 bytes, the other formats 2 bytes.
+ */
+#ifndef NEMICLI_QMV_H
+#define NEMICLI_QMV_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NEMICLI_QMV_ABI_VERSION 1
+
+#define QMV_OK 0
+#define QMV_ERR_FORMAT 1   /* format not one of the six above */
+#define QMV_ERR_SHAPE 2    /* n_in not a positive multiple of the block size, n_out <= 0, ... */
+#define QMV_ERR_ALIGN 3    /* a pointer or stride misses the alignment above */
+#define QMV_ERR_TOKENS 4   /* token / slot count out of range */
+#define QMV_ERR_LAUNCH 5   /* CUDA refused the launch (qmv_last_cuda_error has the cudaError_t) */
+#define QMV_ERR_NULL 6     /* a required pointer is null */
+#define QMV_ERR_DEVICE 7   /* the device status word could not be read */
+
+/* Bits of the device status word (qmv_device_status). */
+#define QMV_DEV_BAD_ADDRESS 1   /* an expert id was outside [0, n_exp) or an address-table entry misaligned */
+
+int qmv_abi_version(void);
+const char* qmv_status_string(int status);
+int qmv_last_cuda_error(void);
+
+/* Values / bytes per block of a format (0 for a format this library does not compute).
+ * Replaces: ggufengine/gguf.py:64-77 (GGML_TYPES) for the six formats. */
+int qmv_block_values(int ggml_type);
+int qmv_block_bytes(int ggml_type);
+
+/* 1 when the kernels take this format and row length.
+ * Replaces: ggufengine/mmvq.py:808 (verfuegbar) and ggufengine/cudakern.py:733 (verfuegbar). */
+int qmv_supported(int ggml_type, int n_in);
+
+/* Quantise n values (fp32 if x_is_f32, else bf16) into an activation input.
+ * Replaces: ggufengine/mmvq.py:77-83 (quant_q8 kernel) as launched by Eingang.__init__ (:829-843). */
+int qmv_quant_q8(const void* x, int x_is_f32, int8_t* xq, int8_t* xq2, float* xd, float* xs, long long n,
+                 void* stream);
+
+/* y[t][r] = W[r, :] . x_t for n_tok tokens (any n_tok >= 1; launched in groups of 8), fp32 output
+ * [n_tok][n_out].  Replaces: ggufengine/mmvq.py:852-865 (mv: int8 path, Q4_K/Q6_K) and
+ * ggufengine/cudakern.py:777-790 (mm) / qlinear.py:210-215 (QuantLinear._mm) for the dense formats. */
+int qmv_mv(int ggml_type, const uint8_t* w, int n_out, int n_in, const int8_t* xq, const int8_t* xq2,
+           const float* xd, const float* xs, int n_tok, float* y, void* stream);
+
+/* Grouped expert matvec driven by device-side ids: y[j][r] = W_{ids[j]}[r, :] . x_{j / x_group}, j < k.
+ * raw: the expert tensor (n_exp experts of per_expert bytes each) or, with per_expert < 0, a device
+ * table of n_exp int64 addresses (one per expert).  Slot j reads activation row j / x_group (rows are
+ * n_in values apart): x_group = k shares one input among all slots, 1 gives each slot its own row,
+ * and k_per_token for tokens x slots.  ids outside [0, n_exp) give zero rows and set
+ * QMV_DEV_BAD_ADDRESS.  Replaces: ggufengine/cudakern.py:756-774 (mv, the mv_<FMT> expert gather
+ * :483-505) as called by PackedExperts.matvec / matvec_je (models/common.py:462-475). */
+int qmv_mv_experts(int ggml_type, const void* raw, long long per_expert, long long n_exp, const long long* ids,
+                   int k, const int8_t* xq, const int8_t* xq2, const float* xd, const float* xs,
+                   int x_group, float* y, int n_out, int n_in, void* stream);
+
+/* Test hook: the int32 sums of one token per (row, unit), unit = the values sharing one weight scale
+ * and one activation scale (16 for Q6_K, else 32): s = sum code * xq, s2 = sum code * xq2, from the
+ * same device code as qmv_mv.  s, s2: int32[n_out][n_in / unit], overwritten.
+ * Replaces: nothing callable — it exposes the dp4a sums of ggufengine/mmvq.py:389-404 / :469-470. */
+int qmv_block_sums(int ggml_type, const uint8_t* w, int n_out, int n_in, const int8_t* xq, const int8_t* xq2,
+                   int32_t* s, int32_t* s2, void* stream);
+
+/* Reads (and with clear != 0 resets) the device status word; synchronises `stream`.  *out is host memory.
+ * Replaces: nothing in the reference (its kernels have no device-side checks). */
+int qmv_device_status(int clear, int* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NEMICLI_QMV_H */

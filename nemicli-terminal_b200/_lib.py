@@ -1,0 +1,87 @@
+"""ctypes binding of libnemiqmv.so (the C ABI of include/nemicli_qmv.h).
+
+The library is built in-tree by build.py.  There is no fallback: if it is missing or a call
+returns a non-zero status, a RuntimeError names the failure.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+from . import build as _build
+
+_lock = threading.Lock()
+_lib = None
+
+P, I, LL = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong
+
+_SIGNATURES = {
+    "qmv_abi_version": ([], I),
+    "qmv_status_string": ([I], ctypes.c_char_p),
+    "qmv_last_cuda_error": ([], I),
+    "qmv_block_values": ([I], I),
+    "qmv_block_bytes": ([I], I),
+    "qmv_supported": ([I, I], I),
+    "qmv_quant_q8": ([P, I, P, P, P, P, LL, P], I),
+    "qmv_mv": ([I, P, I, I, P, P, P, P, I, P, P], I),
+    "qmv_mv_experts": ([I, P, LL, LL, P, I, P, P, P, P, I, P, I, I, P], I),
+    "qmv_block_sums": ([I, P, I, I, P, P, P, P, P], I),
+    "qmv_device_status": ([I, P, P], I),
+}
+
+ABI_VERSION = 1
+
+
+def lib_path() -> str:
+    return _build.LIB_PATH
+
+
+def load() -> ctypes.CDLL:
+    """Load the CUDA library (raises if it was not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            path = lib_path()
+            if not os.path.exists(path):
+                raise RuntimeError(f"CUDA library missing: {path} (build it with nemicli_terminal_b200.build.build())")
+            L = ctypes.CDLL(path)
+            for name, (args, res) in _SIGNATURES.items():
+                fn = getattr(L, name)
+                fn.argtypes = args
+                fn.restype = res
+            if L.qmv_abi_version() != ABI_VERSION:
+                raise RuntimeError(f"{path}: ABI version {L.qmv_abi_version()} != {ABI_VERSION}")
+            _lib = L
+    return _lib
+
+
+def exported_symbols() -> list:
+    return list(_SIGNATURES)
+
+
+def check(status: int, what: str) -> None:
+    if status:
+        L = load()
+        msg = L.qmv_status_string(status).decode()
+        extra = f" (cudaError {L.qmv_last_cuda_error()})" if status == 5 else ""
+        raise RuntimeError(f"{what}: {msg}{extra}")
+
+
+def ptr(t) -> ctypes.c_void_p:
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def stream_ptr(device=None) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def device_status(clear: bool = True, device=None) -> int:
+    """The device status word (bit 1: a refused expert id or address); synchronises the stream."""
+    out = ctypes.c_int(0)
+    check(load().qmv_device_status(int(clear), ctypes.byref(out), stream_ptr(device)), "qmv_device_status")
+    return out.value

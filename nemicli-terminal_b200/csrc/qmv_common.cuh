@@ -1,0 +1,102 @@
+// Shared device helpers of the quantized matvec kernels (sm_100a).
+#pragma once
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace qmv {
+
+// GGML type ids of the six formats (the GGUF type table; reference ggufengine/gguf.py:64-77)
+enum : int { F_Q4_0 = 2, F_Q8_0 = 8, F_Q4_K = 12, F_Q6_K = 14, F_IQ2_XXS = 16, F_TQ2_0 = 35 };
+
+// status codes returned across the C ABI (include/nemicli_qmv.h)
+enum : int {
+    ST_OK = 0,
+    ST_BAD_FORMAT = 1,
+    ST_BAD_SHAPE = 2,
+    ST_BAD_ALIGN = 3,
+    ST_BAD_TOKENS = 4,
+    ST_LAUNCH = 5,
+    ST_NULL = 6,
+    ST_DEVICE = 7,
+};
+
+// bits of the device-side status word (set by kernels, read with qmv_device_status)
+enum : int { DEV_BAD_ADDRESS = 1 };
+
+constexpr int kWarpsPerBlock = 8;
+constexpr int kMaxTokens = 8;           // tokens per launch of the dp4a kernels
+constexpr float kInv254 = 1.0f / 254.0f;
+
+__host__ __device__ constexpr int block_values(int f) {
+    return (f == F_Q4_0 || f == F_Q8_0) ? 32 : 256;
+}
+__host__ __device__ constexpr int block_bytes(int f) {
+    return f == F_Q4_0 ? 18 : f == F_Q8_0 ? 34 : f == F_Q4_K ? 144 : f == F_Q6_K ? 210 : 66;
+}
+// values per integer-sum unit (one weight scale and one activation scale)
+__host__ __device__ constexpr int unit_values(int f) { return f == F_Q6_K ? 16 : 32; }
+
+__host__ __device__ inline bool known_format(int f) {
+    return f == F_Q4_0 || f == F_Q8_0 || f == F_Q4_K || f == F_Q6_K || f == F_IQ2_XXS || f == F_TQ2_0;
+}
+
+// ---- loads --------------------------------------------------------------------------------------
+// Weights are streamed once: non-coherent loads that do not allocate in L1.  Activations are
+// re-read by every row and stay in L1 (__ldg).
+
+__device__ __forceinline__ uint4 ldw16(const uint8_t* p) {            // 16-byte aligned
+    uint4 r;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint32_t ldw4(const uint8_t* p) {          // 4-byte aligned
+    uint32_t r;
+    asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint32_t ldw2(const uint8_t* p) {          // 2-byte aligned
+    unsigned short r;
+    asm("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(r) : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint32_t ldw1(const uint8_t* p) {
+    unsigned short r;
+    asm("ld.global.nc.L1::no_allocate.u8 %0, [%1];" : "=h"(r) : "l"(p));
+    return r & 0xFFu;
+}
+// 16 bytes at a 2-byte aligned address: aligned words, then funnel shifts.  Never reads past p + 16.
+__device__ __forceinline__ uint4 ldw16_a2(const uint8_t* p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(a & ~uintptr_t(3));
+    const uint32_t sh = uint32_t(a & 3) * 8u;                          // 0 or 16
+    const uint32_t w0 = ldw4(b), w1 = ldw4(b + 4), w2 = ldw4(b + 8), w3 = ldw4(b + 12);
+    const uint32_t w4 = sh ? ldw2(b + 16) : 0u;
+    return make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh),
+                      __funnelshift_r(w2, w3, sh), __funnelshift_r(w3, w4, sh));
+}
+__device__ __forceinline__ uint2 ldw8_a2(const uint8_t* p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(a & ~uintptr_t(3));
+    const uint32_t sh = uint32_t(a & 3) * 8u;
+    const uint32_t w0 = ldw4(b), w1 = ldw4(b + 4);
+    const uint32_t w2 = sh ? ldw2(b + 8) : 0u;
+    return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
+}
+
+__device__ __forceinline__ int4 ldx16(const int8_t* p) { return __ldg(reinterpret_cast<const int4*>(p)); }
+__device__ __forceinline__ int2 ldx8(const int8_t* p) { return __ldg(reinterpret_cast<const int2*>(p)); }
+
+__device__ __forceinline__ float h2f(uint32_t bits) { return __half2float(__ushort_as_half((unsigned short)bits)); }
+__device__ __forceinline__ float bf2f(uint16_t bits) { return __uint_as_float(uint32_t(bits) << 16); }
+
+__device__ __forceinline__ int dp4(uint32_t a, int b, int c) { return __dp4a(int(a), b, c); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+}  // namespace qmv

@@ -1,0 +1,473 @@
+// Kernels of the quantized matvec path: activation quantisation and the per-format int8 matvec.
+//
+// Activation input ("Eingang", the reference's name; ggufengine/mmvq.py:825-849): per 32 values
+// an int8 xq with scale xd = amax/127, a second int8 xq2 holding the remainder at scale xd/254,
+// and xs = the fp32 sum of the 32 values.  The matvec computes, per 32-value group g of a row,
+//     y += wscale * xd_g * (S + S2/254) - offs * xs_g,   S = sum code*xq, S2 = sum code*xq2 (int32)
+// with the per-format weight code, weight scale and offset of ggufengine/quant.py.
+#pragma once
+#include "qmv_common.cuh"
+
+namespace qmv {
+
+// ---------------------------------------------------------------------------------------------
+// Activation quantisation (restates ggufengine/mmvq.py:59-83 with IEEE-rounded division)
+// ---------------------------------------------------------------------------------------------
+
+// One warp quantises one group of 32 consecutive values; lane l holds value l of the group.
+__device__ __forceinline__ void quantize_group(float v, long long i, int8_t* __restrict__ xq,
+                                               int8_t* __restrict__ xq2, float* __restrict__ xd,
+                                               float* __restrict__ xs) {
+    float a = fabsf(v);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    const float d = __fdiv_rn(a, 127.0f);
+    const float d2 = __fdiv_rn(d, 254.0f);
+    int q = 0, q2 = 0;
+    if (d > 0.f) {
+        q = __float2int_rn(__fdiv_rn(v, d));
+        const float r = __fmaf_rn(-float(q), d, v);
+        q2 = max(-127, min(127, __float2int_rn(__fdiv_rn(r, d2))));
+    }
+    const float s = warp_sum(v);          // butterfly xor 16..1: the order the oracle restates
+    xq[i] = int8_t(q);
+    xq2[i] = int8_t(q2);
+    if ((threadIdx.x & 31) == 0) {
+        xd[i >> 5] = d;
+        xs[i >> 5] = s;
+    }
+}
+
+__global__ void __launch_bounds__(256) quant_q8_kernel(const void* __restrict__ x, int x_f32,
+                                                       int8_t* __restrict__ xq, int8_t* __restrict__ xq2,
+                                                       float* __restrict__ xd, float* __restrict__ xs,
+                                                       long long n) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if ((i & ~31LL) >= n) return;          // n % 32 == 0: whole warps leave together
+    const float v = x_f32 ? static_cast<const float*>(x)[i] : bf2f(static_cast<const uint16_t*>(x)[i]);
+    quantize_group(v, i, xq, xq2, xd, xs);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Matvec
+// ---------------------------------------------------------------------------------------------
+
+struct MvParams {
+    const uint8_t* w;          // weights; with ids: the expert tensor, or (per_expert < 0) an int64 address table
+    const long long* ids;      // expert id per slot, or nullptr (one slot: w itself)
+    long long per_expert;      // bytes per expert (>= 0), or -1: w is an address table
+    long long row_bytes;       // bytes per weight row
+    const int8_t* xq;
+    const int8_t* xq2;
+    const float* xd;
+    const float* xs;
+    int x_group;               // slots per activation row: slot j reads row j / x_group (rows n_in values apart)
+    float* y;                  // [slot][token][n_out]
+    int32_t* s;                // sums mode: [row][unit] int32 sums of code*xq
+    int32_t* s2;               //            ... and of code*xq2
+    int* status;               // device status word (bits DEV_*)
+    long long n_exp;           // experts addressable through ids (ids outside [0, n_exp) are refused)
+    int n_out, n_in, slots;
+};
+
+// Per-lane work: a warp walks a row group of RW rows; lane = 8 * (superblock % 4) + q, where the
+// 8 lanes of a 256-value superblock split it into eight 32-value pieces (per format below).
+// tb[t]: activation value offset of token t's row start.  acc[r][t]: partial dot products.
+
+template <int T>
+struct Tok {
+    long long tb[T];
+};
+
+// ---- Q4_K: 144 B = d, dmin (f16), 12 B of 6-bit scales/mins, 128 B nibbles (quant.py:111-120).
+// Lane q takes qs bytes 16q..16q+15: the low nibbles are values 16h..16h+15 of sub-block 2p, the
+// high nibbles the same values of sub-block 2p+1 (p = q/2, h = q%2).
+template <int T, int RW, bool SUMS>
+__device__ __forceinline__ void lane_q4k(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                         const Tok<T>& tk, float (&acc)[RW][T], int row0) {
+    const int p = q >> 1, h = q & 1;
+    uint32_t lo[RW][4], hi[RW][4];
+    float d[RW], dm[RW], sc0[RW], sc1[RW], m0[RW], m1[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        const uint8_t* b = rows[r] + (long long)sb * 144;
+        const uint4 hd = ldw16(b);
+        const uint4 v = ldw16(b + 16 + 16 * q);
+        lo[r][0] = v.x & 0x0F0F0F0Fu; hi[r][0] = (v.x >> 4) & 0x0F0F0F0Fu;
+        lo[r][1] = v.y & 0x0F0F0F0Fu; hi[r][1] = (v.y >> 4) & 0x0F0F0F0Fu;
+        lo[r][2] = v.z & 0x0F0F0F0Fu; hi[r][2] = (v.z >> 4) & 0x0F0F0F0Fu;
+        lo[r][3] = v.w & 0x0F0F0F0Fu; hi[r][3] = (v.w >> 4) & 0x0F0F0F0Fu;
+        d[r] = h2f(hd.x & 0xFFFFu);
+        dm[r] = h2f(hd.x >> 16);
+        // 6-bit scales and mins of sub-blocks 0..3 (p < 2) or 4..7, four per word
+        uint32_t scw, mw;
+        if (p < 2) {
+            scw = hd.y & 0x3F3F3F3Fu;
+            mw = hd.z & 0x3F3F3F3Fu;
+        } else {
+            scw = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
+            mw = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
+        }
+        const int sh = 16 * (p & 1);
+        sc0[r] = float((scw >> sh) & 0xFFu);
+        sc1[r] = float((scw >> (sh + 8)) & 0xFFu);
+        m0[r] = float((mw >> sh) & 0xFFu);
+        m1[r] = float((mw >> (sh + 8)) & 0xFFu);
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const long long o = tk.tb[t] + (long long)sb * 256 + 64 * p + 16 * h;
+        const int4 xa = ldx16(P.xq + o), xb = ldx16(P.xq + o + 32);
+        const int4 ya = ldx16(P.xq2 + o), yb = ldx16(P.xq2 + o + 32);
+        const long long g = ((tk.tb[t] + (long long)sb * 256) >> 5) + 2 * p;
+        const float2 dd = __ldg(reinterpret_cast<const float2*>(P.xd + g));
+        const float2 ss = __ldg(reinterpret_cast<const float2*>(P.xs + g));
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            int s0 = dp4(lo[r][0], xa.x, 0); s0 = dp4(lo[r][1], xa.y, s0); s0 = dp4(lo[r][2], xa.z, s0); s0 = dp4(lo[r][3], xa.w, s0);
+            int s1 = dp4(hi[r][0], xb.x, 0); s1 = dp4(hi[r][1], xb.y, s1); s1 = dp4(hi[r][2], xb.z, s1); s1 = dp4(hi[r][3], xb.w, s1);
+            int u0 = dp4(lo[r][0], ya.x, 0); u0 = dp4(lo[r][1], ya.y, u0); u0 = dp4(lo[r][2], ya.z, u0); u0 = dp4(lo[r][3], ya.w, u0);
+            int u1 = dp4(hi[r][0], yb.x, 0); u1 = dp4(hi[r][1], yb.y, u1); u1 = dp4(hi[r][2], yb.z, u1); u1 = dp4(hi[r][3], yb.w, u1);
+            if constexpr (SUMS) {
+                const long long base = (long long)row0 * (P.n_in / 32) + sb * 8 + 2 * p;
+                atomicAdd(P.s + base, s0); atomicAdd(P.s + base + 1, s1);
+                atomicAdd(P.s2 + base, u0); atomicAdd(P.s2 + base + 1, u1);
+            } else {
+                float a = d[r] * (dd.x * sc0[r] * (float(s0) + float(u0) * kInv254)
+                                  + dd.y * sc1[r] * (float(s1) + float(u1) * kInv254));
+                if (h == 0) a -= dm[r] * (m0[r] * ss.x + m1[r] * ss.y);    // the min term once per sub-block
+                acc[r][t] += a;
+            }
+        }
+    }
+}
+
+// ---- Q6_K: 210 B = ql[128], qh[64], int8 scales[16], d (f16) (quant.py:140-159).  Half n holds 128
+// values; group g (0..3) of 32: low 4 bits from ql[64n + 32(g&1) + l] (nibble g>>1), top 2 bits from
+// qh[32n + l] bits 2g.  Lane q (n = q/4, j = q%4) takes ql bytes 64n+16j..+15: groups A = j/2 (low
+// nibble) and A+2 (high nibble), l = 16(j%2)..+15; one int8 scale per 16 values.
+template <int T, int RW, bool SUMS>
+__device__ __forceinline__ void lane_q6k(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                         const Tok<T>& tk, float (&acc)[RW][T], int row0) {
+    const int n = q >> 2, j = q & 3, A = j >> 1, B = A + 2, l0 = 16 * (j & 1);
+    uint32_t wa[RW][4], wb[RW][4];
+    float d[RW], sa[RW], sbs[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        const uint8_t* b = rows[r] + (long long)sb * 210;
+        const uint4 ql = ldw16_a2(b + 64 * n + 16 * j);
+        const uint4 qh = ldw16_a2(b + 128 + 32 * n + l0);
+        sa[r] = float(int8_t(ldw1(b + 192 + 8 * n + 2 * A + (j & 1))));
+        sbs[r] = float(int8_t(ldw1(b + 192 + 8 * n + 2 * B + (j & 1))));
+        d[r] = h2f(ldw2(b + 208));
+        const uint32_t L[4] = {ql.x, ql.y, ql.z, ql.w}, H[4] = {qh.x, qh.y, qh.z, qh.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            wa[r][i] = __vsub4((L[i] & 0x0F0F0F0Fu) | (((H[i] >> (2 * A)) & 0x03030303u) << 4), 0x20202020u);
+            wb[r][i] = __vsub4(((L[i] >> 4) & 0x0F0F0F0Fu) | (((H[i] >> (2 * B)) & 0x03030303u) << 4), 0x20202020u);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const long long o = tk.tb[t] + (long long)sb * 256 + 128 * n + l0;
+        const int4 xa = ldx16(P.xq + o + 32 * A), xb = ldx16(P.xq + o + 32 * B);
+        const int4 ya = ldx16(P.xq2 + o + 32 * A), yb = ldx16(P.xq2 + o + 32 * B);
+        const long long g = ((tk.tb[t] + (long long)sb * 256) >> 5) + 4 * n;
+        const float da = __ldg(P.xd + g + A), db = __ldg(P.xd + g + B);
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            int s0 = dp4(wa[r][0], xa.x, 0); s0 = dp4(wa[r][1], xa.y, s0); s0 = dp4(wa[r][2], xa.z, s0); s0 = dp4(wa[r][3], xa.w, s0);
+            int s1 = dp4(wb[r][0], xb.x, 0); s1 = dp4(wb[r][1], xb.y, s1); s1 = dp4(wb[r][2], xb.z, s1); s1 = dp4(wb[r][3], xb.w, s1);
+            int u0 = dp4(wa[r][0], ya.x, 0); u0 = dp4(wa[r][1], ya.y, u0); u0 = dp4(wa[r][2], ya.z, u0); u0 = dp4(wa[r][3], ya.w, u0);
+            int u1 = dp4(wb[r][0], yb.x, 0); u1 = dp4(wb[r][1], yb.y, u1); u1 = dp4(wb[r][2], yb.z, u1); u1 = dp4(wb[r][3], yb.w, u1);
+            if constexpr (SUMS) {
+                const long long base = (long long)row0 * (P.n_in / 16) + sb * 16 + 8 * n + (j & 1);
+                atomicAdd(P.s + base + 2 * A, s0); atomicAdd(P.s + base + 2 * B, s1);
+                atomicAdd(P.s2 + base + 2 * A, u0); atomicAdd(P.s2 + base + 2 * B, u1);
+            } else {
+                acc[r][t] += d[r] * (sa[r] * da * (float(s0) + float(u0) * kInv254)
+                                     + sbs[r] * db * (float(s1) + float(u1) * kInv254));
+            }
+        }
+    }
+}
+
+// ---- Q4_0: 18 B = d (f16), 16 B nibbles: low nibble = value i, high = value 16+i (quant.py:60-64).
+// Lane q takes block 8*sb + q of the row; the code is the unsigned nibble, the -8 goes with xs.
+template <int T, int RW, bool SUMS>
+__device__ __forceinline__ void lane_q4_0(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                          const Tok<T>& tk, float (&acc)[RW][T], int row0) {
+    const int blk = sb * 8 + q;
+    if (blk >= P.n_in / 32) return;
+    uint32_t lo[RW][4], hi[RW][4];
+    float d[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        const uint8_t* b = rows[r] + (long long)blk * 18;
+        d[r] = h2f(ldw2(b));
+        const uint4 v = ldw16_a2(b + 2);
+        lo[r][0] = v.x & 0x0F0F0F0Fu; hi[r][0] = (v.x >> 4) & 0x0F0F0F0Fu;
+        lo[r][1] = v.y & 0x0F0F0F0Fu; hi[r][1] = (v.y >> 4) & 0x0F0F0F0Fu;
+        lo[r][2] = v.z & 0x0F0F0F0Fu; hi[r][2] = (v.z >> 4) & 0x0F0F0F0Fu;
+        lo[r][3] = v.w & 0x0F0F0F0Fu; hi[r][3] = (v.w >> 4) & 0x0F0F0F0Fu;
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const long long o = tk.tb[t] + (long long)blk * 32;
+        const int4 xa = ldx16(P.xq + o), xb = ldx16(P.xq + o + 16);
+        const int4 ya = ldx16(P.xq2 + o), yb = ldx16(P.xq2 + o + 16);
+        const long long g = (tk.tb[t] >> 5) + blk;
+        const float dd = __ldg(P.xd + g), ss = __ldg(P.xs + g);
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            int s = dp4(lo[r][0], xa.x, 0); s = dp4(lo[r][1], xa.y, s); s = dp4(lo[r][2], xa.z, s); s = dp4(lo[r][3], xa.w, s);
+            s = dp4(hi[r][0], xb.x, s); s = dp4(hi[r][1], xb.y, s); s = dp4(hi[r][2], xb.z, s); s = dp4(hi[r][3], xb.w, s);
+            int u = dp4(lo[r][0], ya.x, 0); u = dp4(lo[r][1], ya.y, u); u = dp4(lo[r][2], ya.z, u); u = dp4(lo[r][3], ya.w, u);
+            u = dp4(hi[r][0], yb.x, u); u = dp4(hi[r][1], yb.y, u); u = dp4(hi[r][2], yb.z, u); u = dp4(hi[r][3], yb.w, u);
+            if constexpr (SUMS) {
+                const long long base = (long long)row0 * (P.n_in / 32) + blk;
+                atomicAdd(P.s + base, s);
+                atomicAdd(P.s2 + base, u);
+            } else {
+                acc[r][t] += d[r] * (dd * (float(s) + float(u) * kInv254) - 8.0f * ss);
+            }
+        }
+    }
+}
+
+// ---- Q8_0: 34 B = d (f16), int8[32] (quant.py:46-50).  Lane q takes block 8*sb + q.
+template <int T, int RW, bool SUMS>
+__device__ __forceinline__ void lane_q8_0(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                          const Tok<T>& tk, float (&acc)[RW][T], int row0) {
+    const int blk = sb * 8 + q;
+    if (blk >= P.n_in / 32) return;
+    uint32_t w[RW][8];
+    float d[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        const uint8_t* b = rows[r] + (long long)blk * 34;
+        d[r] = h2f(ldw2(b));
+        const uint4 v0 = ldw16_a2(b + 2), v1 = ldw16_a2(b + 18);
+        w[r][0] = v0.x; w[r][1] = v0.y; w[r][2] = v0.z; w[r][3] = v0.w;
+        w[r][4] = v1.x; w[r][5] = v1.y; w[r][6] = v1.z; w[r][7] = v1.w;
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const long long o = tk.tb[t] + (long long)blk * 32;
+        const int4 xa = ldx16(P.xq + o), xb = ldx16(P.xq + o + 16);
+        const int4 ya = ldx16(P.xq2 + o), yb = ldx16(P.xq2 + o + 16);
+        const float dd = __ldg(P.xd + (tk.tb[t] >> 5) + blk);
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            int s = dp4(w[r][0], xa.x, 0); s = dp4(w[r][1], xa.y, s); s = dp4(w[r][2], xa.z, s); s = dp4(w[r][3], xa.w, s);
+            s = dp4(w[r][4], xb.x, s); s = dp4(w[r][5], xb.y, s); s = dp4(w[r][6], xb.z, s); s = dp4(w[r][7], xb.w, s);
+            int u = dp4(w[r][0], ya.x, 0); u = dp4(w[r][1], ya.y, u); u = dp4(w[r][2], ya.z, u); u = dp4(w[r][3], ya.w, u);
+            u = dp4(w[r][4], yb.x, u); u = dp4(w[r][5], yb.y, u); u = dp4(w[r][6], yb.z, u); u = dp4(w[r][7], yb.w, u);
+            if constexpr (SUMS) {
+                const long long base = (long long)row0 * (P.n_in / 32) + blk;
+                atomicAdd(P.s + base, s);
+                atomicAdd(P.s2 + base, u);
+            } else {
+                acc[r][t] += d[r] * dd * (float(s) + float(u) * kInv254);
+            }
+        }
+    }
+}
+
+// ---- TQ2_0: 66 B = qs[64], d (f16) at 64 (quant.py:417-421).  Value 128n + 32g + m is bits 2g of
+// byte 32n + m; the code 0..3 stands for code - 1.  Lane q (n = q/4, j = q%4) takes bytes
+// 32n + 8j..+7: values m = 8j..8j+7 of all four groups of half n.
+template <int T, int RW, bool SUMS>
+__device__ __forceinline__ void lane_tq2_0(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                           const Tok<T>& tk, float (&acc)[RW][T], int row0) {
+    const int n = q >> 2, j = q & 3;
+    uint2 c[RW];
+    float d[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        const uint8_t* b = rows[r] + (long long)sb * 66;
+        c[r] = ldw8_a2(b + 32 * n + 8 * j);
+        d[r] = h2f(ldw2(b + 64));
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const long long o = tk.tb[t] + (long long)sb * 256 + 128 * n + 8 * j;
+        const long long g0 = ((tk.tb[t] + (long long)sb * 256) >> 5) + 4 * n;
+        int2 xa[4], ya[4];
+        float dd[4], ss[4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            xa[g] = ldx8(P.xq + o + 32 * g);
+            ya[g] = ldx8(P.xq2 + o + 32 * g);
+            dd[g] = __ldg(P.xd + g0 + g);
+            ss[g] = j == 0 ? __ldg(P.xs + g0 + g) : 0.f;     // the -1 offset once per 32-value group
+        }
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            float a = 0.f;
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                const uint32_t c0 = (c[r].x >> (2 * g)) & 0x03030303u, c1 = (c[r].y >> (2 * g)) & 0x03030303u;
+                const int s = dp4(c1, xa[g].y, dp4(c0, xa[g].x, 0));
+                const int u = dp4(c1, ya[g].y, dp4(c0, ya[g].x, 0));
+                if constexpr (SUMS) {
+                    const long long base = (long long)row0 * (P.n_in / 32) + sb * 8 + 4 * n + g;
+                    atomicAdd(P.s + base, s);
+                    atomicAdd(P.s2 + base, u);
+                } else {
+                    a += dd[g] * (float(s) + float(u) * kInv254) - ss[g];
+                }
+            }
+            if constexpr (!SUMS) acc[r][t] += d[r] * a;
+        }
+    }
+}
+
+// ---- IQ2_XXS: 66 B = d (f16), 8 x 8 B: per 32 values four codebook indices (u8) and a u32 with four
+// 7-bit sign patterns (parity gives the 8th sign) and a 4-bit scale (quant.py:235-245).  Lane q takes
+// sub-block q.  The codebook lives in shared memory as (lo, hi) words of eight magnitudes.
+template <int T, int RW, bool SUMS>
+__device__ __forceinline__ void lane_iq2xxs(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                            const Tok<T>& tk, float (&acc)[RW][T], int row0,
+                                            const uint2* __restrict__ grid) {
+    uint32_t w[RW][8];
+    float sc[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        const uint8_t* b = rows[r] + (long long)sb * 66;
+        const uint2 a = ldw8_a2(b + 2 + 8 * q);
+        sc[r] = h2f(ldw2(b)) * (0.125f + 0.25f * float(a.y >> 28));
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            const uint2 g = grid[(a.x >> (8 * l)) & 0xFFu];
+            const uint32_t s7 = (a.y >> (7 * l)) & 127u;
+            const uint32_t s8 = s7 | (uint32_t(__popc(s7) & 1) << 7);
+            // sign bit k -> byte mask 0xFF at byte k (four bits per word)
+            const uint32_t mlo = (((s8 & 15u) * 0x00204081u) & 0x01010101u) * 0xFFu;
+            const uint32_t mhi = (((s8 >> 4) * 0x00204081u) & 0x01010101u) * 0xFFu;
+            w[r][2 * l] = __vsub4(g.x ^ mlo, mlo);
+            w[r][2 * l + 1] = __vsub4(g.y ^ mhi, mhi);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const long long o = tk.tb[t] + (long long)sb * 256 + 32 * q;
+        const int4 x0 = ldx16(P.xq + o), x1 = ldx16(P.xq + o + 16);
+        const int4 y0 = ldx16(P.xq2 + o), y1 = ldx16(P.xq2 + o + 16);
+        const float dd = __ldg(P.xd + ((tk.tb[t] + (long long)sb * 256) >> 5) + q);
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            int s = dp4(w[r][0], x0.x, 0); s = dp4(w[r][1], x0.y, s); s = dp4(w[r][2], x0.z, s); s = dp4(w[r][3], x0.w, s);
+            s = dp4(w[r][4], x1.x, s); s = dp4(w[r][5], x1.y, s); s = dp4(w[r][6], x1.z, s); s = dp4(w[r][7], x1.w, s);
+            int u = dp4(w[r][0], y0.x, 0); u = dp4(w[r][1], y0.y, u); u = dp4(w[r][2], y0.z, u); u = dp4(w[r][3], y0.w, u);
+            u = dp4(w[r][4], y1.x, u); u = dp4(w[r][5], y1.y, u); u = dp4(w[r][6], y1.z, u); u = dp4(w[r][7], y1.w, u);
+            if constexpr (SUMS) {
+                const long long base = (long long)row0 * (P.n_in / 32) + sb * 8 + q;
+                atomicAdd(P.s + base, s);
+                atomicAdd(P.s2 + base, u);
+            } else {
+                acc[r][t] += sc[r] * dd * (float(s) + float(u) * kInv254);
+            }
+        }
+    }
+}
+
+// IQ2_XXS codebook, 2 bits per magnitude (index into {8, 25, 43}); expanded per block at launch
+__device__ const uint16_t kIq2xxsCodes[256] = {
+#include "iq2xxs_grid.inc"
+};
+
+__device__ __forceinline__ void load_iq2xxs_grid(uint2* grid) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+        const uint32_t c = kIq2xxsCodes[i];
+        uint32_t w[2] = {0u, 0u};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const uint32_t lv = (c >> (2 * k)) & 3u;
+            const uint32_t mag = lv == 0 ? 8u : (lv == 1 ? 25u : 43u);
+            w[k >> 2] |= mag << (8 * (k & 3));
+        }
+        grid[i] = make_uint2(w[0], w[1]);
+    }
+}
+
+// Weight row base of slot `slot`: the dense matrix, expert ids[slot] of a packed expert tensor, or an
+// address-table entry.  Returns nullptr (and flags the status word) for an address that the
+// format's loads cannot use.
+template <int FMT>
+__device__ __forceinline__ const uint8_t* slot_base(const MvParams& P, int slot) {
+    if (P.ids == nullptr) return P.w;
+    const long long e = P.ids[slot];
+    if (e < 0 || e >= P.n_exp) {
+        if (P.status) atomicOr(P.status, DEV_BAD_ADDRESS);
+        return nullptr;
+    }
+    const uint8_t* base = P.per_expert >= 0 ? P.w + e * P.per_expert
+                                            : reinterpret_cast<const uint8_t*>(reinterpret_cast<const long long*>(P.w)[e]);
+    const uintptr_t need = FMT == F_Q4_K ? 15u : 1u;
+    if (reinterpret_cast<uintptr_t>(base) & need) {
+        if (P.status) atomicOr(P.status, DEV_BAD_ADDRESS);
+        return nullptr;
+    }
+    return base;
+}
+
+// y[slot][t][row] = W_slot[row, :] . x(slot, t) for T tokens.  Each warp takes RW consecutive rows
+// of one slot at a time (grid-stride over all slots' row groups); SUMS instead adds the int32 unit
+// sums of one token into P.s / P.s2 (T = RW = 1).
+template <int FMT, int T, int RW, bool SUMS>
+__global__ void __launch_bounds__(256) mv_kernel(const MvParams P) {
+    __shared__ uint2 grid[FMT == F_IQ2_XXS ? 256 : 1];
+    if constexpr (FMT == F_IQ2_XXS) {
+        load_iq2xxs_grid(grid);
+        __syncthreads();
+    }
+    const int lane = threadIdx.x & 31, q = lane & 7, sb0 = lane >> 3;
+    const int groups = (P.n_out + RW - 1) / RW;
+    const long long total = (long long)groups * P.slots;
+    const long long warps = (long long)gridDim.x * kWarpsPerBlock;
+    const int n_sb = (P.n_in + 255) >> 8;                 // 256-value pieces (8 blocks of 32-value formats)
+    for (long long it = (long long)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); it < total; it += warps) {
+        const int slot = int(it / groups);
+        const int row0 = int(it % groups) * RW;
+        const uint8_t* base = slot_base<FMT>(P, slot);
+        if (base == nullptr) {                            // refused slot (whole warp): defined zeros
+            if (!SUMS && lane < RW * T) {
+                const int r = lane / T, t = lane % T;
+                if (row0 + r < P.n_out) P.y[((long long)slot * T + t) * P.n_out + row0 + r] = 0.f;
+            }
+            continue;
+        }
+        const uint8_t* rows[RW];
+#pragma unroll
+        for (int r = 0; r < RW; ++r) rows[r] = base + (long long)min(row0 + r, P.n_out - 1) * P.row_bytes;
+        Tok<T> tk;
+#pragma unroll
+        for (int t = 0; t < T; ++t) tk.tb[t] = (long long)(slot / P.x_group + t) * P.n_in;
+        float acc[RW][T];
+#pragma unroll
+        for (int r = 0; r < RW; ++r)
+#pragma unroll
+            for (int t = 0; t < T; ++t) acc[r][t] = 0.f;
+        for (int sb = sb0; sb < n_sb; sb += 4) {
+            if constexpr (FMT == F_Q4_K) lane_q4k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+            else if constexpr (FMT == F_Q6_K) lane_q6k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+            else if constexpr (FMT == F_Q4_0) lane_q4_0<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+            else if constexpr (FMT == F_Q8_0) lane_q8_0<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+            else if constexpr (FMT == F_TQ2_0) lane_tq2_0<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+            else lane_iq2xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, grid);
+        }
+        if constexpr (!SUMS) {
+#pragma unroll
+            for (int r = 0; r < RW; ++r)
+#pragma unroll
+                for (int t = 0; t < T; ++t) {
+                    const float v = warp_sum(acc[r][t]);
+                    if (lane == 0 && row0 + r < P.n_out)
+                        P.y[((long long)slot * T + t) * P.n_out + row0 + r] = v;
+                }
+        }
+    }
+}
+
+}  // namespace qmv

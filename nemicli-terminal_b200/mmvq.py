@@ -1,0 +1,150 @@
+"""Drop-in for the reference's int8 matvec module (ggufengine/mmvq.py): the same names, argument
+meaning and return shapes, computed by this package's sm_100a kernels through the C ABI.
+
+* `Eingang` — the two-stage int8 activation input (mmvq.py:825-849), one quantisation per input,
+  shared by every matrix that reads it.
+* `mv` — y = W x for up to MMVQ_BIS tokens per call (mmvq.py:852-865), in launches of SPALTEN tokens,
+  each weight byte read once per launch.
+* `mm` — the reference's 17..112-token entry (mmvq.py:902-918); here the same int8 kernels in groups
+  of SPALTEN tokens (the tensor-core tile path for long inputs is a separate, later kernel).
+
+Where the reference takes Q4_K and Q6_K only, these kernels take all six block formats of the path
+(Q4_0, Q8_0, Q4_K, Q6_K, TQ2_0, IQ2_XXS).  Everything runs on torch's current stream and is CUDA-graph
+safe (no host reads, no synchronisation).  Non-CUDA tensors or unsupported formats raise; nothing
+falls back to another implementation.
+"""
+from __future__ import annotations
+
+import contextlib
+import threading
+from typing import Optional
+
+import torch
+
+from . import _lib
+from .formats import FORMATS, TYPE_ID
+
+FORMATE = dict(FORMATS)                 # name -> (values per block, bytes per block)
+SPALTEN = 8                             # tokens per kernel launch (weights read once for all of them)
+MMVQ_BIS = {f: 16 for f in FORMATE}     # up to this many tokens: mv (reference mmvq.py:32)
+MMQ_BIS = {f: 112 for f in FORMATE}     # up to this many tokens: mm (reference mmvq.py:33)
+
+
+def verfuegbar(device, fmt: str, n_in: int) -> bool:
+    """Kernels for this format and row length on this device (reference mmvq.py:808-810)."""
+    device = torch.device(device)
+    if device.type != "cuda" or fmt not in FORMATE:
+        return False
+    return bool(_lib.load().qmv_supported(TYPE_ID[fmt], int(n_in)))
+
+
+def _need_cuda(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{what}: tensor on {t.device}; the quantized matvec path runs on CUDA only")
+
+
+class Eingang:
+    """The int8 input of a vector — quantised once, read by every matrix that takes it
+    (reference mmvq.py:825-849).  Without x only the buffers (a fused producer fills them)."""
+
+    def __init__(self, x: Optional[torch.Tensor] = None, n: int = 0, device=None):
+        if x is not None:
+            _need_cuda(x, "Eingang")
+            x = x.reshape(-1)
+            if x.dtype != torch.float32:
+                x = x.to(torch.bfloat16)
+            x = x.contiguous()
+            n, device = x.numel(), x.device
+        if n % 32:
+            raise ValueError(f"Eingang: {n} values is not a multiple of 32")
+        self.n = n
+        self.xq = torch.empty(n, dtype=torch.int8, device=device)
+        self.xq2 = torch.empty(n, dtype=torch.int8, device=device)          # remainder, scale xd / 254
+        self.xd = torch.empty(n // 32, dtype=torch.float32, device=device)
+        self.xs = torch.empty(n // 32, dtype=torch.float32, device=device)
+        if x is not None:
+            _lib.check(_lib.load().qmv_quant_q8(_lib.ptr(x), int(x.dtype == torch.float32), *self.zeiger(), n,
+                                                _lib.stream_ptr(x.device)), "qmv_quant_q8")
+
+    def zeiger(self, ab: int = 0) -> list:
+        """Pointers to xq, xq2, xd, xs from value `ab` on (the start of a row)."""
+        if not ab:
+            return [_lib.ptr(self.xq), _lib.ptr(self.xq2), _lib.ptr(self.xd), _lib.ptr(self.xs)]
+        return [_lib.ptr(self.xq[ab:]), _lib.ptr(self.xq2[ab:]), _lib.ptr(self.xd[ab // 32:]),
+                _lib.ptr(self.xs[ab // 32:])]
+
+
+def _check_raw(fmt: str, raw: torch.Tensor, n_out: int, n_in: int) -> None:
+    _need_cuda(raw, f"mv {fmt}")
+    if fmt not in FORMATE:
+        raise RuntimeError(f"format {fmt} has no kernel in this path")
+    bv, bb = FORMATE[fmt]
+    if n_in % bv:
+        raise RuntimeError(f"{fmt}: n_in {n_in} is not a multiple of {bv}")
+    if raw.dtype != torch.uint8 or raw.numel() < n_out * (n_in // bv) * bb or not raw.is_contiguous():
+        raise RuntimeError(f"{fmt}: raw must be contiguous uint8 with {n_out * (n_in // bv) * bb} bytes")
+
+
+def mv(fmt: str, raw: torch.Tensor, x, n_out: int, n_in: int) -> torch.Tensor:
+    """raw: (n_out, n_in) in block format on the GPU; x: (M, n_in) or (n_in,) bf16/float32, or an
+    Eingang with M rows -> (M, n_out) float32, or (n_out,) for a vector."""
+    _check_raw(fmt, raw, n_out, n_in)
+    e = x if isinstance(x, Eingang) else Eingang(x)
+    if e.n % n_in:
+        raise RuntimeError(f"mv: input of {e.n} values is not a whole number of rows of {n_in}")
+    M = e.n // n_in
+    y = torch.empty(M, n_out, dtype=torch.float32, device=raw.device)
+    _lib.check(_lib.load().qmv_mv(TYPE_ID[fmt], _lib.ptr(raw), n_out, n_in, *e.zeiger(), M, _lib.ptr(y),
+                                  _lib.stream_ptr(raw.device)), f"qmv_mv {fmt}")
+    vektor = M == 1 if isinstance(x, Eingang) else x.dim() == 1
+    return y[0] if vektor else y
+
+
+_TEILEN = threading.local()
+
+
+@contextlib.contextmanager
+def eingang_teilen():
+    """Matrices with the same input (q/k/v, gate/up): inside this block an input tensor is quantised
+    once (reference mmvq.py:871-879)."""
+    alt = getattr(_TEILEN, "werte", None)
+    _TEILEN.werte = {}
+    try:
+        yield
+    finally:
+        _TEILEN.werte = alt
+
+
+def _eingang(x2: torch.Tensor) -> Eingang:
+    geteilt = getattr(_TEILEN, "werte", None)
+    schluessel = (x2.data_ptr(), tuple(x2.shape), x2.dtype)
+    if geteilt is not None and schluessel in geteilt:
+        return geteilt[schluessel][0]
+    e = Eingang(x2)
+    if geteilt is not None:
+        geteilt[schluessel] = (e, x2)          # keep x2 alive while its address is a key
+    return e
+
+
+def mm(fmt: str, raw: torch.Tensor, x: torch.Tensor, n_out: int, n_in: int) -> torch.Tensor:
+    """Several tokens: x (M, n_in) -> (M, n_out) float32 (reference mmvq.py:902-918)."""
+    _check_raw(fmt, raw, n_out, n_in)
+    x2 = x.reshape(-1, n_in)
+    e = _eingang(x2)
+    M = x2.shape[0]
+    y = torch.empty(M, n_out, dtype=torch.float32, device=raw.device)
+    _lib.check(_lib.load().qmv_mv(TYPE_ID[fmt], _lib.ptr(raw), n_out, n_in, *e.zeiger(), M, _lib.ptr(y),
+                                  _lib.stream_ptr(raw.device)), f"qmv_mv {fmt}")
+    return y
+
+
+def block_sums(fmt: str, raw: torch.Tensor, e: Eingang, n_out: int, n_in: int):
+    """Test hook: the int32 sums (code*xq, code*xq2) per row and unit of one token (include/nemicli_qmv.h)."""
+    _check_raw(fmt, raw, n_out, n_in)
+    unit = 16 if fmt == "Q6_K" else 32
+    s = torch.empty(n_out, n_in // unit, dtype=torch.int32, device=raw.device)
+    s2 = torch.empty_like(s)
+    _lib.check(_lib.load().qmv_block_sums(TYPE_ID[fmt], _lib.ptr(raw), n_out, n_in, _lib.ptr(e.xq), _lib.ptr(e.xq2),
+                                          _lib.ptr(s), _lib.ptr(s2), _lib.stream_ptr(raw.device)),
+               f"qmv_block_sums {fmt}")
+    return s, s2

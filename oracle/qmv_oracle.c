@@ -1,0 +1,360 @@
+/*
+ * TEST INFRASTRUCTURE ONLY — the CPU oracle for the quantized matvec hot path.
+ *
+ * Only tests/, __graft_entry__.smoke() and bench.py (its cpu_baseline leg and `--impl reference`)
+ * may load this library, and only as the checker or the timed CPU baseline.  The product path
+ * (nemicli-terminal_b200/) never calls it and fails loudly without its CUDA library.
+ *
+ * What it restates (paths relative to the reference checkout):
+ *   - activation quantisation into the two-stage int8 input ("Eingang"): ggufengine/mmvq.py:59-74
+ *     (quant32) and :77-83 (quant_q8).  The reference compiles it with --use_fast_math; this
+ *     restatement uses IEEE-rounded division and an explicit fused multiply-add so that it is
+ *     reproducible bit for bit on the GPU (the kernels do the same).  Against the reference's
+ *     fast-math build a quantised value can differ by one unit on a rounding tie.
+ *   - the block dequantisers of ggufengine/quant.py for the six in-scope formats:
+ *     deq_q4_0 :60, deq_q8_0 :46, deq_q4_k :111 (+ _scale_min_k4 :99), deq_q6_k :140,
+ *     deq_tq2_0 :417, deq_iq2_xxs :235 (codebook ggufengine/iqtabellen.py:11).  The operation
+ *     order of each fp32 expression follows quant.py, so results are bit-identical.
+ *   - the integer dot products of the reference's int8 path (ggufengine/mmvq.py:341-419 for
+ *     Q4_K: per lane S = sum nibble*xq and S2 = sum nibble*xq2; :421-482 for Q6_K with signed
+ *     q-32), and the same formula family for Q4_0, Q8_0, TQ2_0 and IQ2_XXS (which the reference
+ *     only has as float kernels, ggufengine/cudakern.py:315,307,432,187).  Integer sums do not
+ *     depend on how a kernel groups them, so the per-unit sums below are the exact values any
+ *     correct kernel must produce from the same Eingang.
+ *
+ * Sum units (the values that share one weight scale and one activation scale):
+ *   Q4_K, Q4_0, Q8_0, TQ2_0, IQ2_XXS: 32 values (n_in/32 units per row); Q6_K: 16 values.
+ *   Q4_0 and TQ2_0 sums use the unsigned code (the -8 / -1 offset is applied with xs).
+ *
+ * Parity pins: the dequantisers are pinned to golden vectors generated from the reference's own
+ * quant.dequantize (tests/golden/make_golden.py); the quantiser is pinned to the reference test's
+ * invariants (tests/test_mmvq.py:123-127 there: xq*xd ~ x, + xq2*xd/254 ~ x, xs = sum x) and to
+ * the formula; the integer path is pinned by an exact fp64 identity against the dequantised
+ * weights.  No reference artefact pins the int32 sums themselves (the reference tests compare
+ * floats only).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+enum { T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14, T_IQ2_XXS = 16, T_TQ2_0 = 35 };
+
+static const uint16_t IQ2XXS_CODES[256] = {
+#include "../nemicli-terminal_b200/csrc/iq2xxs_grid.inc"
+};
+static const uint8_t IQ2XXS_LEVELS[3] = {8, 25, 43};
+
+/* ---- scalars -------------------------------------------------------------------------------- */
+
+static float f16(const uint8_t* p) {
+    /* IEEE binary16 (little endian) -> binary32, exact */
+    uint32_t h = (uint32_t)p[0] | ((uint32_t)p[1] << 8);
+    uint32_t sign = (h & 0x8000u) << 16, exp = (h >> 10) & 0x1F, man = h & 0x3FF, bits;
+    if (exp == 0) {
+        if (man == 0) {
+            bits = sign;
+        } else {                                  /* subnormal: renormalise */
+            int e = -1;
+            do { man <<= 1; ++e; } while (!(man & 0x400));
+            bits = sign | ((uint32_t)(127 - 15 - e) << 23) | ((man & 0x3FF) << 13);
+        }
+    } else if (exp == 31) {
+        bits = sign | 0x7F800000u | (man << 13);
+    } else {
+        bits = sign | ((exp + 112) << 23) | (man << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+static float bf16(uint16_t u) {
+    uint32_t bits = (uint32_t)u << 16;
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+static uint32_t rd32(const uint8_t* p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+
+int orc_block_values(int fmt) {
+    switch (fmt) {
+    case T_Q4_0: case T_Q8_0: return 32;
+    case T_Q4_K: case T_Q6_K: case T_IQ2_XXS: case T_TQ2_0: return 256;
+    }
+    return 0;
+}
+
+int orc_block_bytes(int fmt) {
+    switch (fmt) {
+    case T_Q4_0: return 18;
+    case T_Q8_0: return 34;
+    case T_Q4_K: return 144;
+    case T_Q6_K: return 210;
+    case T_IQ2_XXS: return 66;
+    case T_TQ2_0: return 66;
+    }
+    return 0;
+}
+
+/* values per integer-sum unit */
+int orc_unit_values(int fmt) { return fmt == T_Q6_K ? 16 : 32; }
+
+/* ---- activation quantisation (mmvq.py:59-83) ----------------------------------------------- */
+
+/* Sum of 32 values in the order of a warp butterfly (xor 16, 8, 4, 2, 1): the order the GPU uses. */
+static float butterfly_sum32(const float* v) {
+    float a[16], b[8], c[4], d[2];
+    for (int i = 0; i < 16; ++i) a[i] = v[i] + v[i + 16];
+    for (int i = 0; i < 8; ++i) b[i] = a[i] + a[i + 8];
+    for (int i = 0; i < 4; ++i) c[i] = b[i] + b[i + 4];
+    for (int i = 0; i < 2; ++i) d[i] = c[i] + c[i + 2];
+    return d[0] + d[1];
+}
+
+static int clamp127(int v) { return v < -127 ? -127 : (v > 127 ? 127 : v); }
+
+/* x: n values, fp32 (x_is_f32) or bf16; n % 32 == 0 */
+void orc_quant_q8(const void* x, int x_is_f32, long long n, int8_t* xq, int8_t* xq2, float* xd, float* xs) {
+    for (long long g = 0; g < n / 32; ++g) {
+        float v[32], amax = 0.f;
+        for (int i = 0; i < 32; ++i) {
+            v[i] = x_is_f32 ? ((const float*)x)[32 * g + i] : bf16(((const uint16_t*)x)[32 * g + i]);
+            float a = fabsf(v[i]);
+            amax = a > amax ? a : amax;
+        }
+        const float d = amax / 127.0f;
+        const float d2 = d / 254.0f;
+        for (int i = 0; i < 32; ++i) {
+            int q = 0, q2 = 0;
+            if (d > 0.f) {
+                q = (int)rintf(v[i] / d);
+                const float r = fmaf(-(float)q, d, v[i]);
+                q2 = clamp127((int)rintf(r / d2));
+            }
+            xq[32 * g + i] = (int8_t)q;
+            xq2[32 * g + i] = (int8_t)q2;
+        }
+        xd[g] = d;
+        xs[g] = butterfly_sum32(v);
+    }
+}
+
+/* ---- dequantisation (quant.py) ------------------------------------------------------------- */
+
+static void scale_min_k4(const uint8_t* s, int* sc, int* mn) {   /* quant.py:99-108 */
+    for (int j = 0; j < 4; ++j) {
+        sc[j] = s[j] & 63;
+        mn[j] = s[j + 4] & 63;
+        sc[j + 4] = (s[j + 8] & 15) | ((s[j] >> 6) << 4);
+        mn[j + 4] = (s[j + 8] >> 4) | ((s[j + 4] >> 6) << 4);
+    }
+}
+
+static void iq2xxs_entry(int idx, uint8_t out[8]) {
+    for (int j = 0; j < 8; ++j) out[j] = IQ2XXS_LEVELS[(IQ2XXS_CODES[idx] >> (2 * j)) & 3];
+}
+
+static uint32_t ksign8(uint32_t s7) {   /* 7 stored sign bits + parity as the 8th */
+    return s7 | ((uint32_t)(__builtin_popcount(s7) & 1) << 7);
+}
+
+/* signed value of element e (0..31) of sub-block ib of an IQ2_XXS block, without the scale */
+static int iq2xxs_value(const uint8_t* b, int ib, int e) {
+    const uint8_t* q = b + 2 + 8 * ib;
+    const uint32_t aux1 = rd32(q + 4);
+    const int l = e >> 3, j = e & 7;
+    uint8_t g[8];
+    iq2xxs_entry(q[l], g);
+    const uint32_t s = ksign8((aux1 >> (7 * l)) & 127);
+    return (s >> j) & 1 ? -(int)g[j] : (int)g[j];
+}
+
+int orc_dequant(int fmt, const uint8_t* raw, long long n_values, float* out) {
+    const int bv = orc_block_values(fmt), bb = orc_block_bytes(fmt);
+    if (!bv || n_values % bv) return 2;
+    for (long long blk = 0; blk < n_values / bv; ++blk) {
+        const uint8_t* b = raw + blk * bb;
+        float* o = out + blk * bv;
+        switch (fmt) {
+        case T_Q4_0: {
+            const float d = f16(b);
+            for (int i = 0; i < 16; ++i) {
+                o[i] = d * (float)((b[2 + i] & 15) - 8);
+                o[i + 16] = d * (float)((b[2 + i] >> 4) - 8);
+            }
+            break;
+        }
+        case T_Q8_0: {
+            const float d = f16(b);
+            for (int i = 0; i < 32; ++i) o[i] = d * (float)(int8_t)b[2 + i];
+            break;
+        }
+        case T_Q4_K: {
+            const float d = f16(b), dmin = f16(b + 2);
+            int sc[8], mn[8];
+            scale_min_k4(b + 4, sc, mn);
+            for (int j = 0; j < 8; ++j) {
+                const float a = d * (float)sc[j], m = dmin * (float)mn[j];
+                for (int i = 0; i < 32; ++i) {
+                    const int q = (b[16 + 32 * (j >> 1) + i] >> (4 * (j & 1))) & 15;
+                    o[32 * j + i] = a * (float)q - m;
+                }
+            }
+            break;
+        }
+        case T_Q6_K: {
+            const uint8_t* ql = b;
+            const uint8_t* qh = b + 128;
+            const int8_t* sc = (const int8_t*)(b + 192);
+            const float d = f16(b + 208);
+            for (int n = 0; n < 2; ++n)
+                for (int g = 0; g < 4; ++g)
+                    for (int l = 0; l < 32; ++l) {
+                        const int q = ((ql[64 * n + 32 * (g & 1) + l] >> (4 * (g >> 1))) & 15)
+                                      | (((qh[32 * n + l] >> (2 * g)) & 3) << 4);
+                        o[128 * n + 32 * g + l] = d * (float)sc[8 * n + 2 * g + l / 16] * (float)(q - 32);
+                    }
+            break;
+        }
+        case T_TQ2_0: {
+            const float d = f16(b + 64);
+            for (int n = 0; n < 2; ++n)
+                for (int g = 0; g < 4; ++g)
+                    for (int m = 0; m < 32; ++m)
+                        o[128 * n + 32 * g + m] = d * (float)(((b[32 * n + m] >> (2 * g)) & 3) - 1);
+            break;
+        }
+        case T_IQ2_XXS: {
+            const float d = f16(b);
+            for (int ib = 0; ib < 8; ++ib) {
+                const uint32_t aux1 = rd32(b + 2 + 8 * ib + 4);
+                const float db = d * (0.125f + 0.25f * (float)(aux1 >> 28));
+                for (int e = 0; e < 32; ++e) o[32 * ib + e] = (float)iq2xxs_value(b, ib, e) * db;
+            }
+            break;
+        }
+        default:
+            return 1;
+        }
+    }
+    return 0;
+}
+
+/* ---- integer sums and the epilogue --------------------------------------------------------- */
+
+/* integer weight code of value v (0 <= v < block values) of block b, as used by the dot product */
+static int code_of(int fmt, const uint8_t* b, int v) {
+    switch (fmt) {
+    case T_Q4_0: return v < 16 ? (b[2 + v] & 15) : (b[2 + v - 16] >> 4);
+    case T_Q8_0: return (int8_t)b[2 + v];
+    case T_Q4_K: { const int j = v >> 5, i = v & 31; return (b[16 + 32 * (j >> 1) + i] >> (4 * (j & 1))) & 15; }
+    case T_Q6_K: {
+        const int n = v >> 7, g = (v >> 5) & 3, l = v & 31;
+        const int q = ((b[64 * n + 32 * (g & 1) + l] >> (4 * (g >> 1))) & 15) | (((b[128 + 32 * n + l] >> (2 * g)) & 3) << 4);
+        return q - 32;
+    }
+    case T_TQ2_0: { const int n = v >> 7, g = (v >> 5) & 3, m = v & 31; return (b[32 * n + m] >> (2 * g)) & 3; }
+    case T_IQ2_XXS: return iq2xxs_value(b, v >> 5, v & 31);
+    }
+    return 0;
+}
+
+/* s, s2: [n_out][n_in / unit] int32 sums of code * xq and code * xq2 (one token) */
+int orc_block_sums(int fmt, const uint8_t* w, int n_out, int n_in, const int8_t* xq, const int8_t* xq2,
+                   int32_t* s, int32_t* s2) {
+    const int bv = orc_block_values(fmt), bb = orc_block_bytes(fmt), uv = orc_unit_values(fmt);
+    if (!bv || n_in % bv) return 2;
+    const long long row_bytes = (long long)(n_in / bv) * bb;
+    const int units = n_in / uv;
+    for (int r = 0; r < n_out; ++r)
+        for (int u = 0; u < units; ++u) {
+            int32_t a = 0, a2 = 0;
+            for (int i = 0; i < uv; ++i) {
+                const int v = u * uv + i;
+                const int c = code_of(fmt, w + r * row_bytes + (long long)(v / bv) * bb, v % bv);
+                a += c * xq[v];
+                a2 += c * xq2[v];
+            }
+            s[(long long)r * units + u] = a;
+            s2[(long long)r * units + u] = a2;
+        }
+    return 0;
+}
+
+/* weight scale (multiplies xd*(S + S2/254)) and offset (multiplies xs) of unit u of block b */
+static void unit_scales(int fmt, const uint8_t* b, int u, double* wscale, double* offs) {
+    switch (fmt) {
+    case T_Q4_0: *wscale = f16(b); *offs = 8.0 * f16(b); return;
+    case T_Q8_0: *wscale = f16(b); *offs = 0.0; return;
+    case T_Q4_K: {
+        int sc[8], mn[8];
+        scale_min_k4(b + 4, sc, mn);
+        *wscale = (double)f16(b) * sc[u];
+        *offs = (double)f16(b + 2) * mn[u];
+        return;
+    }
+    case T_Q6_K: *wscale = (double)f16(b + 208) * (double)(int8_t)b[192 + u]; *offs = 0.0; return;
+    case T_TQ2_0: *wscale = f16(b + 64); *offs = f16(b + 64); return;
+    case T_IQ2_XXS: {
+        const uint32_t aux1 = rd32(b + 2 + 8 * u + 4);
+        *wscale = (double)f16(b) * (0.125 + 0.25 * (double)(aux1 >> 28));
+        *offs = 0.0;
+        return;
+    }
+    }
+    *wscale = *offs = 0.0;
+}
+
+/*
+ * y[t][r] (fp64) of the integer path for n_tok tokens, from exact int32 sums:
+ *   sum over units u of  wscale_u * xd_g * (S_u + S2_u / 254) - offs_u * xs_g   (g: 32-value group of u;
+ *   the offset term is applied once per 32-value group)
+ * n_threads > 0 parallelises over rows with OpenMP.
+ */
+int orc_mv(int fmt, const uint8_t* w, int n_out, int n_in, const int8_t* xq, const int8_t* xq2,
+           const float* xd, const float* xs, int n_tok, double* y, int n_threads) {
+    const int bv = orc_block_values(fmt), bb = orc_block_bytes(fmt), uv = orc_unit_values(fmt);
+    if (!bv || n_in % bv) return 2;
+    const long long row_bytes = (long long)(n_in / bv) * bb;
+    const int upb = bv / uv;   /* units per block */
+#ifdef _OPENMP
+    if (n_threads > 0) omp_set_num_threads(n_threads);
+#pragma omp parallel for schedule(static) if (n_threads > 1)
+#endif
+    for (int r = 0; r < n_out; ++r) {
+        for (int t = 0; t < n_tok; ++t) {
+            const int8_t* q = xq + (long long)t * n_in;
+            const int8_t* q2 = xq2 + (long long)t * n_in;
+            const float* dd = xd + (long long)t * (n_in / 32);
+            const float* ss = xs + (long long)t * (n_in / 32);
+            double acc = 0.0;
+            for (int blk = 0; blk < n_in / bv; ++blk) {
+                const uint8_t* b = w + r * row_bytes + (long long)blk * bb;
+                for (int ub = 0; ub < upb; ++ub) {
+                    int32_t a = 0, a2 = 0;
+                    const int v0 = blk * bv + ub * uv;
+                    for (int i = 0; i < uv; ++i) {
+                        const int c = code_of(fmt, b, ub * uv + i);
+                        a += c * q[v0 + i];
+                        a2 += c * q2[v0 + i];
+                    }
+                    double wscale, offs;
+                    unit_scales(fmt, b, ub, &wscale, &offs);
+                    const int g = v0 / 32;
+                    acc += wscale * (double)dd[g] * ((double)a + (double)a2 / 254.0);
+                    if (v0 % 32 == 0) acc -= offs * (double)ss[g];
+                }
+            }
+            y[(long long)t * n_out + r] = acc;
+        }
+    }
+    return 0;
+}
+
+int orc_version(void) { return 1; }

@@ -1,0 +1,25 @@
+"""pytest setup: the `gpu` marker and import paths.
+
+Tests marked `gpu` need a CUDA device and the built CUDA library; the rest run on any CPU box.
+The oracle (oracle/) is test infrastructure and is only imported here as the checker.
+"""
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200) and the built CUDA library")
+
+
+@pytest.fixture(scope="session")
+def cuda():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda", 0)

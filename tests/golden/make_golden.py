@@ -1,0 +1,99 @@
+"""Generates tests/golden/dequant_golden.npz from the reference engine's own dequantiser.
+
+Run once where the reference checkout is available (it does not travel to the GPU box):
+
+    python tests/golden/make_golden.py <reference root>
+
+For each in-scope format it stores seeded raw GGUF blocks, the reference's
+ggufengine.quant.dequantize output for them (fp32), a seeded fp32 activation and the fp64 product
+dequant @ x.  Scale fields are set to small finite fp16 values (the pattern of the reference's
+tests/test_gguf_iq.py:81-101, zufallsbloecke).  Extra cases pin the corners:
+
+* IQ2_XXS blocks whose grid indices run through all 256 codebook entries and whose sign indices
+  run through all 128 patterns,
+* TQ2_0 blocks with every 2-bit code, including the never-drawn code 3,
+* Q4_K blocks with 6-bit scales and mins at 0 and 63.
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+FORMATS = {"Q4_0": (2, 32, 18), "Q8_0": (8, 32, 34), "Q4_K": (12, 256, 144), "Q6_K": (14, 256, 210),
+           "IQ2_XXS": (16, 256, 66), "TQ2_0": (35, 256, 66)}
+SCALE_OFFSETS = {"Q4_0": (0,), "Q8_0": (0,), "Q4_K": (0, 2), "Q6_K": (208,), "IQ2_XXS": (0,), "TQ2_0": (64,)}
+ROWS, COLS = 3, 512          # a (3, 512) matrix per format
+
+
+def random_blocks(name: str, n_blocks: int, rng: np.random.Generator) -> np.ndarray:
+    _, _, size = FORMATS[name]
+    raw = rng.integers(0, 256, (n_blocks, size), dtype=np.uint8)
+    for o in SCALE_OFFSETS[name]:
+        d = (rng.random(n_blocks) * 0.01 + 0.001).astype(np.float16)
+        raw[:, o:o + 2] = d.view(np.uint8).reshape(n_blocks, 2)
+    return raw
+
+
+def iq2xxs_cover(rng: np.random.Generator) -> np.ndarray:
+    """8 blocks = 64 sub-blocks = 256 grid slots: grid index k at slot k; sign index k % 128."""
+    raw = random_blocks("IQ2_XXS", 8, rng)
+    for sb in range(64):
+        blk, ib = divmod(sb, 8)
+        o = 2 + 8 * ib
+        idx = [4 * sb + l for l in range(4)]
+        raw[blk, o:o + 4] = np.array(idx, dtype=np.uint8)
+        signs = [(4 * sb + l) % 128 for l in range(4)]
+        aux1 = signs[0] | (signs[1] << 7) | (signs[2] << 14) | (signs[3] << 21) | ((sb % 16) << 28)
+        raw[blk, o + 4:o + 8] = np.frombuffer(np.uint32(aux1).tobytes(), dtype=np.uint8)
+    return raw
+
+
+def tq2_cover(rng: np.random.Generator) -> np.ndarray:
+    raw = random_blocks("TQ2_0", 2, rng)
+    raw[:, :64] = np.arange(128, dtype=np.uint8).reshape(2, 64) * 2 + 1    # mixes all 2-bit codes
+    raw[0, :4] = 0xFF                                                       # code 3 everywhere
+    return raw
+
+
+def q4k_cover(rng: np.random.Generator) -> np.ndarray:
+    raw = random_blocks("Q4_K", 2, rng)
+    raw[0, 4:16] = 0xFF        # every 6-bit scale and min = 63
+    raw[1, 4:16] = 0x00        # every 6-bit scale and min = 0
+    return raw
+
+
+def main(ref_root: str) -> None:
+    sys.path.insert(0, ref_root)
+    import torch
+    from ggufengine.quant import dequantize      # the reference's dequantiser (ggufengine/quant.py:484)
+
+    rng = np.random.default_rng(20260101)
+    out = {}
+
+    def add(key: str, name: str, raw: np.ndarray, rows: int, cols: int) -> None:
+        t, bv, bb = FORMATS[name]
+        flat = np.ascontiguousarray(raw.reshape(-1))
+        assert flat.size == rows * cols // bv * bb
+        deq = dequantize(torch.from_numpy(flat.copy()), t, rows * cols, torch.float32).numpy()
+        x = rng.standard_normal((2, cols)).astype(np.float32)
+        y = x.astype(np.float64) @ deq.reshape(rows, cols).astype(np.float64).T
+        out[f"{key}__raw"] = flat
+        out[f"{key}__deq"] = deq.astype(np.float32)
+        out[f"{key}__x"] = x
+        out[f"{key}__y"] = y
+        out[f"{key}__shape"] = np.array([FORMATS[name][0], rows, cols], dtype=np.int64)
+
+    for name, (_, bv, _) in FORMATS.items():
+        add(name, name, random_blocks(name, ROWS * COLS // bv, rng), ROWS, COLS)
+    add("IQ2_XXS_cover", "IQ2_XXS", iq2xxs_cover(rng), 8, 256)
+    add("TQ2_0_cover", "TQ2_0", tq2_cover(rng), 2, 256)
+    add("Q4_K_cover", "Q4_K", q4k_cover(rng), 2, 256)
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "dequant_golden.npz")
+    np.savez_compressed(path, **out)
+    print(f"wrote {path}: {len(out)} arrays")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("NEMICLI_REFERENCE", ""))

@@ -1,0 +1,76 @@
+"""The C-ABI library: it loads without a GPU, exports every symbol include/nemicli_qmv.h declares,
+and refuses bad arguments before any CUDA work (no compute calls here)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from nemicli_terminal_b200 import _lib
+from nemicli_terminal_b200.formats import FORMATS, TYPE_ID
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "nemicli_qmv.h")
+
+
+def declared():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\**(qmv_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_the_bound_symbols():
+    assert declared() == sorted(_lib.exported_symbols())
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.load()
+    for name in declared():
+        assert hasattr(L, name), name
+
+
+def test_abi_and_status_strings():
+    L = _lib.load()
+    assert L.qmv_abi_version() == _lib.ABI_VERSION
+    for st in range(8):
+        assert L.qmv_status_string(st)
+    assert L.qmv_status_string(0) == b"ok"
+
+
+@pytest.mark.parametrize("fmt", list(FORMATS))
+def test_block_geometry_matches_format_table(fmt):
+    L = _lib.load()
+    bv, bb = FORMATS[fmt]
+    assert L.qmv_block_values(TYPE_ID[fmt]) == bv
+    assert L.qmv_block_bytes(TYPE_ID[fmt]) == bb
+    assert L.qmv_supported(TYPE_ID[fmt], bv * 3) == 1
+    assert L.qmv_supported(TYPE_ID[fmt], bv * 3 + 16) == 0
+    assert L.qmv_supported(TYPE_ID[fmt], 0) == 0
+
+
+def test_unknown_formats_are_refused():
+    L = _lib.load()
+    for t in (0, 1, 3, 10, 13, 23, 39):
+        assert L.qmv_supported(t, 4096) == 0
+        assert L.qmv_block_values(t) == 0
+    st = L.qmv_mv(13, ctypes.c_void_p(16), 1, 256, ctypes.c_void_p(16), ctypes.c_void_p(16),
+                  ctypes.c_void_p(16), ctypes.c_void_p(16), 1, ctypes.c_void_p(16), None)
+    assert st == 1
+
+
+def test_argument_checks_precede_any_launch():
+    L = _lib.load()
+    a = ctypes.c_void_p(4096)           # never dereferenced: every call below is refused first
+    Q4K = TYPE_ID["Q4_K"]
+    assert L.qmv_mv(Q4K, None, 1, 256, a, a, a, a, 1, a, None) == 6                 # null
+    assert L.qmv_mv(Q4K, a, 0, 256, a, a, a, a, 1, a, None) == 2                    # n_out
+    assert L.qmv_mv(Q4K, a, 4, 100, a, a, a, a, 1, a, None) == 2                    # n_in
+    assert L.qmv_mv(Q4K, a, 4, 256, a, a, a, a, 0, a, None) == 4                    # tokens
+    assert L.qmv_mv(Q4K, ctypes.c_void_p(4098), 4, 256, a, a, a, a, 1, a, None) == 3   # Q4_K wants 16 B
+    assert L.qmv_mv(Q4K, a, 4, 256, ctypes.c_void_p(4097), a, a, a, 1, a, None) == 3   # xq alignment
+    assert L.qmv_mv_experts(Q4K, a, 144, 4, None, 1, a, a, a, a, 1, a, 1, 256, None) == 6
+    assert L.qmv_mv_experts(Q4K, a, 144, 4, a, 0, a, a, a, a, 1, a, 1, 256, None) == 4
+    assert L.qmv_mv_experts(Q4K, a, 144, 0, a, 1, a, a, a, a, 1, a, 1, 256, None) == 2
+    assert L.qmv_mv_experts(Q4K, a, 100, 4, a, 1, a, a, a, a, 1, a, 1, 256, None) == 2   # expert too small
+    assert L.qmv_mv_experts(Q4K, a, 144, 4, a, 1, a, a, a, a, 0, a, 1, 256, None) == 2   # x_group
+    assert L.qmv_quant_q8(a, 1, a, a, a, a, 33, None) == 2
+    assert L.qmv_quant_q8(None, 1, a, a, a, a, 32, None) == 6
+    assert L.qmv_block_sums(Q4K, a, 4, 300, a, a, a, a, None) == 2
