@@ -78,6 +78,28 @@ int qmv_mv_experts(int ggml_type, const void* raw, long long per_expert, long lo
                    int k, const int8_t* xq, const int8_t* xq2, const float* xd, const float* xs,
                    int x_group, float* y, int n_out, int n_in, void* stream);
 
+/* Several matrices reading the same single-token input in one launch (q/k/v, gate/up): for j < n_jobs
+ * (at most 4), y[j][r] = W_j[r, :] . x.  w, n_out, y: host arrays of n_jobs entries (device pointers).
+ * Replaces: the separate mmvq.mv calls the reference makes for matrices sharing an Eingang
+ * (ggufengine/models/baukasten.py:222-240, _mal per matrix). */
+int qmv_mv_multi(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
+                 const int8_t* xq, const int8_t* xq2, const float* xd, const float* xs, void* stream);
+
+/* Single token, raw activation: like qmv_mv_multi, but x (n_in values, fp32 if x_is_f32 else bf16) is
+ * quantised inside the kernel (the same arithmetic as qmv_quant_q8), so no activation buffers and no
+ * separate launch are needed.  Returns QMV_ERR_SHAPE for a row length the staged kernel does not take
+ * (then quantise with qmv_quant_q8 and call qmv_mv).  Replaces: Eingang(x) + mv in one call
+ * (ggufengine/mmvq.py:829-865), as PackedLinear._rechnen does for one token (models/common.py:404-405). */
+int qmv_mv_x(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
+             const void* x, int x_is_f32, void* stream);
+
+/* Programmatic dependent launch for the staged single-token kernels (default off): when on, each such
+ * kernel lets the next kernel of the stream start early and streams its weights before the previous
+ * kernel has finished; its inputs are read only after the previous kernel completed.  Turn it on only
+ * when no kernel launched right before a matvec writes that matvec's weights.  Returns the old value.
+ * Replaces: nothing in the reference (its decoder relies on plain stream order, models/common.py:1185). */
+int qmv_set_pdl(int enabled);
+
 /* Test hook: the int32 sums of one token per (row, unit), unit = the values sharing one weight scale
  * and one activation scale (16 for Q6_K, else 32): s = sum code * xq, s2 = sum code * xq2, from the
  * same device code as qmv_mv.  s, s2: int32[n_out][n_in / unit], overwritten.

@@ -29,6 +29,9 @@ _SIGNATURES = {
     "qmv_mv": ([I, P, I, I, P, P, P, P, I, P, P], I),
     "qmv_mv_experts": ([I, P, LL, LL, P, I, P, P, P, P, I, P, I, I, P], I),
     "qmv_block_sums": ([I, P, I, I, P, P, P, P, P], I),
+    "qmv_mv_multi": ([I, I, P, P, P, I, P, P, P, P, P], I),
+    "qmv_mv_x": ([I, I, P, P, P, I, P, I, P], I),
+    "qmv_set_pdl": ([I], I),
     "qmv_device_status": ([I, P, P], I),
 }
 

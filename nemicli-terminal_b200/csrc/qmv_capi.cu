@@ -1,8 +1,10 @@
 // C ABI of the quantized matvec path (declarations and contracts: include/nemicli_qmv.h).
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "qmv_kernels.cuh"
+#include "qmv_tma.cuh"
 #include "../../include/nemicli_qmv.h"
 
 using namespace qmv;
@@ -82,6 +84,7 @@ int launch_fmt(const MvParams& P, int T, cudaStream_t st) {
 }
 
 int launch(int fmt, const MvParams& P, int T, cudaStream_t st) {
+    if (P.x_group < 1 || P.slots < 1) return ST_BAD_SHAPE;
     switch (fmt) {
     case F_Q4_0: return launch_fmt<F_Q4_0>(P, T, st);
     case F_Q8_0: return launch_fmt<F_Q8_0>(P, T, st);
@@ -94,6 +97,7 @@ int launch(int fmt, const MvParams& P, int T, cudaStream_t st) {
 }
 
 int launch_sums(int fmt, const MvParams& P, cudaStream_t st) {
+    if (P.x_group != 1 || P.slots != 1) return ST_BAD_SHAPE;
     switch (fmt) {
     case F_Q4_0: return launch_t<F_Q4_0, 1, true>(P, st);
     case F_Q8_0: return launch_t<F_Q8_0, 1, true>(P, st);
@@ -103,6 +107,167 @@ int launch_sums(int fmt, const MvParams& P, cudaStream_t st) {
     case F_TQ2_0: return launch_t<F_TQ2_0, 1, true>(P, st);
     }
     return ST_BAD_FORMAT;
+}
+
+
+// ---- TMA-staged single-token path ------------------------------------------------------------------
+
+constexpr int kSmemCap = 232448;          // dynamic shared memory per block on sm_100a (227 KB)
+constexpr int kSmemHalf = 113 * 1024;     // two CTAs per SM (the next kernel's CTA can prefetch alongside)
+int g_pdl = 0;                            // programmatic dependent launch (qmv_set_pdl)
+
+struct TmaPlan {
+    int NCW, G, UPL, R, S, smem;
+};
+
+__host__ __device__ constexpr int unit_vals(int fmt) { return fmt == F_Q4_K ? 64 : 32; }
+
+// Tuning knobs read once from the environment (benchmark sweeps): NEMICLI_QMV_TMA=0 sends every call
+// to the fallback kernel, NEMICLI_QMV_TMA_G forces the team width (16..512) where it fits.
+struct TmaKnobs {
+    int enabled = 1, force_g = 0, ncw = 16;
+    TmaKnobs() {
+        if (const char* e = std::getenv("NEMICLI_QMV_TMA")) enabled = std::atoi(e) != 0;
+        if (const char* g = std::getenv("NEMICLI_QMV_TMA_G")) force_g = std::atoi(g);
+        if (const char* n = std::getenv("NEMICLI_QMV_NCW")) ncw = std::atoi(n) == 8 ? 8 : 16;
+    }
+};
+const TmaKnobs& knobs() {
+    static const TmaKnobs k;
+    return k;
+}
+
+// Team width G (lanes per row), units per lane, rows per tile R = 4 rows per team (fewer when a stage
+// would not fit twice), stages S; false if the shape needs the fallback kernel.  One unit per lane
+// when a team of <= 512 lanes covers the row; fused quantisation reserves 2.25 * n_in bytes.
+bool tma_plan(int fmt, int n_in, long long row_bytes, bool fused, TmaPlan& pl) {
+    if (!knobs().enabled || row_bytes % 16 || n_in % unit_vals(fmt)) return false;
+    const int ncw = knobs().ncw;
+    const int cap = ncw <= 8 ? kSmemHalf : kSmemCap;
+    const int U = n_in / unit_vals(fmt);
+    int G = 16;
+    while (G < U && G < 32 * ncw) G *= 2;
+    const int f = knobs().force_g;
+    if (f >= 16 && f <= 32 * ncw && (f & (f - 1)) == 0 && 2 * f >= U) G = f;
+    const int UPL = (U + G - 1) / G;
+    if (UPL > 2) return false;
+    const int teams = 32 * ncw / G;
+    const long long other = tma_red_bytes(ncw) + 2048 + (fused ? tma_act_bytes(n_in) : 0) + 2 * 8 * 32;
+    long long R = (long long)kTmaRowsPerTeam * teams;
+    while (R > 1 && 2 * R * row_bytes > cap - other) R = R > teams ? R - teams : R / 2;
+    const long long stage = R * row_bytes;
+    long long S = (cap - other) / stage;
+    if (S > 32) S = 32;
+    if (S < 2) return false;
+    pl.NCW = ncw;
+    pl.G = G;
+    pl.UPL = UPL;
+    pl.R = int(R);
+    pl.S = int(S);
+    pl.smem = int(S * stage + other);
+    return true;
+}
+
+template <int FMT, int NCW, int G, int UPL, int XF, bool SUMS>
+int launch_tma_k(const TmaParams& P, int grid, int smem, cudaStream_t st) {
+    auto kern = mv_tma_kernel<FMT, NCW, G, UPL, XF, SUMS>;
+    static int configured[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap) != cudaSuccess)
+            return launched();
+        configured[dev] = 1;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(32 * (NCW + 1));
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = (g_pdl && !SUMS) ? 1 : 0;
+    if (cudaLaunchKernelEx(&cfg, kern, P) != cudaSuccess) return launched();
+    return launched();
+}
+
+template <int FMT, int NCW, int XF, bool SUMS>
+int launch_tma_g(const TmaParams& P, const TmaPlan& pl, int grid, cudaStream_t st) {
+    switch (pl.G) {
+    case 16: return launch_tma_k<FMT, NCW, 16, 1, XF, SUMS>(P, grid, pl.smem, st);
+    case 32: return launch_tma_k<FMT, NCW, 32, 1, XF, SUMS>(P, grid, pl.smem, st);
+    case 64: return launch_tma_k<FMT, NCW, 64, 1, XF, SUMS>(P, grid, pl.smem, st);
+    case 128: return launch_tma_k<FMT, NCW, 128, 1, XF, SUMS>(P, grid, pl.smem, st);
+    case 256:
+        return pl.UPL == 1 ? launch_tma_k<FMT, NCW, 256, 1, XF, SUMS>(P, grid, pl.smem, st)
+                           : launch_tma_k<FMT, NCW, 256, 2, XF, SUMS>(P, grid, pl.smem, st);
+    case 512:
+        if constexpr (NCW >= 16)
+            return pl.UPL == 1 ? launch_tma_k<FMT, NCW, 512, 1, XF, SUMS>(P, grid, pl.smem, st)
+                               : launch_tma_k<FMT, NCW, 512, 2, XF, SUMS>(P, grid, pl.smem, st);
+    }
+    return ST_BAD_SHAPE;
+}
+
+template <int FMT, int XF, bool SUMS>
+int launch_tma_fmt(const TmaParams& P, const TmaPlan& pl, int grid, cudaStream_t st) {
+    return pl.NCW == 16 ? launch_tma_g<FMT, 16, XF, SUMS>(P, pl, grid, st) : launch_tma_g<FMT, 8, XF, SUMS>(P, pl, grid, st);
+}
+
+template <int XF, bool SUMS>
+int launch_tma(int fmt, TmaParams& P, const TmaPlan& pl, cudaStream_t st) {
+    P.rows_per_tile = pl.R;
+    P.stages = pl.S;
+    P.status = device_status_ptr();
+    long long grid = sm_count();
+    if (grid > P.total_rows) grid = P.total_rows;
+    if (grid < 1) return ST_OK;
+    switch (fmt) {
+    case F_Q4_0: return launch_tma_fmt<F_Q4_0, XF, SUMS>(P, pl, int(grid), st);
+    case F_Q8_0: return launch_tma_fmt<F_Q8_0, XF, SUMS>(P, pl, int(grid), st);
+    case F_Q4_K: return launch_tma_fmt<F_Q4_K, XF, SUMS>(P, pl, int(grid), st);
+    case F_Q6_K: return launch_tma_fmt<F_Q6_K, XF, SUMS>(P, pl, int(grid), st);
+    case F_IQ2_XXS: return launch_tma_fmt<F_IQ2_XXS, XF, SUMS>(P, pl, int(grid), st);
+    case F_TQ2_0: return launch_tma_fmt<F_TQ2_0, XF, SUMS>(P, pl, int(grid), st);
+    }
+    return ST_BAD_FORMAT;
+}
+
+// dense jobs sharing one activation row (n_jobs <= kMaxJobs): pre-quantised (x == nullptr) or raw x
+// (x_kind 1 = fp32, 2 = bf16) quantised in the kernel.  false -> the caller uses the fallback kernel.
+bool tma_dense(int fmt, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
+               const int8_t* xq, const int8_t* xq2, const float* xd, const float* xs, const void* x, int x_kind,
+               int32_t* s, int32_t* s2, cudaStream_t st, int* status) {
+    const long long row_bytes = (long long)(n_in / block_values(fmt)) * block_bytes(fmt);
+    TmaPlan pl;
+    if (!tma_plan(fmt, n_in, row_bytes, x != nullptr, pl)) return false;
+    for (int j = 0; j < n_jobs; ++j)
+        if (!aligned(w[j], 16)) return false;
+    TmaParams P{};
+    long long rows = 0;
+    for (int j = 0; j < n_jobs; ++j) {
+        P.w[j] = w[j];
+        P.y[j] = y ? y[j] : nullptr;
+        P.n_out[j] = n_out[j];
+        P.row_start[j] = rows;
+        rows += n_out[j];
+    }
+    P.row_start[n_jobs] = rows;
+    P.n_jobs = n_jobs;
+    P.x_group = 1;
+    P.xq = xq; P.xq2 = xq2; P.xd = xd; P.xs = xs;
+    P.x = x;
+    P.row_bytes = row_bytes;
+    P.n_in = n_in;
+    P.total_rows = rows;
+    P.s = s; P.s2 = s2;
+    if (s) *status = launch_tma<0, true>(fmt, P, pl, st);
+    else if (!x) *status = launch_tma<0, false>(fmt, P, pl, st);
+    else if (x_kind == 1) *status = launch_tma<1, false>(fmt, P, pl, st);
+    else *status = launch_tma<2, false>(fmt, P, pl, st);
+    return true;
 }
 
 }  // namespace
@@ -160,6 +325,14 @@ int qmv_mv(int ggml_type, const uint8_t* w, int n_out, int n_in, const int8_t* x
     P.n_out = n_out;
     P.n_in = n_in;
     P.slots = 1;
+    if (n_tok == 1) {
+        float* ys[1] = {y};
+        const uint8_t* ws[1] = {w};
+        const int nos[1] = {n_out};
+        if (tma_dense(ggml_type, 1, ws, nos, ys, n_in, xq, xq2, xd, xs, nullptr, 0, nullptr, nullptr,
+                      static_cast<cudaStream_t>(stream), &st))
+            return st;
+    }
     for (int c0 = 0; c0 < n_tok; c0 += kMaxTokens) {
         const int T = n_tok - c0 < kMaxTokens ? n_tok - c0 : kMaxTokens;
         const long long off = (long long)c0 * n_in;
@@ -206,6 +379,23 @@ int qmv_mv_experts(int ggml_type, const void* raw, long long per_expert, long lo
     P.n_in = n_in;
     P.slots = k;
     P.n_exp = n_exp;
+    TmaPlan pl;
+    if (tma_plan(ggml_type, n_in, row_bytes, false, pl) && aligned(raw, 16) && (per_expert < 0 || per_expert % 16 == 0)) {
+        TmaParams Q{};
+        Q.w[0] = static_cast<const uint8_t*>(raw);
+        Q.y[0] = y;
+        Q.n_out[0] = n_out;
+        Q.n_jobs = 1;
+        Q.ids = ids;
+        Q.per_expert = per_expert >= 0 ? per_expert : -1;
+        Q.n_exp = n_exp;
+        Q.x_group = x_group;
+        Q.xq = xq; Q.xq2 = xq2; Q.xd = xd; Q.xs = xs;
+        Q.row_bytes = row_bytes;
+        Q.n_in = n_in;
+        Q.total_rows = (long long)n_out * k;
+        return launch_tma<0, false>(ggml_type, Q, pl, static_cast<cudaStream_t>(stream));
+    }
     return launch(ggml_type, P, 1, static_cast<cudaStream_t>(stream));
 }
 
@@ -223,6 +413,13 @@ int qmv_block_sums(int ggml_type, const uint8_t* w, int n_out, int n_in, const i
         g_last_cuda_error = int(cudaGetLastError());
         return ST_LAUNCH;
     }
+    {
+        const uint8_t* ws[1] = {w};
+        const int nos[1] = {n_out};
+        int rc = ST_OK;
+        if (tma_dense(ggml_type, 1, ws, nos, nullptr, n_in, xq, xq2, nullptr, nullptr, nullptr, 0, s, s2, st, &rc))
+            return rc;
+    }
     MvParams P{};
     P.w = w;
     P.row_bytes = (long long)(n_in / block_values(ggml_type)) * block_bytes(ggml_type);
@@ -230,11 +427,55 @@ int qmv_block_sums(int ggml_type, const uint8_t* w, int n_out, int n_in, const i
     P.xq2 = xq2;
     P.s = s;
     P.s2 = s2;
+    P.x_group = 1;
     P.status = device_status_ptr();
     P.n_out = n_out;
     P.n_in = n_in;
     P.slots = 1;
     return launch_sums(ggml_type, P, st);
+}
+
+int qmv_mv_multi(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
+                 const int8_t* xq, const int8_t* xq2, const float* xd, const float* xs, void* stream) {
+    if (!w || !n_out || !y) return ST_NULL;
+    if (n_jobs < 1 || n_jobs > kMaxJobs) return ST_BAD_TOKENS;
+    for (int j = 0; j < n_jobs; ++j) {
+        const int st = check_mv(ggml_type, w[j], n_out[j], n_in, xq, xq2, xd, xs, y[j]);
+        if (st) return st;
+        if (!aligned(w[j], ggml_type == F_Q4_K ? 16 : 2)) return ST_BAD_ALIGN;
+    }
+    int st = ST_OK;
+    if (tma_dense(ggml_type, n_jobs, w, n_out, y, n_in, xq, xq2, xd, xs, nullptr, 0, nullptr, nullptr,
+                  static_cast<cudaStream_t>(stream), &st))
+        return st;
+    for (int j = 0; j < n_jobs; ++j)
+        if ((st = qmv_mv(ggml_type, w[j], n_out[j], n_in, xq, xq2, xd, xs, 1, y[j], stream))) return st;
+    return ST_OK;
+}
+
+int qmv_mv_x(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
+             const void* x, int x_is_f32, void* stream) {
+    if (!w || !n_out || !y || !x) return ST_NULL;
+    if (!known_format(ggml_type)) return ST_BAD_FORMAT;
+    if (n_jobs < 1 || n_jobs > kMaxJobs) return ST_BAD_TOKENS;
+    if (n_in <= 0 || n_in % block_values(ggml_type)) return ST_BAD_SHAPE;
+    if (!aligned(x, x_is_f32 ? 4 : 2)) return ST_BAD_ALIGN;
+    for (int j = 0; j < n_jobs; ++j) {
+        if (!w[j] || !y[j]) return ST_NULL;
+        if (n_out[j] <= 0) return ST_BAD_SHAPE;
+        if (!aligned(w[j], ggml_type == F_Q4_K ? 16 : 2) || !aligned(y[j], 4)) return ST_BAD_ALIGN;
+    }
+    int st = ST_OK;
+    if (tma_dense(ggml_type, n_jobs, w, n_out, y, n_in, nullptr, nullptr, nullptr, nullptr, x, x_is_f32 ? 1 : 2,
+                  nullptr, nullptr, static_cast<cudaStream_t>(stream), &st))
+        return st;
+    return ST_BAD_SHAPE;        // the shape needs the fallback kernel: quantise with qmv_quant_q8, then qmv_mv
+}
+
+int qmv_set_pdl(int enabled) {
+    const int old = g_pdl;
+    g_pdl = enabled ? 1 : 0;
+    return old;
 }
 
 int qmv_device_status(int clear, int* out, void* stream) {

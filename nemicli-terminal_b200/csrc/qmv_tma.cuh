@@ -1,0 +1,637 @@
+// Single-token matvec with bulk-copy (TMA) staged weight tiles — the batch-1 hot path on sm_100a.
+//
+// A persistent CTA per SM: one producer warp streams tiles of R consecutive weight rows from HBM
+// into a ring of shared-memory stages with cp.async.bulk (one copy per tile, completion counted on
+// an mbarrier); NCW consumer warps hold their slice of the activation input in registers for the
+// whole launch and read the weights from shared memory.  A row's units (32 or 64 values) are split
+// across a team of G lanes (unit u -> lane u % G, then u + G, ...); 32*NCW / G teams take rows side by
+// side.  Teams wider than a warp combine their partial sums through shared memory behind a named
+// barrier of their own.  No TMA multicast is used.
+//
+// Every wait on an mbarrier is bounded in time (~1 s of %globaltimer): on expiry the waiter sets
+// DEV_TIMEOUT in the status word, keeps stepping through the remaining barriers without work, and
+// the producer drains the copies it issued before the CTA leaves.
+#pragma once
+#include "qmv_common.cuh"
+#include "qmv_kernels.cuh"
+
+namespace qmv {
+
+constexpr int kMaxJobs = 4;
+constexpr unsigned long long kWaitNs = 1000000000ull;    // bound of every mbarrier wait
+enum : int { DEV_TIMEOUT = 2 };
+
+struct TmaParams {
+    // slots: either dense jobs (ids == nullptr; w/y/n_out per job, all sharing the activation) or the
+    // k experts picked by ids (w[0] = expert tensor or address table, y[0] = [slot][n_out])
+    const uint8_t* w[kMaxJobs];
+    float* y[kMaxJobs];
+    int n_out[kMaxJobs];
+    long long row_start[kMaxJobs + 1]; // dense jobs: first global row of each job (prefix sums of n_out)
+    int n_jobs;
+    const long long* ids;
+    long long per_expert;             // >= 0: expert stride in bytes; < 0: w[0] is an address table
+    long long n_exp;
+    int x_group;                      // slot j reads activation row j / x_group (experts)
+    const int8_t* xq;
+    const int8_t* xq2;
+    const float* xd;
+    const float* xs;
+    long long row_bytes;              // multiple of 16
+    int n_in;
+    int rows_per_tile;                // R
+    int stages;
+    long long total_rows;             // rows of all jobs (dense) or k * n_out (experts)
+    int* status;
+    int32_t* s;                       // sums mode (test hook): int32 sums per (row, sum unit)
+    int32_t* s2;
+    const void* x;                    // fused quantisation (XF != 0): the raw activation row, fp32 or bf16
+};
+
+// ---- shared-memory access -----------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds16u(uint32_t a) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds8u(uint32_t a) {
+    unsigned short v;
+    asm volatile("ld.shared.u8 %0, [%1];" : "=h"(v) : "r"(a));
+    return v & 0xFFu;
+}
+// 16 / 8 bytes at a 2-byte aligned shared address (aligned words + funnel shifts; the extra word
+// read past the end stays inside the CTA's shared memory: stages are followed by other buffers)
+__device__ __forceinline__ uint4 lds16_a2(uint32_t a) {
+    const uint32_t b = a & ~3u, sh = (a & 3u) * 8u;
+    const uint32_t w0 = lds32(b), w1 = lds32(b + 4), w2 = lds32(b + 8), w3 = lds32(b + 12), w4 = lds32(b + 16);
+    return make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh), __funnelshift_r(w2, w3, sh),
+                      __funnelshift_r(w3, w4, sh));
+}
+__device__ __forceinline__ uint2 lds8_a2(uint32_t a) {
+    const uint32_t b = a & ~3u, sh = (a & 3u) * 8u;
+    const uint32_t w0 = lds32(b), w1 = lds32(b + 4), w2 = lds32(b + 8);
+    return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
+}
+
+// ---- mbarriers and bulk copies ------------------------------------------------------------------
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("{ .reg .b64 st; mbarrier.arrive.shared::cta.b64 st, [%0]; }" :: "r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("{ .reg .b64 st; mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1; }" :: "r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+// try_wait that lets the hardware suspend the warp until the phase completes (up to ~hint ns)
+__device__ __forceinline__ bool mbar_try_suspend(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(ok) : "r"(bar), "r"(parity), "r"(1000000u) : "memory");
+    return ok != 0;
+}
+// bounded wait: true when the phase with this parity completed, false after ~kWaitNs
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    if (mbar_try(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (;;) {
+        if (mbar_try_suspend(bar, parity)) return true;
+        if (global_ns() - t0 > kWaitNs) return false;
+    }
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+__device__ __forceinline__ void named_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(threads) : "memory");
+}
+
+// exact float of an integer 0 <= v < 2^23 without the conversion unit: the bits of 2^23 + v, minus 2^23
+__device__ __forceinline__ float small_u2f(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.0f; }
+
+// unsigned bytes of a times signed bytes of b, plus c
+__device__ __forceinline__ int dp4us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dot4(const uint32_t (&w)[4], const int4& x) {
+    return dp4(w[3], x.w, dp4(w[2], x.z, dp4(w[1], x.y, dp4(w[0], x.x, 0))));
+}
+__device__ __forceinline__ int dot4us(const uint32_t (&w)[4], const int4& x) {
+    return dp4us(w[3], x.w, dp4us(w[2], x.z, dp4us(w[1], x.y, dp4us(w[0], x.x, 0))));
+}
+
+// ---- per-format units ---------------------------------------------------------------------------
+//
+// A unit is the piece of a row one lane takes: VPU values, with NS scale groups.
+//   Q4_K    64 values: the 32 qs bytes 32p..32p+31 of superblock b (sub-blocks 2p low, 2p+1 high nibbles)
+//   Q6_K    32 values: ql bytes 64n+16j..+15 of superblock b: 16 values of group j/2 and of j/2 + 2
+//   Q4_0    32 values: one block
+//   Q8_0    32 values: one block
+//   TQ2_0   32 values: qs bytes 32n+8j..+7 of superblock b: 8 values of each of the four groups of half n
+//   IQ2_XXS 32 values: one sub-block (4 codebook entries)
+
+template <int FMT> struct UnitTraits { static constexpr int VPU = 32, NS = 1, NQ = 2; };
+template <> struct UnitTraits<F_Q4_K> { static constexpr int VPU = 64, NS = 2, NQ = 4; };
+template <> struct UnitTraits<F_Q6_K> { static constexpr int VPU = 32, NS = 2, NQ = 2; };
+template <> struct UnitTraits<F_TQ2_0> { static constexpr int VPU = 32, NS = 4, NQ = 2; };
+
+template <int FMT>
+struct Act {                              // the activation of one unit, in registers
+    int4 q[UnitTraits<FMT>::NQ];          // xq bytes
+    int4 r[UnitTraits<FMT>::NQ];          // xq2 bytes
+    float d[UnitTraits<FMT>::NS];         // xd / 254 of each scale group
+    float s[UnitTraits<FMT>::NS];         // xs of each group (0 where another lane applies the offset)
+};
+
+template <bool GLOBAL>
+__device__ __forceinline__ int4 ldq16(const int8_t* p) {
+    if constexpr (GLOBAL) return __ldg(reinterpret_cast<const int4*>(p));
+    return *reinterpret_cast<const int4*>(p);
+}
+template <bool GLOBAL>
+__device__ __forceinline__ int2 ldq8(const int8_t* p) {
+    if constexpr (GLOBAL) return __ldg(reinterpret_cast<const int2*>(p));
+    return *reinterpret_cast<const int2*>(p);
+}
+template <bool GLOBAL, bool SCALES>
+__device__ __forceinline__ float ldf(const float* p, int i) {
+    if constexpr (!SCALES) return 0.f;
+    if constexpr (GLOBAL) return __ldg(p + i);
+    return p[i];
+}
+
+// xq/xq2/xd/xs point at the start of the activation row (global memory, or shared memory when
+// GLOBAL = false).  SCALES = false (the int32-sums test hook) reads xq/xq2 only: xd/xs may be null.
+template <int FMT, bool SCALES, bool GLOBAL = true>
+__device__ __forceinline__ void load_act(Act<FMT>& a, int u, const int8_t* xq, const int8_t* xq2, const float* xd,
+                                         const float* xs) {
+    constexpr int NS = UnitTraits<FMT>::NS;
+#pragma unroll
+    for (int i = 0; i < NS; ++i) a.d[i] = a.s[i] = 0.f;
+    if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0 || FMT == F_IQ2_XXS) {
+        const int o = 32 * u;
+        a.q[0] = ldq16<GLOBAL>(xq + o); a.q[1] = ldq16<GLOBAL>(xq + o + 16);
+        a.r[0] = ldq16<GLOBAL>(xq2 + o); a.r[1] = ldq16<GLOBAL>(xq2 + o + 16);
+        a.d[0] = ldf<GLOBAL, SCALES>(xd, u) * kInv254;
+        if (FMT == F_Q4_0) a.s[0] = ldf<GLOBAL, SCALES>(xs, u);
+    } else if constexpr (FMT == F_Q4_K) {
+        const int b = u >> 2, p = u & 3, o = b * 256 + 64 * p;
+        a.q[0] = ldq16<GLOBAL>(xq + o); a.q[1] = ldq16<GLOBAL>(xq + o + 16);
+        a.q[2] = ldq16<GLOBAL>(xq + o + 32); a.q[3] = ldq16<GLOBAL>(xq + o + 48);
+        a.r[0] = ldq16<GLOBAL>(xq2 + o); a.r[1] = ldq16<GLOBAL>(xq2 + o + 16);
+        a.r[2] = ldq16<GLOBAL>(xq2 + o + 32); a.r[3] = ldq16<GLOBAL>(xq2 + o + 48);
+        a.d[0] = ldf<GLOBAL, SCALES>(xd, b * 8 + 2 * p) * kInv254;
+        a.d[1] = ldf<GLOBAL, SCALES>(xd, b * 8 + 2 * p + 1) * kInv254;
+        a.s[0] = ldf<GLOBAL, SCALES>(xs, b * 8 + 2 * p);
+        a.s[1] = ldf<GLOBAL, SCALES>(xs, b * 8 + 2 * p + 1);
+    } else if constexpr (FMT == F_Q6_K) {
+        const int b = u >> 3, q = u & 7, n = q >> 2, j = q & 3, A = j >> 1, B = A + 2, o = b * 256 + 128 * n + 16 * (j & 1);
+        a.q[0] = ldq16<GLOBAL>(xq + o + 32 * A); a.q[1] = ldq16<GLOBAL>(xq + o + 32 * B);
+        a.r[0] = ldq16<GLOBAL>(xq2 + o + 32 * A); a.r[1] = ldq16<GLOBAL>(xq2 + o + 32 * B);
+        a.d[0] = ldf<GLOBAL, SCALES>(xd, b * 8 + 4 * n + A) * kInv254;
+        a.d[1] = ldf<GLOBAL, SCALES>(xd, b * 8 + 4 * n + B) * kInv254;
+    } else {   // TQ2_0
+        const int b = u >> 3, q = u & 7, n = q >> 2, j = q & 3, o = b * 256 + 128 * n + 8 * j;
+        const int2 g0 = ldq8<GLOBAL>(xq + o), g1 = ldq8<GLOBAL>(xq + o + 32), g2 = ldq8<GLOBAL>(xq + o + 64),
+                   g3 = ldq8<GLOBAL>(xq + o + 96);
+        const int2 h0 = ldq8<GLOBAL>(xq2 + o), h1 = ldq8<GLOBAL>(xq2 + o + 32), h2 = ldq8<GLOBAL>(xq2 + o + 64),
+                   h3 = ldq8<GLOBAL>(xq2 + o + 96);
+        a.q[0] = make_int4(g0.x, g0.y, g1.x, g1.y); a.q[1] = make_int4(g2.x, g2.y, g3.x, g3.y);
+        a.r[0] = make_int4(h0.x, h0.y, h1.x, h1.y); a.r[1] = make_int4(h2.x, h2.y, h3.x, h3.y);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            a.d[g] = ldf<GLOBAL, SCALES>(xd, b * 8 + 4 * n + g) * kInv254;
+            if (j == 0) a.s[g] = ldf<GLOBAL, SCALES>(xs, b * 8 + 4 * n + g);
+        }
+    }
+}
+
+// Integer stage of one unit: weight codes of the staged row at shared address `rs` times xq and xq2.
+// s[k], u[k]: int32 sums of scale group k; wsc[k]: weight scale; off[k]: weight offset (times xs).
+template <int FMT>
+struct UnitSums {
+    int s[UnitTraits<FMT>::NS], u[UnitTraits<FMT>::NS];
+    float wsc[UnitTraits<FMT>::NS], off[UnitTraits<FMT>::NS];
+};
+// Q4_K keeps its 6-bit scales / mins as integers and applies d, dmin once per unit
+template <>
+struct UnitSums<F_Q4_K> {
+    int s[2], u[2], isc[2];
+    uint32_t imn[2];
+    float d, dm;
+};
+
+template <int FMT>
+__device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a, UnitSums<FMT>& o, const uint2* grid) {
+    if constexpr (FMT == F_Q4_K) {
+        const int b = u >> 2, p = u & 3;
+        const uint32_t sb = rs + b * 144;
+        const uint4 hd = lds128(sb), v0 = lds128(sb + 16 + 32 * p), v1 = lds128(sb + 32 + 32 * p);
+        const uint32_t l0[4] = {v0.x & 0x0F0F0F0Fu, v0.y & 0x0F0F0F0Fu, v0.z & 0x0F0F0F0Fu, v0.w & 0x0F0F0F0Fu};
+        const uint32_t l1[4] = {v1.x & 0x0F0F0F0Fu, v1.y & 0x0F0F0F0Fu, v1.z & 0x0F0F0F0Fu, v1.w & 0x0F0F0F0Fu};
+        const uint32_t h0[4] = {v0.x & 0xF0F0F0F0u, v0.y & 0xF0F0F0F0u, v0.z & 0xF0F0F0F0u, v0.w & 0xF0F0F0F0u};
+        const uint32_t h1[4] = {v1.x & 0xF0F0F0F0u, v1.y & 0xF0F0F0F0u, v1.z & 0xF0F0F0F0u, v1.w & 0xF0F0F0F0u};
+        // sub-block 2p: low nibbles of the 32 bytes; 2p+1: high nibbles (16 x the nibble, shifted out below)
+        o.s[0] = dot4(l1, a.q[1]) + dot4(l0, a.q[0]);
+        o.u[0] = dot4(l1, a.r[1]) + dot4(l0, a.r[0]);
+        o.s[1] = (dot4us(h1, a.q[3]) + dot4us(h0, a.q[2])) >> 4;
+        o.u[1] = (dot4us(h1, a.r[3]) + dot4us(h0, a.r[2])) >> 4;
+        // 6-bit scales / mins of sub-blocks 0..3 and 4..7 (quant.py:99-108), four per word; no branch on p
+        const uint32_t sc_lo = hd.y & 0x3F3F3F3Fu, m_lo = hd.z & 0x3F3F3F3Fu;
+        const uint32_t sc_hi = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
+        const uint32_t m_hi = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
+        const uint32_t scw = p < 2 ? sc_lo : sc_hi, mw = p < 2 ? m_lo : m_hi;
+        const int sh = 16 * (p & 1);
+        o.isc[0] = int((scw >> sh) & 0xFFu);
+        o.isc[1] = int((scw >> (sh + 8)) & 0xFFu);
+        o.imn[0] = (mw >> sh) & 0xFFu;
+        o.imn[1] = (mw >> (sh + 8)) & 0xFFu;
+        o.d = h2f(hd.x & 0xFFFFu);
+        o.dm = h2f(hd.x >> 16);
+    } else if constexpr (FMT == F_Q6_K) {
+        const int b = u >> 3, q = u & 7, n = q >> 2, j = q & 3, A = j >> 1, B = A + 2, l0 = 16 * (j & 1);
+        const uint32_t sb = rs + b * 210;
+        const uint4 ql = lds16_a2(sb + 64 * n + 16 * j), qh = lds16_a2(sb + 128 + 32 * n + l0);
+        const uint32_t L[4] = {ql.x, ql.y, ql.z, ql.w}, H[4] = {qh.x, qh.y, qh.z, qh.w};
+        uint32_t wa[4], wb[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            wa[i] = __vsub4((L[i] & 0x0F0F0F0Fu) | (((H[i] >> (2 * A)) & 0x03030303u) << 4), 0x20202020u);
+            wb[i] = __vsub4(((L[i] >> 4) & 0x0F0F0F0Fu) | (((H[i] >> (2 * B)) & 0x03030303u) << 4), 0x20202020u);
+        }
+        o.s[0] = dot4(wa, a.q[0]); o.s[1] = dot4(wb, a.q[1]);
+        o.u[0] = dot4(wa, a.r[0]); o.u[1] = dot4(wb, a.r[1]);
+        const float d = h2f(lds16u(sb + 208));
+        o.wsc[0] = d * float(int8_t(lds8u(sb + 192 + 8 * n + 2 * A + (j & 1))));
+        o.wsc[1] = d * float(int8_t(lds8u(sb + 192 + 8 * n + 2 * B + (j & 1))));
+        o.off[0] = o.off[1] = 0.f;
+    } else if constexpr (FMT == F_Q4_0) {
+        const uint32_t bl = rs + u * 18;
+        const uint4 v = lds16_a2(bl + 2);
+        const uint32_t lo[4] = {v.x & 0x0F0F0F0Fu, v.y & 0x0F0F0F0Fu, v.z & 0x0F0F0F0Fu, v.w & 0x0F0F0F0Fu};
+        const uint32_t hi[4] = {v.x & 0xF0F0F0F0u, v.y & 0xF0F0F0F0u, v.z & 0xF0F0F0F0u, v.w & 0xF0F0F0F0u};
+        o.s[0] = dot4(lo, a.q[0]) + (dot4us(hi, a.q[1]) >> 4);
+        o.u[0] = dot4(lo, a.r[0]) + (dot4us(hi, a.r[1]) >> 4);
+        const float d = h2f(lds16u(bl));
+        o.wsc[0] = d;
+        o.off[0] = 8.0f * d;
+    } else if constexpr (FMT == F_Q8_0) {
+        const uint32_t bl = rs + u * 34;
+        const uint4 v0 = lds16_a2(bl + 2), v1 = lds16_a2(bl + 18);
+        const uint32_t w0[4] = {v0.x, v0.y, v0.z, v0.w}, w1[4] = {v1.x, v1.y, v1.z, v1.w};
+        o.s[0] = dot4(w1, a.q[1]) + dot4(w0, a.q[0]);
+        o.u[0] = dot4(w1, a.r[1]) + dot4(w0, a.r[0]);
+        o.wsc[0] = h2f(lds16u(bl));
+        o.off[0] = 0.f;
+    } else if constexpr (FMT == F_TQ2_0) {
+        const int b = u >> 3, q = u & 7, n = q >> 2, j = q & 3;
+        const uint32_t sb = rs + b * 66;
+        const uint2 c = lds8_a2(sb + 32 * n + 8 * j);
+        const float d = h2f(lds16u(sb + 64));
+        const int xq[8] = {a.q[0].x, a.q[0].y, a.q[0].z, a.q[0].w, a.q[1].x, a.q[1].y, a.q[1].z, a.q[1].w};
+        const int xr[8] = {a.r[0].x, a.r[0].y, a.r[0].z, a.r[0].w, a.r[1].x, a.r[1].y, a.r[1].z, a.r[1].w};
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            const uint32_t c0 = (c.x >> (2 * g)) & 0x03030303u, c1 = (c.y >> (2 * g)) & 0x03030303u;
+            o.s[g] = dp4(c1, xq[2 * g + 1], dp4(c0, xq[2 * g], 0));
+            o.u[g] = dp4(c1, xr[2 * g + 1], dp4(c0, xr[2 * g], 0));
+            o.wsc[g] = d;
+            o.off[g] = d;
+        }
+    } else {   // IQ2_XXS
+        const int b = u >> 3, q = u & 7;
+        const uint32_t sb = rs + b * 66;
+        const uint2 ax = lds8_a2(sb + 2 + 8 * q);
+        uint32_t w[8];
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            const uint2 g = grid[(ax.x >> (8 * l)) & 0xFFu];
+            const uint32_t s7 = (ax.y >> (7 * l)) & 127u;
+            const uint32_t s8 = s7 | (uint32_t(__popc(s7) & 1) << 7);
+            const uint32_t mlo = (((s8 & 15u) * 0x00204081u) & 0x01010101u) * 0xFFu;
+            const uint32_t mhi = (((s8 >> 4) * 0x00204081u) & 0x01010101u) * 0xFFu;
+            w[2 * l] = __vsub4(g.x ^ mlo, mlo);
+            w[2 * l + 1] = __vsub4(g.y ^ mhi, mhi);
+        }
+        const uint32_t w0[4] = {w[0], w[1], w[2], w[3]}, w1[4] = {w[4], w[5], w[6], w[7]};
+        o.s[0] = dot4(w1, a.q[1]) + dot4(w0, a.q[0]);
+        o.u[0] = dot4(w1, a.r[1]) + dot4(w0, a.r[0]);
+        o.wsc[0] = h2f(lds16u(sb)) * (0.125f + 0.25f * float(ax.y >> 28));
+        o.off[0] = 0.f;
+    }
+}
+
+// sum-unit index (values sharing both scales: 16 for Q6_K, 32 otherwise) of scale group k of unit u
+template <int FMT>
+__device__ __forceinline__ int sum_unit(int u, int k) {
+    if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0 || FMT == F_IQ2_XXS) return u;
+    if constexpr (FMT == F_Q4_K) return 2 * u + k;          // unit u = sub-blocks 2u, 2u + 1 of the row
+    const int b = u >> 3, q = u & 7;
+    if constexpr (FMT == F_Q6_K) {
+        const int n = q >> 2, j = q & 3, A = j >> 1;
+        return b * 16 + 8 * n + 2 * (k == 0 ? A : A + 2) + (j & 1);
+    }
+    return b * 8 + 4 * (q >> 2) + k;    // TQ2_0
+}
+
+// the unit's contribution: sum over scale groups of wsc * (xd/254) * (254 S + S2) - off * xs
+template <int FMT>
+__device__ __forceinline__ float unit_dot(uint32_t rs, int u, const Act<FMT>& a, const uint2* grid) {
+    UnitSums<FMT> o;
+    unit_sums<FMT>(rs, u, a, o, grid);
+    if constexpr (FMT == F_Q4_K) {
+        // d * sum_k sc_k * (254 S_k + S2_k) * xd_k / 254  -  dmin * sum_k m_k * xs_k
+        const float w = float(o.isc[0] * (254 * o.s[0] + o.u[0])) * a.d[0]
+                      + float(o.isc[1] * (254 * o.s[1] + o.u[1])) * a.d[1];
+        const float m = small_u2f(o.imn[0]) * a.s[0] + small_u2f(o.imn[1]) * a.s[1];
+        return o.d * w - o.dm * m;
+    } else {
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < UnitTraits<FMT>::NS; ++k)
+            acc += o.wsc[k] * a.d[k] * float(254 * o.s[k] + o.u[k]) - o.off[k] * a.s[k];
+        return acc;
+    }
+}
+
+// ---- the kernel ---------------------------------------------------------------------------------
+
+struct TileInfo {
+    int slot, row0, nrows, job;
+};
+
+// The rows of all jobs / slots form one global row space; CTA c takes the contiguous range
+// [c * total / grid, (c + 1) * total / grid) (equal bytes per CTA within one row) and walks it in
+// tiles of at most R rows that never cross a job or slot boundary.
+__device__ __forceinline__ long long cta_row_begin(const TmaParams& P, int c) {
+    return (long long)c * P.total_rows / gridDim.x;
+}
+
+// the tile starting at global row g (< end of this CTA's range `hi`)
+__device__ __forceinline__ TileInfo tile_at(const TmaParams& P, long long g, long long hi) {
+    TileInfo t;
+    long long start, stop;
+    if (P.ids == nullptr) {
+        int j = 0;
+        while (j + 1 < P.n_jobs && g >= P.row_start[j + 1]) ++j;
+        t.job = t.slot = j;
+        start = P.row_start[j];
+        stop = P.row_start[j + 1];
+    } else {
+        t.job = 0;
+        t.slot = int(g / P.n_out[0]);
+        start = (long long)t.slot * P.n_out[0];
+        stop = start + P.n_out[0];
+    }
+    t.row0 = int(g - start);
+    const long long lim = min(stop, hi);
+    t.nrows = int(min((long long)P.rows_per_tile, lim - g));
+    return t;
+}
+
+// weight base of a slot, or nullptr for a refused expert id / misaligned table entry
+__device__ __forceinline__ const uint8_t* tma_slot_base(const TmaParams& P, int slot) {
+    if (P.ids == nullptr) return P.w[slot];
+    const long long e = P.ids[slot];
+    if (e < 0 || e >= P.n_exp) return nullptr;
+    const uint8_t* base = P.per_expert >= 0 ? P.w[0] + e * P.per_expert
+                                            : reinterpret_cast<const uint8_t*>(reinterpret_cast<const long long*>(P.w[0])[e]);
+    return (reinterpret_cast<uintptr_t>(base) & 15u) ? nullptr : base;
+}
+
+// shared-memory layout: [stages x stage bytes][reduction 2 x NCW x R floats][codebook 2 KB]
+//                      [fused activation: xq K, xq2 K, xd K/32, xs K/32 (XF only)][mbarriers]
+constexpr int kTmaRowsPerTeam = 4;          // rows of a full tile per team (compile-time fast path)
+__host__ __device__ constexpr int tma_red_bytes(int ncw) { return 2 * ncw * kTmaRowsPerTeam * 4; }
+__host__ __device__ constexpr long long tma_act_bytes(int n_in) { return 2LL * n_in + n_in / 4; }
+constexpr int kConsumerBarrier = 15;        // named barrier of all consumer warps (teams use 1..8)
+
+// XF: 0 = the activation comes pre-quantised (P.xq ...), 1 = fp32 row in P.x, 2 = bf16 row in P.x,
+// quantised by the CTA itself into shared memory (same arithmetic as quant_q8_kernel).
+template <int FMT, int NCW, int G, int UPL, int XF, bool SUMS>
+__global__ void __launch_bounds__(32 * (NCW + 1), NCW <= 8 ? 2 : 1) mv_tma_kernel(const TmaParams P) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int TEAMS = 32 * NCW / G;                  // rows processed side by side
+    constexpr int WPT = G >= 32 ? G / 32 : 1;            // warps per team
+    constexpr int NPER = kTmaRowsPerTeam;
+    constexpr int VPU = UnitTraits<FMT>::VPU;
+    const int R = P.rows_per_tile;
+    const int S = P.stages;
+    const long long stage_bytes = (long long)R * P.row_bytes;
+    uint8_t* red_p = smem + S * stage_bytes;
+    float* red = reinterpret_cast<float*>(red_p);
+    uint2* grid = reinterpret_cast<uint2*>(red_p + tma_red_bytes(NCW));
+    uint8_t* act_p = red_p + tma_red_bytes(NCW) + 2048;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(act_p + (XF ? tma_act_bytes(P.n_in) : 0));
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S);
+    const uint32_t stage0 = smem_u32(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    // the next kernel in the stream may start launching (its weight prefetch does not read our outputs)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, NCW);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if constexpr (FMT == F_IQ2_XXS) load_iq2xxs_grid(grid);
+    __syncthreads();
+
+    if (warp == NCW) {
+        // ---------------- producer: weights only, no dependence on the previous kernel ----------------
+        if (lane != 0) return;
+        int it = 0;
+        bool ok = true;
+        const long long hi = cta_row_begin(P, blockIdx.x + 1);
+        for (long long g = cta_row_begin(P, blockIdx.x); g < hi; ++it) {
+            const int s = it % S;
+            if (it >= S && !mbar_wait(empty0 + 8 * s, ((it / S) & 1) ^ 1)) {
+                ok = false;
+                break;
+            }
+            const TileInfo ti = tile_at(P, g, hi);
+            g += ti.nrows;
+            const uint8_t* base = tma_slot_base(P, ti.slot);
+            if (base == nullptr) {
+                if (P.status) atomicOr(P.status, DEV_BAD_ADDRESS);
+                mbar_arrive(full0 + 8 * s);                   // nothing to copy: consumers write zeros
+            } else {
+                const uint32_t bytes = uint32_t((long long)ti.nrows * P.row_bytes);
+                mbar_arrive_tx(full0 + 8 * s, bytes);
+                bulk_g2s(stage0 + uint32_t(s * stage_bytes), base + (long long)ti.row0 * P.row_bytes, bytes,
+                         full0 + 8 * s);
+            }
+        }
+        if (!ok) {
+            if (P.status) atomicOr(P.status, DEV_TIMEOUT);
+            // drain: wait (bounded) for the copies of the last S iterations before leaving
+            for (int k = (it > S ? it - S : 0); k < it; ++k) mbar_wait(full0 + 8 * (k % S), (k / S) & 1);
+        }
+        return;
+    }
+
+    // ---------------- consumers ----------------
+    // Every consumer thread walks the same tiles and its team's named barriers, also after a timed-out
+    // wait (then it only skips the work), so a failed wait can never leave a barrier short.
+    const int cl = threadIdx.x;                 // 0 .. 32*NCW-1
+    const int team = cl / G, li = cl % G;       // team (row slot), lane within the team
+    const int U = P.n_in / VPU;                 // units per row
+    // inputs written by the previous kernel are read only after it has completed
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int8_t* sxq = nullptr;
+    const int8_t* sxq2 = nullptr;
+    const float* sxd = nullptr;
+    const float* sxs = nullptr;
+    if constexpr (XF != 0) {
+        int8_t* wq = reinterpret_cast<int8_t*>(act_p);
+        int8_t* wq2 = wq + P.n_in;
+        float* wd = reinterpret_cast<float*>(wq2 + P.n_in);
+        float* ws = wd + P.n_in / 32;
+        for (int grp = warp; grp < P.n_in / 32; grp += NCW) {
+            const int i = 32 * grp + lane;
+            const float v = XF == 1 ? static_cast<const float*>(P.x)[i] : bf2f(static_cast<const uint16_t*>(P.x)[i]);
+            quantize_group(v, i, wq, wq2, wd, ws);
+        }
+        named_sync(kConsumerBarrier, 32 * NCW);
+        sxq = wq; sxq2 = wq2; sxd = wd; sxs = ws;
+    }
+    Act<FMT> act[UPL];
+    long long cur_row = -1;
+    bool dead = false;
+    int it = 0;
+    const long long hi = cta_row_begin(P, blockIdx.x + 1);
+    for (long long g = cta_row_begin(P, blockIdx.x); g < hi; ++it) {
+        const TileInfo ti = tile_at(P, g, hi);
+        g += ti.nrows;
+        const long long arow = P.ids == nullptr ? 0 : ti.slot / P.x_group;
+        if (arow != cur_row) {
+            const long long off = arow * P.n_in;
+#pragma unroll
+            for (int i = 0; i < UPL; ++i) {
+                const int u = li + G * i;
+                if (u < U) {
+                    if constexpr (XF != 0) load_act<FMT, true, false>(act[i], u, sxq, sxq2, sxd, sxs);
+                    else load_act<FMT, !SUMS>(act[i], u, P.xq + off, P.xq2 + off, P.xd + off / 32, P.xs + off / 32);
+                }
+            }
+            cur_row = arow;
+        }
+        const int s = it % S;
+        const bool got = !dead && mbar_wait(full0 + 8 * s, (it / S) & 1);
+        if (!got && !dead) {
+            dead = true;
+            if (lane == 0 && P.status) atomicOr(P.status, DEV_TIMEOUT);
+        }
+        const bool work = got && !(P.ids != nullptr && tma_slot_base(P, ti.slot) == nullptr);
+        const uint32_t st = stage0 + uint32_t(s * stage_bytes);
+        float acc[NPER];
+#pragma unroll
+        for (int i = 0; i < NPER; ++i) acc[i] = 0.f;
+        if (work && ti.nrows == NPER * TEAMS && R == NPER * TEAMS && !SUMS) {
+            // full tile: NPER independent rows per lane, no per-row guards (the compiler interleaves them)
+#pragma unroll
+            for (int k = 0; k < UPL; ++k) {
+                const int u = li + G * k;
+                if (u < U) {
+#pragma unroll
+                    for (int i = 0; i < NPER; ++i)
+                        acc[i] += unit_dot<FMT>(st + uint32_t((team + TEAMS * i) * P.row_bytes), u, act[k], grid);
+                }
+            }
+        } else if (work) {
+#pragma unroll
+            for (int i = 0; i < NPER; ++i) {
+                const int r = team + TEAMS * i;
+                if (r < ti.nrows) {
+                    const uint32_t rs = st + uint32_t(r * P.row_bytes);
+#pragma unroll
+                    for (int k = 0; k < UPL; ++k) {
+                        const int u = li + G * k;
+                        if (u < U) {
+                            if constexpr (SUMS) {
+                                UnitSums<FMT> o;
+                                unit_sums<FMT>(rs, u, act[k], o, grid);
+                                const long long row = ti.row0 + r;
+                                const int upr = P.n_in / unit_values(FMT);
+#pragma unroll
+                                for (int q = 0; q < UnitTraits<FMT>::NS; ++q) {
+                                    atomicAdd(P.s + row * upr + sum_unit<FMT>(u, q), o.s[q]);
+                                    atomicAdd(P.s2 + row * upr + sum_unit<FMT>(u, q), o.u[q]);
+                                }
+                            } else {
+                                acc[i] += unit_dot<FMT>(rs, u, act[k], grid);
+                            }
+                        }
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (got && lane == 0) mbar_arrive(empty0 + 8 * s);   // this warp is done with the stage
+        if constexpr (!SUMS) {
+            float* y = P.ids == nullptr ? P.y[ti.job] : P.y[0] + (long long)ti.slot * P.n_out[0];
+            if constexpr (G <= 32) {
+#pragma unroll
+                for (int i = 0; i < NPER; ++i) {
+                    float v = acc[i];
+#pragma unroll
+                    for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    const int r = team + TEAMS * i;
+                    if (li == 0 && got && r < ti.nrows) y[ti.row0 + r] = v;
+                }
+            } else {
+                float* rb = red + (it & 1) * NCW * NPER;
+#pragma unroll
+                for (int i = 0; i < NPER; ++i) {
+                    const float v = warp_sum(acc[i]);
+                    if (lane == 0) rb[warp * NPER + i] = v;
+                }
+                named_sync(1 + team, G);                     // this team's warps only
+                const int wt = li >> 5;                      // warp within the team
+                if (got && wt == 0 && lane < NPER) {         // lane i of the team's first warp: row team + TEAMS*i
+                    const int r = team + TEAMS * lane;
+                    if (r < ti.nrows) {
+                        float v = 0.f;
+#pragma unroll
+                        for (int w = 0; w < WPT; ++w) v += rb[(team * WPT + w) * NPER + lane];
+                        y[ti.row0 + r] = v;
+                    }
+                }
+            }
+        }
+    }
+}
+
+}  // namespace qmv

@@ -16,6 +16,7 @@ falls back to another implementation.
 from __future__ import annotations
 
 import contextlib
+import ctypes
 import threading
 from typing import Optional
 
@@ -85,10 +86,52 @@ def _check_raw(fmt: str, raw: torch.Tensor, n_out: int, n_in: int) -> None:
         raise RuntimeError(f"{fmt}: raw must be contiguous uint8 with {n_out * (n_in // bv) * bb} bytes")
 
 
+def pdl(enabled: bool) -> bool:
+    """Programmatic dependent launch for the single-token kernels (off by default; see
+    include/nemicli_qmv.h, qmv_set_pdl): the next matvec streams its weights while the previous kernel
+    finishes.  Only for weights that no kernel launched right before the matvec writes."""
+    return bool(_lib.load().qmv_set_pdl(int(bool(enabled))))
+
+
+def _raw_x(x: torch.Tensor, n_in: int):
+    """A one-token activation as the fused kernels take it (fp32 stays fp32, anything else bf16)."""
+    x = x.reshape(-1)
+    if x.numel() != n_in:
+        return None
+    if x.dtype != torch.float32:
+        x = x.to(torch.bfloat16)
+    return x.contiguous()
+
+
+def _fused(fmt: str, mats, x: torch.Tensor, n_in: int):
+    """One launch that quantises x itself; None where the staged kernel does not take the shape."""
+    xr = _raw_x(x, n_in)
+    if xr is None:
+        return None
+    _need_cuda(xr, f"mv {fmt}")
+    dev = mats[0][0].device
+    ys = [torch.empty(n_out, dtype=torch.float32, device=dev) for _, n_out in mats]
+    n = len(mats)
+    w_arr = (ctypes.c_void_p * n)(*[raw.data_ptr() for raw, _ in mats])
+    n_arr = (ctypes.c_int * n)(*[n_out for _, n_out in mats])
+    y_arr = (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys])
+    st = _lib.load().qmv_mv_x(TYPE_ID[fmt], n, w_arr, n_arr, y_arr, n_in, _lib.ptr(xr),
+                              int(xr.dtype == torch.float32), _lib.stream_ptr(dev))
+    if st == 2:                       # row length the staged kernel does not take
+        return None
+    _lib.check(st, f"qmv_mv_x {fmt}")
+    return ys
+
+
 def mv(fmt: str, raw: torch.Tensor, x, n_out: int, n_in: int) -> torch.Tensor:
     """raw: (n_out, n_in) in block format on the GPU; x: (M, n_in) or (n_in,) bf16/float32, or an
-    Eingang with M rows -> (M, n_out) float32, or (n_out,) for a vector."""
+    Eingang with M rows -> (M, n_out) float32, or (n_out,) for a vector.  One token given as a tensor
+    is quantised inside the matvec kernel (no separate Eingang)."""
     _check_raw(fmt, raw, n_out, n_in)
+    if not isinstance(x, Eingang) and x.numel() == n_in:
+        ys = _fused(fmt, [(raw, n_out)], x, n_in)
+        if ys is not None:
+            return ys[0] if x.dim() == 1 else ys[0].view(1, n_out)
     e = x if isinstance(x, Eingang) else Eingang(x)
     if e.n % n_in:
         raise RuntimeError(f"mv: input of {e.n} values is not a whole number of rows of {n_in}")
@@ -98,6 +141,32 @@ def mv(fmt: str, raw: torch.Tensor, x, n_out: int, n_in: int) -> torch.Tensor:
                                   _lib.stream_ptr(raw.device)), f"qmv_mv {fmt}")
     vektor = M == 1 if isinstance(x, Eingang) else x.dim() == 1
     return y[0] if vektor else y
+
+
+def mv_geteilt(fmt: str, mats, x, n_in: int) -> list:
+    """Several matrices that read the same single-token input (q/k/v, gate/up) in one launch:
+    mats = [(raw, n_out), ...] (at most 4) -> [y (n_out,) float32, ...].  Each weight byte is read once;
+    the input is quantised once.  New entry point (the reference launches each matrix on its own)."""
+    if not 1 <= len(mats) <= 4:
+        raise RuntimeError("mv_geteilt: 1 to 4 matrices")
+    for raw, n_out in mats:
+        _check_raw(fmt, raw, n_out, n_in)
+    if not isinstance(x, Eingang):
+        ys = _fused(fmt, mats, x, n_in)
+        if ys is not None:
+            return ys
+    e = x if isinstance(x, Eingang) else Eingang(x)
+    if e.n != n_in:
+        raise RuntimeError(f"mv_geteilt: one token of {n_in} values expected, got {e.n}")
+    dev = mats[0][0].device
+    ys = [torch.empty(n_out, dtype=torch.float32, device=dev) for _, n_out in mats]
+    n = len(mats)
+    w_arr = (ctypes.c_void_p * n)(*[raw.data_ptr() for raw, _ in mats])
+    n_arr = (ctypes.c_int * n)(*[n_out for _, n_out in mats])
+    y_arr = (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys])
+    _lib.check(_lib.load().qmv_mv_multi(TYPE_ID[fmt], n, w_arr, n_arr, y_arr, n_in, *e.zeiger(),
+                                        _lib.stream_ptr(dev)), f"qmv_mv_multi {fmt}")
+    return ys
 
 
 _TEILEN = threading.local()

@@ -137,3 +137,17 @@ def test_moe_ffn(cuda, L):
             ref[t] += wc[t, j] * (Wd[e] @ a)
     assert O.max_rel(out.cpu().numpy(), ref.numpy()) < 1e-3
     assert torch.equal(out, ffn(x, idx, w))                # run to run (the reference's test_moe.py:80)
+
+
+@pytest.mark.parametrize("fmt", H.FMTS)
+def test_shared_input_launch(cuda, fmt):
+    """mv_geteilt: q/k/v-like matrices sharing one input, one launch == separate launches (bit for bit)."""
+    from nemicli_terminal_b200 import mmvq
+    n_in = 4096
+    shapes = [512, 128, 128] if fmt != "Q8_0" else [256, 64]
+    raws = [synth.blocks(fmt, n, n_in, seed=i).to(cuda) for i, n in enumerate(shapes)]
+    x = synth.activations(1, n_in, seed=3, device=cuda)[0]
+    e = mmvq.Eingang(x)
+    ys = mmvq.mv_geteilt(fmt, list(zip(raws, shapes)), e, n_in)
+    for raw, n, y in zip(raws, shapes, ys):
+        assert torch.equal(y, mmvq.mv(fmt, raw, e, n, n_in))
