@@ -135,6 +135,26 @@ def step_fn(stack, xs, batch):
     return outs
 
 
+def build_chain(stack, device, seed: int = 0):
+    """The stack as one decode chain: per layer RMSNORM -> q,k,v | o (reads q's output: attention
+    stand-in) | RMSNORM(h + o) -> gate,up | SILU_MUL -> down, the residual stream carried across layers."""
+    from nemicli_terminal_b200 import chain, synth
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    h0 = synth.activations(1, 4096, seed=seed + 11, device=device)[0].contiguous()
+    stages, h, r, outs = [], h0, None, []
+    for i, mats in enumerate(stack):
+        m = {name: (fmt, raw, n_out, n_in) for name, fmt, n_out, n_in, slot, raw in mats}
+        wa = (torch.rand(4096, generator=g, device=device) + 0.5).contiguous()
+        wf = (torch.rand(4096, generator=g, device=device) + 0.5).contiguous()
+        st, h_mid, y_down = chain.layer_stages(m["q"], m["k"], m["v"], m["o"], m["gate"], m["up"], m["down"],
+                                               h_in=h, resid_in=r, attn_norm=wa, ffn_norm=wf, first=i == 0)
+        stages += st
+        outs += [y for s_ in st for y in s_.ys]
+        h, r = h_mid, y_down
+    return chain.Chain(stages), h0, r, outs
+
+
 def capture(fn):
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
@@ -258,17 +278,29 @@ def run_ours(args):
     lb = layer_bytes()
     step_bytes = lb * args.layers
     results = {}
+    mode_used = args.mode
+    if args.mode == "chain":
+        ch, h0_dev, last_out, chain_outs = build_chain(stack, device, seed=100000 * rank)
+        g1, _ = capture(lambda: ch.run())
+        with Clocks(local) as clk:
+            t = time_graph(g1, args.steps, max(3, args.warmup), dist)
+        clocks = clk.summary()
+        t = max_over_ranks(t, dist, device)
+        results[1] = {"s_per_step": t / args.steps, "steps": args.steps}
     for batch in ([1] + [b for b in args.batches if b != 1]):
+        if batch == 1 and args.mode == "chain":
+            continue
         xs = [[synth.activations(batch, n, seed=7919 * l + s + batch, device=device) for s, n in enumerate(INPUTS)]
               for l in range(args.layers)]
         g, outs = capture(lambda: step_fn(stack, xs, batch))
         steps = args.steps if batch == 1 else max(5, args.steps // 2)
-        t = time_graph(g, steps, max(3, args.warmup), dist) if batch != 1 else None
         if batch == 1:
             with Clocks(local) as clk:
                 t = time_graph(g, steps, max(3, args.warmup), dist)
             clocks = clk.summary()
             g1, xs1, outs1 = g, xs, outs
+        else:
+            t = time_graph(g, steps, max(3, args.warmup), dist)
         t = max_over_ranks(t, dist, device)
         results[batch] = {"s_per_step": t / steps, "steps": steps}
         if batch != 1:
@@ -276,35 +308,48 @@ def run_ours(args):
     t1 = results[1]["s_per_step"]
     value = world * step_bytes / t1 / 1e9
 
-    # dominant kernel alone: the 32 gate_proj launches (Q4_K 14336x4096, 33.0 MB each) of the stack
-    gate_raw = [mats[4][5] for mats in stack]
-    x_gate = xs1[0][2]
-    gk, _ = capture(lambda: [mmvq.mv("Q4_K", r, x_gate, 14336, 4096) for r in gate_raw])
-    reps = 20
-    tk = time_graph(gk, reps, 3) / (reps * len(gate_raw))
-    gate_bytes = 14336 * (4096 // 256) * 144
-    achieved = gate_bytes / tk / 1e9
+    if args.mode == "chain":
+        # the whole step is one kernel (the chain): its launch time is the step time
+        kernel_name = f"chain_kernel (Q4_K 4096 + Q6_K 14336 configs), {len(ch.stages)} stages"
+        tk, kbytes = t1, step_bytes
+    else:
+        # dominant kernel alone: the gate_proj launches (Q4_K 14336x4096, 33.0 MB each) of the stack
+        gate_raw = [mats[4][5] for mats in stack]
+        x_gate = xs1[0][2]
+        gk, _ = capture(lambda: [mmvq.mv("Q4_K", r, x_gate, 14336, 4096) for r in gate_raw])
+        reps = 20
+        tk = time_graph(gk, reps, 3) / (reps * len(gate_raw))
+        kbytes = 14336 * (4096 // 256) * 144
+        kernel_name = "mv_tma_kernel<Q4_K> gate_proj 14336x4096 (fused quantisation)"
+    achieved = kbytes / tk / 1e9
     traffic = None
-    tf = os.path.join(ROOT, "profiles", "traffic_q4k_gate.txt")
+    tf = os.path.join(ROOT, "profiles", "traffic.txt")
     if os.path.exists(tf):
         for line in open(tf):
-            if line.startswith("dram_bytes_per_launch="):
+            if line.startswith(f"{args.mode}_dram_bytes_per_launch="):
                 traffic = int(line.split("=")[1])
 
-    # e2e: pinned host inputs -> device, the captured step, all outputs -> pinned host
-    h_in = [[x.cpu().pin_memory() for x in row] for row in xs1]
-    h_out = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs1]
+    # e2e: the step's inputs from pinned host memory to the device, the step, its results back
+    if args.mode == "chain":
+        h_in = [[h0_dev.cpu().pin_memory()]]
+        dev_in = [[h0_dev]]
+        res_dev = [last_out]
+    else:
+        h_in = [[x.cpu().pin_memory() for x in row] for row in xs1]
+        dev_in = xs1
+        res_dev = outs1
+    h_out = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in res_dev]
     h2d = sum(x.numel() * x.element_size() for row in h_in for x in row)
-    d2h = sum(o.numel() * o.element_size() for o in outs1)
+    d2h = sum(o.numel() * o.element_size() for o in res_dev)
     e_steps = max(3, args.steps // 2)
 
     def e2e_step():
-        for row_h, row_d in zip(h_in, xs1):
-            for h, d in zip(row_h, row_d):
-                d.copy_(h, non_blocking=True)
+        for row_h, row_d in zip(h_in, dev_in):
+            for hh, d in zip(row_h, row_d):
+                d.copy_(hh, non_blocking=True)
         g1.replay()
-        for h, d in zip(h_out, outs1):
-            h.copy_(d, non_blocking=True)
+        for hh, d in zip(h_out, res_dev):
+            hh.copy_(d, non_blocking=True)
 
     for _ in range(2):
         e2e_step()
@@ -320,27 +365,29 @@ def run_ours(args):
     te = max_over_ranks(a.elapsed_time(b) / 1e3 / e_steps, dist, device)
 
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
-    launches_per_step = args.layers * 4           # per layer: 4 matvec launches (quantisation fused)
+    launches_per_step = 1 if args.mode == "chain" else args.layers * 4   # chain: one launch per step
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t1 * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded, config-2 distributions)",
             "config": {"workload": "config2: decode step of a 32-layer Llama-3-8B projection stack "
-                                   "(q,k,v,o,gate,up Q4_K; down Q6_K), batch 1",
+                                   "(q,k,v,o,gate,up Q4_K; down Q6_K), batch 1" + (
+                                       "; chain: RMS norm + residual and SiLU gate fused as stage inputs, "
+                                       "o_proj reads q_proj's output in place of attention" if args.mode == "chain" else ""),
                        "layers": args.layers, "batch": 1, "weight_bytes_per_step": step_bytes,
                        "l2": "inputs larger than L2 (4.41 GB distinct weights per step), no flush",
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "graph": "whole step captured once in a CUDA graph",
+                       "mode": args.mode,
                        "pdl": not args.no_pdl},
             "tok_s": world / t1, "hbm_frac_per_gpu": value / world / peak,
             "batches": {str(b): {"gbs": world * step_bytes / r["s_per_step"] / 1e9,
                                  "tok_s": world * b / r["s_per_step"], "ms_per_step": r["s_per_step"] * 1e3}
                         for b, r in results.items()},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic,
-                         "kernel": "mv_tma_kernel<Q4_K> gate_proj 14336x4096 (fused quantisation)",
-                         "algorithmic_bytes_per_launch": gate_bytes, "peak_kind": f"{peak_kind} hbm_gbs",
+                         "frac": achieved / peak, "traffic": traffic, "kernel": kernel_name,
+                         "algorithmic_bytes_per_launch": kbytes, "peak_kind": f"{peak_kind} hbm_gbs",
                          "launch_us": tk * 1e6},
             "cpu_baseline": cpu,
             "e2e": {"value": world * step_bytes / te / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
@@ -364,6 +411,8 @@ def main():
     ap.add_argument("--batches", type=int, nargs="*", default=[1, 4, 8])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-pdl", action="store_true", help="plain stream order between the matvec launches")
+    ap.add_argument("--mode", choices=["chain", "calls"], default="calls",
+                    help="chain: the step as one decode-chain launch; calls: one launch per matrix group")
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers in the stack (profiling runs use fewer)")
     args = ap.parse_args()
     if args.impl == "reference":

@@ -100,6 +100,41 @@ int qmv_mv_x(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_ou
  * Replaces: nothing in the reference (its decoder relies on plain stream order, models/common.py:1185). */
 int qmv_set_pdl(int enabled);
 
+/* ---- decode chain ------------------------------------------------------------------------------- */
+
+#define QMV_INPUT_RAW 0        /* x = a */
+#define QMV_INPUT_RMSNORM 1    /* v = a (+ b, written to h_out when given); x = v * rsqrt(mean(v^2) + eps) * norm_w */
+#define QMV_INPUT_SILU_MUL 2   /* x = silu(a) * b (b == NULL: silu(a)) */
+
+/* One stage of a decode chain: 1..4 matrices of one format and row length n_in that read the same
+ * input x, built by a fused producer from fp32 device vectors (a, b, norm_w: n_in values).
+ * wait = 1: the stage reads outputs (y or h_out) of earlier stages, so all CTAs finish the previous
+ * stage first.  Buffers the chain writes (y, h_out) must not be read by an earlier stage. */
+typedef struct qmv_stage {
+    int ggml_type;
+    int n_jobs;
+    const uint8_t* w[4];
+    int n_out[4];
+    float* y[4];
+    int n_in;
+    int input;
+    const float* a;
+    const float* b;
+    const float* norm_w;
+    float eps;
+    float* h_out;
+    int wait;
+} qmv_stage;
+
+/* A list of dependent single-token matvec stages (a decode step's projections with their RMS-norm and
+ * SiLU-gate producers fused in) in one persistent, cooperative launch.  stages: host array of n_stages
+ * (at most 128).  Shapes taken: Q4_K with n_in 4096 or 14336, Q6_K with n_in 4096 or 14336, Q8_0 with
+ * n_in 4096 (others: QMV_ERR_SHAPE).  workspace: n_stages ints of device memory (grid-barrier counters),
+ * cleared by the call on `stream`.  Replaces: the reference's fused one-token layer step
+ * (ggufengine/models/baukasten.py:217-240: norm_q8 -> mv(q,k,v) -> ... -> akt_q8 -> mv(down)) for its
+ * matvec and producer kernels (mmvq.py:102-134, 852-865). */
+int qmv_chain(const qmv_stage* stages, int n_stages, int* workspace, void* stream);
+
 /* Test hook: the int32 sums of one token per (row, unit), unit = the values sharing one weight scale
  * and one activation scale (16 for Q6_K, else 32): s = sum code * xq, s2 = sum code * xq2, from the
  * same device code as qmv_mv.  s, s2: int32[n_out][n_in / unit], overwritten.

@@ -1,10 +1,12 @@
 // C ABI of the quantized matvec path (declarations and contracts: include/nemicli_qmv.h).
 #include <cstdio>
 #include <cstdlib>
+#include <algorithm>
 #include <mutex>
 
 #include "qmv_kernels.cuh"
 #include "qmv_tma.cuh"
+#include "qmv_chain.cuh"
 #include "../../include/nemicli_qmv.h"
 
 using namespace qmv;
@@ -470,6 +472,106 @@ int qmv_mv_x(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_ou
                   nullptr, nullptr, static_cast<cudaStream_t>(stream), &st))
         return st;
     return ST_BAD_SHAPE;        // the shape needs the fallback kernel: quantise with qmv_quant_q8, then qmv_mv
+}
+
+int qmv_chain(const qmv_stage* stages, int n_stages, int* workspace, void* stream) {
+    if (!stages || !workspace) return ST_NULL;
+    if (n_stages < 1 || n_stages > kChainMaxStages) return ST_BAD_TOKENS;
+    static ChainParams P;                     // host staging of the kernel parameters (25 KB)
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    P = ChainParams{};
+    long long slot = 0;
+    int max_n = 0;
+    for (int k = 0; k < n_stages; ++k) {
+        const qmv_stage& q = stages[k];
+        ChainStage& c = P.st[k];
+        int cfg = -1;
+        if (q.ggml_type == F_Q4_K && q.n_in == 4096) cfg = CFG_Q4K_4096;
+        else if (q.ggml_type == F_Q6_K && q.n_in == 14336) cfg = CFG_Q6K_14336;
+        else if (q.ggml_type == F_Q4_K && q.n_in == 14336) cfg = CFG_Q4K_14336;
+        else if (q.ggml_type == F_Q6_K && q.n_in == 4096) cfg = CFG_Q6K_4096;
+        else if (q.ggml_type == F_Q8_0 && q.n_in == 4096) cfg = CFG_Q8_0_4096;
+        if (cfg < 0) return known_format(q.ggml_type) ? ST_BAD_SHAPE : ST_BAD_FORMAT;
+        if (q.n_jobs < 1 || q.n_jobs > kMaxJobs) return ST_BAD_TOKENS;
+        if (!q.a || (q.input == QMV_INPUT_RMSNORM && !q.norm_w)) return ST_NULL;
+        if (q.input < 0 || q.input > 2) return ST_BAD_SHAPE;
+        if (!aligned(q.a, 4) || (q.b && !aligned(q.b, 4))) return ST_BAD_ALIGN;
+        c.cfg = cfg;
+        c.n_jobs = q.n_jobs;
+        c.n_in = q.n_in;
+        c.row_bytes = (long long)(q.n_in / block_values(q.ggml_type)) * block_bytes(q.ggml_type);
+        long long rows = 0;
+        for (int j = 0; j < q.n_jobs; ++j) {
+            if (!q.w[j] || !q.y[j]) return ST_NULL;
+            if (q.n_out[j] <= 0) return ST_BAD_SHAPE;
+            if (!aligned(q.w[j], 16) || !aligned(q.y[j], 4)) return ST_BAD_ALIGN;
+            c.w[j] = q.w[j];
+            c.y[j] = q.y[j];
+            c.n_out[j] = q.n_out[j];
+            c.row_start[j] = rows;
+            rows += q.n_out[j];
+        }
+        c.row_start[q.n_jobs] = rows;
+        c.total_rows = rows;
+        c.R = chain_cfg_nper(cfg) * (32 * kChainNcw / chain_cfg_g(cfg));
+        c.in_kind = q.input;
+        c.a = q.a;
+        c.b = q.b;
+        c.norm_w = q.norm_w;
+        c.eps = q.eps;
+        c.h_out = q.h_out;
+        c.wait = q.wait;
+        slot = std::max(slot, (long long)c.R * c.row_bytes);
+        max_n = std::max(max_n, q.n_in);
+    }
+    // the kernel instance that carries every configuration this chain uses (at most two)
+    int used = 0;
+    for (int k = 0; k < n_stages; ++k) used |= 1 << P.st[k].cfg;
+    const int pairs[4][2] = {{CFG_Q4K_4096, CFG_Q6K_14336}, {CFG_Q4K_4096, CFG_Q4K_14336},
+                             {CFG_Q6K_4096, CFG_Q6K_14336}, {CFG_Q8_0_4096, CFG_Q6K_4096}};
+    int pair = -1;
+    for (int i = 0; i < 4 && pair < 0; ++i)
+        if ((used & ~((1 << pairs[i][0]) | (1 << pairs[i][1]))) == 0) pair = i;
+    if (pair < 0) return ST_BAD_SHAPE;           // more than two row shapes: split the chain
+    slot = (slot + 127) / 128 * 128;
+    const long long other = chain_red_bytes(kChainNcw) + tma_act_bytes(max_n) + 2 * 8 * 32;
+    long long S = (kSmemCap - other) / slot;
+    if (S > 32) S = 32;
+    if (S < 2) return ST_BAD_SHAPE;
+    P.n_stages = n_stages;
+    P.S = int(S);
+    P.slot_bytes = int(slot);
+    P.max_n_in = max_n;
+    P.ws = workspace;
+    P.status = device_status_ptr();
+    const int smem = int(S * slot + other);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (cudaMemsetAsync(workspace, 0, sizeof(int) * n_stages, st) != cudaSuccess) return launched();
+    void (*kern)(const ChainParams) = pair == 0 ? chain_kernel<kChainNcw, CFG_Q4K_4096, CFG_Q6K_14336>
+                                    : pair == 1 ? chain_kernel<kChainNcw, CFG_Q4K_4096, CFG_Q4K_14336>
+                                    : pair == 2 ? chain_kernel<kChainNcw, CFG_Q6K_4096, CFG_Q6K_14336>
+                                                : chain_kernel<kChainNcw, CFG_Q8_0_4096, CFG_Q6K_4096>;
+    static int configured[64][4] = {{0}};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev][pair]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap) != cudaSuccess)
+            return launched();
+        configured[dev][pair] = 1;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sm_count());
+    cfg.blockDim = dim3(32 * (kChainNcw + 1));
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, P) != cudaSuccess) return launched();
+    return launched();
 }
 
 int qmv_set_pdl(int enabled) {

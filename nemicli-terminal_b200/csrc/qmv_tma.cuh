@@ -171,6 +171,8 @@ struct Act {                              // the activation of one unit, in regi
     int4 r[UnitTraits<FMT>::NQ];          // xq2 bytes
     float d[UnitTraits<FMT>::NS];         // xd / 254 of each scale group
     float s[UnitTraits<FMT>::NS];         // xs of each group (0 where another lane applies the offset)
+    int sq[FMT == F_Q6_K ? 2 : 1];        // Q6_K: sum of the 16 xq of each group (the -32 of the codes)
+    int sr[FMT == F_Q6_K ? 2 : 1];        //       sum of the 16 xq2 of each group
 };
 
 template <bool GLOBAL>
@@ -220,6 +222,14 @@ __device__ __forceinline__ void load_act(Act<FMT>& a, int u, const int8_t* xq, c
         a.r[0] = ldq16<GLOBAL>(xq2 + o + 32 * A); a.r[1] = ldq16<GLOBAL>(xq2 + o + 32 * B);
         a.d[0] = ldf<GLOBAL, SCALES>(xd, b * 8 + 4 * n + A) * kInv254;
         a.d[1] = ldf<GLOBAL, SCALES>(xd, b * 8 + 4 * n + B) * kInv254;
+        if constexpr (FMT == F_Q6_K) {
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+                const int4 x = a.q[g], y = a.r[g];
+                a.sq[g] = dp4(0x01010101u, x.w, dp4(0x01010101u, x.z, dp4(0x01010101u, x.y, dp4(0x01010101u, x.x, 0))));
+                a.sr[g] = dp4(0x01010101u, y.w, dp4(0x01010101u, y.z, dp4(0x01010101u, y.y, dp4(0x01010101u, y.x, 0))));
+            }
+        }
     } else {   // TQ2_0
         const int b = u >> 3, q = u & 7, n = q >> 2, j = q & 3, o = b * 256 + 128 * n + 8 * j;
         const int2 g0 = ldq8<GLOBAL>(xq + o), g1 = ldq8<GLOBAL>(xq + o + 32), g2 = ldq8<GLOBAL>(xq + o + 64),
@@ -283,14 +293,19 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
         const uint32_t sb = rs + b * 210;
         const uint4 ql = lds16_a2(sb + 64 * n + 16 * j), qh = lds16_a2(sb + 128 + 32 * n + l0);
         const uint32_t L[4] = {ql.x, ql.y, ql.z, ql.w}, H[4] = {qh.x, qh.y, qh.z, qh.w};
+        // unsigned 6-bit codes: group A = low nibble | qh bits 2A..2A+1 moved to bits 4..5, group A + 2 =
+        // high nibble | qh bits 2A+4..2A+5; the -32 of every code is subtracted with the activation sums
+        const int shA = 4 - 2 * A, shB = 2 * A;
         uint32_t wa[4], wb[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            wa[i] = __vsub4((L[i] & 0x0F0F0F0Fu) | (((H[i] >> (2 * A)) & 0x03030303u) << 4), 0x20202020u);
-            wb[i] = __vsub4(((L[i] >> 4) & 0x0F0F0F0Fu) | (((H[i] >> (2 * B)) & 0x03030303u) << 4), 0x20202020u);
+            wa[i] = (L[i] & 0x0F0F0F0Fu) | ((H[i] << shA) & 0x30303030u);
+            wb[i] = ((L[i] >> 4) & 0x0F0F0F0Fu) | ((H[i] >> shB) & 0x30303030u);
         }
-        o.s[0] = dot4(wa, a.q[0]); o.s[1] = dot4(wb, a.q[1]);
-        o.u[0] = dot4(wa, a.r[0]); o.u[1] = dot4(wb, a.r[1]);
+        o.s[0] = dot4(wa, a.q[0]) - 32 * a.sq[0];
+        o.s[1] = dot4(wb, a.q[1]) - 32 * a.sq[1];
+        o.u[0] = dot4(wa, a.r[0]) - 32 * a.sr[0];
+        o.u[1] = dot4(wb, a.r[1]) - 32 * a.sr[1];
         const float d = h2f(lds16u(sb + 208));
         o.wsc[0] = d * float(int8_t(lds8u(sb + 192 + 8 * n + 2 * A + (j & 1))));
         o.wsc[1] = d * float(int8_t(lds8u(sb + 192 + 8 * n + 2 * B + (j & 1))));
@@ -432,7 +447,9 @@ __device__ __forceinline__ const uint8_t* tma_slot_base(const TmaParams& P, int 
 // shared-memory layout: [stages x stage bytes][reduction 2 x NCW x R floats][codebook 2 KB]
 //                      [fused activation: xq K, xq2 K, xd K/32, xs K/32 (XF only)][mbarriers]
 constexpr int kTmaRowsPerTeam = 4;          // rows of a full tile per team (compile-time fast path)
-__host__ __device__ constexpr int tma_red_bytes(int ncw) { return 2 * ncw * kTmaRowsPerTeam * 4; }
+// partial sums of rows spread over several warps: [row in window][warp in team], reduced once per window
+constexpr int kPartFloats = 2048;
+__host__ __device__ constexpr int tma_red_bytes(int ncw) { return kPartFloats * 4 + 0 * ncw; }
 __host__ __device__ constexpr long long tma_act_bytes(int n_in) { return 2LL * n_in + n_in / 4; }
 constexpr int kConsumerBarrier = 15;        // named barrier of all consumer warps (teams use 1..8)
 
@@ -531,6 +548,24 @@ __global__ void __launch_bounds__(32 * (NCW + 1), NCW <= 8 ? 2 : 1) mv_tma_kerne
     long long cur_row = -1;
     bool dead = false;
     int it = 0;
+    // window of rows whose cross-warp partial sums wait in shared memory (teams wider than a warp)
+    constexpr int PR = kPartFloats / WPT;
+    float* part = red;
+    int w_job = 0, w_row0 = 0, w_rows = 0;
+    auto flush = [&]() {                                    // every consumer thread, uniformly
+        named_sync(kConsumerBarrier, 32 * NCW);
+        if (!dead) {
+            float* y = P.ids == nullptr ? P.y[w_job] : P.y[0] + (long long)w_job * P.n_out[0];
+            for (int rl = cl; rl < w_rows; rl += 32 * NCW) {
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < WPT; ++w) v += part[rl * WPT + w];
+                y[w_row0 + rl] = v;
+            }
+        }
+        named_sync(kConsumerBarrier, 32 * NCW);
+        w_rows = 0;
+    };
     const long long hi = cta_row_begin(P, blockIdx.x + 1);
     for (long long g = cta_row_begin(P, blockIdx.x); g < hi; ++it) {
         const TileInfo ti = tile_at(P, g, hi);
@@ -601,8 +636,8 @@ __global__ void __launch_bounds__(32 * (NCW + 1), NCW <= 8 ? 2 : 1) mv_tma_kerne
         __syncwarp();
         if (got && lane == 0) mbar_arrive(empty0 + 8 * s);   // this warp is done with the stage
         if constexpr (!SUMS) {
-            float* y = P.ids == nullptr ? P.y[ti.job] : P.y[0] + (long long)ti.slot * P.n_out[0];
             if constexpr (G <= 32) {
+                float* y = P.ids == nullptr ? P.y[ti.job] : P.y[0] + (long long)ti.slot * P.n_out[0];
 #pragma unroll
                 for (int i = 0; i < NPER; ++i) {
                     float v = acc[i];
@@ -612,25 +647,25 @@ __global__ void __launch_bounds__(32 * (NCW + 1), NCW <= 8 ? 2 : 1) mv_tma_kerne
                     if (li == 0 && got && r < ti.nrows) y[ti.row0 + r] = v;
                 }
             } else {
-                float* rb = red + (it & 1) * NCW * NPER;
+                const int wjob = P.ids == nullptr ? ti.job : ti.slot;
+                if (w_rows > 0 && (wjob != w_job || ti.row0 != w_row0 + w_rows || w_rows + ti.nrows > PR)) flush();
+                if (w_rows == 0) {
+                    w_job = wjob;
+                    w_row0 = ti.row0;
+                }
+                const int wt = li >> 5;                      // warp within the team
 #pragma unroll
                 for (int i = 0; i < NPER; ++i) {
                     const float v = warp_sum(acc[i]);
-                    if (lane == 0) rb[warp * NPER + i] = v;
+                    const int r = team + TEAMS * i;
+                    if (lane == 0 && r < ti.nrows) part[(w_rows + r) * WPT + wt] = v;
                 }
-                named_sync(1 + team, G);                     // this team's warps only
-                const int wt = li >> 5;                      // warp within the team
-                if (got && wt == 0 && lane < NPER) {         // lane i of the team's first warp: row team + TEAMS*i
-                    const int r = team + TEAMS * lane;
-                    if (r < ti.nrows) {
-                        float v = 0.f;
-#pragma unroll
-                        for (int w = 0; w < WPT; ++w) v += rb[(team * WPT + w) * NPER + lane];
-                        y[ti.row0 + r] = v;
-                    }
-                }
+                w_rows += ti.nrows;
             }
         }
+    }
+    if constexpr (!SUMS && G > 32) {
+        if (w_rows > 0) flush();
     }
 }
 
