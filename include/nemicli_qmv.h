@@ -39,6 +39,7 @@ extern "C" {
 #define QMV_ERR_LAUNCH 5   /* CUDA refused the launch (qmv_last_cuda_error has the cudaError_t) */
 #define QMV_ERR_NULL 6     /* a required pointer is null */
 #define QMV_ERR_DEVICE 7   /* the device status word could not be read */
+#define QMV_ERR_TOO_LARGE 8 /* a size beyond the fixed maximum of a no-allocation entry point */
 
 /* Bits of the device status word (qmv_device_status). */
 #define QMV_DEV_BAD_ADDRESS 1   /* an expert id was outside [0, n_exp) or an address-table entry misaligned */
@@ -134,6 +135,20 @@ typedef struct qmv_stage {
  * (ggufengine/models/baukasten.py:217-240: norm_q8 -> mv(q,k,v) -> ... -> akt_q8 -> mv(down)) for its
  * matvec and producer kernels (mmvq.py:102-134, 852-865). */
 int qmv_chain(const qmv_stage* stages, int n_stages, int* workspace, void* stream);
+
+/* qmv_chain without a caller-provided workspace, for callers that cannot allocate device memory at
+ * the call site: a runtime that owns every allocation up front (an arena or a caching allocator it
+ * must not re-enter from inside a kernel-launch callback), or an FFI host (cgo, JNI, ctypes) with no
+ * device allocator of its own.  The grid-barrier counters live in a fixed array in the library's
+ * device image (QMV_CHAIN_NOALLOC_MAX_STAGES ints, 512 bytes); n_stages above that returns
+ * QMV_ERR_TOO_LARGE, and nothing is allocated or freed by the call.  The counters are cleared on
+ * `stream` before the launch.  The first call on each device looks up the array's address with that
+ * device current (module loading can happen then), so make that first call before any stream capture.
+ * All calls on one device share the one array: calls that overlap in time (other streams, other host
+ * threads) race on it, so serialise them; use qmv_chain with a workspace each for concurrent chains.
+ * Replaces: nothing — it has no counterpart in the reference (whose decoder allocates through torch). */
+#define QMV_CHAIN_NOALLOC_MAX_STAGES 128
+int qmv_chain_noalloc(const qmv_stage* stages, int n_stages, void* stream);
 
 /* Test hook: the int32 sums of one token per (row, unit), unit = the values sharing one weight scale
  * and one activation scale (16 for Q6_K, else 32): s = sum code * xq, s2 = sum code * xq2, from the

@@ -33,6 +33,7 @@ _SIGNATURES = {
     "qmv_mv_x": ([I, I, P, P, P, I, P, I, P], I),
     "qmv_set_pdl": ([I], I),
     "qmv_chain": ([P, I, P, P], I),
+    "qmv_chain_noalloc": ([P, I, P], I),
     "qmv_device_status": ([I, P, P], I),
 }
 

@@ -16,6 +16,31 @@ namespace {
 thread_local int g_last_cuda_error = 0;
 __device__ int g_device_status = 0;
 
+// Grid-barrier counters of qmv_chain_noalloc: one int per stage, for callers that cannot allocate.
+static __device__ __align__(256) int g_chain_counters[QMV_CHAIN_NOALLOC_MAX_STAGES];
+static_assert(QMV_CHAIN_NOALLOC_MAX_STAGES <= kChainMaxStages, "counter array larger than a chain");
+
+// Address of g_chain_counters on the current device, looked up once per device (with that device
+// current) and cached; null if the lookup fails (its cudaError_t goes to qmv_last_cuda_error).
+int* chain_counters_ptr() {
+    static std::mutex mu;
+    static int* cache[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!cache[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_chain_counters);
+        if (e != cudaSuccess || !p) {
+            g_last_cuda_error = int(e);
+            cudaGetLastError();                // do not leave the error for the next launch check
+            return nullptr;
+        }
+        cache[dev] = static_cast<int*>(p);
+    }
+    return cache[dev];
+}
+
 int sm_count() {
     static std::mutex mu;
     static int cache[64] = {0};
@@ -288,6 +313,7 @@ const char* qmv_status_string(int status) {
     case ST_LAUNCH: return "CUDA launch failed";
     case ST_NULL: return "null pointer";
     case ST_DEVICE: return "device status query failed";
+    case QMV_ERR_TOO_LARGE: return "size beyond the fixed maximum of a no-allocation entry point";
     }
     return "unknown status";
 }
@@ -572,6 +598,15 @@ int qmv_chain(const qmv_stage* stages, int n_stages, int* workspace, void* strea
     cfg.numAttrs = 1;
     if (cudaLaunchKernelEx(&cfg, kern, P) != cudaSuccess) return launched();
     return launched();
+}
+
+int qmv_chain_noalloc(const qmv_stage* stages, int n_stages, void* stream) {
+    if (!stages) return ST_NULL;
+    if (n_stages > QMV_CHAIN_NOALLOC_MAX_STAGES) return QMV_ERR_TOO_LARGE;
+    if (n_stages < 1) return ST_BAD_TOKENS;
+    int* counters = chain_counters_ptr();
+    if (!counters) return ST_DEVICE;
+    return qmv_chain(stages, n_stages, counters, stream);     // clears the counters on `stream`
 }
 
 int qmv_set_pdl(int enabled) {
