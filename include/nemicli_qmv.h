@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define NEMICLI_QMV_ABI_VERSION 1
+#define NEMICLI_QMV_ABI_VERSION 2
 
 #define QMV_OK 0
 #define QMV_ERR_FORMAT 1   /* format not one of the six above */
@@ -130,22 +130,32 @@ typedef struct qmv_stage {
 /* A list of dependent single-token matvec stages (a decode step's projections with their RMS-norm and
  * SiLU-gate producers fused in) in one persistent, cooperative launch.  stages: host array of n_stages
  * (at most 128).  Shapes taken: Q4_K with n_in 4096 or 14336, Q6_K with n_in 4096 or 14336, Q8_0 with
- * n_in 4096 (others: QMV_ERR_SHAPE).  workspace: n_stages ints of device memory (grid-barrier counters),
- * cleared by the call on `stream`.  Replaces: the reference's fused one-token layer step
- * (ggufengine/models/baukasten.py:217-240: norm_q8 -> mv(q,k,v) -> ... -> akt_q8 -> mv(down)) for its
- * matvec and producer kernels (mmvq.py:102-134, 852-865). */
-int qmv_chain(const qmv_stage* stages, int n_stages, int* workspace, void* stream);
+ * n_in 4096 (others: QMV_ERR_SHAPE).  workspace: QMV_CHAIN_WORKSPACE_BYTES bytes of device memory,
+ * 256-byte aligned (grid-barrier and group counters, cleared by the call on `stream`, and the
+ * quantised activations); chains that run at the same time need separate workspaces.
+ * A stage whose every input vector that the previous stage writes is one whole output of it has its
+ * input quantised by the previous stage's CTAs as the 32-value groups complete; other stages quantise
+ * their input at their start.  The quantised RMSNORM input is u = v * norm_w with the 1/rms factor
+ * applied to its scales, so it can differ from quantising x itself by rounding.
+ * Replaces: the reference's fused one-token layer step (ggufengine/models/baukasten.py:217-240:
+ * norm_q8 -> mv(q,k,v) -> ... -> akt_q8 -> mv(down)) for its matvec and producer kernels
+ * (mmvq.py:102-134, 852-865). */
+#define QMV_CHAIN_WORKSPACE_BYTES 72704
+int qmv_chain(const qmv_stage* stages, int n_stages, void* workspace, void* stream);
+
+/* Bytes of workspace qmv_chain needs (QMV_CHAIN_WORKSPACE_BYTES).  Replaces: nothing in the reference. */
+int64_t qmv_chain_workspace_bytes(void);
 
 /* qmv_chain without a caller-provided workspace, for callers that cannot allocate device memory at
  * the call site: a runtime that owns every allocation up front (an arena or a caching allocator it
  * must not re-enter from inside a kernel-launch callback), or an FFI host (cgo, JNI, ctypes) with no
- * device allocator of its own.  The grid-barrier counters live in a fixed array in the library's
- * device image (QMV_CHAIN_NOALLOC_MAX_STAGES ints, 512 bytes); n_stages above that returns
- * QMV_ERR_TOO_LARGE, and nothing is allocated or freed by the call.  The counters are cleared on
- * `stream` before the launch.  The first call on each device looks up the array's address with that
- * device current (module loading can happen then), so make that first call before any stream capture.
- * All calls on one device share the one array: calls that overlap in time (other streams, other host
- * threads) race on it, so serialise them; use qmv_chain with a workspace each for concurrent chains.
+ * device allocator of its own.  The workspace is a fixed array in the library's device image
+ * (QMV_CHAIN_WORKSPACE_BYTES); n_stages above QMV_CHAIN_NOALLOC_MAX_STAGES returns QMV_ERR_TOO_LARGE,
+ * and nothing is allocated or freed by the call.  Its counters are cleared on `stream` before the
+ * launch.  The first call on each device looks up the array's address with that device current
+ * (module loading can happen then), so make that first call before any stream capture.  All calls on
+ * one device share the one array: calls that overlap in time (other streams, other host threads) race
+ * on it, so serialise them; use qmv_chain with a workspace each for concurrent chains.
  * Replaces: nothing — it has no counterpart in the reference (whose decoder allocates through torch). */
 #define QMV_CHAIN_NOALLOC_MAX_STAGES 128
 int qmv_chain_noalloc(const qmv_stage* stages, int n_stages, void* stream);

@@ -34,10 +34,11 @@ _SIGNATURES = {
     "qmv_set_pdl": ([I], I),
     "qmv_chain": ([P, I, P, P], I),
     "qmv_chain_noalloc": ([P, I, P], I),
+    "qmv_chain_workspace_bytes": ([], LL),
     "qmv_device_status": ([I, P, P], I),
 }
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 
 def lib_path() -> str:

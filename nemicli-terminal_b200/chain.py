@@ -92,7 +92,7 @@ class Chain:
             s.a, s.b, s.norm_w, s.h_out = _p(st.a), _p(st.b), _p(st.norm_w), _p(st.h_out)
             s.eps = st.eps
             s.wait = int(st.wait)
-        self.workspace = torch.zeros(len(stages), dtype=torch.int32, device=dev)
+        self.workspace = torch.zeros(_lib.load().qmv_chain_workspace_bytes(), dtype=torch.uint8, device=dev)
         self.device = dev
 
     def run(self) -> None:

@@ -16,27 +16,29 @@ namespace {
 thread_local int g_last_cuda_error = 0;
 __device__ int g_device_status = 0;
 
-// Grid-barrier counters of qmv_chain_noalloc: one int per stage, for callers that cannot allocate.
-static __device__ __align__(256) int g_chain_counters[QMV_CHAIN_NOALLOC_MAX_STAGES];
-static_assert(QMV_CHAIN_NOALLOC_MAX_STAGES <= kChainMaxStages, "counter array larger than a chain");
+// Workspace of qmv_chain_noalloc (barrier and group counters, activation buffers), for callers that
+// cannot allocate.
+static __device__ __align__(256) uint8_t g_chain_workspace[QMV_CHAIN_WORKSPACE_BYTES];
+static_assert(QMV_CHAIN_NOALLOC_MAX_STAGES <= kChainMaxStages, "more stages than a chain takes");
+static_assert(QMV_CHAIN_WORKSPACE_BYTES == kChainWorkspaceBytes, "workspace size in the header is stale");
 
-// Address of g_chain_counters on the current device, looked up once per device (with that device
+// Address of g_chain_workspace on the current device, looked up once per device (with that device
 // current) and cached; null if the lookup fails (its cudaError_t goes to qmv_last_cuda_error).
-int* chain_counters_ptr() {
+void* chain_workspace_ptr() {
     static std::mutex mu;
-    static int* cache[64] = {nullptr};
+    static void* cache[64] = {nullptr};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
     std::lock_guard<std::mutex> lock(mu);
     if (!cache[dev]) {
         void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_chain_counters);
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_chain_workspace);
         if (e != cudaSuccess || !p) {
             g_last_cuda_error = int(e);
             cudaGetLastError();                // do not leave the error for the next launch check
             return nullptr;
         }
-        cache[dev] = static_cast<int*>(p);
+        cache[dev] = p;
     }
     return cache[dev];
 }
@@ -500,15 +502,15 @@ int qmv_mv_x(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_ou
     return ST_BAD_SHAPE;        // the shape needs the fallback kernel: quantise with qmv_quant_q8, then qmv_mv
 }
 
-int qmv_chain(const qmv_stage* stages, int n_stages, int* workspace, void* stream) {
+int qmv_chain(const qmv_stage* stages, int n_stages, void* workspace, void* stream) {
     if (!stages || !workspace) return ST_NULL;
     if (n_stages < 1 || n_stages > kChainMaxStages) return ST_BAD_TOKENS;
-    static ChainParams P;                     // host staging of the kernel parameters (25 KB)
+    if (!aligned(workspace, 256)) return ST_BAD_ALIGN;
+    static ChainParams P;                     // host staging of the kernel parameters (~25 KB)
     static std::mutex mu;
     std::lock_guard<std::mutex> lock(mu);
     P = ChainParams{};
     long long slot = 0;
-    int max_n = 0;
     for (int k = 0; k < n_stages; ++k) {
         const qmv_stage& q = stages[k];
         ChainStage& c = P.st[k];
@@ -543,13 +545,34 @@ int qmv_chain(const qmv_stage* stages, int n_stages, int* workspace, void* strea
         c.R = chain_cfg_nper(cfg) * (32 * kChainNcw / chain_cfg_g(cfg));
         c.in_kind = q.input;
         c.a = q.a;
-        c.b = q.b;
+        c.b = q.input == QMV_INPUT_RAW ? nullptr : q.b;
         c.norm_w = q.norm_w;
         c.eps = q.eps;
         c.h_out = q.h_out;
-        c.wait = q.wait;
+        c.wait = k > 0 && q.wait;
         slot = std::max(slot, (long long)c.R * c.row_bytes);
-        max_n = std::max(max_n, q.n_in);
+    }
+    // fed stages: every input vector that the previous stage writes is one whole job output of it; the
+    // previous stage's CTAs then quantise the input group by group as they complete it
+    for (int k = 1; k < n_stages; ++k) {
+        ChainStage& c = P.st[k];
+        ChainStage& pv = P.st[k - 1];
+        if (!c.wait) continue;
+        auto job_of = [&](const float* v) -> int {
+            for (int j = 0; j < pv.n_jobs; ++j)
+                if (v && pv.y[j] == v && pv.n_out[j] == c.n_in) return j;
+            return -1;
+        };
+        const int ja = job_of(c.a), jb = job_of(c.b);
+        bool ok = false;
+        if (c.in_kind == CH_RAW) ok = ja >= 0;
+        else if (c.in_kind == CH_SILU_MUL) ok = ja >= 0 && (c.b == nullptr || jb >= 0);
+        else ok = ja >= 0 || jb >= 0;
+        if (!ok) continue;
+        const int mask = (ja >= 0 ? 1 << ja : 0) | (jb >= 0 ? 1 << jb : 0);
+        c.fed = 1;
+        pv.feed_mask = mask;
+        pv.feed_target = 32 * __builtin_popcount(mask);
     }
     // the kernel instance that carries every configuration this chain uses (at most two)
     int used = 0;
@@ -561,19 +584,33 @@ int qmv_chain(const qmv_stage* stages, int n_stages, int* workspace, void* strea
         if ((used & ~((1 << pairs[i][0]) | (1 << pairs[i][1]))) == 0) pair = i;
     if (pair < 0) return ST_BAD_SHAPE;           // more than two row shapes: split the chain
     slot = (slot + 127) / 128 * 128;
-    const long long other = chain_red_bytes(kChainNcw) + tma_act_bytes(max_n) + 2 * 8 * 32;
+    const long long other = chain_red_bytes() + 2 * 8 * 32 + 16;
     long long S = (kSmemCap - other) / slot;
+    static const int env_slots = getenv("NEMICLI_CHAIN_SLOTS") ? atoi(getenv("NEMICLI_CHAIN_SLOTS")) : 0;
+    static const int env_bt = getenv("NEMICLI_CHAIN_BOUNDARY") ? atoi(getenv("NEMICLI_CHAIN_BOUNDARY")) : -1;
+    if (env_slots >= 2 && env_slots < S) S = env_slots;
+    else if (env_slots == 0 && S > 4) S = 4;      // deeper rings only add queueing latency (measured)
     if (S > 32) S = 32;
     if (S < 2) return ST_BAD_SHAPE;
     P.n_stages = n_stages;
     P.S = int(S);
     P.slot_bytes = int(slot);
-    P.max_n_in = max_n;
-    P.ws = workspace;
+    P.boundary_tiles = env_bt >= 0 ? env_bt : 2;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    P.bar = reinterpret_cast<int*>(ws);
+    P.cnt = P.bar + 2 * kChainMaxStages;
+    for (int b = 0; b < 2; ++b) {
+        uint8_t* base = ws + kChainCounterBytes + b * kChainActBytes;
+        P.xq[b] = reinterpret_cast<int8_t*>(base);
+        P.xq2[b] = P.xq[b] + kChainMaxIn;
+        P.xd[b] = reinterpret_cast<float*>(P.xq2[b] + kChainMaxIn);
+        P.xs[b] = P.xd[b] + kChainMaxGroups;
+        P.pss[b] = P.xs[b] + kChainMaxGroups;
+    }
     P.status = device_status_ptr();
     const int smem = int(S * slot + other);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (cudaMemsetAsync(workspace, 0, sizeof(int) * n_stages, st) != cudaSuccess) return launched();
+    if (cudaMemsetAsync(workspace, 0, kChainCounterBytes, st) != cudaSuccess) return launched();
     void (*kern)(const ChainParams) = pair == 0 ? chain_kernel<kChainNcw, CFG_Q4K_4096, CFG_Q6K_14336>
                                     : pair == 1 ? chain_kernel<kChainNcw, CFG_Q4K_4096, CFG_Q4K_14336>
                                     : pair == 2 ? chain_kernel<kChainNcw, CFG_Q6K_4096, CFG_Q6K_14336>
@@ -600,13 +637,15 @@ int qmv_chain(const qmv_stage* stages, int n_stages, int* workspace, void* strea
     return launched();
 }
 
+int64_t qmv_chain_workspace_bytes(void) { return kChainWorkspaceBytes; }
+
 int qmv_chain_noalloc(const qmv_stage* stages, int n_stages, void* stream) {
     if (!stages) return ST_NULL;
     if (n_stages > QMV_CHAIN_NOALLOC_MAX_STAGES) return QMV_ERR_TOO_LARGE;
     if (n_stages < 1) return ST_BAD_TOKENS;
-    int* counters = chain_counters_ptr();
-    if (!counters) return ST_DEVICE;
-    return qmv_chain(stages, n_stages, counters, stream);     // clears the counters on `stream`
+    void* ws = chain_workspace_ptr();
+    if (!ws) return ST_DEVICE;
+    return qmv_chain(stages, n_stages, ws, stream);           // clears the counters on `stream`
 }
 
 int qmv_set_pdl(int enabled) {

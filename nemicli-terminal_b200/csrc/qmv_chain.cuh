@@ -1,15 +1,25 @@
 // Decode chain: a list of dependent single-token matvec stages in one persistent, cooperative launch.
 //
-// A stage is 1..4 matrices that read one input vector (q/k/v, o, gate/up, down).  Its input is built
-// inside the kernel by a fused producer from earlier outputs (the reference runs these as separate
-// kernels: norm_q8, akt_q8, the Eingang of mmvq.py:102-134, 825-849):
+// A stage is 1..4 matrices that read one input vector (q/k/v, o, gate/up, down).  Its input x is built
+// from fp32 vectors by a fused producer (the reference runs these as separate kernels: norm_q8,
+// akt_q8, the Eingang of mmvq.py:102-134, 825-849):
 //   RAW       x = a
 //   RMSNORM   v = a (+ b, written to h_out), x = v * rsqrt(mean(v^2) + eps) * norm_w
 //   SILU_MUL  x = silu(a) * b  (b == null: silu(a))
-// and quantised into the two-stage int8 activation in shared memory.  Between a stage and the
-// earlier stages it reads, the CTAs meet at a grid barrier (a counter per stage in the workspace,
-// every spin bounded in time).  The producer warp never waits at these barriers: the weights do not
-// depend on them, so it streams the next stages' tiles into the ring while the consumers wait.
+// and quantised into the two-stage int8 activation (xq, xq2, xd, xs per 32 values) ONCE, in a global
+// buffer of the workspace, 32 values (one group) per warp:
+//   fed stage     the CTA that writes the last rows of a group of the previous stage's outputs (a
+//                 counter per group in the workspace tells it) quantises that group right away;
+//   other stages  the groups are split over the CTAs at the start of the stage, then a grid barrier.
+// RMSNORM groups are quantised before the norm scale is known (u = v * norm_w, with the group's sum of
+// v^2 stored beside it); the consumers multiply xd and xs by the scale when they load the activation.
+// After a grid barrier every consumer lane loads its slice of the activation into registers and keeps
+// it for the stage.  The producer warp never waits at these barriers: the weights do not depend on
+// them, so it streams the next stages' tiles into the ring while the consumers wait.
+//
+// Two activation buffers alternate by stage parity: a buffer is rewritten only after a grid barrier
+// that follows every CTA's last read of it.  Every spin (grid barrier, mbarrier) is bounded in time and
+// sets a status bit on expiry.
 #pragma once
 #include "qmv_tma.cuh"
 
@@ -20,7 +30,18 @@ enum : int { CH_RAW = 0, CH_RMSNORM = 1, CH_SILU_MUL = 2 };
 enum : int { CFG_Q4K_4096 = 0, CFG_Q6K_14336 = 1, CFG_Q4K_14336 = 2, CFG_Q6K_4096 = 3, CFG_Q8_0_4096 = 4, CFG_COUNT = 5 };
 constexpr int kChainMaxStages = 128;
 constexpr int kChainNcw = 16;
+constexpr int kChainMaxIn = 14336;                  // longest input vector a chain stage takes
+constexpr int kChainMaxGroups = kChainMaxIn / 32;
+constexpr int kChainPartFloats = 1024;              // deferred cross-warp partial sums (shared memory)
+constexpr int kChainStageIn = 4096;                 // inputs up to this length are staged in shared memory
+constexpr int kChainActSmem = 2 * kChainStageIn + 8 * (kChainStageIn / 32);
 enum : int { DEV_BARRIER_TIMEOUT = 4 };
+
+// workspace: [barrier counters 2 x kChainMaxStages][group counters 2 x kChainMaxGroups] (zeroed per
+// launch), then two activation buffers [xq N][xq2 N][xd N/32][xs N/32][sum of squares N/32], N = kChainMaxIn
+constexpr long long kChainCounterBytes = 4LL * (2 * kChainMaxStages + 2 * kChainMaxGroups);
+constexpr long long kChainActBytes = 2LL * kChainMaxIn + 3LL * 4 * kChainMaxGroups;
+constexpr long long kChainWorkspaceBytes = kChainCounterBytes + 2 * kChainActBytes;
 
 struct ChainStage {
     const uint8_t* w[kMaxJobs];
@@ -35,6 +56,9 @@ struct ChainStage {
     float eps;
     int n_out[kMaxJobs];
     int n_jobs, cfg, n_in, R, in_kind, wait;
+    int fed;              // 1: the previous stage's CTAs quantise this stage's input as its groups complete
+    int feed_mask;        // bit j: output of job j is an input vector of the NEXT stage (which is fed)
+    int feed_target;      // rows of this stage that complete one group of the next stage's input
 };
 
 struct ChainParams {
@@ -42,32 +66,44 @@ struct ChainParams {
     int n_stages;
     int S;                 // ring slots
     int slot_bytes;
-    int max_n_in;
-    int* ws;               // one counter per stage (zeroed before the launch)
+    int boundary_tiles;    // tiles of a stage the producer issues before that stage's consumers start
+    int* bar;              // grid-barrier counters: stage k done at [k], its input ready at [kChainMaxStages + k]
+    int* cnt;              // group counters [buffer][group]
+    int8_t* xq[2];
+    int8_t* xq2[2];
+    float* xd[2];
+    float* xs[2];
+    float* pss[2];         // per group: sum of v^2 (RMSNORM inputs)
     int* status;
 };
 
 template <int CFG> struct ChainCfg;
+// tiles of 27..37 KB (R = NPER * 512 / G rows): six ring slots fit in shared memory
 template <> struct ChainCfg<CFG_Q4K_4096> { static constexpr int FMT = F_Q4_K, G = 64, UPL = 1, NPER = 2; };
-template <> struct ChainCfg<CFG_Q6K_14336> { static constexpr int FMT = F_Q6_K, G = 256, UPL = 2, NPER = 2; };
+template <> struct ChainCfg<CFG_Q6K_14336> { static constexpr int FMT = F_Q6_K, G = 512, UPL = 1, NPER = 3; };
 template <> struct ChainCfg<CFG_Q4K_14336> { static constexpr int FMT = F_Q4_K, G = 256, UPL = 1, NPER = 2; };
 template <> struct ChainCfg<CFG_Q6K_4096> { static constexpr int FMT = F_Q6_K, G = 128, UPL = 1, NPER = 2; };
 template <> struct ChainCfg<CFG_Q8_0_4096> { static constexpr int FMT = F_Q8_0, G = 128, UPL = 1, NPER = 2; };
 
 __host__ __device__ constexpr int chain_cfg_g(int cfg) {
-    return cfg == CFG_Q4K_4096 ? 64 : cfg == CFG_Q6K_14336 ? 256 : cfg == CFG_Q4K_14336 ? 256 : 128;
+    return cfg == CFG_Q4K_4096 ? 64 : cfg == CFG_Q6K_14336 ? 512 : cfg == CFG_Q4K_14336 ? 256 : 128;
 }
-__host__ __device__ constexpr int chain_cfg_nper(int cfg) { return 2; }
+__host__ __device__ constexpr int chain_cfg_nper(int cfg) { return cfg == CFG_Q6K_14336 ? 3 : 2; }
 __host__ __device__ constexpr int chain_cfg_fmt(int cfg) {
     return cfg == CFG_Q4K_4096 || cfg == CFG_Q4K_14336 ? F_Q4_K : cfg == CFG_Q8_0_4096 ? F_Q8_0 : F_Q6_K;
 }
 __host__ __device__ constexpr int chain_cfg_nin(int cfg) {
     return cfg == CFG_Q6K_14336 || cfg == CFG_Q4K_14336 ? 14336 : 4096;
 }
+// the activation goes through shared memory when several teams would load the same units (every CTA
+// reading the same few L2 lines many times over is slow); otherwise each lane loads its own units
+__host__ __device__ constexpr bool chain_cfg_staged(int cfg) {
+    return 32 * kChainNcw / chain_cfg_g(cfg) > 1 && chain_cfg_nin(cfg) <= kChainStageIn;
+}
 
 // rows [c * total / grid, (c + 1) * total / grid) of a stage belong to CTA c
-__device__ __forceinline__ long long chain_row_begin(const ChainStage& st, int c) {
-    return (long long)c * st.total_rows / gridDim.x;
+__device__ __forceinline__ int chain_row_begin(const ChainStage& st, int c) {
+    return int((long long)c * st.total_rows / gridDim.x);
 }
 
 __device__ __forceinline__ TileInfo chain_tile_at(const ChainStage& st, long long g, long long hi) {
@@ -87,205 +123,225 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
     return v;
 }
 
-// ---- fused input producers (all consumer threads; x quantised into shared memory) ----------------
-
+// grid barrier, arrive side: this CTA's writes (ordered before by the preceding CTA barrier) are
+// released, then counted
+__device__ __forceinline__ void grid_arrive(int* counter) {
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(counter, 1);
+    }
+}
+// wait side: thread 0 spins (bounded) until every CTA has arrived, then all consumer threads go on
 template <int NCW>
-__device__ __forceinline__ float consumer_block_sum(float v, float* red) {
-    v = warp_sum(v);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+__device__ __forceinline__ void grid_wait(const int* counter, bool& dead, int* status) {
+    if (threadIdx.x == 0 && !dead) {
+        const unsigned long long t0 = global_ns();
+        while (ld_acquire(counter) < int(gridDim.x)) {
+            if (global_ns() - t0 > kWaitNs) {
+                dead = true;
+                if (status) atomicOr(status, DEV_BARRIER_TIMEOUT);
+                break;
+            }
+        }
+    }
     named_sync(kConsumerBarrier, 32 * NCW);
-    if (lane == 0) red[warp] = v;
-    named_sync(kConsumerBarrier, 32 * NCW);
-    float s = 0.f;
-#pragma unroll
-    for (int w = 0; w < NCW; ++w) s += red[w];           // same order in every thread and every CTA
-    return s;
 }
 
-// Each warp takes 32-value groups warp, warp + NCW, ... ; lane l holds value l of each.  Loads are
-// issued CH groups at a time (independent loads, one L2 round trip per chunk) before any use.
-template <int NCW>
-__device__ void chain_input(const ChainStage& st, int8_t* xq, int8_t* xq2, float* xd, float* xs, float* red) {
-    constexpr int CH = 8;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n = st.n_in, ng = n / 32;
-    const int mine = (ng - warp + NCW - 1) / NCW;             // groups of this warp
-    const bool rms = st.in_kind == CH_RMSNORM, silu = st.in_kind == CH_SILU_MUL;
-    const float* __restrict__ A = st.a;
-    const float* __restrict__ B = st.b;
-    float keep[CH];                                            // the values, when one chunk holds them all
-    float scale = 1.f;
-    if (rms) {
-        float ss = 0.f;
-        for (int c0 = 0; c0 < mine; c0 += CH) {
-            float v[CH];
-#pragma unroll
-            for (int k = 0; k < CH; ++k) {
-                const int i = 32 * (warp + NCW * (c0 + k)) + lane;
-                v[k] = c0 + k < mine ? __ldcg(A + i) : 0.f;
-            }
-            if (B) {
-#pragma unroll
-                for (int k = 0; k < CH; ++k) {
-                    const int i = 32 * (warp + NCW * (c0 + k)) + lane;
-                    if (c0 + k < mine) v[k] += __ldcg(B + i);
-                }
-            }
-#pragma unroll
-            for (int k = 0; k < CH; ++k) {
-                ss = fmaf(v[k], v[k], ss);
-                keep[k] = v[k];
-            }
-        }
-        scale = rsqrtf(consumer_block_sum<NCW>(ss, red) / float(n) + st.eps);
-        if (st.h_out && B) {                          // the new residual stream: this CTA's share of it
-            const long long lo = (long long)blockIdx.x * n / gridDim.x, hi = (long long)(blockIdx.x + 1) * n / gridDim.x;
-            for (long long i = lo + threadIdx.x; i < hi; i += 32 * NCW) st.h_out[i] = __ldcg(A + i) + __ldcg(B + i);
-        }
+// producer side of the boundary throttle: bounded spin until the consumers have started stage `want - 1`
+__device__ __forceinline__ bool wait_go(volatile int* go, int want) {
+    if (*go >= want) return true;
+    const unsigned long long t0 = global_ns();
+    while (*go < want) {
+        __nanosleep(64);
+        if (global_ns() - t0 > kWaitNs) return false;
     }
-    for (int c0 = 0; c0 < mine; c0 += CH) {
-        float v[CH], w[CH];
-        if (rms && mine <= CH) {
-#pragma unroll
-            for (int k = 0; k < CH; ++k) v[k] = keep[k];
-        } else {
-#pragma unroll
-            for (int k = 0; k < CH; ++k) {
-                const int i = 32 * (warp + NCW * (c0 + k)) + lane;
-                v[k] = c0 + k < mine ? __ldcg(A + i) : 0.f;
-            }
-            if (B) {
-#pragma unroll
-                for (int k = 0; k < CH; ++k) {
-                    const int i = 32 * (warp + NCW * (c0 + k)) + lane;
-                    w[k] = c0 + k < mine ? __ldcg(B + i) : 0.f;
-                }
-#pragma unroll
-                for (int k = 0; k < CH; ++k) v[k] = silu ? v[k] : v[k] + w[k];
-            }
+    return true;
+}
+
+// ---- input production: one warp quantises group g (32 values) of stage `ns`'s input into buffer nb --
+
+__device__ __forceinline__ void produce_group(const ChainParams& P, const ChainStage& ns, int nb, int g) {
+    const int lane = threadIdx.x & 31;
+    const int i = 32 * g + lane;
+    float v = __ldcg(ns.a + i);
+    if (ns.in_kind == CH_RMSNORM) {
+        if (ns.b) {
+            v += __ldcg(ns.b + i);
+            if (ns.h_out) ns.h_out[i] = v;             // the residual stream after this add
         }
-        if (rms) {
-#pragma unroll
-            for (int k = 0; k < CH; ++k) {
-                const int i = 32 * (warp + NCW * (c0 + k)) + lane;
-                w[k] = c0 + k < mine ? __ldg(st.norm_w + i) : 0.f;
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < CH; ++k) {
-            if (c0 + k < mine) {                               // warp-uniform
-                const int i = 32 * (warp + NCW * (c0 + k)) + lane;
-                float x = v[k];
-                if (rms) {
-                    x = x * scale * w[k];
-                } else if (silu) {
-                    x = x / (1.0f + expf(-x));
-                    if (B) x *= w[k];
-                }
-                quantize_group(x, i, xq, xq2, xd, xs);
-            }
-        }
+        const float ss = warp_sum(v * v);
+        if (lane == 0) P.pss[nb][g] = ss;
+        v *= __ldg(ns.norm_w + i);                   // the 1/rms factor is applied by the consumers
+    } else if (ns.in_kind == CH_SILU_MUL) {
+        v = v / (1.0f + expf(-v));
+        if (ns.b) v *= __ldcg(ns.b + i);
     }
-    named_sync(kConsumerBarrier, 32 * NCW);
+    quantize_group(v, i, P.xq[nb], P.xq2[nb], P.xd[nb], P.xs[nb]);
 }
 
 // ---- consumers of one stage ------------------------------------------------------------------------
 
+// Not inlined: a kernel instance carries two configurations, and two inlined copies of this loop
+// would share one register allocation and spill.  Returns the next ring iteration; *dead_io is the
+// timed-out flag (read and written once per stage).
 template <int CFG, int NCW>
-__device__ void chain_consume(const ChainStage& st, int& it, bool& dead, const int8_t* sxq, const int8_t* sxq2,
-                              const float* sxd, const float* sxs, float* red, uint32_t stage0, uint32_t slot_bytes,
-                              int S, uint32_t full0, uint32_t empty0, int* status) {
+__device__ __noinline__ int chain_consume(const ChainParams& P, const ChainStage& st, int k_stage, int it, int* dead_io,
+                                          float* part, uint8_t* act_smem, volatile int* go, uint32_t stage0,
+                                          uint32_t full0, uint32_t empty0) {
+    bool dead = *dead_io != 0;
+    const int buf = k_stage & 1;
     using C = ChainCfg<CFG>;
     constexpr int FMT = C::FMT, G = C::G, UPL = C::UPL, NPER = C::NPER;
     constexpr int TEAMS = 32 * NCW / G;
     constexpr int WPT = G >= 32 ? G / 32 : 1;
     constexpr int VPU = UnitTraits<FMT>::VPU;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int PR = kChainPartFloats / WPT;          // rows per window of deferred partial sums
+    const int S = P.S;
+    const uint32_t slot_bytes = uint32_t(P.slot_bytes);
+    const int lane = threadIdx.x & 31;
     const int cl = threadIdx.x, team = cl / G, li = cl % G;
     const int U = st.n_in / VPU;
-    const uint2* grid = nullptr;
-    Act<FMT> act[UPL];
-#pragma unroll
-    for (int i = 0; i < UPL; ++i) {
-        const int u = li + G * i;
-        if (u < U) load_act<FMT, true, false>(act[i], u, sxq, sxq2, sxd, sxs);
-    }
-    const long long hi = chain_row_begin(st, blockIdx.x + 1);
-    for (long long g = chain_row_begin(st, blockIdx.x); g < hi; ++it) {
-        const TileInfo ti = chain_tile_at(st, g, hi);
-        g += ti.nrows;
-        const int s = it % S;
-        const bool got = !dead && mbar_wait(full0 + 8 * s, (it / S) & 1);
-        if (!got && !dead) {
-            dead = true;
-            if (lane == 0 && status) atomicOr(status, DEV_TIMEOUT);
+    // the 1/rms factor of an RMSNORM input (warp 0: the groups' sums of squares in a fixed order)
+    float* s_scale = reinterpret_cast<float*>(act_smem + kChainActSmem);
+    if (threadIdx.x < 32) {
+        float scale = 1.f;
+        if (st.in_kind == CH_RMSNORM) {
+            const int ng = st.n_in / 32;
+            float ss = 0.f;
+            for (int g = lane; g < ng; g += 32) ss += __ldcg(P.pss[buf] + g);
+            scale = rsqrtf(warp_sum(ss) / float(st.n_in) + st.eps);
         }
-        const uint32_t stg = stage0 + uint32_t(s) * slot_bytes;
-        float acc[NPER];
+        if (lane == 0) *s_scale = scale;
+    }
+    Act<FMT> act[UPL];
+    if constexpr (chain_cfg_staged(CFG)) {
+        int8_t* sq = reinterpret_cast<int8_t*>(act_smem);
+        int8_t* sq2 = sq + kChainStageIn;
+        float* sd = reinterpret_cast<float*>(sq2 + kChainStageIn);
+        float* ss_ = sd + kChainStageIn / 32;
+        const int n16 = st.n_in / 16, ng = st.n_in / 32;
+        for (int i = cl; i < n16; i += 32 * NCW) {
+            reinterpret_cast<int4*>(sq)[i] = __ldcg(reinterpret_cast<const int4*>(P.xq[buf]) + i);
+            reinterpret_cast<int4*>(sq2)[i] = __ldcg(reinterpret_cast<const int4*>(P.xq2[buf]) + i);
+        }
+        for (int i = cl; i < ng; i += 32 * NCW) {
+            sd[i] = __ldcg(P.xd[buf] + i);
+            ss_[i] = __ldcg(P.xs[buf] + i);
+        }
+        named_sync(kConsumerBarrier, 32 * NCW);
 #pragma unroll
-        for (int i = 0; i < NPER; ++i) acc[i] = 0.f;
-        if (got && ti.nrows == NPER * TEAMS && st.R == NPER * TEAMS) {
+        for (int i = 0; i < UPL; ++i) {
+            const int u = li + G * i;
+            if (u < U) load_act<FMT, true, SRC_SMEM>(act[i], u, sq, sq2, sd, ss_);
+        }
+    } else {
 #pragma unroll
-            for (int k = 0; k < UPL; ++k) {
-                const int u = li + G * k;
-                if (u < U) {
+        for (int i = 0; i < UPL; ++i) {
+            const int u = li + G * i;
+            if (u < U) load_act<FMT, true, SRC_CG>(act[i], u, P.xq[buf], P.xq2[buf], P.xd[buf], P.xs[buf]);
+        }
+        named_sync(kConsumerBarrier, 32 * NCW);
+    }
+    if (st.in_kind == CH_RMSNORM) {
+        const float scale = *s_scale;
 #pragma unroll
-                    for (int i = 0; i < NPER; ++i)
-                        acc[i] += unit_dot<FMT>(stg + uint32_t((team + TEAMS * i) * st.row_bytes), u, act[k], grid);
-                }
+        for (int i = 0; i < UPL; ++i) {
+#pragma unroll
+            for (int k = 0; k < UnitTraits<FMT>::NS; ++k) {
+                act[i].d[k] *= scale;
+                act[i].s[k] *= scale;
             }
-        } else if (got) {
+        }
+    }
+    // the activation loads are out: the producer may stream the rest of this stage's tiles
+    if (threadIdx.x == 0) *go = k_stage + 1;
+    int w_job = 0, w_row0 = 0, w_rows = 0;
+    auto flush = [&]() {                                    // every consumer thread, uniformly
+        named_sync(kConsumerBarrier, 32 * NCW);
+        if (!dead) {
+            float* y = st.y[w_job];
+            for (int rl = cl; rl < w_rows; rl += 32 * NCW) {
+                float v = 0.f;
 #pragma unroll
-            for (int i = 0; i < NPER; ++i) {
-                const int r = team + TEAMS * i;
-                if (r < ti.nrows) {
+                for (int w = 0; w < WPT; ++w) v += part[rl * WPT + w];
+                y[w_row0 + rl] = v;
+            }
+        }
+        named_sync(kConsumerBarrier, 32 * NCW);
+        w_rows = 0;
+    };
+    const int lo = chain_row_begin(st, blockIdx.x), hi = chain_row_begin(st, blockIdx.x + 1);
+    const int R = st.R;
+    const uint32_t row_bytes = uint32_t(st.row_bytes);
+    for (int j = 0; j < st.n_jobs; ++j) {
+        const int js = int(st.row_start[j]);
+        const int r0 = max(lo, js), r1 = min(hi, int(st.row_start[j + 1]));
+        for (int g = r0; g < r1; g += R, ++it) {
+            const int row0 = g - js, nrows = min(R, r1 - g);
+            const int s = it % S;
+            const bool got = !dead && mbar_wait(full0 + 8 * s, (it / S) & 1);
+            if (!got && !dead) {
+                dead = true;
+                if (lane == 0 && P.status) atomicOr(P.status, DEV_TIMEOUT);
+            }
+            const uint32_t stg = stage0 + uint32_t(s) * slot_bytes;
+            float acc[NPER];
 #pragma unroll
-                    for (int k = 0; k < UPL; ++k) {
-                        const int u = li + G * k;
-                        if (u < U) acc[i] += unit_dot<FMT>(stg + uint32_t(r * st.row_bytes), u, act[k], grid);
+            for (int i = 0; i < NPER; ++i) acc[i] = 0.f;
+            // every tile runs the full-tile code: rows past a partial tile's end read stale bytes of the
+            // slot (inside the slot, since R rows always fit) and their sums are never stored
+            if (got) {
+#pragma unroll
+                for (int k = 0; k < UPL; ++k) {
+                    const int u = li + G * k;
+                    if (u < U) {
+#pragma unroll
+                        for (int i = 0; i < NPER; ++i)
+                            acc[i] += unit_dot<FMT>(stg + uint32_t(team + TEAMS * i) * row_bytes, u, act[k], nullptr);
                     }
                 }
             }
-        }
-        __syncwarp();
-        if (got && lane == 0) mbar_arrive(empty0 + 8 * s);
-        float* y = st.y[ti.job];
-        if constexpr (G <= 32) {
+            __syncwarp();
+            if (got && lane == 0) mbar_arrive(empty0 + 8 * s);
+            if constexpr (G <= 32) {
+                float* y = st.y[j];
 #pragma unroll
-            for (int i = 0; i < NPER; ++i) {
-                float v = acc[i];
+                for (int i = 0; i < NPER; ++i) {
+                    float v = acc[i];
 #pragma unroll
-                for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                const int r = team + TEAMS * i;
-                if (li == 0 && got && r < ti.nrows) y[ti.row0 + r] = v;
-            }
-        } else {
-            float* rb = red + (it & 1) * NCW * NPER;
-#pragma unroll
-            for (int i = 0; i < NPER; ++i) {
-                const float v = warp_sum(acc[i]);
-                if (lane == 0) rb[warp * NPER + i] = v;
-            }
-            named_sync(1 + team, G);
-            const int wt = li >> 5;
-            if (got && wt == 0 && lane < NPER) {
-                const int r = team + TEAMS * lane;
-                if (r < ti.nrows) {
-                    float v = 0.f;
-#pragma unroll
-                    for (int w = 0; w < WPT; ++w) v += rb[(team * WPT + w) * NPER + lane];
-                    y[ti.row0 + r] = v;
+                    for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    const int r = team + TEAMS * i;
+                    if (li == 0 && got && r < nrows) y[row0 + r] = v;
                 }
+            } else {
+                if (w_rows > 0 && (j != w_job || row0 != w_row0 + w_rows || w_rows + nrows > PR)) flush();
+                if (w_rows == 0) {
+                    w_job = j;
+                    w_row0 = row0;
+                }
+                const int wt = li >> 5;
+#pragma unroll
+                for (int i = 0; i < NPER; ++i) {
+                    const float v = warp_sum(acc[i]);
+                    const int r = team + TEAMS * i;
+                    if (lane == 0 && r < nrows) part[(w_rows + r) * WPT + wt] = v;
+                }
+                w_rows += nrows;
             }
         }
     }
+    if constexpr (G > 32) {
+        if (w_rows > 0) flush();
+    }
+    *dead_io = dead;
+    return it;
 }
 
 // ---- the kernel ---------------------------------------------------------------------------------------
-// shared memory: [S slots x slot_bytes][reduction 2 x NCW x 4 floats][block-sum 32 floats]
-//                [activation xq K, xq2 K, xd K/32, xs K/32 (K = max n_in)][mbarriers]
+// shared memory: [S slots x slot_bytes][partial sums kChainPartFloats floats]
+//                [staged activation kChainActSmem][scale 16 B][mbarriers 2 S][go flag]
 
-__host__ __device__ constexpr int chain_red_bytes(int ncw) { return 2 * ncw * 4 * 4 + 32 * 4; }
+__host__ __device__ constexpr int chain_red_bytes() { return kChainPartFloats * 4 + kChainActSmem + 16; }
 
 // CA, CB: the two consumer configurations this instance carries (a chain uses at most two; one
 // kernel with all of them would spill registers)
@@ -293,15 +349,10 @@ template <int NCW, int CA, int CB>
 __global__ void __launch_bounds__(32 * (NCW + 1), 1) chain_kernel(const __grid_constant__ ChainParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int S = P.S;
-    uint8_t* red_p = smem + (long long)S * P.slot_bytes;
-    float* red = reinterpret_cast<float*>(red_p);
-    float* bsum = red + 2 * NCW * 4;
-    uint8_t* act_p = red_p + chain_red_bytes(NCW);
-    int8_t* sxq = reinterpret_cast<int8_t*>(act_p);
-    int8_t* sxq2 = sxq + P.max_n_in;
-    float* sxd = reinterpret_cast<float*>(sxq2 + P.max_n_in);
-    float* sxs = sxd + P.max_n_in / 32;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(act_p + tma_act_bytes(P.max_n_in));
+    float* part = reinterpret_cast<float*>(smem + (long long)S * P.slot_bytes);
+    uint8_t* act_smem = smem + (long long)S * P.slot_bytes + kChainPartFloats * 4;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (long long)S * P.slot_bytes + chain_red_bytes());
+    volatile int* go = reinterpret_cast<volatile int*>(bars + 2 * S);   // stages whose consumers have started
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S);
     const uint32_t stage0 = smem_u32(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -312,29 +363,43 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) chain_kernel(const __grid_c
             mbar_init(empty0 + 8 * s, NCW);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        *go = 0;
     }
     __syncthreads();
 
     if (warp == NCW) {
         // ---------------- producer: every stage's weight tiles, in order ----------------
+        // At a stage boundary only boundary_tiles tiles of the next stage go out before its consumers
+        // have issued their activation loads: a full ring of copies in flight would queue those loads
+        // (and the grid barrier's atomics and polls) behind megabytes of weight traffic.
         if (lane != 0) return;
         int it = 0;
         bool ok = true;
         for (int k = 0; k < P.n_stages && ok; ++k) {
             const ChainStage& st = P.st[k];
-            const long long hi = chain_row_begin(st, blockIdx.x + 1);
-            for (long long g = chain_row_begin(st, blockIdx.x); g < hi; ++it) {
-                const int s = it % S;
-                if (it >= S && !mbar_wait(empty0 + 8 * s, ((it / S) & 1) ^ 1)) {
-                    ok = false;
-                    break;
+            const int lo = chain_row_begin(st, blockIdx.x), hi = chain_row_begin(st, blockIdx.x + 1);
+            const int R = st.R;
+            const long long row_bytes = st.row_bytes;
+            int issued = 0;
+            for (int j = 0; j < st.n_jobs && ok; ++j) {
+                const int js = int(st.row_start[j]);
+                const int r0 = max(lo, js), r1 = min(hi, int(st.row_start[j + 1]));
+                const uint8_t* w = st.w[j];
+                for (int g = r0; g < r1; g += R, ++it, ++issued) {
+                    if (issued == P.boundary_tiles && !wait_go(go, k + 1)) {
+                        ok = false;
+                        break;
+                    }
+                    const int s = it % S;
+                    if (it >= S && !mbar_wait(empty0 + 8 * s, ((it / S) & 1) ^ 1)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t bytes = uint32_t(min(R, r1 - g) * row_bytes);
+                    mbar_arrive_tx(full0 + 8 * s, bytes);
+                    bulk_g2s(stage0 + uint32_t(s) * uint32_t(P.slot_bytes), w + (long long)(g - js) * row_bytes, bytes,
+                             full0 + 8 * s);
                 }
-                const TileInfo ti = chain_tile_at(st, g, hi);
-                g += ti.nrows;
-                const uint32_t bytes = uint32_t((long long)ti.nrows * st.row_bytes);
-                mbar_arrive_tx(full0 + 8 * s, bytes);
-                bulk_g2s(stage0 + uint32_t(s) * uint32_t(P.slot_bytes), st.w[ti.job] + (long long)ti.row0 * st.row_bytes,
-                         bytes, full0 + 8 * s);
             }
         }
         if (!ok) {
@@ -349,31 +414,56 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) chain_kernel(const __grid_c
     bool dead = false;
     for (int k = 0; k < P.n_stages; ++k) {
         const ChainStage& st = P.st[k];
-        if (st.wait && k > 0) {
-            // grid barrier: every CTA has written its rows of stage k-1 (and so of all earlier stages)
-            if (threadIdx.x == 0 && !dead) {
-                const unsigned long long t0 = global_ns();
-                while (ld_acquire(P.ws + (k - 1)) < int(gridDim.x)) {
-                    if (global_ns() - t0 > kWaitNs) {
-                        dead = true;
-                        if (P.status) atomicOr(P.status, DEV_BARRIER_TIMEOUT);
-                        break;
+        const int buf = k & 1;
+        if (st.wait && k > 0) grid_wait<NCW>(P.bar + (k - 1), dead, P.status);
+        if (!st.fed) {
+            // this stage quantises its own input: groups split over the CTAs, then a grid barrier
+            const int ng = st.n_in / 32;
+            const int g0 = int((long long)blockIdx.x * ng / gridDim.x), g1 = int((long long)(blockIdx.x + 1) * ng / gridDim.x);
+            for (int g = g0 + warp; g < g1; g += NCW) produce_group(P, st, buf, g);
+            named_sync(kConsumerBarrier, 32 * NCW);
+            grid_arrive(P.bar + kChainMaxStages + k);
+            grid_wait<NCW>(P.bar + kChainMaxStages + k, dead, P.status);
+        }
+        int dead_io = dead;
+        if (st.cfg == CA)
+            it = chain_consume<CA, NCW>(P, st, k, it, &dead_io, part, act_smem, go, stage0, full0, empty0);
+        else
+            it = chain_consume<CB, NCW>(P, st, k, it, &dead_io, part, act_smem, go, stage0, full0, empty0);
+        dead = dead_io != 0;
+        named_sync(kConsumerBarrier, 32 * NCW);            // this CTA's rows of stage k are written
+        if (k + 1 < P.n_stages && P.st[k + 1].fed) {
+            // quantise every group of the next stage's input whose last rows this CTA wrote
+            const ChainStage& ns = P.st[k + 1];
+            const int nb = (k + 1) & 1;
+            int* cnt = P.cnt + nb * kChainMaxGroups;
+            const int lo = chain_row_begin(st, blockIdx.x), hi = chain_row_begin(st, blockIdx.x + 1);
+            int p = 0;
+            for (int j = 0; j < st.n_jobs; ++j) {
+                if (!((st.feed_mask >> j) & 1)) continue;
+                const int js = int(st.row_start[j]);
+                const int a0 = max(lo, js) - js, a1 = min(hi, int(st.row_start[j + 1])) - js;
+                if (a1 <= a0) continue;
+                for (int g = a0 / 32; g <= (a1 - 1) / 32; ++g, ++p) {
+                    if (p % NCW != warp) continue;
+                    int last = 0;
+                    if (lane == 0) {
+                        const int mine = int(min(a1, 32 * g + 32) - max(a0, 32 * g));
+                        __threadfence();
+                        const int old = atomicAdd(cnt + g, mine);
+                        last = old + mine == st.feed_target;
+                        if (last) cnt[g] = 0;                // all contributions are in: ready for reuse
+                    }
+                    last = __shfl_sync(0xffffffffu, last, 0);
+                    if (last && !dead) {
+                        __threadfence();
+                        produce_group(P, ns, nb, g);
                     }
                 }
             }
             named_sync(kConsumerBarrier, 32 * NCW);
         }
-        chain_input<NCW>(st, sxq, sxq2, sxd, sxs, bsum);
-        if (st.cfg == CA)
-            chain_consume<CA, NCW>(st, it, dead, sxq, sxq2, sxd, sxs, red, stage0, P.slot_bytes, S, full0, empty0, P.status);
-        else
-            chain_consume<CB, NCW>(st, it, dead, sxq, sxq2, sxd, sxs, red, stage0, P.slot_bytes, S, full0, empty0, P.status);
-        // this CTA's rows of stage k are written: count it (the stores are ordered before the release)
-        named_sync(kConsumerBarrier, 32 * NCW);
-        if (threadIdx.x == 0) {
-            __threadfence();
-            atomicAdd(P.ws + k, 1);
-        }
+        grid_arrive(P.bar + k);
     }
 }
 

@@ -175,26 +175,32 @@ struct Act {                              // the activation of one unit, in regi
     int sr[FMT == F_Q6_K ? 2 : 1];        //       sum of the 16 xq2 of each group
 };
 
-template <bool GLOBAL>
+// activation sources: SRC_SMEM shared memory; SRC_NC global through the read-only path (inputs that
+// no kernel in flight writes); SRC_CG global through L2 only (written earlier in the same launch)
+enum : int { SRC_SMEM = 0, SRC_NC = 1, SRC_CG = 2 };
+template <int SRC>
 __device__ __forceinline__ int4 ldq16(const int8_t* p) {
-    if constexpr (GLOBAL) return __ldg(reinterpret_cast<const int4*>(p));
+    if constexpr (SRC == SRC_NC) return __ldg(reinterpret_cast<const int4*>(p));
+    if constexpr (SRC == SRC_CG) return __ldcg(reinterpret_cast<const int4*>(p));
     return *reinterpret_cast<const int4*>(p);
 }
-template <bool GLOBAL>
+template <int SRC>
 __device__ __forceinline__ int2 ldq8(const int8_t* p) {
-    if constexpr (GLOBAL) return __ldg(reinterpret_cast<const int2*>(p));
+    if constexpr (SRC == SRC_NC) return __ldg(reinterpret_cast<const int2*>(p));
+    if constexpr (SRC == SRC_CG) return __ldcg(reinterpret_cast<const int2*>(p));
     return *reinterpret_cast<const int2*>(p);
 }
-template <bool GLOBAL, bool SCALES>
+template <int SRC, bool SCALES>
 __device__ __forceinline__ float ldf(const float* p, int i) {
     if constexpr (!SCALES) return 0.f;
-    if constexpr (GLOBAL) return __ldg(p + i);
+    if constexpr (SRC == SRC_NC) return __ldg(p + i);
+    if constexpr (SRC == SRC_CG) return __ldcg(p + i);
     return p[i];
 }
 
-// xq/xq2/xd/xs point at the start of the activation row (global memory, or shared memory when
-// GLOBAL = false).  SCALES = false (the int32-sums test hook) reads xq/xq2 only: xd/xs may be null.
-template <int FMT, bool SCALES, bool GLOBAL = true>
+// xq/xq2/xd/xs point at the start of the activation row (in memory of kind SRC).  SCALES = false
+// (the int32-sums test hook) reads xq/xq2 only: xd/xs may be null.
+template <int FMT, bool SCALES, int GLOBAL = SRC_NC>
 __device__ __forceinline__ void load_act(Act<FMT>& a, int u, const int8_t* xq, const int8_t* xq2, const float* xd,
                                          const float* xs) {
     constexpr int NS = UnitTraits<FMT>::NS;
@@ -577,7 +583,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), NCW <= 8 ? 2 : 1) mv_tma_kerne
             for (int i = 0; i < UPL; ++i) {
                 const int u = li + G * i;
                 if (u < U) {
-                    if constexpr (XF != 0) load_act<FMT, true, false>(act[i], u, sxq, sxq2, sxd, sxs);
+                    if constexpr (XF != 0) load_act<FMT, true, SRC_SMEM>(act[i], u, sxq, sxq2, sxd, sxs);
                     else load_act<FMT, !SUMS>(act[i], u, P.xq + off, P.xq2 + off, P.xd + off / 32, P.xs + off / 32);
                 }
             }
