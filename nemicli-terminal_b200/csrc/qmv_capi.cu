@@ -595,7 +595,9 @@ int qmv_chain(const qmv_stage* stages, int n_stages, void* workspace, void* stre
     P.n_stages = n_stages;
     P.S = int(S);
     P.slot_bytes = int(slot);
-    P.boundary_tiles = env_bt >= 0 ? env_bt : 2;
+    P.boundary_tiles = env_bt >= 0 ? env_bt : 1 << 30;
+    static const long long env_pf = getenv("NEMICLI_CHAIN_L2PF") ? atoll(getenv("NEMICLI_CHAIN_L2PF")) : 0;
+    P.l2_prefetch = env_pf / 16 * 16;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     P.bar = reinterpret_cast<int*>(ws);
     P.cnt = P.bar + 2 * kChainMaxStages;

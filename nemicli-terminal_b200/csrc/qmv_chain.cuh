@@ -67,6 +67,7 @@ struct ChainParams {
     int S;                 // ring slots
     int slot_bytes;
     int boundary_tiles;    // tiles of a stage the producer issues before that stage's consumers start
+    long long l2_prefetch; // bytes of each stage (per CTA) requested into L2 when its first tile is issued
     int* bar;              // grid-barrier counters: stage k done at [k], its input ready at [kChainMaxStages + k]
     int* cnt;              // group counters [buffer][group]
     int8_t* xq[2];
@@ -123,13 +124,15 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
     return v;
 }
 
-// grid barrier, arrive side: this CTA's writes (ordered before by the preceding CTA barrier) are
-// released, then counted
+// grid barrier, arrive side: a release reduction by one thread after a CTA barrier makes the CTA's
+// writes visible before the count
 __device__ __forceinline__ void grid_arrive(int* counter) {
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(counter, 1);
-    }
+    if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" :: "l"(counter) : "memory");
+}
+__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
 }
 // wait side: thread 0 spins (bounded) until every CTA has arrived, then all consumer threads go on
 template <int NCW>
@@ -201,18 +204,21 @@ __device__ __noinline__ int chain_consume(const ChainParams& P, const ChainStage
     const int lane = threadIdx.x & 31;
     const int cl = threadIdx.x, team = cl / G, li = cl % G;
     const int U = st.n_in / VPU;
-    // the 1/rms factor of an RMSNORM input (warp 0: the groups' sums of squares in a fixed order)
+    // the 1/rms factor of an RMSNORM input (warp 0, after its activation loads are out: the groups'
+    // sums of squares in a fixed order)
     float* s_scale = reinterpret_cast<float*>(act_smem + kChainActSmem);
-    if (threadIdx.x < 32) {
-        float scale = 1.f;
-        if (st.in_kind == CH_RMSNORM) {
-            const int ng = st.n_in / 32;
-            float ss = 0.f;
-            for (int g = lane; g < ng; g += 32) ss += __ldcg(P.pss[buf] + g);
-            scale = rsqrtf(warp_sum(ss) / float(st.n_in) + st.eps);
+    auto norm_scale = [&]() {
+        if (threadIdx.x < 32) {
+            float scale = 1.f;
+            if (st.in_kind == CH_RMSNORM) {
+                const int ng = st.n_in / 32;
+                float ss = 0.f;
+                for (int g = lane; g < ng; g += 32) ss += __ldcg(P.pss[buf] + g);
+                scale = rsqrtf(warp_sum(ss) / float(st.n_in) + st.eps);
+            }
+            if (lane == 0) *s_scale = scale;
         }
-        if (lane == 0) *s_scale = scale;
-    }
+    };
     Act<FMT> act[UPL];
     if constexpr (chain_cfg_staged(CFG)) {
         int8_t* sq = reinterpret_cast<int8_t*>(act_smem);
@@ -221,13 +227,18 @@ __device__ __noinline__ int chain_consume(const ChainParams& P, const ChainStage
         float* ss_ = sd + kChainStageIn / 32;
         const int n16 = st.n_in / 16, ng = st.n_in / 32;
         for (int i = cl; i < n16; i += 32 * NCW) {
-            reinterpret_cast<int4*>(sq)[i] = __ldcg(reinterpret_cast<const int4*>(P.xq[buf]) + i);
-            reinterpret_cast<int4*>(sq2)[i] = __ldcg(reinterpret_cast<const int4*>(P.xq2[buf]) + i);
+            const int4 a = __ldcg(reinterpret_cast<const int4*>(P.xq[buf]) + i);
+            const int4 b = __ldcg(reinterpret_cast<const int4*>(P.xq2[buf]) + i);
+            const float d = i < ng ? __ldcg(P.xd[buf] + i) : 0.f;
+            const float e = i < ng ? __ldcg(P.xs[buf] + i) : 0.f;
+            reinterpret_cast<int4*>(sq)[i] = a;
+            reinterpret_cast<int4*>(sq2)[i] = b;
+            if (i < ng) {
+                sd[i] = d;
+                ss_[i] = e;
+            }
         }
-        for (int i = cl; i < ng; i += 32 * NCW) {
-            sd[i] = __ldcg(P.xd[buf] + i);
-            ss_[i] = __ldcg(P.xs[buf] + i);
-        }
+        norm_scale();
         named_sync(kConsumerBarrier, 32 * NCW);
 #pragma unroll
         for (int i = 0; i < UPL; ++i) {
@@ -240,6 +251,7 @@ __device__ __noinline__ int chain_consume(const ChainParams& P, const ChainStage
             const int u = li + G * i;
             if (u < U) load_act<FMT, true, SRC_CG>(act[i], u, P.xq[buf], P.xq2[buf], P.xd[buf], P.xs[buf]);
         }
+        norm_scale();
         named_sync(kConsumerBarrier, 32 * NCW);
     }
     if (st.in_kind == CH_RMSNORM) {
@@ -381,6 +393,24 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) chain_kernel(const __grid_c
             const int R = st.R;
             const long long row_bytes = st.row_bytes;
             int issued = 0;
+            if (P.l2_prefetch > 0) {
+                // this CTA's rows of the stage, after the first S tiles, go to L2 now: the copies that
+                // follow a stage boundary then come from L2 while HBM would otherwise idle there
+                long long skip = (long long)S * R * row_bytes, budget = P.l2_prefetch;
+                for (int j = 0; j < st.n_jobs && budget > 0; ++j) {
+                    const int js = int(st.row_start[j]);
+                    const int r0 = max(lo, js), r1 = min(hi, int(st.row_start[j + 1]));
+                    if (r1 <= r0) continue;
+                    long long off = (long long)(r0 - js) * row_bytes, len = (long long)(r1 - r0) * row_bytes;
+                    const long long sk = min(skip, len);
+                    off += sk; len -= sk; skip -= sk;
+                    len = min(len, budget);
+                    if (len > 0) {
+                        bulk_prefetch_l2(st.w[j] + off, uint32_t(len));
+                        budget -= len;
+                    }
+                }
+            }
             for (int j = 0; j < st.n_jobs && ok; ++j) {
                 const int js = int(st.row_start[j]);
                 const int r0 = max(lo, js), r1 = min(hi, int(st.row_start[j + 1]));
@@ -448,15 +478,14 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) chain_kernel(const __grid_c
                     if (p % NCW != warp) continue;
                     int last = 0;
                     if (lane == 0) {
-                        const int mine = int(min(a1, 32 * g + 32) - max(a0, 32 * g));
-                        __threadfence();
-                        const int old = atomicAdd(cnt + g, mine);
+                        const int mine = min(a1, 32 * g + 32) - max(a0, 32 * g);
+                        const int old = atom_add_acq_rel(cnt + g, mine);   // releases this CTA's rows
                         last = old + mine == st.feed_target;
                         if (last) cnt[g] = 0;                // all contributions are in: ready for reuse
                     }
                     last = __shfl_sync(0xffffffffu, last, 0);
                     if (last && !dead) {
-                        __threadfence();
+                        asm volatile("fence.acq_rel.gpu;" ::: "memory");
                         produce_group(P, ns, nb, g);
                     }
                 }
