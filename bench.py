@@ -50,7 +50,7 @@ def peaks():
 
 
 class Clocks:
-    """Samples nvidia-smi every 200 ms while running (SM clock, throttle reasons)."""
+    """Samples nvidia-smi every 20 ms while running (SM clock, throttle reasons)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -63,8 +63,9 @@ class Clocks:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.5)                      # the sampler is running before the timed region starts
         except OSError:
             self.proc = None
         return self
@@ -405,13 +406,13 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--batches", type=int, nargs="*", default=[1, 4, 8])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-pdl", action="store_true", help="plain stream order between the matvec launches")
-    ap.add_argument("--mode", choices=["chain", "calls"], default="calls",
+    ap.add_argument("--mode", choices=["chain", "calls"], default="chain",
                     help="chain: the step as one decode-chain launch; calls: one launch per matrix group")
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers in the stack (profiling runs use fewer)")
     args = ap.parse_args()

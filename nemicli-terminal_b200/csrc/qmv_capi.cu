@@ -584,20 +584,16 @@ int qmv_chain(const qmv_stage* stages, int n_stages, void* workspace, void* stre
         if ((used & ~((1 << pairs[i][0]) | (1 << pairs[i][1]))) == 0) pair = i;
     if (pair < 0) return ST_BAD_SHAPE;           // more than two row shapes: split the chain
     slot = (slot + 127) / 128 * 128;
-    const long long other = chain_red_bytes() + 2 * 8 * 32 + 16;
+    const long long other = chain_red_bytes() + 2 * 8 * 32;
     long long S = (kSmemCap - other) / slot;
-    static const int env_slots = getenv("NEMICLI_CHAIN_SLOTS") ? atoi(getenv("NEMICLI_CHAIN_SLOTS")) : 0;
-    static const int env_bt = getenv("NEMICLI_CHAIN_BOUNDARY") ? atoi(getenv("NEMICLI_CHAIN_BOUNDARY")) : -1;
+    // three slots: deeper rings only add queueing latency to every other memory access (measured)
+    static const int env_slots = getenv("NEMICLI_CHAIN_SLOTS") ? atoi(getenv("NEMICLI_CHAIN_SLOTS")) : 3;
     if (env_slots >= 2 && env_slots < S) S = env_slots;
-    else if (env_slots == 0 && S > 4) S = 4;      // deeper rings only add queueing latency (measured)
     if (S > 32) S = 32;
     if (S < 2) return ST_BAD_SHAPE;
     P.n_stages = n_stages;
     P.S = int(S);
     P.slot_bytes = int(slot);
-    P.boundary_tiles = env_bt >= 0 ? env_bt : 1 << 30;
-    static const long long env_pf = getenv("NEMICLI_CHAIN_L2PF") ? atoll(getenv("NEMICLI_CHAIN_L2PF")) : 0;
-    P.l2_prefetch = env_pf / 16 * 16;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     P.bar = reinterpret_cast<int*>(ws);
     P.cnt = P.bar + 2 * kChainMaxStages;

@@ -66,8 +66,6 @@ struct ChainParams {
     int n_stages;
     int S;                 // ring slots
     int slot_bytes;
-    int boundary_tiles;    // tiles of a stage the producer issues before that stage's consumers start
-    long long l2_prefetch; // bytes of each stage (per CTA) requested into L2 when its first tile is issued
     int* bar;              // grid-barrier counters: stage k done at [k], its input ready at [kChainMaxStages + k]
     int* cnt;              // group counters [buffer][group]
     int8_t* xq[2];
@@ -150,17 +148,6 @@ __device__ __forceinline__ void grid_wait(const int* counter, bool& dead, int* s
     named_sync(kConsumerBarrier, 32 * NCW);
 }
 
-// producer side of the boundary throttle: bounded spin until the consumers have started stage `want - 1`
-__device__ __forceinline__ bool wait_go(volatile int* go, int want) {
-    if (*go >= want) return true;
-    const unsigned long long t0 = global_ns();
-    while (*go < want) {
-        __nanosleep(64);
-        if (global_ns() - t0 > kWaitNs) return false;
-    }
-    return true;
-}
-
 // ---- input production: one warp quantises group g (32 values) of stage `ns`'s input into buffer nb --
 
 __device__ __forceinline__ void produce_group(const ChainParams& P, const ChainStage& ns, int nb, int g) {
@@ -189,8 +176,8 @@ __device__ __forceinline__ void produce_group(const ChainParams& P, const ChainS
 // timed-out flag (read and written once per stage).
 template <int CFG, int NCW>
 __device__ __noinline__ int chain_consume(const ChainParams& P, const ChainStage& st, int k_stage, int it, int* dead_io,
-                                          float* part, uint8_t* act_smem, volatile int* go, uint32_t stage0,
-                                          uint32_t full0, uint32_t empty0) {
+                                          float* part, uint8_t* act_smem, uint32_t stage0, uint32_t full0,
+                                          uint32_t empty0) {
     bool dead = *dead_io != 0;
     const int buf = k_stage & 1;
     using C = ChainCfg<CFG>;
@@ -265,8 +252,6 @@ __device__ __noinline__ int chain_consume(const ChainParams& P, const ChainStage
             }
         }
     }
-    // the activation loads are out: the producer may stream the rest of this stage's tiles
-    if (threadIdx.x == 0) *go = k_stage + 1;
     int w_job = 0, w_row0 = 0, w_rows = 0;
     auto flush = [&]() {                                    // every consumer thread, uniformly
         named_sync(kConsumerBarrier, 32 * NCW);
@@ -351,7 +336,7 @@ __device__ __noinline__ int chain_consume(const ChainParams& P, const ChainStage
 
 // ---- the kernel ---------------------------------------------------------------------------------------
 // shared memory: [S slots x slot_bytes][partial sums kChainPartFloats floats]
-//                [staged activation kChainActSmem][scale 16 B][mbarriers 2 S][go flag]
+//                [staged activation kChainActSmem][scale 16 B][mbarriers 2 S]
 
 __host__ __device__ constexpr int chain_red_bytes() { return kChainPartFloats * 4 + kChainActSmem + 16; }
 
@@ -364,7 +349,6 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) chain_kernel(const __grid_c
     float* part = reinterpret_cast<float*>(smem + (long long)S * P.slot_bytes);
     uint8_t* act_smem = smem + (long long)S * P.slot_bytes + kChainPartFloats * 4;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (long long)S * P.slot_bytes + chain_red_bytes());
-    volatile int* go = reinterpret_cast<volatile int*>(bars + 2 * S);   // stages whose consumers have started
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S);
     const uint32_t stage0 = smem_u32(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -375,15 +359,11 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) chain_kernel(const __grid_c
             mbar_init(empty0 + 8 * s, NCW);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        *go = 0;
     }
     __syncthreads();
 
     if (warp == NCW) {
         // ---------------- producer: every stage's weight tiles, in order ----------------
-        // At a stage boundary only boundary_tiles tiles of the next stage go out before its consumers
-        // have issued their activation loads: a full ring of copies in flight would queue those loads
-        // (and the grid barrier's atomics and polls) behind megabytes of weight traffic.
         if (lane != 0) return;
         int it = 0;
         bool ok = true;
@@ -392,34 +372,11 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) chain_kernel(const __grid_c
             const int lo = chain_row_begin(st, blockIdx.x), hi = chain_row_begin(st, blockIdx.x + 1);
             const int R = st.R;
             const long long row_bytes = st.row_bytes;
-            int issued = 0;
-            if (P.l2_prefetch > 0) {
-                // this CTA's rows of the stage, after the first S tiles, go to L2 now: the copies that
-                // follow a stage boundary then come from L2 while HBM would otherwise idle there
-                long long skip = (long long)S * R * row_bytes, budget = P.l2_prefetch;
-                for (int j = 0; j < st.n_jobs && budget > 0; ++j) {
-                    const int js = int(st.row_start[j]);
-                    const int r0 = max(lo, js), r1 = min(hi, int(st.row_start[j + 1]));
-                    if (r1 <= r0) continue;
-                    long long off = (long long)(r0 - js) * row_bytes, len = (long long)(r1 - r0) * row_bytes;
-                    const long long sk = min(skip, len);
-                    off += sk; len -= sk; skip -= sk;
-                    len = min(len, budget);
-                    if (len > 0) {
-                        bulk_prefetch_l2(st.w[j] + off, uint32_t(len));
-                        budget -= len;
-                    }
-                }
-            }
             for (int j = 0; j < st.n_jobs && ok; ++j) {
                 const int js = int(st.row_start[j]);
                 const int r0 = max(lo, js), r1 = min(hi, int(st.row_start[j + 1]));
                 const uint8_t* w = st.w[j];
-                for (int g = r0; g < r1; g += R, ++it, ++issued) {
-                    if (issued == P.boundary_tiles && !wait_go(go, k + 1)) {
-                        ok = false;
-                        break;
-                    }
+                for (int g = r0; g < r1; g += R, ++it) {
                     const int s = it % S;
                     if (it >= S && !mbar_wait(empty0 + 8 * s, ((it / S) & 1) ^ 1)) {
                         ok = false;
@@ -457,9 +414,9 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) chain_kernel(const __grid_c
         }
         int dead_io = dead;
         if (st.cfg == CA)
-            it = chain_consume<CA, NCW>(P, st, k, it, &dead_io, part, act_smem, go, stage0, full0, empty0);
+            it = chain_consume<CA, NCW>(P, st, k, it, &dead_io, part, act_smem, stage0, full0, empty0);
         else
-            it = chain_consume<CB, NCW>(P, st, k, it, &dead_io, part, act_smem, go, stage0, full0, empty0);
+            it = chain_consume<CB, NCW>(P, st, k, it, &dead_io, part, act_smem, stage0, full0, empty0);
         dead = dead_io != 0;
         named_sync(kConsumerBarrier, 32 * NCW);            // this CTA's rows of stage k are written
         if (k + 1 < P.n_stages && P.st[k + 1].fed) {
