@@ -403,6 +403,189 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+VOCAB_ROWS, VOCAB_IN = 128256, 4096
+# single-matrix workloads: config 1 (Q4_0) and config 5 (ternary / 2-bit codebook formats)
+MATRIX_WORKLOADS = {
+    "cfg1": [("Q4_0", 4096, 4096)],
+    "cfg5": [("TQ2_0", 14336, 4096), ("TQ2_0", 4096, 14336), ("IQ2_XXS", 14336, 4096), ("IQ2_XXS", 4096, 14336)],
+}
+MOE_EXPERTS, MOE_DIM, MOE_FF, MOE_K = 128, 2048, 768, 8
+
+
+def _init_rank():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    from nemicli_terminal_b200 import build as nbuild
+    nbuild.build()
+    return world, rank, local, device, dist
+
+
+def run_matrices(args):
+    """Configs 1 and 5: batch-1 matvecs of single matrices (mmvq.mv with the in-kernel quantisation),
+    each in a CUDA graph over enough distinct copies to read more than twice L2 per replay.  N > 1:
+    independent replicas (weak scaling)."""
+    world, rank, local, device, dist = _init_rank()
+    from nemicli_terminal_b200 import mmvq, synth
+    from nemicli_terminal_b200.formats import row_bytes
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    peak, peak_kind = peaks()
+    per = {}
+    tot_bytes, tot_s = 0, 0.0
+    for fmt, n_out, n_in in MATRIX_WORKLOADS[args.workload]:
+        mb = n_out * row_bytes(fmt, n_in)
+        copies = max(1, -(-2 * l2 // mb))
+        mats = [synth.blocks(fmt, n_out, n_in, seed=900 + 31 * rank + c, device=device) for c in range(copies)]
+        x = synth.activations(1, n_in, seed=901, device=device)[0].contiguous()
+        g, _ = capture(lambda: [mmvq.mv(fmt, m, x, n_out, n_in) for m in mats])
+        t = time_graph(g, args.steps, max(3, args.warmup), dist) / (args.steps * copies)
+        t = max_over_ranks(t, dist, device)
+        per[f"{fmt} {n_out}x{n_in}"] = {"gbs": mb / t / 1e9, "us": t * 1e6, "bytes": mb, "copies": copies,
+                                        "hbm_frac": mb / t / 1e9 / peak}
+        tot_bytes += mb
+        tot_s += t
+        del g
+    if rank == 0:
+        line = {"metric": f"weight GB/s of batch-1 quant matvec ({args.workload})",
+                "value": world * tot_bytes / tot_s / 1e9, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": tot_s * 1e3, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "int8", "data": f"synthetic (seeded, {args.workload} distributions)",
+                "config": {"workload": args.workload + ": " + ", ".join(per), "batch": 1,
+                           "l2": "distinct copies of each matrix totalling > 2x L2 per replay"},
+                "matrices": per, "peak": peak, "peak_kind": peak_kind}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_moe(args):
+    """Config 4: MoE FFN of 128 Q4_K experts (gate/up 768x2048, down 2048x768), top-8 routing, batch
+    1 / 4 / 16.  One GPU: moe.MoeFFN captured in a CUDA graph over rotating routings.  N GPUs:
+    shard.ExpertShardedMoE (experts split, all-to-all exchanges; each rank has its own tokens), timed
+    with events (the exchange sizes cross to the host).  Bytes per call = distinct experts touched x
+    2,654,208."""
+    world, rank, local, device, dist = _init_rank()
+    from nemicli_terminal_b200 import moe, shard, synth
+    from nemicli_terminal_b200.formats import TYPE_ID, row_bytes
+    from nemicli_terminal_b200.layers import PackedExperts
+    lo, hi = shard.shard_range(MOE_EXPERTS, world, rank)
+    ne = hi - lo
+    shapes = ((MOE_FF, MOE_DIM), (MOE_FF, MOE_DIM), (MOE_DIM, MOE_FF))
+    ex = [PackedExperts(synth.blocks("Q4_K", ne * o, i, seed=700 + 7 * rank + s_, device=device), TYPE_ID["Q4_K"],
+                        ne, o, i, torch.float32) for s_, (o, i) in enumerate(shapes)]
+    per_expert = sum(o * row_bytes("Q4_K", i) for o, i in shapes)
+    results = {}
+    for B in (1, 4, 16):
+        n_rot = 16
+        xs = [synth.activations(B, MOE_DIM, seed=710 + r + 97 * rank, device=device) for r in range(n_rot)]
+        routes = [moe.route(synth.router_logits(B, MOE_EXPERTS, seed=720 + r + 97 * rank, device=device), MOE_K)
+                  for r in range(n_rot)]
+        uniq = sum(int(torch.unique(ix).numel()) for ix, _ in routes) / n_rot
+        if world == 1:
+            ffn = moe.MoeFFN(*ex)
+            g, _ = capture(lambda: [ffn(x, ix, w) for x, (ix, w) in zip(xs, routes)])
+            t = time_graph(g, args.steps, max(3, args.warmup), None) / (args.steps * n_rot)
+            del g
+        else:
+            layer = shard.ExpertShardedMoE(*ex, MOE_EXPERTS, MOE_DIM)
+            for _ in range(max(3, args.warmup)):
+                for x, (ix, w) in zip(xs, routes):
+                    layer(x, ix, w)
+            torch.cuda.synchronize()
+            dist.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            reps = max(2, args.steps // 10)
+            for _ in range(reps):
+                for x, (ix, w) in zip(xs, routes):
+                    layer(x, ix, w)
+            b.record()
+            torch.cuda.synchronize()
+            t = a.elapsed_time(b) / 1e3 / (reps * n_rot)
+        t = max_over_ranks(t, dist, device)
+        results[str(B)] = {"us_per_call": t * 1e6, "unique_experts": uniq, "gbs": uniq * per_expert / t / 1e9 * world}
+    if rank == 0:
+        line = {"metric": "MoE FFN expert weight GB/s (config 4, top-8 of 128 Q4_K experts)",
+                "value": results["1"]["gbs"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": results["1"]["us_per_call"] / 1e3, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded, config-4 distributions)",
+                "config": {"workload": "config4: 128 experts x {gate, up 768x2048, down 2048x768} Q4_K, top-8, "
+                                       + ("one GPU, graph-captured" if world == 1 else f"expert-sharded over {world} GPUs, "
+                                          "own tokens per rank, all-to-all exchanges"),
+                           "bytes_per_expert": per_expert, "rotating_routings": 16},
+                "batches": results}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_vocab(args):
+    """Config 3: the vocabulary projection (128256 x 4096, Q8_0 or Q6_K) row-sharded over the N ranks
+    (shard.RowShardedLinear: local matvec + one NCCL all-gather of the fp32 logits), batch 1.  Each rank
+    rotates over enough copies of its shard to read more than twice its L2 between repeats.  value:
+    whole-matrix weight bytes per second of the sharded call (strong scaling: the matrix is fixed)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    from nemicli_terminal_b200 import build as nbuild
+    nbuild.build()
+    from nemicli_terminal_b200 import shard, synth
+    from nemicli_terminal_b200.formats import row_bytes
+    fmt = args.vocab_format
+    lo, hi = shard.shard_range(VOCAB_ROWS, world, rank)
+    local_bytes = (hi - lo) * row_bytes(fmt, VOCAB_IN)
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    copies = max(1, -(-2 * l2 // local_bytes))
+    lins = [shard.RowShardedLinear(fmt, synth.blocks(fmt, hi - lo, VOCAB_IN, seed=500 + 17 * rank + c, device=device),
+                                   VOCAB_ROWS, VOCAB_IN) for c in range(copies)]
+    x = synth.activations(1, VOCAB_IN, seed=501, device=device)[0].contiguous()
+    g_local, _ = capture(lambda: [lin.local(x) for lin in lins])
+    g_full, outs = capture(lambda: [lin(x) for lin in lins])
+    with Clocks(local) as clk:
+        t_full = time_graph(g_full, args.steps, max(3, args.warmup), dist) / (args.steps * copies)
+    clocks = clk.summary()
+    t_local = time_graph(g_local, args.steps, max(3, args.warmup), dist) / (args.steps * copies)
+    t_full = max_over_ranks(t_full, dist, device)
+    t_local = max_over_ranks(t_local, dist, device)
+    total = VOCAB_ROWS * row_bytes(fmt, VOCAB_IN)
+    peak, peak_kind = peaks()
+    if rank == 0:
+        line = {"metric": "vocab projection weight GB/s (row-sharded, all-gathered logits)",
+                "value": total / t_full / 1e9, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": t_full * 1e3, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+                "data": "synthetic (seeded, config-3 distributions)",
+                "config": {"workload": f"config3: {VOCAB_ROWS}x{VOCAB_IN} {fmt} vocabulary projection, batch 1, "
+                                       f"rows split over {world} GPU(s), NCCL all-gather of fp32 logits",
+                           "weight_bytes": total, "shard_bytes": local_bytes, "copies_rotated": copies,
+                           "l2": "each rank rotates over copies of its shard totalling > 2x L2"},
+                "compute_only": {"value": total / t_local / 1e9, "unit": "GB/s", "us": t_local * 1e6,
+                                 "hbm_frac_per_gpu": local_bytes / t_local / 1e9 / peak},
+                "gather_us": (t_full - t_local) * 1e6, "peak": peak, "peak_kind": peak_kind,
+                "gpu_launches": copies * args.steps * (1 if world == 1 else 2), "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    del g_local, g_full
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -415,9 +598,19 @@ def main():
     ap.add_argument("--mode", choices=["chain", "calls"], default="chain",
                     help="chain: the step as one decode-chain launch; calls: one launch per matrix group")
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers in the stack (profiling runs use fewer)")
+    ap.add_argument("--workload", choices=["stack", "vocab", "moe", "cfg1", "cfg5"], default="stack",
+                    help="stack: config 2 (the headline); vocab: config 3 row-sharded over the GPUs; "
+                         "moe: config 4; cfg1 / cfg5: the single-matrix configs")
+    ap.add_argument("--vocab-format", choices=["Q8_0", "Q6_K"], default="Q8_0")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "vocab":
+        run_vocab(args)
+    elif args.workload == "moe":
+        run_moe(args)
+    elif args.workload in MATRIX_WORKLOADS:
+        run_matrices(args)
     else:
         run_ours(args)
 

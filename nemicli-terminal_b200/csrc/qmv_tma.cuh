@@ -372,6 +372,51 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
     }
 }
 
+// Q6_K unit with a known alignment of its superblock in shared memory: EVEN = superblock index even
+// (4-byte aligned: plain word loads), else 2 bytes past a word (byte-permuted word pairs).  Same sums
+// as unit_sums<F_Q6_K>.
+template <bool EVEN>
+__device__ __forceinline__ uint4 lds16_q6(uint32_t a) {
+    if constexpr (EVEN) return make_uint4(lds32(a), lds32(a + 4), lds32(a + 8), lds32(a + 12));
+    const uint32_t b = a - 2;
+    const uint32_t w0 = lds32(b), w1 = lds32(b + 4), w2 = lds32(b + 8), w3 = lds32(b + 12), w4 = lds32(b + 16);
+    return make_uint4(__byte_perm(w0, w1, 0x5432), __byte_perm(w1, w2, 0x5432), __byte_perm(w2, w3, 0x5432),
+                      __byte_perm(w3, w4, 0x5432));
+}
+template <bool EVEN>
+__device__ __forceinline__ float unit_dot_q6(uint32_t rs, int u, const Act<F_Q6_K>& a) {
+    const int b = u >> 3, q = u & 7, n = q >> 2, j = q & 3, A = j >> 1, B = A + 2, l0 = 16 * (j & 1);
+    const uint32_t sb = rs + b * 210;
+    const uint4 ql = lds16_q6<EVEN>(sb + 64 * n + 16 * j), qh = lds16_q6<EVEN>(sb + 128 + 32 * n + l0);
+    const uint32_t L[4] = {ql.x, ql.y, ql.z, ql.w}, H[4] = {qh.x, qh.y, qh.z, qh.w};
+    const int shA = 4 - 2 * A, shB = 2 * A;
+    uint32_t wa[4], wb[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        wa[i] = (L[i] & 0x0F0F0F0Fu) | ((H[i] << shA) & 0x30303030u);
+        wb[i] = ((L[i] >> 4) & 0x0F0F0F0Fu) | ((H[i] >> shB) & 0x30303030u);
+    }
+    const int s0 = dp4(wa[1], a.q[0].y, dp4(wa[0], a.q[0].x, 0)) + dp4(wa[3], a.q[0].w, dp4(wa[2], a.q[0].z, 0));
+    const int s1 = dp4(wb[1], a.q[1].y, dp4(wb[0], a.q[1].x, 0)) + dp4(wb[3], a.q[1].w, dp4(wb[2], a.q[1].z, 0));
+    const int u0 = dp4(wa[1], a.r[0].y, dp4(wa[0], a.r[0].x, 0)) + dp4(wa[3], a.r[0].w, dp4(wa[2], a.r[0].z, 0));
+    const int u1 = dp4(wb[1], a.r[1].y, dp4(wb[0], a.r[1].x, 0)) + dp4(wb[3], a.r[1].w, dp4(wb[2], a.r[1].z, 0));
+    // 254 S + S2 of each group, the -32 of every code taken off with the activation sums (sq, sr hold
+    // 32 * (254 sum xq + sum xq2) for this path)
+    const int f0 = 254 * s0 + u0 - a.sq[0], f1 = 254 * s1 + u1 - a.sq[1];
+    const float d = h2f(lds16u(sb + 208));
+    const float w0 = d * float(int8_t(lds8u(sb + 192 + 8 * n + 2 * A + (j & 1))));
+    const float w1 = d * float(int8_t(lds8u(sb + 192 + 8 * n + 2 * B + (j & 1))));
+    return w0 * a.d[0] * float(f0) + w1 * a.d[1] * float(f1);
+}
+// the lane -> Q6_K unit map used with unit_dot_q6: virtual index v (lane in team + G * k) covers units
+// so that the 32 lanes of a warp read 4 superblocks b, b+2, b+4, b+6 of one parity: their 210-byte
+// strides fall on four different bank phases (no conflicts) and the parity, hence the alignment, is
+// the same in the whole warp.  A bijection on [0, U) when the row has a multiple of 8 superblocks.
+__device__ __forceinline__ int q6_unit_of(int v) {
+    const int m = v >> 6, p = (v >> 5) & 1, i = (v >> 3) & 3, q = v & 7;
+    return 8 * (8 * m + p + 2 * i) + q;
+}
+
 // sum-unit index (values sharing both scales: 16 for Q6_K, 32 otherwise) of scale group k of unit u
 template <int FMT>
 __device__ __forceinline__ int sum_unit(int u, int k) {
