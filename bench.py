@@ -468,10 +468,9 @@ def run_matrices(args):
 
 def run_moe(args):
     """Config 4: MoE FFN of 128 Q4_K experts (gate/up 768x2048, down 2048x768), top-8 routing, batch
-    1 / 4 / 16.  One GPU: moe.MoeFFN captured in a CUDA graph over rotating routings.  N GPUs:
-    shard.ExpertShardedMoE (experts split, all-to-all exchanges; each rank has its own tokens), timed
-    with events (the exchange sizes cross to the host).  Bytes per call = distinct experts touched x
-    2,654,208."""
+    1 / 4 / 16, captured in a CUDA graph over 16 rotating routings.  One GPU: moe.MoeFFN.  N GPUs:
+    shard.ExpertShardedMoE (experts split, fixed-capacity all-to-all exchanges; each rank has its own
+    tokens).  Bytes per call = distinct experts touched x 2,654,208 (per rank)."""
     world, rank, local, device, dist = _init_rank()
     from nemicli_terminal_b200 import moe, shard, synth
     from nemicli_terminal_b200.formats import TYPE_ID, row_bytes
@@ -489,27 +488,10 @@ def run_moe(args):
         routes = [moe.route(synth.router_logits(B, MOE_EXPERTS, seed=720 + r + 97 * rank, device=device), MOE_K)
                   for r in range(n_rot)]
         uniq = sum(int(torch.unique(ix).numel()) for ix, _ in routes) / n_rot
-        if world == 1:
-            ffn = moe.MoeFFN(*ex)
-            g, _ = capture(lambda: [ffn(x, ix, w) for x, (ix, w) in zip(xs, routes)])
-            t = time_graph(g, args.steps, max(3, args.warmup), None) / (args.steps * n_rot)
-            del g
-        else:
-            layer = shard.ExpertShardedMoE(*ex, MOE_EXPERTS, MOE_DIM)
-            for _ in range(max(3, args.warmup)):
-                for x, (ix, w) in zip(xs, routes):
-                    layer(x, ix, w)
-            torch.cuda.synchronize()
-            dist.barrier()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            reps = max(2, args.steps // 10)
-            for _ in range(reps):
-                for x, (ix, w) in zip(xs, routes):
-                    layer(x, ix, w)
-            b.record()
-            torch.cuda.synchronize()
-            t = a.elapsed_time(b) / 1e3 / (reps * n_rot)
+        layer = moe.MoeFFN(*ex) if world == 1 else shard.ExpertShardedMoE(*ex, MOE_EXPERTS, MOE_DIM)
+        g, _ = capture(lambda: [layer(x, ix, w) for x, (ix, w) in zip(xs, routes)])
+        t = time_graph(g, args.steps, max(3, args.warmup), dist) / (args.steps * n_rot)
+        del g
         t = max_over_ranks(t, dist, device)
         results[str(B)] = {"us_per_call": t * 1e6, "unique_experts": uniq, "gbs": uniq * per_expert / t / 1e9 * world}
     if rank == 0:
@@ -519,7 +501,7 @@ def run_moe(args):
                 "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded, config-4 distributions)",
                 "config": {"workload": "config4: 128 experts x {gate, up 768x2048, down 2048x768} Q4_K, top-8, "
                                        + ("one GPU, graph-captured" if world == 1 else f"expert-sharded over {world} GPUs, "
-                                          "own tokens per rank, all-to-all exchanges"),
+                                          "own tokens per rank, fixed-capacity all-to-all exchanges, graph-captured"),
                            "bytes_per_expert": per_expert, "rotating_routings": 16},
                 "batches": results}
         print(json.dumps(line), flush=True)

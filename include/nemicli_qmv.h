@@ -72,7 +72,8 @@ int qmv_mv(int ggml_type, const uint8_t* w, int n_out, int n_in, const int8_t* x
  * raw: the expert tensor (n_exp experts of per_expert bytes each) or, with per_expert < 0, a device
  * table of n_exp int64 addresses (one per expert).  Slot j reads activation row j / x_group (rows are
  * n_in values apart): x_group = k shares one input among all slots, 1 gives each slot its own row,
- * and k_per_token for tokens x slots.  ids outside [0, n_exp) give zero rows and set
+ * and k_per_token for tokens x slots.  An id of -1 marks an unused slot (a padded exchange buffer):
+ * zero rows, no weight read, no error.  Other ids outside [0, n_exp) give zero rows and set
  * QMV_DEV_BAD_ADDRESS.  Replaces: ggufengine/cudakern.py:756-774 (mv, the mv_<FMT> expert gather
  * :483-505) as called by PackedExperts.matvec / matvec_je (models/common.py:462-475). */
 int qmv_mv_experts(int ggml_type, const void* raw, long long per_expert, long long n_exp, const long long* ids,

@@ -23,6 +23,7 @@ enum : int {
 
 // bits of the device-side status word (set by kernels, read with qmv_device_status)
 enum : int { DEV_BAD_ADDRESS = 1 };
+constexpr long long kPadSlot = -1;     // expert id of an unused slot: its output rows are zeros
 
 constexpr int kWarpsPerBlock = 8;
 constexpr int kMaxTokens = 8;           // tokens per launch of the dp4a kernels

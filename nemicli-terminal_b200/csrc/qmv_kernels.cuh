@@ -399,7 +399,8 @@ __device__ __forceinline__ const uint8_t* slot_base(const MvParams& P, int slot)
     if (P.ids == nullptr) return P.w;
     const long long e = P.ids[slot];
     if (e < 0 || e >= P.n_exp) {
-        if (P.status) atomicOr(P.status, DEV_BAD_ADDRESS);
+        // -1 marks an unused slot (a padded exchange buffer): zeros, no error
+        if (e != kPadSlot && P.status) atomicOr(P.status, DEV_BAD_ADDRESS);
         return nullptr;
     }
     const uint8_t* base = P.per_expert >= 0 ? P.w + e * P.per_expert

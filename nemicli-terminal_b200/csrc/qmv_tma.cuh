@@ -485,7 +485,8 @@ __device__ __forceinline__ TileInfo tile_at(const TmaParams& P, long long g, lon
     return t;
 }
 
-// weight base of a slot, or nullptr for a refused expert id / misaligned table entry
+// weight base of a slot, or nullptr for an unused slot (id -1), a refused expert id or a misaligned
+// table entry
 __device__ __forceinline__ const uint8_t* tma_slot_base(const TmaParams& P, int slot) {
     if (P.ids == nullptr) return P.w[slot];
     const long long e = P.ids[slot];
@@ -553,7 +554,8 @@ __global__ void __launch_bounds__(32 * (NCW + 1), NCW <= 8 ? 2 : 1) mv_tma_kerne
             g += ti.nrows;
             const uint8_t* base = tma_slot_base(P, ti.slot);
             if (base == nullptr) {
-                if (P.status) atomicOr(P.status, DEV_BAD_ADDRESS);
+                // a refused id sets the status bit; an unused slot (id -1) is just zeros
+                if (P.status && P.ids[ti.slot] != kPadSlot) atomicOr(P.status, DEV_BAD_ADDRESS);
                 mbar_arrive(full0 + 8 * s);                   // nothing to copy: consumers write zeros
             } else {
                 const uint32_t bytes = uint32_t((long long)ti.nrows * P.row_bytes);

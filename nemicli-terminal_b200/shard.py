@@ -15,10 +15,9 @@ ExpertShardedMoE   rank g holds experts [g*E/G, (g+1)*E/G).  Tokens stay on thei
                    the results come back (all-to-all) and the home rank forms the weighted sum in slot
                    order.
 
-The exchanges take their sizes from the routing on the host (one device-to-host copy of the pair
-counts per call), so an expert-sharded call is not captured in a CUDA graph; the row-sharded call is
-(its sizes are fixed).  Remote bytes always arrive through the collective into this GPU's memory
-before a kernel reads them.
+Both exchanges have fixed sizes (the expert exchange sends fixed-capacity blocks with unused slots
+marked), so nothing is read on the host and both calls can be captured in a CUDA graph.  Remote bytes
+always arrive through the collective into this GPU's memory before a kernel reads them.
 """
 from __future__ import annotations
 
@@ -119,7 +118,8 @@ class ExpertShardedMoE:
 
     gate, up, down: this rank's experts (PackedExperts holding shard_range(n_exp, world, rank)).
     ffn(local_ids, a) -> (P, E) float32: optional replacement of the local expert computation (the
-    default runs gate/up -> act -> down through the CUDA kernels, each pair on its own input)."""
+    default runs gate/up -> act -> down through the CUDA kernels, each pair on its own input); ids of
+    -1 mark unused slots, whose rows are ignored."""
 
     def __init__(self, gate: Optional[PackedExperts], up: Optional[PackedExperts], down: Optional[PackedExperts],
                  n_exp: int, dim: int, group=None, act: Optional[Callable] = None,
@@ -137,51 +137,52 @@ class ExpertShardedMoE:
                 raise ValueError("ExpertShardedMoE: gate/up/down shapes do not chain")
         self.gate, self.up, self.down = gate, up, down
         self._ffn = ffn or self._ffn_cuda
-        self.last_load: Optional[List[int]] = None
+        self.last_load: Optional[torch.Tensor] = None
+        self._lo_tab = {}                       # device -> first expert of every rank
 
     def _ffn_cuda(self, ids: torch.Tensor, a: torch.Tensor) -> torch.Tensor:
         g = self.gate.matvec_je(ids, a)
         u = self.up.matvec_je(ids, a)
         return self.down.matvec_je(ids, (self.act(g) * u).contiguous())
 
-    def _exchange(self, send: torch.Tensor, send_counts: List[int], recv_counts: List[int]) -> torch.Tensor:
-        recv = torch.empty((sum(recv_counts),) + tuple(send.shape[1:]), dtype=send.dtype, device=send.device)
-        dist.all_to_all_single(recv, send, output_split_sizes=recv_counts, input_split_sizes=send_counts,
-                               group=self.group)
+    def _a2a(self, send: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return send
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=self.group)      # equal splits: world blocks
         return recv
 
     def __call__(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-        """x (L, dim) this rank's tokens, idx (L, k) expert ids, w (L, k) weights -> (L, dim) float32."""
+        """x (L, dim) this rank's tokens, idx (L, k) expert ids, w (L, k) weights -> (L, dim) float32.
+
+        Every rank sends every rank a buffer of C = L * k pair slots (the most pairs one owner can
+        receive from it): each pair's activation at its owner's block, in pair order, unused slots
+        with expert id -1.  All sizes are fixed, nothing is read on the host, so the call can be
+        captured in a CUDA graph.  Owners skip unused slots (the kernels write zeros for id -1)."""
         L, k = idx.shape
         dev = x.device
+        P = L * k
         pair_e = idx.reshape(-1).to(torch.int64)
         dest = owner_of(pair_e, self.n_exp, self.world)
-        order = torch.argsort(dest * (L * k) + torch.arange(L * k, device=dev))   # by owner, stable
-        send_counts_t = torch.bincount(dest, minlength=self.world)
-        if self.world > 1:
-            recv_counts_t = torch.empty_like(send_counts_t)
-            dist.all_to_all_single(recv_counts_t, send_counts_t, group=self.group)
-        else:
-            recv_counts_t = send_counts_t
-        send_counts = [int(c) for c in send_counts_t.cpu()]
-        recv_counts = [int(c) for c in recv_counts_t.cpu()]
-        self.last_load = recv_counts
-        token = order // k
-        a_send = x.float()[token].contiguous()                      # (L*k, dim), grouped by owner
-        e_send = pair_e[order]
-        if self.world > 1:
-            a_recv = self._exchange(a_send, send_counts, recv_counts)
-            e_recv = self._exchange(e_send, send_counts, recv_counts)
-        else:
-            a_recv, e_recv = a_send, e_send
-        if e_recv.numel():
-            y_recv = self._ffn((e_recv - self.lo).contiguous(), a_recv).float()
-        else:
-            y_recv = torch.zeros(0, self.dim, dtype=torch.float32, device=dev)
-        y_back = self._exchange(y_recv.contiguous(), recv_counts, send_counts) if self.world > 1 else y_recv
-        y_pairs = torch.empty(L * k, self.dim, dtype=torch.float32, device=dev)
-        y_pairs[order] = y_back
-        return combine(y_pairs.view(L, k, self.dim), w)
+        onehot = (dest[:, None] == torch.arange(self.world, device=dev)[None, :]).to(torch.int64)
+        pos = (onehot.cumsum(0) - 1).gather(1, dest[:, None]).squeeze(1)   # rank among pairs to that owner
+        slot = dest * P + pos
+        lo_tab = self._lo_tab.get(dev)
+        if lo_tab is None:                      # built on the first call (before any graph capture)
+            lo_tab = torch.tensor([shard_range(self.n_exp, self.world, r)[0] for r in range(self.world)],
+                                  dtype=torch.int64, device=dev)
+            self._lo_tab[dev] = lo_tab
+        send_e = torch.full((self.world * P,), -1, dtype=torch.int64, device=dev)
+        send_e[slot] = pair_e - lo_tab[dest]
+        send_a = torch.zeros(self.world * P, self.dim, dtype=torch.float32, device=dev)
+        send_a[slot] = x.float()[torch.arange(P, device=dev) // k]
+        recv_e = self._a2a(send_e)
+        recv_a = self._a2a(send_a)
+        self.last_load = self._a2a(onehot.sum(0))                   # pairs received from each rank
+        y_recv = self._ffn(recv_e, recv_a).float()
+        y_recv = torch.where(recv_e[:, None] >= 0, y_recv, torch.zeros_like(y_recv))
+        y_back = self._a2a(y_recv.contiguous())
+        return combine(y_back[slot].view(L, k, self.dim), w)
 
 
 def combine(y: torch.Tensor, w: torch.Tensor) -> torch.Tensor:

@@ -28,6 +28,9 @@ def _ffn_ref(wg, wu, wd, ids, a):
     """Per pair: down_e(silu(gate_e a) * up_e a) in float64 -> float32."""
     out = []
     for e, v in zip(ids.tolist(), a.double()):
+        if e < 0:                                                    # unused exchange slot
+            out.append(torch.zeros(wd.shape[1], dtype=torch.float64))
+            continue
         h = F.silu(wg[e] @ v) * (wu[e] @ v)
         out.append(wd[e] @ h)
     return torch.stack(out).float() if out else torch.zeros(0, wd.shape[1])
@@ -66,7 +69,7 @@ def check_experts(rank, world, skew):
     idx, w = moe.route(logits, k)
 
     def ffn(local_ids, a):
-        return _ffn_ref(wg, wu, wd, local_ids + lo, a)
+        return _ffn_ref(wg, wu, wd, torch.where(local_ids >= 0, local_ids + lo, local_ids), a)
 
     moe_layer = shard.ExpertShardedMoE(None, None, None, n_exp, dim, ffn=ffn)
     y = moe_layer(x, idx, w)
@@ -74,7 +77,8 @@ def check_experts(rank, world, skew):
     ref = shard.combine(pairs, w)
     assert torch.equal(y, ref), f"expert shard differs by {float((y - ref).abs().max())}"
     if skew:                                     # pairs received from each rank: all land on rank 0
-        assert moe_layer.last_load == ([L * k] * world if rank == 0 else [0] * world), moe_layer.last_load
+        got = moe_layer.last_load.tolist()
+        assert got == ([L * k] * world if rank == 0 else [0] * world), got
 
 
 def worker(rank, world, port, result_dir):

@@ -58,7 +58,7 @@ def test_refused_ids_give_zeros_and_flag(cuda):
     fmt, n_in = "Q4_K", 256
     raw = _experts(fmt, 3, 8, n_in, seed=1).to(cuda)
     _lib.device_status(clear=True)
-    ids = torch.tensor([0, 7, -1, 2], device=cuda)
+    ids = torch.tensor([0, 7, -3, 2], device=cuda)
     x = synth.activations(1, n_in, seed=2, device=cuda)[0]
     y = cudakern.mv(fmt, raw, ids, x, 8, n_in)
     assert _lib.device_status(clear=True) & 1
@@ -66,6 +66,21 @@ def test_refused_ids_give_zeros_and_flag(cuda):
     ok = cudakern.mv(fmt, raw, torch.tensor([0, 2], device=cuda), x, 8, n_in)
     assert torch.equal(y[0], ok[0]) and torch.equal(y[3], ok[1])
     assert _lib.device_status(clear=True) == 0
+
+
+@pytest.mark.parametrize("n_in", [256, 4096])
+def test_padding_slots_give_zeros_without_flag(cuda, n_in):
+    """Expert id -1 marks an unused slot of a padded exchange buffer: zero rows, no error bit
+    (256: fallback kernel, 4096: staged kernel)."""
+    fmt = "Q4_K"
+    raw = _experts(fmt, 3, 64, n_in, seed=3).to(cuda)
+    _lib.device_status(clear=True)
+    x = synth.activations(1, n_in, seed=4, device=cuda)[0]
+    y = cudakern.mv(fmt, raw, torch.tensor([1, -1, -1, 2], device=cuda), x, 64, n_in)
+    assert _lib.device_status(clear=True) == 0
+    assert (y[1] == 0).all() and (y[2] == 0).all()
+    ok = cudakern.mv(fmt, raw, torch.tensor([1, 2], device=cuda), x, 64, n_in)
+    assert torch.equal(y[0], ok[0]) and torch.equal(y[3], ok[1])
 
 
 def test_cuda_graph_replay_with_new_ids(cuda):
