@@ -149,7 +149,7 @@ struct TmaPlan {
     int NCW, G, UPL, R, S, smem;
 };
 
-__host__ __device__ constexpr int unit_vals(int fmt) { return fmt == F_Q4_K ? 64 : 32; }
+__host__ __device__ constexpr int unit_vals(int fmt) { return fmt == F_Q4_K || fmt == F_Q6_K ? 64 : 32; }   // UnitTraits::VPU
 
 // Tuning knobs read once from the environment (benchmark sweeps): NEMICLI_QMV_TMA=0 sends every call
 // to the fallback kernel, NEMICLI_QMV_TMA_G forces the team width (16..512) where it fits.

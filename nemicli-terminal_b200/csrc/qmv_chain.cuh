@@ -77,17 +77,19 @@ struct ChainParams {
 };
 
 template <int CFG> struct ChainCfg;
-// tiles of 27..37 KB (R = NPER * 512 / G rows): six ring slots fit in shared memory
+// tiles of 27..47 KB (R = NPER * 512 / G rows; 4 Q6_K rows give every CTA the same tile count for
+// a 4096-row down projection).  Q6_K uses 32-value units here (F_Q6_K_U32): the 64-value units of the
+// staged kernel need more registers than this non-inlined loop has without spilling.
 template <> struct ChainCfg<CFG_Q4K_4096> { static constexpr int FMT = F_Q4_K, G = 64, UPL = 1, NPER = 2; };
-template <> struct ChainCfg<CFG_Q6K_14336> { static constexpr int FMT = F_Q6_K, G = 512, UPL = 1, NPER = 3; };
+template <> struct ChainCfg<CFG_Q6K_14336> { static constexpr int FMT = F_Q6_K_U32, G = 512, UPL = 1, NPER = 4; };
 template <> struct ChainCfg<CFG_Q4K_14336> { static constexpr int FMT = F_Q4_K, G = 256, UPL = 1, NPER = 2; };
-template <> struct ChainCfg<CFG_Q6K_4096> { static constexpr int FMT = F_Q6_K, G = 128, UPL = 1, NPER = 2; };
+template <> struct ChainCfg<CFG_Q6K_4096> { static constexpr int FMT = F_Q6_K_U32, G = 128, UPL = 1, NPER = 2; };
 template <> struct ChainCfg<CFG_Q8_0_4096> { static constexpr int FMT = F_Q8_0, G = 128, UPL = 1, NPER = 2; };
 
 __host__ __device__ constexpr int chain_cfg_g(int cfg) {
     return cfg == CFG_Q4K_4096 ? 64 : cfg == CFG_Q6K_14336 ? 512 : cfg == CFG_Q4K_14336 ? 256 : 128;
 }
-__host__ __device__ constexpr int chain_cfg_nper(int cfg) { return cfg == CFG_Q6K_14336 ? 3 : 2; }
+__host__ __device__ constexpr int chain_cfg_nper(int cfg) { return cfg == CFG_Q6K_14336 ? 4 : 2; }
 __host__ __device__ constexpr int chain_cfg_fmt(int cfg) {
     return cfg == CFG_Q4K_4096 || cfg == CFG_Q4K_14336 ? F_Q4_K : cfg == CFG_Q8_0_4096 ? F_Q8_0 : F_Q6_K;
 }
@@ -105,15 +107,13 @@ __device__ __forceinline__ int chain_row_begin(const ChainStage& st, int c) {
     return int((long long)c * st.total_rows / gridDim.x);
 }
 
-__device__ __forceinline__ TileInfo chain_tile_at(const ChainStage& st, long long g, long long hi) {
-    TileInfo t;
+// A CTA's rows [lo, lo + n) of a stage's concatenated row space go in tiles of R rows from lo (the last
+// one shorter).  A tile may span two jobs (one copy per job segment), so a CTA whose range crosses a
+// job boundary runs no extra tile for it.
+__device__ __forceinline__ int chain_job_of(const ChainStage& st, int g) {
     int j = 0;
-    while (j + 1 < st.n_jobs && g >= st.row_start[j + 1]) ++j;
-    t.job = t.slot = j;
-    t.row0 = int(g - st.row_start[j]);
-    const long long lim = min(st.row_start[j + 1], hi);
-    t.nrows = int(min((long long)st.R, lim - g));
-    return t;
+    while (j + 1 < st.n_jobs && g >= int(st.row_start[j + 1])) ++j;
+    return j;
 }
 
 __device__ __forceinline__ int ld_acquire(const int* p) {
@@ -252,79 +252,74 @@ __device__ __noinline__ int chain_consume(const ChainParams& P, const ChainStage
             }
         }
     }
-    int w_job = 0, w_row0 = 0, w_rows = 0;
+    int w_g0 = 0, w_rows = 0;                              // window: rows [w_g0, w_g0 + w_rows)
     auto flush = [&]() {                                    // every consumer thread, uniformly
         named_sync(kConsumerBarrier, 32 * NCW);
         if (!dead) {
-            float* y = st.y[w_job];
             for (int rl = cl; rl < w_rows; rl += 32 * NCW) {
                 float v = 0.f;
 #pragma unroll
                 for (int w = 0; w < WPT; ++w) v += part[rl * WPT + w];
-                y[w_row0 + rl] = v;
+                const int g = w_g0 + rl, j = chain_job_of(st, g);
+                st.y[j][g - int(st.row_start[j])] = v;
             }
         }
         named_sync(kConsumerBarrier, 32 * NCW);
         w_rows = 0;
     };
-    const int lo = chain_row_begin(st, blockIdx.x), hi = chain_row_begin(st, blockIdx.x + 1);
-    const int R = st.R;
+    const int lo = chain_row_begin(st, blockIdx.x), n = chain_row_begin(st, blockIdx.x + 1) - lo;
+    const int R = st.R, tiles = (n + R - 1) / R;
     const uint32_t row_bytes = uint32_t(st.row_bytes);
-    for (int j = 0; j < st.n_jobs; ++j) {
-        const int js = int(st.row_start[j]);
-        const int r0 = max(lo, js), r1 = min(hi, int(st.row_start[j + 1]));
-        for (int g = r0; g < r1; g += R, ++it) {
-            const int row0 = g - js, nrows = min(R, r1 - g);
-            const int s = it % S;
-            const bool got = !dead && mbar_wait(full0 + 8 * s, (it / S) & 1);
-            if (!got && !dead) {
-                dead = true;
-                if (lane == 0 && P.status) atomicOr(P.status, DEV_TIMEOUT);
-            }
-            const uint32_t stg = stage0 + uint32_t(s) * slot_bytes;
-            float acc[NPER];
+    for (int i = 0; i < tiles; ++i, ++it) {
+        const int t0 = lo + i * R, nrows = min(R, n - i * R);
+        const int s = it % S;
+        const bool got = !dead && mbar_wait(full0 + 8 * s, (it / S) & 1);
+        if (!got && !dead) {
+            dead = true;
+            if (lane == 0 && P.status) atomicOr(P.status, DEV_TIMEOUT);
+        }
+        const uint32_t stg = stage0 + uint32_t(s) * slot_bytes;
+        float acc[NPER];
 #pragma unroll
-            for (int i = 0; i < NPER; ++i) acc[i] = 0.f;
-            // every tile runs the full-tile code: rows past a partial tile's end read stale bytes of the
-            // slot (inside the slot, since R rows always fit) and their sums are never stored
-            if (got) {
+        for (int r = 0; r < NPER; ++r) acc[r] = 0.f;
+        // every tile runs the full-tile code: rows past a short tile's end read stale bytes of the slot
+        // (inside the slot, since R rows always fit) and their sums are never stored
+        if (got) {
 #pragma unroll
-                for (int k = 0; k < UPL; ++k) {
-                    const int u = li + G * k;
-                    if (u < U) {
+            for (int k = 0; k < UPL; ++k) {
+                const int u = li + G * k;
+                if (u < U) {
 #pragma unroll
-                        for (int i = 0; i < NPER; ++i)
-                            acc[i] += unit_dot<FMT>(stg + uint32_t(team + TEAMS * i) * row_bytes, u, act[k], nullptr);
-                    }
+                    for (int r = 0; r < NPER; ++r)
+                        acc[r] += unit_dot<FMT>(stg + uint32_t(team + TEAMS * r) * row_bytes, u, act[k], nullptr);
                 }
             }
-            __syncwarp();
-            if (got && lane == 0) mbar_arrive(empty0 + 8 * s);
-            if constexpr (G <= 32) {
-                float* y = st.y[j];
+        }
+        __syncwarp();
+        if (got && lane == 0) mbar_arrive(empty0 + 8 * s);
+        if constexpr (G <= 32) {
 #pragma unroll
-                for (int i = 0; i < NPER; ++i) {
-                    float v = acc[i];
+            for (int r = 0; r < NPER; ++r) {
+                float v = acc[r];
 #pragma unroll
-                    for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                    const int r = team + TEAMS * i;
-                    if (li == 0 && got && r < nrows) y[row0 + r] = v;
+                for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                const int rr = team + TEAMS * r;
+                if (li == 0 && got && rr < nrows) {
+                    const int g = t0 + rr, j = chain_job_of(st, g);
+                    st.y[j][g - int(st.row_start[j])] = v;
                 }
-            } else {
-                if (w_rows > 0 && (j != w_job || row0 != w_row0 + w_rows || w_rows + nrows > PR)) flush();
-                if (w_rows == 0) {
-                    w_job = j;
-                    w_row0 = row0;
-                }
-                const int wt = li >> 5;
-#pragma unroll
-                for (int i = 0; i < NPER; ++i) {
-                    const float v = warp_sum(acc[i]);
-                    const int r = team + TEAMS * i;
-                    if (lane == 0 && r < nrows) part[(w_rows + r) * WPT + wt] = v;
-                }
-                w_rows += nrows;
             }
+        } else {
+            if (w_rows > 0 && (t0 != w_g0 + w_rows || w_rows + nrows > PR)) flush();
+            if (w_rows == 0) w_g0 = t0;
+            const int wt = li >> 5;
+#pragma unroll
+            for (int r = 0; r < NPER; ++r) {
+                const float v = warp_sum(acc[r]);
+                const int rr = team + TEAMS * r;
+                if (lane == 0 && rr < nrows) part[(w_rows + rr) * WPT + wt] = v;
+            }
+            w_rows += nrows;
         }
     }
     if constexpr (G > 32) {
@@ -369,22 +364,24 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) chain_kernel(const __grid_c
         bool ok = true;
         for (int k = 0; k < P.n_stages && ok; ++k) {
             const ChainStage& st = P.st[k];
-            const int lo = chain_row_begin(st, blockIdx.x), hi = chain_row_begin(st, blockIdx.x + 1);
-            const int R = st.R;
+            const int lo = chain_row_begin(st, blockIdx.x), n = chain_row_begin(st, blockIdx.x + 1) - lo;
+            const int R = st.R, tiles = (n + R - 1) / R;
             const long long row_bytes = st.row_bytes;
-            for (int j = 0; j < st.n_jobs && ok; ++j) {
-                const int js = int(st.row_start[j]);
-                const int r0 = max(lo, js), r1 = min(hi, int(st.row_start[j + 1]));
-                const uint8_t* w = st.w[j];
-                for (int g = r0; g < r1; g += R, ++it) {
-                    const int s = it % S;
-                    if (it >= S && !mbar_wait(empty0 + 8 * s, ((it / S) & 1) ^ 1)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t bytes = uint32_t(min(R, r1 - g) * row_bytes);
-                    mbar_arrive_tx(full0 + 8 * s, bytes);
-                    bulk_g2s(stage0 + uint32_t(s) * uint32_t(P.slot_bytes), w + (long long)(g - js) * row_bytes, bytes,
+            for (int i = 0; i < tiles; ++i, ++it) {
+                const int s = it % S;
+                if (it >= S && !mbar_wait(empty0 + 8 * s, ((it / S) & 1) ^ 1)) {
+                    ok = false;
+                    break;
+                }
+                const int t0 = lo + i * R, t1 = min(lo + n, t0 + R);
+                mbar_arrive_tx(full0 + 8 * s, uint32_t((t1 - t0) * row_bytes));
+                // one copy per job segment of the tile, into consecutive rows of the slot
+                for (int j = 0; j < st.n_jobs; ++j) {
+                    const int js = int(st.row_start[j]);
+                    const int a0 = max(t0, js), a1 = min(t1, int(st.row_start[j + 1]));
+                    if (a1 <= a0) continue;
+                    bulk_g2s(stage0 + uint32_t(s) * uint32_t(P.slot_bytes) + uint32_t((a0 - t0) * row_bytes),
+                             st.w[j] + (long long)(a0 - js) * row_bytes, uint32_t((a1 - a0) * row_bytes),
                              full0 + 8 * s);
                 }
             }

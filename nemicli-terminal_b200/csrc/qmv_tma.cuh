@@ -154,7 +154,8 @@ __device__ __forceinline__ int dot4us(const uint32_t (&w)[4], const int4& x) {
 //
 // A unit is the piece of a row one lane takes: VPU values, with NS scale groups.
 //   Q4_K    64 values: the 32 qs bytes 32p..32p+31 of superblock b (sub-blocks 2p low, 2p+1 high nibbles)
-//   Q6_K    32 values: ql bytes 64n+16j..+15 of superblock b: 16 values of group j/2 and of j/2 + 2
+//   Q6_K    64 values: positions 16h..16h+15 of half n of superblock b in all four 32-value groups
+//           (ql bytes 64n+16h.., 64n+32+16h.., qh bytes 128+32n+16h..: one qh load serves four groups)
 //   Q4_0    32 values: one block
 //   Q8_0    32 values: one block
 //   TQ2_0   32 values: qs bytes 32n+8j..+7 of superblock b: 8 values of each of the four groups of half n
@@ -162,7 +163,11 @@ __device__ __forceinline__ int dot4us(const uint32_t (&w)[4], const int4& x) {
 
 template <int FMT> struct UnitTraits { static constexpr int VPU = 32, NS = 1, NQ = 2; };
 template <> struct UnitTraits<F_Q4_K> { static constexpr int VPU = 64, NS = 2, NQ = 4; };
-template <> struct UnitTraits<F_Q6_K> { static constexpr int VPU = 32, NS = 2, NQ = 2; };
+template <> struct UnitTraits<F_Q6_K> { static constexpr int VPU = 64, NS = 4, NQ = 4; };
+// Q6_K with 32-value units (ql bytes 64n+16j..+15 of superblock b: 16 values of group j/2 and of j/2 + 2):
+// a smaller activation footprint, for the decode chain's register budget.  Internal tag only.
+constexpr int F_Q6_K_U32 = 0x100 | F_Q6_K;
+template <> struct UnitTraits<F_Q6_K_U32> { static constexpr int VPU = 32, NS = 2, NQ = 2; };
 template <> struct UnitTraits<F_TQ2_0> { static constexpr int VPU = 32, NS = 4, NQ = 2; };
 
 template <int FMT>
@@ -171,8 +176,9 @@ struct Act {                              // the activation of one unit, in regi
     int4 r[UnitTraits<FMT>::NQ];          // xq2 bytes
     float d[UnitTraits<FMT>::NS];         // xd / 254 of each scale group
     float s[UnitTraits<FMT>::NS];         // xs of each group (0 where another lane applies the offset)
-    int sq[FMT == F_Q6_K ? 2 : 1];        // Q6_K: sum of the 16 xq of each group (the -32 of the codes)
-    int sr[FMT == F_Q6_K ? 2 : 1];        //       sum of the 16 xq2 of each group
+    int sq[FMT == F_Q6_K ? 4 : FMT == F_Q6_K_U32 ? 2 : 1];   // Q6_K: sum of the 16 xq of each group
+    int sr[FMT == F_Q6_K ? 4 : FMT == F_Q6_K_U32 ? 2 : 1];   //       sum of the 16 xq2 of each group
+    int kk[FMT == F_Q6_K ? 4 : 1];        //       32 * (254 sq + sr): the -32 of 254 S + S2
 };
 
 // activation sources: SRC_SMEM shared memory; SRC_NC global through the read-only path (inputs that
@@ -222,19 +228,29 @@ __device__ __forceinline__ void load_act(Act<FMT>& a, int u, const int8_t* xq, c
         a.d[1] = ldf<GLOBAL, SCALES>(xd, b * 8 + 2 * p + 1) * kInv254;
         a.s[0] = ldf<GLOBAL, SCALES>(xs, b * 8 + 2 * p);
         a.s[1] = ldf<GLOBAL, SCALES>(xs, b * 8 + 2 * p + 1);
-    } else if constexpr (FMT == F_Q6_K) {
+    } else if constexpr (FMT == F_Q6_K_U32) {
         const int b = u >> 3, q = u & 7, n = q >> 2, j = q & 3, A = j >> 1, B = A + 2, o = b * 256 + 128 * n + 16 * (j & 1);
         a.q[0] = ldq16<GLOBAL>(xq + o + 32 * A); a.q[1] = ldq16<GLOBAL>(xq + o + 32 * B);
         a.r[0] = ldq16<GLOBAL>(xq2 + o + 32 * A); a.r[1] = ldq16<GLOBAL>(xq2 + o + 32 * B);
         a.d[0] = ldf<GLOBAL, SCALES>(xd, b * 8 + 4 * n + A) * kInv254;
         a.d[1] = ldf<GLOBAL, SCALES>(xd, b * 8 + 4 * n + B) * kInv254;
-        if constexpr (FMT == F_Q6_K) {
 #pragma unroll
-            for (int g = 0; g < 2; ++g) {
-                const int4 x = a.q[g], y = a.r[g];
-                a.sq[g] = dp4(0x01010101u, x.w, dp4(0x01010101u, x.z, dp4(0x01010101u, x.y, dp4(0x01010101u, x.x, 0))));
-                a.sr[g] = dp4(0x01010101u, y.w, dp4(0x01010101u, y.z, dp4(0x01010101u, y.y, dp4(0x01010101u, y.x, 0))));
-            }
+        for (int g = 0; g < 2; ++g) {
+            const int4 x = a.q[g], y = a.r[g];
+            a.sq[g] = dp4(0x01010101u, x.w, dp4(0x01010101u, x.z, dp4(0x01010101u, x.y, dp4(0x01010101u, x.x, 0))));
+            a.sr[g] = dp4(0x01010101u, y.w, dp4(0x01010101u, y.z, dp4(0x01010101u, y.y, dp4(0x01010101u, y.x, 0))));
+        }
+    } else if constexpr (FMT == F_Q6_K) {
+        const int b = u >> 2, n = (u >> 1) & 1, h = u & 1, o = b * 256 + 128 * n + 16 * h;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            a.q[g] = ldq16<GLOBAL>(xq + o + 32 * g);
+            a.r[g] = ldq16<GLOBAL>(xq2 + o + 32 * g);
+            a.d[g] = ldf<GLOBAL, SCALES>(xd, b * 8 + 4 * n + g) * kInv254;
+            const int4 x = a.q[g], y = a.r[g];
+            a.sq[g] = dp4(0x01010101u, x.w, dp4(0x01010101u, x.z, dp4(0x01010101u, x.y, dp4(0x01010101u, x.x, 0))));
+            a.sr[g] = dp4(0x01010101u, y.w, dp4(0x01010101u, y.z, dp4(0x01010101u, y.y, dp4(0x01010101u, y.x, 0))));
+            a.kk[g] = 32 * (254 * a.sq[g] + a.sr[g]);
         }
     } else {   // TQ2_0
         const int b = u >> 3, q = u & 7, n = q >> 2, j = q & 3, o = b * 256 + 128 * n + 8 * j;
@@ -267,6 +283,22 @@ struct UnitSums<F_Q4_K> {
     float d, dm;
 };
 
+// unsigned 6-bit codes of a Q6_K unit (w[g][i]: 4 codes of group g, positions 16h + 4i..): group g's low
+// four bits from ql (low nibbles for g = 0, 1, high for g = 2, 3), bits 4..5 from qh bits 2g..2g+1; the
+// -32 of every code is taken off with the activation sums
+__device__ __forceinline__ void q6k_codes(uint32_t sb, int n, int h, uint32_t (&w)[4][4]) {
+    const uint4 l0 = lds16_a2(sb + 64 * n + 16 * h), l1 = lds16_a2(sb + 64 * n + 32 + 16 * h);
+    const uint4 qh = lds16_a2(sb + 128 + 32 * n + 16 * h);
+    const uint32_t A[4] = {l0.x, l0.y, l0.z, l0.w}, B[4] = {l1.x, l1.y, l1.z, l1.w}, H[4] = {qh.x, qh.y, qh.z, qh.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        w[0][i] = (A[i] & 0x0F0F0F0Fu) | ((H[i] << 4) & 0x30303030u);
+        w[1][i] = (B[i] & 0x0F0F0F0Fu) | ((H[i] << 2) & 0x30303030u);
+        w[2][i] = ((A[i] >> 4) & 0x0F0F0F0Fu) | (H[i] & 0x30303030u);
+        w[3][i] = ((B[i] >> 4) & 0x0F0F0F0Fu) | ((H[i] >> 2) & 0x30303030u);
+    }
+}
+
 template <int FMT>
 __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a, UnitSums<FMT>& o, const uint2* grid) {
     if constexpr (FMT == F_Q4_K) {
@@ -294,7 +326,7 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
         o.imn[1] = (mw >> (sh + 8)) & 0xFFu;
         o.d = h2f(hd.x & 0xFFFFu);
         o.dm = h2f(hd.x >> 16);
-    } else if constexpr (FMT == F_Q6_K) {
+    } else if constexpr (FMT == F_Q6_K_U32) {
         const int b = u >> 3, q = u & 7, n = q >> 2, j = q & 3, A = j >> 1, B = A + 2, l0 = 16 * (j & 1);
         const uint32_t sb = rs + b * 210;
         const uint4 ql = lds16_a2(sb + 64 * n + 16 * j), qh = lds16_a2(sb + 128 + 32 * n + l0);
@@ -316,6 +348,19 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
         o.wsc[0] = d * float(int8_t(lds8u(sb + 192 + 8 * n + 2 * A + (j & 1))));
         o.wsc[1] = d * float(int8_t(lds8u(sb + 192 + 8 * n + 2 * B + (j & 1))));
         o.off[0] = o.off[1] = 0.f;
+    } else if constexpr (FMT == F_Q6_K) {
+        const int b = u >> 2, n = (u >> 1) & 1, h = u & 1;
+        const uint32_t sb = rs + b * 210;
+        uint32_t w[4][4];
+        q6k_codes(sb, n, h, w);
+        const float d = h2f(lds16u(sb + 208));
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            o.s[g] = dot4(w[g], a.q[g]) - 32 * a.sq[g];
+            o.u[g] = dot4(w[g], a.r[g]) - 32 * a.sr[g];
+            o.wsc[g] = d * float(int8_t(lds8u(sb + 192 + 8 * n + 2 * g + h)));
+            o.off[g] = 0.f;
+        }
     } else if constexpr (FMT == F_Q4_0) {
         const uint32_t bl = rs + u * 18;
         const uint4 v = lds16_a2(bl + 2);
@@ -372,51 +417,6 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
     }
 }
 
-// Q6_K unit with a known alignment of its superblock in shared memory: EVEN = superblock index even
-// (4-byte aligned: plain word loads), else 2 bytes past a word (byte-permuted word pairs).  Same sums
-// as unit_sums<F_Q6_K>.
-template <bool EVEN>
-__device__ __forceinline__ uint4 lds16_q6(uint32_t a) {
-    if constexpr (EVEN) return make_uint4(lds32(a), lds32(a + 4), lds32(a + 8), lds32(a + 12));
-    const uint32_t b = a - 2;
-    const uint32_t w0 = lds32(b), w1 = lds32(b + 4), w2 = lds32(b + 8), w3 = lds32(b + 12), w4 = lds32(b + 16);
-    return make_uint4(__byte_perm(w0, w1, 0x5432), __byte_perm(w1, w2, 0x5432), __byte_perm(w2, w3, 0x5432),
-                      __byte_perm(w3, w4, 0x5432));
-}
-template <bool EVEN>
-__device__ __forceinline__ float unit_dot_q6(uint32_t rs, int u, const Act<F_Q6_K>& a) {
-    const int b = u >> 3, q = u & 7, n = q >> 2, j = q & 3, A = j >> 1, B = A + 2, l0 = 16 * (j & 1);
-    const uint32_t sb = rs + b * 210;
-    const uint4 ql = lds16_q6<EVEN>(sb + 64 * n + 16 * j), qh = lds16_q6<EVEN>(sb + 128 + 32 * n + l0);
-    const uint32_t L[4] = {ql.x, ql.y, ql.z, ql.w}, H[4] = {qh.x, qh.y, qh.z, qh.w};
-    const int shA = 4 - 2 * A, shB = 2 * A;
-    uint32_t wa[4], wb[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        wa[i] = (L[i] & 0x0F0F0F0Fu) | ((H[i] << shA) & 0x30303030u);
-        wb[i] = ((L[i] >> 4) & 0x0F0F0F0Fu) | ((H[i] >> shB) & 0x30303030u);
-    }
-    const int s0 = dp4(wa[1], a.q[0].y, dp4(wa[0], a.q[0].x, 0)) + dp4(wa[3], a.q[0].w, dp4(wa[2], a.q[0].z, 0));
-    const int s1 = dp4(wb[1], a.q[1].y, dp4(wb[0], a.q[1].x, 0)) + dp4(wb[3], a.q[1].w, dp4(wb[2], a.q[1].z, 0));
-    const int u0 = dp4(wa[1], a.r[0].y, dp4(wa[0], a.r[0].x, 0)) + dp4(wa[3], a.r[0].w, dp4(wa[2], a.r[0].z, 0));
-    const int u1 = dp4(wb[1], a.r[1].y, dp4(wb[0], a.r[1].x, 0)) + dp4(wb[3], a.r[1].w, dp4(wb[2], a.r[1].z, 0));
-    // 254 S + S2 of each group, the -32 of every code taken off with the activation sums (sq, sr hold
-    // 32 * (254 sum xq + sum xq2) for this path)
-    const int f0 = 254 * s0 + u0 - a.sq[0], f1 = 254 * s1 + u1 - a.sq[1];
-    const float d = h2f(lds16u(sb + 208));
-    const float w0 = d * float(int8_t(lds8u(sb + 192 + 8 * n + 2 * A + (j & 1))));
-    const float w1 = d * float(int8_t(lds8u(sb + 192 + 8 * n + 2 * B + (j & 1))));
-    return w0 * a.d[0] * float(f0) + w1 * a.d[1] * float(f1);
-}
-// the lane -> Q6_K unit map used with unit_dot_q6: virtual index v (lane in team + G * k) covers units
-// so that the 32 lanes of a warp read 4 superblocks b, b+2, b+4, b+6 of one parity: their 210-byte
-// strides fall on four different bank phases (no conflicts) and the parity, hence the alignment, is
-// the same in the whole warp.  A bijection on [0, U) when the row has a multiple of 8 superblocks.
-__device__ __forceinline__ int q6_unit_of(int v) {
-    const int m = v >> 6, p = (v >> 5) & 1, i = (v >> 3) & 3, q = v & 7;
-    return 8 * (8 * m + p + 2 * i) + q;
-}
-
 // sum-unit index (values sharing both scales: 16 for Q6_K, 32 otherwise) of scale group k of unit u
 template <int FMT>
 __device__ __forceinline__ int sum_unit(int u, int k) {
@@ -424,8 +424,8 @@ __device__ __forceinline__ int sum_unit(int u, int k) {
     if constexpr (FMT == F_Q4_K) return 2 * u + k;          // unit u = sub-blocks 2u, 2u + 1 of the row
     const int b = u >> 3, q = u & 7;
     if constexpr (FMT == F_Q6_K) {
-        const int n = q >> 2, j = q & 3, A = j >> 1;
-        return b * 16 + 8 * n + 2 * (k == 0 ? A : A + 2) + (j & 1);
+        const int b6 = u >> 2, n = (u >> 1) & 1, h = u & 1;     // group k: values 128n + 32k + 16h.. of b6
+        return b6 * 16 + 8 * n + 2 * k + h;
     }
     return b * 8 + 4 * (q >> 2) + k;    // TQ2_0
 }
@@ -435,7 +435,24 @@ template <int FMT>
 __device__ __forceinline__ float unit_dot(uint32_t rs, int u, const Act<FMT>& a, const uint2* grid) {
     UnitSums<FMT> o;
     unit_sums<FMT>(rs, u, a, o, grid);
-    if constexpr (FMT == F_Q4_K) {
+    if constexpr (FMT == F_Q6_K) {
+        // sum_g d sc_g * (xd_g / 254) * (254 S_g + S2_g), the codes' -32 folded into kk
+        const int b = u >> 2, n = (u >> 1) & 1, h = u & 1;
+        const uint32_t sb = rs + b * 210;
+        uint32_t w[4][4];
+        q6k_codes(sb, n, h, w);
+        const float d = h2f(lds16u(sb + 208));
+        float acc = 0.f;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            const int4 x = a.q[g], y = a.r[g];
+            const int s_ = dp4(w[g][1], x.y, dp4(w[g][0], x.x, 0)) + dp4(w[g][3], x.w, dp4(w[g][2], x.z, 0));
+            const int t_ = dp4(w[g][1], y.y, dp4(w[g][0], y.x, 0)) + dp4(w[g][3], y.w, dp4(w[g][2], y.z, 0));
+            const float wsc = d * float(int8_t(lds8u(sb + 192 + 8 * n + 2 * g + h)));
+            acc = fmaf(wsc * a.d[g], float(254 * s_ + t_ - a.kk[g]), acc);
+        }
+        return acc;
+    } else if constexpr (FMT == F_Q4_K) {
         // d * sum_k sc_k * (254 S_k + S2_k) * xd_k / 254  -  dmin * sum_k m_k * xs_k
         const float w = float(o.isc[0] * (254 * o.s[0] + o.u[0])) * a.d[0]
                       + float(o.isc[1] * (254 * o.s[1] + o.u[1])) * a.d[1];
