@@ -7,6 +7,7 @@
 #include "qmv_kernels.cuh"
 #include "qmv_tma.cuh"
 #include "qmv_chain.cuh"
+#include "qmv_mma.cuh"
 #include "../../include/nemicli_qmv.h"
 
 using namespace qmv;
@@ -301,6 +302,40 @@ bool tma_dense(int fmt, int n_jobs, const uint8_t* const* w, const int* n_out, f
 
 }  // namespace
 
+namespace {
+// Few-token Q4_K matvec on the tensor cores; false when the shape or alignment does not qualify.
+bool mma_q4k(const uint8_t* w, int n_out, int n_in, long long row_bytes, const int8_t* xq, const int8_t* xq2,
+             const float* xd, const float* xs, int T, float* y, int fmt, cudaStream_t st, int* status) {
+    if (fmt != F_Q4_K || T < 2 || T > kMmaMaxTok || n_in % 256 || n_in > kMmaMaxIn || !knobs().enabled) return false;
+    if (!aligned(w, 16) || !aligned(xq, 16) || !aligned(xq2, 16) || row_bytes % 16) return false;
+    constexpr int NCW = 16;
+    const long long other = mma_act_bytes(n_in) + mma_red_bytes(NCW) + 2 * 8 * 32;
+    const long long slot = kMmaRows * mma_row_stride(row_bytes);
+    long long S = (kSmemCap - other) / slot;
+    if (S > 4) S = 4;
+    if (S < 2) return false;
+    MmaParams P{};
+    P.w = w; P.y = y; P.xq = xq; P.xq2 = xq2; P.xd = xd; P.xs = xs;
+    P.row_bytes = row_bytes; P.n_out = n_out; P.n_in = n_in; P.n_tok = T; P.stages = int(S);
+    P.status = device_status_ptr();
+    static int configured[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        if (cudaFuncSetAttribute(mv_mma_q4k_kernel<NCW>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap) != cudaSuccess) {
+            *status = launched();
+            return true;
+        }
+        configured[dev] = 1;
+    }
+    const int tiles = (n_out + kMmaRows - 1) / kMmaRows;
+    const int grid = std::min(tiles, sm_count());
+    mv_mma_q4k_kernel<NCW><<<grid, 32 * (NCW + 1), int(S * slot + other), st>>>(P);
+    *status = launched();
+    return true;
+}
+}  // namespace
+
 extern "C" {
 
 int qmv_abi_version(void) { return NEMICLI_QMV_ABI_VERSION; }
@@ -366,6 +401,12 @@ int qmv_mv(int ggml_type, const uint8_t* w, int n_out, int n_in, const int8_t* x
     for (int c0 = 0; c0 < n_tok; c0 += kMaxTokens) {
         const int T = n_tok - c0 < kMaxTokens ? n_tok - c0 : kMaxTokens;
         const long long off = (long long)c0 * n_in;
+        // 2..8 tokens of Q4_K rows up to kMmaMaxIn values: the tensor-core kernel
+        if (T >= 2 && mma_q4k(w, n_out, n_in, P.row_bytes, xq + off, xq2 + off, xd + off / 32, xs + off / 32, T,
+                              y + (long long)c0 * n_out, ggml_type, static_cast<cudaStream_t>(stream), &st)) {
+            if (st) return st;
+            continue;
+        }
         P.xq = xq + off;
         P.xq2 = xq2 + off;
         P.xd = xd + off / 32;
