@@ -334,6 +334,40 @@ bool mma_q4k(const uint8_t* w, int n_out, int n_in, long long row_bytes, const i
     *status = launched();
     return true;
 }
+
+// Few-token Q6_K matvec on the tensor cores (rows of a multiple of 2048 values).
+bool mma_q6k(const uint8_t* w, int n_out, int n_in, long long row_bytes, const int8_t* xq, const int8_t* xq2,
+             const float* xd, int T, float* y, int fmt, cudaStream_t st, int* status) {
+    if (fmt != F_Q6_K || T < 2 || T > kMmaMaxTok || n_in % kQ6Chunk || !knobs().enabled) return false;
+    if (!aligned(w, 16) || !aligned(xq, 16) || !aligned(xq2, 16) || row_bytes % 16) return false;
+    constexpr int NCW = 16;
+    const int n_rb = (n_out + kMmaRows - 1) / kMmaRows;
+    const int grid = std::min(n_rb, sm_count());
+    if ((n_rb + grid - 1) / grid > kQ6MaxBlocks) return false;
+    if (!aligned(xd, 16)) return false;
+    const long long other = 2LL * kQ6ActBytes + mma_red_bytes(NCW) + 4LL * kQ6MaxBlocks * kMmaRows * kMmaMaxTok + 2 * 8 * 32;
+    const long long slot = (long long)kMmaRows * kQ6ChunkBytes;
+    long long S = (kSmemCap - other) / slot;
+    if (S > 6) S = 6;
+    if (S < 2) return false;
+    MmaParams P{};
+    P.w = w; P.y = y; P.xq = xq; P.xq2 = xq2; P.xd = xd; P.xs = nullptr;
+    P.row_bytes = row_bytes; P.n_out = n_out; P.n_in = n_in; P.n_tok = T; P.stages = int(S);
+    P.status = device_status_ptr();
+    static int configured[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        if (cudaFuncSetAttribute(mv_mma_q6k_kernel<NCW>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap) != cudaSuccess) {
+            *status = launched();
+            return true;
+        }
+        configured[dev] = 1;
+    }
+    mv_mma_q6k_kernel<NCW><<<grid, 32 * (NCW + 1), int(S * slot + other), st>>>(P);
+    *status = launched();
+    return true;
+}
 }  // namespace
 
 extern "C" {
@@ -402,8 +436,10 @@ int qmv_mv(int ggml_type, const uint8_t* w, int n_out, int n_in, const int8_t* x
         const int T = n_tok - c0 < kMaxTokens ? n_tok - c0 : kMaxTokens;
         const long long off = (long long)c0 * n_in;
         // 2..8 tokens of Q4_K rows up to kMmaMaxIn values: the tensor-core kernel
-        if (T >= 2 && mma_q4k(w, n_out, n_in, P.row_bytes, xq + off, xq2 + off, xd + off / 32, xs + off / 32, T,
-                              y + (long long)c0 * n_out, ggml_type, static_cast<cudaStream_t>(stream), &st)) {
+        if (T >= 2 && (mma_q4k(w, n_out, n_in, P.row_bytes, xq + off, xq2 + off, xd + off / 32, xs + off / 32, T,
+                               y + (long long)c0 * n_out, ggml_type, static_cast<cudaStream_t>(stream), &st) ||
+                       mma_q6k(w, n_out, n_in, P.row_bytes, xq + off, xq2 + off, xd + off / 32, T,
+                               y + (long long)c0 * n_out, ggml_type, static_cast<cudaStream_t>(stream), &st))) {
             if (st) return st;
             continue;
         }

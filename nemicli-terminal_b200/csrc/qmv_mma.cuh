@@ -207,3 +207,199 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) mv_mma_q4k_kernel(const Mma
 }
 
 }  // namespace qmv
+
+namespace qmv {
+
+// ---- few-token Q6_K (rows of any multiple of 2048 values) -----------------------------------------
+// Tiles are 16 rows x one 2048-value chunk of K (16 copies of 1680 bytes: eight superblocks per row;
+// 1680 = 16 mod 128, so the eight rows of a fragment fall on distinct banks).  A CTA walks its row
+// blocks chunk by chunk, K-chunk major, keeping each row block's running sums per (row, token) in
+// shared memory (added in chunk order: deterministic).  The activation chunk of every token (xq, xq2
+// 2048 bytes each, xd 64 floats) is brought into one of two shared buffers by the producer's bulk
+// copies ahead of the chunk's weight tiles (own mbarriers), token rows padded by 16 bytes for
+// conflict-free B fragments.  Per 16-value group (one Q6_K scale): A = code - 32 as signed bytes,
+// mma.sync.m16n8k16 with xq and with xq2, y[r][t] += d_r sc_rg * (xd_tg / 254) * (254 S + S2).
+
+constexpr int kQ6Chunk = 2048;                     // values per K-chunk
+constexpr int kQ6ChunkBytes = kQ6Chunk / 256 * 210;  // 1680
+constexpr int kQ6MaxBlocks = 64;                   // row blocks per CTA whose sums fit in shared memory
+constexpr int kQ6ActStride = kQ6Chunk + 16;        // bytes per token row of a staged activation chunk
+// one staged chunk: xq [8][stride], xq2 [8][stride], xd [8][64 + 4] floats
+constexpr int kQ6ActBytes = 2 * kMmaMaxTok * kQ6ActStride + kMmaMaxTok * (kQ6Chunk / 32 + 4) * 4;
+
+__device__ __forceinline__ void mma_s8s8_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5}, {%6}, {%0, %1, %2, %3};"
+                 : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(b0));
+}
+// four unsigned 6-bit codes -> code - 32 as signed bytes (no carries between bytes)
+__device__ __forceinline__ uint32_t q6_signed(uint32_t c) {
+    return ((c | 0x80808080u) - 0x20202020u) ^ 0x80808080u;
+}
+// 4 bytes at a 2-byte aligned shared address
+__device__ __forceinline__ uint32_t lds32_a2(uint32_t a) {
+    const uint32_t b = a & ~3u, sh = (a & 3u) * 8u;
+    return __funnelshift_r(lds32(b), lds32(b + 4), sh);
+}
+
+template <int NCW>
+__global__ void __launch_bounds__(32 * (NCW + 1), 1) mv_mma_q6k_kernel(const MmaParams P) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int S = P.stages;
+    const uint32_t slot_bytes = kMmaRows * kQ6ChunkBytes;
+    uint8_t* actb = smem + (long long)S * slot_bytes;                // two staged activation chunks
+    float* red = reinterpret_cast<float*>(actb + 2 * kQ6ActBytes);
+    float* run = red + NCW * kMmaRows * kMmaMaxTok;                 // [local block][row][token]
+    const int n_rb = (P.n_out + kMmaRows - 1) / kMmaRows, n_kc = P.n_in / kQ6Chunk;
+    const int my_rb = (n_rb - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(run + kQ6MaxBlocks * kMmaRows * kMmaMaxTok);
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S), stage0 = smem_u32(smem);
+    const uint32_t afull0 = smem_u32(bars + 2 * S), aempty0 = smem_u32(bars + 2 * S + 2);
+    const int ng = P.n_in / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, NCW);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(afull0 + 8 * b, 1);
+            mbar_init(aempty0 + 8 * b, NCW);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == NCW) {
+        // ---------------- producer: per chunk kc its activation, then tiles (kc, rb), rb = blockIdx.x + grid i ----
+        if (lane != 0) return;
+        int it = 0;
+        bool ok = true;
+        for (int kc = 0; kc < n_kc && ok; ++kc) {
+            const int ab = kc & 1;
+            if (kc >= 2 && !mbar_wait(aempty0 + 8 * ab, ((kc / 2) & 1) ^ 1)) {
+                ok = false;
+                break;
+            }
+            const uint32_t abuf = smem_u32(actb + ab * kQ6ActBytes);
+            mbar_arrive_tx(afull0 + 8 * ab, uint32_t(P.n_tok * (2 * kQ6Chunk + 4 * (kQ6Chunk / 32))));
+            for (int t = 0; t < P.n_tok; ++t) {
+                const long long o = (long long)t * P.n_in + (long long)kc * kQ6Chunk;
+                bulk_g2s(abuf + t * kQ6ActStride, P.xq + o, kQ6Chunk, afull0 + 8 * ab);
+                bulk_g2s(abuf + (kMmaMaxTok + t) * kQ6ActStride, P.xq2 + o, kQ6Chunk, afull0 + 8 * ab);
+                bulk_g2s(abuf + 2 * kMmaMaxTok * kQ6ActStride + t * (kQ6Chunk / 32 + 4) * 4,
+                         P.xd + (long long)t * ng + kc * (kQ6Chunk / 32), 4 * (kQ6Chunk / 32), afull0 + 8 * ab);
+            }
+            for (int i = 0; i < my_rb; ++i, ++it) {
+                const int s = it % S;
+                if (it >= S && !mbar_wait(empty0 + 8 * s, ((it / S) & 1) ^ 1)) {
+                    ok = false;
+                    break;
+                }
+                const int r0 = (int(blockIdx.x) + int(gridDim.x) * i) * kMmaRows, nr = min(kMmaRows, P.n_out - r0);
+                mbar_arrive_tx(full0 + 8 * s, uint32_t(nr * kQ6ChunkBytes));
+                for (int r = 0; r < nr; ++r)
+                    bulk_g2s(stage0 + uint32_t(s) * slot_bytes + uint32_t(r * kQ6ChunkBytes),
+                             P.w + (long long)(r0 + r) * P.row_bytes + (long long)kc * kQ6ChunkBytes, kQ6ChunkBytes,
+                             full0 + 8 * s);
+            }
+        }
+        if (!ok) {
+            if (P.status) atomicOr(P.status, DEV_TIMEOUT);
+            for (int k = (it > S ? it - S : 0); k < it; ++k) mbar_wait(full0 + 8 * (k % S), (k / S) & 1);
+        }
+        return;
+    }
+
+    // ---------------- consumers ----------------
+    const int cl = threadIdx.x, nthr = 32 * NCW;
+    for (int i = cl; i < my_rb * kMmaRows * kMmaMaxTok; i += nthr) run[i] = 0.f;
+    const int gid = lane >> 2, tig = lane & 3;
+    const int sbw = warp >> 1, nw = warp & 1;           // this warp: superblock sbw of the chunk, half nw
+    const bool tok_ok = gid < P.n_tok;                  // B fragment: token gid (zero beyond n_tok)
+    const int t0 = 2 * tig, t1 = 2 * tig + 1;           // tokens of this thread's C values
+    bool dead = false;
+    int it = 0;
+    for (int kc = 0; kc < n_kc; ++kc) {
+        const int ab = kc & 1;
+        const bool agot = !dead && mbar_wait(afull0 + 8 * ab, (kc / 2) & 1);
+        if (!agot && !dead) {
+            dead = true;
+            if (lane == 0 && P.status) atomicOr(P.status, DEV_TIMEOUT);
+        }
+        const int8_t* axq = reinterpret_cast<const int8_t*>(actb + ab * kQ6ActBytes);
+        const int8_t* axq2 = axq + kMmaMaxTok * kQ6ActStride;
+        const float* axd = reinterpret_cast<const float*>(axq + 2 * kMmaMaxTok * kQ6ActStride);
+        for (int i = 0; i < my_rb; ++i, ++it) {
+            const int s = it % S;
+            const bool got = !dead && mbar_wait(full0 + 8 * s, (it / S) & 1);
+            if (!got && !dead) {
+                dead = true;
+                if (lane == 0 && P.status) atomicOr(P.status, DEV_TIMEOUT);
+            }
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            if (got && sbw < kQ6Chunk / 256) {
+                const uint32_t tile = stage0 + uint32_t(s) * slot_bytes;
+                const uint32_t bg = tile + uint32_t(gid * kQ6ChunkBytes + sbw * 210);
+                const uint32_t bh = tile + uint32_t((gid + 8) * kQ6ChunkBytes + sbw * 210);
+                const float dg = h2f(lds16u(bg + 208)), dh = h2f(lds16u(bh + 208));
+                const int vbase = sbw * 256 + 128 * nw;      // value index of this half within the chunk
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    // positions 16h + 4 tig.. of half nw: ql runs (groups 0/2 and 1/3) and the qh run
+                    const uint32_t lo = 64 * nw + 16 * h + 4 * tig, qo = 128 + 32 * nw + 16 * h + 4 * tig;
+                    const uint32_t Lg0 = lds32_a2(bg + lo), Lg1 = lds32_a2(bg + lo + 32), Hg = lds32_a2(bg + qo);
+                    const uint32_t Lh0 = lds32_a2(bh + lo), Lh1 = lds32_a2(bh + lo + 32), Hh = lds32_a2(bh + qo);
+#pragma unroll
+                    for (int grp = 0; grp < 4; ++grp) {
+                        const uint32_t Lg = (grp & 1) ? Lg1 : Lg0, Lh = (grp & 1) ? Lh1 : Lh0;
+                        const int ls = 4 * (grp >> 1), hs = 2 * grp;
+                        const uint32_t a0 = q6_signed(((Lg >> ls) & 0x0F0F0F0Fu) | (((Hg >> hs) & 0x03030303u) << 4));
+                        const uint32_t a1 = q6_signed(((Lh >> ls) & 0x0F0F0F0Fu) | (((Hh >> hs) & 0x03030303u) << 4));
+                        const int k0 = vbase + 32 * grp + 16 * h + 4 * tig;        // B: token gid, k0..k0+3
+                        const uint32_t b = tok_ok ? *reinterpret_cast<const uint32_t*>(axq + gid * kQ6ActStride + k0) : 0u;
+                        const uint32_t c = tok_ok ? *reinterpret_cast<const uint32_t*>(axq2 + gid * kQ6ActStride + k0) : 0u;
+                        int s1[4] = {0, 0, 0, 0}, s2[4] = {0, 0, 0, 0};
+                        mma_s8s8_k16(s1, a0, a1, b);
+                        mma_s8s8_k16(s2, a0, a1, c);
+                        // scale of this 16-value group (scale index 8 nw + 2 grp + h) and the tokens' xd
+                        const int si = 192 + 8 * nw + 2 * grp + h;
+                        const float wg = dg * float(int8_t(lds8u(bg + si))), wh = dh * float(int8_t(lds8u(bh + si)));
+                        const int blk = (vbase + 32 * grp) / 32;
+                        const float x0 = t0 < P.n_tok ? axd[t0 * (kQ6Chunk / 32 + 4) + blk] * kInv254 : 0.f;
+                        const float x1 = t1 < P.n_tok ? axd[t1 * (kQ6Chunk / 32 + 4) + blk] * kInv254 : 0.f;
+                        acc[0] += wg * x0 * float(254 * s1[0] + s2[0]);
+                        acc[1] += wg * x1 * float(254 * s1[1] + s2[1]);
+                        acc[2] += wh * x0 * float(254 * s1[2] + s2[2]);
+                        acc[3] += wh * x1 * float(254 * s1[3] + s2[3]);
+                    }
+                }
+            }
+            __syncwarp();
+            if (got && lane == 0) mbar_arrive(empty0 + 8 * s);
+            float* rw = red + warp * kMmaRows * kMmaMaxTok;
+            rw[gid * kMmaMaxTok + t0] = acc[0];
+            rw[gid * kMmaMaxTok + t1] = acc[1];
+            rw[(gid + 8) * kMmaMaxTok + t0] = acc[2];
+            rw[(gid + 8) * kMmaMaxTok + t1] = acc[3];
+            named_sync(kConsumerBarrier, nthr);
+            if (cl < kMmaRows * kMmaMaxTok) {
+                float v = 0.f;
+                for (int w = 0; w < NCW; ++w) v += red[w * kMmaRows * kMmaMaxTok + cl];   // fixed order
+                run[i * kMmaRows * kMmaMaxTok + cl] += v;
+            }
+            named_sync(kConsumerBarrier, nthr);
+        }
+        if (agot && lane == 0) mbar_arrive(aempty0 + 8 * ab);     // this warp is done with the chunk
+    }
+    for (int i = 0; i < my_rb; ++i) {
+        const int r0 = (int(blockIdx.x) + int(gridDim.x) * i) * kMmaRows;
+        if (cl < kMmaRows * kMmaMaxTok && !dead) {
+            const int r = cl / kMmaMaxTok, tk = cl % kMmaMaxTok;
+            if (tk < P.n_tok && r0 + r < P.n_out) P.y[(long long)tk * P.n_out + r0 + r] = run[i * kMmaRows * kMmaMaxTok + cl];
+        }
+    }
+}
+
+}  // namespace qmv

@@ -32,7 +32,7 @@ def _shapes(fmt):
     bv = FORMATS[fmt][0]
     if bv == 32:
         return [(256, 512), (1024, 4096), (300, 1280), (7, 96), (33, 32)]
-    return [(256, 512), (1024, 4096), (300, 1280), (5, 256)]
+    return [(256, 512), (1024, 4096), (300, 1280), (5, 256), (300, 2048)]
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
