@@ -119,6 +119,7 @@ int launch(int fmt, const MvParams& P, int T, cudaStream_t st) {
     case F_Q4_0: return launch_fmt<F_Q4_0>(P, T, st);
     case F_Q8_0: return launch_fmt<F_Q8_0>(P, T, st);
     case F_Q4_K: return launch_fmt<F_Q4_K>(P, T, st);
+    case F_Q5_K: return launch_fmt<F_Q5_K>(P, T, st);
     case F_Q6_K: return launch_fmt<F_Q6_K>(P, T, st);
     case F_IQ2_XXS: return launch_fmt<F_IQ2_XXS>(P, T, st);
     case F_TQ2_0: return launch_fmt<F_TQ2_0>(P, T, st);
@@ -132,6 +133,7 @@ int launch_sums(int fmt, const MvParams& P, cudaStream_t st) {
     case F_Q4_0: return launch_t<F_Q4_0, 1, true>(P, st);
     case F_Q8_0: return launch_t<F_Q8_0, 1, true>(P, st);
     case F_Q4_K: return launch_t<F_Q4_K, 1, true>(P, st);
+    case F_Q5_K: return launch_t<F_Q5_K, 1, true>(P, st);
     case F_Q6_K: return launch_t<F_Q6_K, 1, true>(P, st);
     case F_IQ2_XXS: return launch_t<F_IQ2_XXS, 1, true>(P, st);
     case F_TQ2_0: return launch_t<F_TQ2_0, 1, true>(P, st);
@@ -150,7 +152,7 @@ struct TmaPlan {
     int NCW, G, UPL, R, S, smem;
 };
 
-__host__ __device__ constexpr int unit_vals(int fmt) { return fmt == F_Q4_K || fmt == F_Q6_K ? 64 : 32; }   // UnitTraits::VPU
+__host__ __device__ constexpr int unit_vals(int fmt) { return fmt == F_Q4_K || fmt == F_Q5_K || fmt == F_Q6_K ? 64 : 32; }   // UnitTraits::VPU
 
 // Tuning knobs read once from the environment (benchmark sweeps): NEMICLI_QMV_TMA=0 sends every call
 // to the fallback kernel, NEMICLI_QMV_TMA_G forces the team width (16..512) where it fits.
@@ -258,6 +260,7 @@ int launch_tma(int fmt, TmaParams& P, const TmaPlan& pl, cudaStream_t st) {
     case F_Q4_0: return launch_tma_fmt<F_Q4_0, XF, SUMS>(P, pl, int(grid), st);
     case F_Q8_0: return launch_tma_fmt<F_Q8_0, XF, SUMS>(P, pl, int(grid), st);
     case F_Q4_K: return launch_tma_fmt<F_Q4_K, XF, SUMS>(P, pl, int(grid), st);
+    case F_Q5_K: return launch_tma_fmt<F_Q5_K, XF, SUMS>(P, pl, int(grid), st);
     case F_Q6_K: return launch_tma_fmt<F_Q6_K, XF, SUMS>(P, pl, int(grid), st);
     case F_IQ2_XXS: return launch_tma_fmt<F_IQ2_XXS, XF, SUMS>(P, pl, int(grid), st);
     case F_TQ2_0: return launch_tma_fmt<F_TQ2_0, XF, SUMS>(P, pl, int(grid), st);
@@ -413,7 +416,7 @@ int qmv_mv(int ggml_type, const uint8_t* w, int n_out, int n_in, const int8_t* x
     int st = check_mv(ggml_type, w, n_out, n_in, xq, xq2, xd, xs, y);
     if (st) return st;
     if (n_tok <= 0) return ST_BAD_TOKENS;
-    if (!aligned(w, ggml_type == F_Q4_K ? 16 : 2)) return ST_BAD_ALIGN;
+    if (!aligned(w, weight_align(ggml_type))) return ST_BAD_ALIGN;
     MvParams P{};
     P.w = w;
     P.ids = nullptr;
@@ -465,7 +468,7 @@ int qmv_mv_experts(int ggml_type, const void* raw, long long per_expert, long lo
     const long long row_bytes = (long long)(n_in / block_values(ggml_type)) * block_bytes(ggml_type);
     if (per_expert >= 0) {
         if (per_expert < row_bytes * n_out) return ST_BAD_SHAPE;
-        if (!aligned(raw, ggml_type == F_Q4_K ? 16 : 2) || per_expert % (ggml_type == F_Q4_K ? 16 : 2))
+        if (!aligned(raw, weight_align(ggml_type)) || per_expert % (weight_align(ggml_type)))
             return ST_BAD_ALIGN;
     } else if (!aligned(raw, 8)) {
         return ST_BAD_ALIGN;
@@ -512,7 +515,7 @@ int qmv_block_sums(int ggml_type, const uint8_t* w, int n_out, int n_in, const i
     if (!w || !xq || !xq2 || !s || !s2) return ST_NULL;
     if (n_out <= 0 || n_in <= 0 || n_in % block_values(ggml_type)) return ST_BAD_SHAPE;
     if (!aligned(xq, 16) || !aligned(xq2, 16) || !aligned(s, 4) || !aligned(s2, 4)) return ST_BAD_ALIGN;
-    if (!aligned(w, ggml_type == F_Q4_K ? 16 : 2)) return ST_BAD_ALIGN;
+    if (!aligned(w, weight_align(ggml_type))) return ST_BAD_ALIGN;
     const long long units = (long long)n_out * (n_in / unit_values(ggml_type));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (cudaMemsetAsync(s, 0, units * sizeof(int32_t), st) != cudaSuccess ||
@@ -549,7 +552,7 @@ int qmv_mv_multi(int ggml_type, int n_jobs, const uint8_t* const* w, const int* 
     for (int j = 0; j < n_jobs; ++j) {
         const int st = check_mv(ggml_type, w[j], n_out[j], n_in, xq, xq2, xd, xs, y[j]);
         if (st) return st;
-        if (!aligned(w[j], ggml_type == F_Q4_K ? 16 : 2)) return ST_BAD_ALIGN;
+        if (!aligned(w[j], weight_align(ggml_type))) return ST_BAD_ALIGN;
     }
     int st = ST_OK;
     if (tma_dense(ggml_type, n_jobs, w, n_out, y, n_in, xq, xq2, xd, xs, nullptr, 0, nullptr, nullptr,
@@ -570,7 +573,7 @@ int qmv_mv_x(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_ou
     for (int j = 0; j < n_jobs; ++j) {
         if (!w[j] || !y[j]) return ST_NULL;
         if (n_out[j] <= 0) return ST_BAD_SHAPE;
-        if (!aligned(w[j], ggml_type == F_Q4_K ? 16 : 2) || !aligned(y[j], 4)) return ST_BAD_ALIGN;
+        if (!aligned(w[j], weight_align(ggml_type)) || !aligned(y[j], 4)) return ST_BAD_ALIGN;
     }
     int st = ST_OK;
     if (tma_dense(ggml_type, n_jobs, w, n_out, y, n_in, nullptr, nullptr, nullptr, nullptr, x, x_is_f32 ? 1 : 2,

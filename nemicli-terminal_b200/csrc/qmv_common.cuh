@@ -6,8 +6,8 @@
 
 namespace qmv {
 
-// GGML type ids of the six formats (the GGUF type table; reference ggufengine/gguf.py:64-77)
-enum : int { F_Q4_0 = 2, F_Q8_0 = 8, F_Q4_K = 12, F_Q6_K = 14, F_IQ2_XXS = 16, F_TQ2_0 = 35 };
+// GGML type ids of the seven formats (the GGUF type table; reference ggufengine/gguf.py:64-77)
+enum : int { F_Q4_0 = 2, F_Q8_0 = 8, F_Q4_K = 12, F_Q5_K = 13, F_Q6_K = 14, F_IQ2_XXS = 16, F_TQ2_0 = 35 };
 
 // status codes returned across the C ABI (include/nemicli_qmv.h)
 enum : int {
@@ -33,13 +33,16 @@ __host__ __device__ constexpr int block_values(int f) {
     return (f == F_Q4_0 || f == F_Q8_0) ? 32 : 256;
 }
 __host__ __device__ constexpr int block_bytes(int f) {
-    return f == F_Q4_0 ? 18 : f == F_Q8_0 ? 34 : f == F_Q4_K ? 144 : f == F_Q6_K ? 210 : 66;
+    return f == F_Q4_0 ? 18 : f == F_Q8_0 ? 34 : f == F_Q4_K ? 144 : f == F_Q5_K ? 176 : f == F_Q6_K ? 210 : 66;
 }
 // values per integer-sum unit (one weight scale and one activation scale)
 __host__ __device__ constexpr int unit_values(int f) { return f == F_Q6_K ? 16 : 32; }
 
 __host__ __device__ inline bool known_format(int f) {
-    return f == F_Q4_0 || f == F_Q8_0 || f == F_Q4_K || f == F_Q6_K || f == F_IQ2_XXS || f == F_TQ2_0;
+    return f == F_Q4_0 || f == F_Q8_0 || f == F_Q4_K || f == F_Q5_K || f == F_Q6_K || f == F_IQ2_XXS || f == F_TQ2_0;
+}
+// weight rows and blocks of the K-quant formats with 16-byte header words are read 16 bytes at a time
+__host__ __device__ constexpr int weight_align(int f) { return f == F_Q4_K || f == F_Q5_K ? 16 : 2;
 }
 
 // ---- loads --------------------------------------------------------------------------------------

@@ -82,7 +82,9 @@ struct Tok {
 // ---- Q4_K: 144 B = d, dmin (f16), 12 B of 6-bit scales/mins, 128 B nibbles (quant.py:111-120).
 // Lane q takes qs bytes 16q..16q+15: the low nibbles are values 16h..16h+15 of sub-block 2p, the
 // high nibbles the same values of sub-block 2p+1 (p = q/2, h = q%2).
-template <int T, int RW, bool SUMS>
+// Q5_K (Q5 = true): 176 B = the same header, qh[32] at 16, qs[128] at 48 (quant.py:123-137); bit 2p
+// (low nibbles) or 2p+1 (high nibbles) of qh[16h + i] is bit 4 of the code, unsigned 0..31.
+template <int T, int RW, bool SUMS, bool Q5 = false>
 __device__ __forceinline__ void lane_q4k(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
                                          const Tok<T>& tk, float (&acc)[RW][T], int row0) {
     const int p = q >> 1, h = q & 1;
@@ -90,13 +92,22 @@ __device__ __forceinline__ void lane_q4k(const uint8_t* const (&rows)[RW], int s
     float d[RW], dm[RW], sc0[RW], sc1[RW], m0[RW], m1[RW];
 #pragma unroll
     for (int r = 0; r < RW; ++r) {
-        const uint8_t* b = rows[r] + (long long)sb * 144;
+        const uint8_t* b = rows[r] + (long long)sb * (Q5 ? 176 : 144);
         const uint4 hd = ldw16(b);
-        const uint4 v = ldw16(b + 16 + 16 * q);
+        const uint4 v = ldw16(b + (Q5 ? 48 : 16) + 16 * q);
         lo[r][0] = v.x & 0x0F0F0F0Fu; hi[r][0] = (v.x >> 4) & 0x0F0F0F0Fu;
         lo[r][1] = v.y & 0x0F0F0F0Fu; hi[r][1] = (v.y >> 4) & 0x0F0F0F0Fu;
         lo[r][2] = v.z & 0x0F0F0F0Fu; hi[r][2] = (v.z >> 4) & 0x0F0F0F0Fu;
         lo[r][3] = v.w & 0x0F0F0F0Fu; hi[r][3] = (v.w >> 4) & 0x0F0F0F0Fu;
+        if constexpr (Q5) {
+            const uint4 qh = ldw16(b + 16 + 16 * h);
+            const uint32_t H[4] = {qh.x, qh.y, qh.z, qh.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                lo[r][i] |= ((H[i] >> (2 * p)) & 0x01010101u) << 4;
+                hi[r][i] |= ((H[i] >> (2 * p + 1)) & 0x01010101u) << 4;
+            }
+        }
         d[r] = h2f(hd.x & 0xFFFFu);
         dm[r] = h2f(hd.x >> 16);
         // 6-bit scales and mins of sub-blocks 0..3 (p < 2) or 4..7, four per word
@@ -405,7 +416,7 @@ __device__ __forceinline__ const uint8_t* slot_base(const MvParams& P, int slot)
     }
     const uint8_t* base = P.per_expert >= 0 ? P.w + e * P.per_expert
                                             : reinterpret_cast<const uint8_t*>(reinterpret_cast<const long long*>(P.w)[e]);
-    const uintptr_t need = FMT == F_Q4_K ? 15u : 1u;
+    const uintptr_t need = uintptr_t(weight_align(FMT) - 1);
     if (reinterpret_cast<uintptr_t>(base) & need) {
         if (P.status) atomicOr(P.status, DEV_BAD_ADDRESS);
         return nullptr;
@@ -452,6 +463,7 @@ __global__ void __launch_bounds__(256) mv_kernel(const MvParams P) {
             for (int t = 0; t < T; ++t) acc[r][t] = 0.f;
         for (int sb = sb0; sb < n_sb; sb += 4) {
             if constexpr (FMT == F_Q4_K) lane_q4k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+            else if constexpr (FMT == F_Q5_K) lane_q4k<T, RW, SUMS, true>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (FMT == F_Q6_K) lane_q6k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (FMT == F_Q4_0) lane_q4_0<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (FMT == F_Q8_0) lane_q8_0<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);

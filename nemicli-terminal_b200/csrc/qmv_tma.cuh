@@ -163,6 +163,7 @@ __device__ __forceinline__ int dot4us(const uint32_t (&w)[4], const int4& x) {
 
 template <int FMT> struct UnitTraits { static constexpr int VPU = 32, NS = 1, NQ = 2; };
 template <> struct UnitTraits<F_Q4_K> { static constexpr int VPU = 64, NS = 2, NQ = 4; };
+template <> struct UnitTraits<F_Q5_K> { static constexpr int VPU = 64, NS = 2, NQ = 4; };
 template <> struct UnitTraits<F_Q6_K> { static constexpr int VPU = 64, NS = 4, NQ = 4; };
 // Q6_K with 32-value units (ql bytes 64n+16j..+15 of superblock b: 16 values of group j/2 and of j/2 + 2):
 // a smaller activation footprint, for the decode chain's register budget.  Internal tag only.
@@ -218,7 +219,7 @@ __device__ __forceinline__ void load_act(Act<FMT>& a, int u, const int8_t* xq, c
         a.r[0] = ldq16<GLOBAL>(xq2 + o); a.r[1] = ldq16<GLOBAL>(xq2 + o + 16);
         a.d[0] = ldf<GLOBAL, SCALES>(xd, u) * kInv254;
         if (FMT == F_Q4_0) a.s[0] = ldf<GLOBAL, SCALES>(xs, u);
-    } else if constexpr (FMT == F_Q4_K) {
+    } else if constexpr (FMT == F_Q4_K || FMT == F_Q5_K) {
         const int b = u >> 2, p = u & 3, o = b * 256 + 64 * p;
         a.q[0] = ldq16<GLOBAL>(xq + o); a.q[1] = ldq16<GLOBAL>(xq + o + 16);
         a.q[2] = ldq16<GLOBAL>(xq + o + 32); a.q[3] = ldq16<GLOBAL>(xq + o + 48);
@@ -282,6 +283,22 @@ struct UnitSums<F_Q4_K> {
     uint32_t imn[2];
     float d, dm;
 };
+template <>
+struct UnitSums<F_Q5_K> : UnitSums<F_Q4_K> {};
+
+// 6-bit scales / mins of sub-blocks 2p, 2p + 1 from a K-quant header word hd (quant.py:99-108), four per
+// word; no branch on p
+__device__ __forceinline__ void kquant_scales(const uint4& hd, int p, int (&isc)[2], uint32_t (&imn)[2]) {
+    const uint32_t sc_lo = hd.y & 0x3F3F3F3Fu, m_lo = hd.z & 0x3F3F3F3Fu;
+    const uint32_t sc_hi = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
+    const uint32_t m_hi = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
+    const uint32_t scw = p < 2 ? sc_lo : sc_hi, mw = p < 2 ? m_lo : m_hi;
+    const int sh = 16 * (p & 1);
+    isc[0] = int((scw >> sh) & 0xFFu);
+    isc[1] = int((scw >> (sh + 8)) & 0xFFu);
+    imn[0] = (mw >> sh) & 0xFFu;
+    imn[1] = (mw >> (sh + 8)) & 0xFFu;
+}
 
 // unsigned 6-bit codes of a Q6_K unit (w[g][i]: 4 codes of group g, positions 16h + 4i..): group g's low
 // four bits from ql (low nibbles for g = 0, 1, high for g = 2, 3), bits 4..5 from qh bits 2g..2g+1; the
@@ -314,16 +331,32 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
         o.u[0] = dot4(l1, a.r[1]) + dot4(l0, a.r[0]);
         o.s[1] = (dot4us(h1, a.q[3]) + dot4us(h0, a.q[2])) >> 4;
         o.u[1] = (dot4us(h1, a.r[3]) + dot4us(h0, a.r[2])) >> 4;
-        // 6-bit scales / mins of sub-blocks 0..3 and 4..7 (quant.py:99-108), four per word; no branch on p
-        const uint32_t sc_lo = hd.y & 0x3F3F3F3Fu, m_lo = hd.z & 0x3F3F3F3Fu;
-        const uint32_t sc_hi = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
-        const uint32_t m_hi = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
-        const uint32_t scw = p < 2 ? sc_lo : sc_hi, mw = p < 2 ? m_lo : m_hi;
-        const int sh = 16 * (p & 1);
-        o.isc[0] = int((scw >> sh) & 0xFFu);
-        o.isc[1] = int((scw >> (sh + 8)) & 0xFFu);
-        o.imn[0] = (mw >> sh) & 0xFFu;
-        o.imn[1] = (mw >> (sh + 8)) & 0xFFu;
+        kquant_scales(hd, p, o.isc, o.imn);
+        o.d = h2f(hd.x & 0xFFFFu);
+        o.dm = h2f(hd.x >> 16);
+    } else if constexpr (FMT == F_Q5_K) {
+        // Q5_K (quant.py:123-137): the Q4_K header, qh[32] at 16, qs[128] at 48; the unsigned 5-bit code
+        // of value i of sub-block 2p (2p+1) is the low (high) nibble of qs[32p + i] with bit 2p (2p+1)
+        // of qh[i] as bit 4
+        const int b = u >> 2, p = u & 3;
+        const uint32_t sb = rs + b * 176;
+        const uint4 hd = lds128(sb), q0 = lds128(sb + 16), q1 = lds128(sb + 32);
+        const uint4 v0 = lds128(sb + 48 + 32 * p), v1 = lds128(sb + 64 + 32 * p);
+        const uint32_t H0[4] = {q0.x, q0.y, q0.z, q0.w}, H1[4] = {q1.x, q1.y, q1.z, q1.w};
+        const uint32_t V0[4] = {v0.x, v0.y, v0.z, v0.w}, V1[4] = {v1.x, v1.y, v1.z, v1.w};
+        uint32_t l0[4], l1[4], g0[4], g1[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            l0[i] = (V0[i] & 0x0F0F0F0Fu) | (((H0[i] >> (2 * p)) & 0x01010101u) << 4);
+            l1[i] = (V1[i] & 0x0F0F0F0Fu) | (((H1[i] >> (2 * p)) & 0x01010101u) << 4);
+            g0[i] = ((V0[i] >> 4) & 0x0F0F0F0Fu) | (((H0[i] >> (2 * p + 1)) & 0x01010101u) << 4);
+            g1[i] = ((V1[i] >> 4) & 0x0F0F0F0Fu) | (((H1[i] >> (2 * p + 1)) & 0x01010101u) << 4);
+        }
+        o.s[0] = dot4(l1, a.q[1]) + dot4(l0, a.q[0]);
+        o.u[0] = dot4(l1, a.r[1]) + dot4(l0, a.r[0]);
+        o.s[1] = dot4(g1, a.q[3]) + dot4(g0, a.q[2]);
+        o.u[1] = dot4(g1, a.r[3]) + dot4(g0, a.r[2]);
+        kquant_scales(hd, p, o.isc, o.imn);
         o.d = h2f(hd.x & 0xFFFFu);
         o.dm = h2f(hd.x >> 16);
     } else if constexpr (FMT == F_Q6_K_U32) {
@@ -421,7 +454,7 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
 template <int FMT>
 __device__ __forceinline__ int sum_unit(int u, int k) {
     if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0 || FMT == F_IQ2_XXS) return u;
-    if constexpr (FMT == F_Q4_K) return 2 * u + k;          // unit u = sub-blocks 2u, 2u + 1 of the row
+    if constexpr (FMT == F_Q4_K || FMT == F_Q5_K) return 2 * u + k;   // unit u = sub-blocks 2u, 2u + 1 of the row
     const int b = u >> 3, q = u & 7;
     if constexpr (FMT == F_Q6_K) {
         const int b6 = u >> 2, n = (u >> 1) & 1, h = u & 1;     // group k: values 128n + 32k + 16h.. of b6
@@ -452,7 +485,7 @@ __device__ __forceinline__ float unit_dot(uint32_t rs, int u, const Act<FMT>& a,
             acc = fmaf(wsc * a.d[g], float(254 * s_ + t_ - a.kk[g]), acc);
         }
         return acc;
-    } else if constexpr (FMT == F_Q4_K) {
+    } else if constexpr (FMT == F_Q4_K || FMT == F_Q5_K) {
         // d * sum_k sc_k * (254 S_k + S2_k) * xd_k / 254  -  dmin * sum_k m_k * xs_k
         const float w = float(o.isc[0] * (254 * o.s[0] + o.u[0])) * a.d[0]
                       + float(o.isc[1] * (254 * o.s[1] + o.u[1])) * a.d[1];

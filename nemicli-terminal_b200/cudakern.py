@@ -1,4 +1,4 @@
-"""Drop-in for the reference's per-format block kernels (ggufengine/cudakern.py) for the six block
+"""Drop-in for the reference's per-format block kernels (ggufengine/cudakern.py) for the seven block
 formats of this path: the expert gather `mv` driven by device-side ids (cudakern.py:756-774) and the
 few-row `mm` (cudakern.py:777-790).
 

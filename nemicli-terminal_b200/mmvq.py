@@ -8,8 +8,8 @@ meaning and return shapes, computed by this package's sm_100a kernels through th
 * `mm` — the reference's 17..112-token entry (mmvq.py:902-918); here the same int8 kernels in groups
   of SPALTEN tokens (the tensor-core tile path for long inputs is a separate, later kernel).
 
-Where the reference takes Q4_K and Q6_K only, these kernels take all six block formats of the path
-(Q4_0, Q8_0, Q4_K, Q6_K, TQ2_0, IQ2_XXS).  Everything runs on torch's current stream and is CUDA-graph
+Where the reference takes Q4_K and Q6_K only, these kernels take all seven block formats of the path
+(Q4_0, Q8_0, Q4_K, Q5_K, Q6_K, TQ2_0, IQ2_XXS).  Everything runs on torch's current stream and is CUDA-graph
 safe (no host reads, no synchronisation).  Non-CUDA tensors or unsupported formats raise; nothing
 falls back to another implementation.
 """

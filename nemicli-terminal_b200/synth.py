@@ -2,7 +2,7 @@
 
 The reference names no dataset or public benchmark for this path; its configs are synthetic.  The
 generators below follow each config's stated distributions and write the exact GGUF block layouts
-(ggufengine/quant.py documents them: Q4_0 :60, Q8_0 :46, Q4_K :111, Q6_K :140, TQ2_0 :417,
+(ggufengine/quant.py documents them: Q4_0 :60, Q8_0 :46, Q4_K :111, Q5_K :123, Q6_K :140, TQ2_0 :417,
 IQ2_XXS :235).  Everything is torch, so it runs on the CPU (tests) or on the GPU (bench, where the
 largest stacks are several GB).
 """
@@ -66,6 +66,12 @@ def blocks(fmt: str, n_rows: int, n_in: int, seed: int = 0, device="cpu",
         sc = torch.randint(0, 64, (nb, 8), generator=g, device=device, dtype=torch.int32)
         mn = torch.randint(0, 64, (nb, 8), generator=g, device=device, dtype=torch.int32)
         out = torch.cat([d, dmin, pack_scale_min_k4(sc, mn), _bytes(nb, 128, g, device)], 1)
+    elif fmt == "Q5_K":                     # as Q4_K, plus the fifth bits qh[32] uniform
+        d = _f16_bytes(_abs_normal(nb, 0.005, g, device))
+        dmin = _f16_bytes(_abs_normal(nb, 0.005, g, device))
+        sc = torch.randint(0, 64, (nb, 8), generator=g, device=device, dtype=torch.int32)
+        mn = torch.randint(0, 64, (nb, 8), generator=g, device=device, dtype=torch.int32)
+        out = torch.cat([d, dmin, pack_scale_min_k4(sc, mn), _bytes(nb, 160, g, device)], 1)
     elif fmt == "Q6_K":                     # ql/qh uniform; int8 scales uniform -32..31; d = |N| * 0.005
         ql = _bytes(nb, 192, g, device)
         sc = torch.randint(-32, 32, (nb, 16), generator=g, device=device, dtype=torch.int16).to(torch.int8)

@@ -22,9 +22,9 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libqmv_oracle.so")
 
-# GGML type ids (ggufengine/gguf.py:64-77) of the six in-scope formats
-TYPES = {"Q4_0": 2, "Q8_0": 8, "Q4_K": 12, "Q6_K": 14, "IQ2_XXS": 16, "TQ2_0": 35}
-BLOCK = {"Q4_0": (32, 18), "Q8_0": (32, 34), "Q4_K": (256, 144), "Q6_K": (256, 210),
+# GGML type ids (ggufengine/gguf.py:64-77) of the seven in-scope formats
+TYPES = {"Q4_0": 2, "Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "IQ2_XXS": 16, "TQ2_0": 35}
+BLOCK = {"Q4_0": (32, 18), "Q8_0": (32, 34), "Q4_K": (256, 144), "Q5_K": (256, 176), "Q6_K": (256, 210),
          "IQ2_XXS": (256, 66), "TQ2_0": (256, 66)}
 
 _lock = threading.Lock()

@@ -11,19 +11,20 @@
  *     restatement uses IEEE-rounded division and an explicit fused multiply-add so that it is
  *     reproducible bit for bit on the GPU (the kernels do the same).  Against the reference's
  *     fast-math build a quantised value can differ by one unit on a rounding tie.
- *   - the block dequantisers of ggufengine/quant.py for the six in-scope formats:
- *     deq_q4_0 :60, deq_q8_0 :46, deq_q4_k :111 (+ _scale_min_k4 :99), deq_q6_k :140,
+ *   - the block dequantisers of ggufengine/quant.py for the seven in-scope formats:
+ *     deq_q4_0 :60, deq_q8_0 :46, deq_q4_k :111 (+ _scale_min_k4 :99), deq_q5_k :123, deq_q6_k :140,
  *     deq_tq2_0 :417, deq_iq2_xxs :235 (codebook ggufengine/iqtabellen.py:11).  The operation
  *     order of each fp32 expression follows quant.py, so results are bit-identical.
  *   - the integer dot products of the reference's int8 path (ggufengine/mmvq.py:341-419 for
  *     Q4_K: per lane S = sum nibble*xq and S2 = sum nibble*xq2; :421-482 for Q6_K with signed
- *     q-32), and the same formula family for Q4_0, Q8_0, TQ2_0 and IQ2_XXS (which the reference
- *     only has as float kernels, ggufengine/cudakern.py:315,307,432,187).  Integer sums do not
+ *     q-32), and the same formula family for Q4_0, Q8_0, Q5_K, TQ2_0 and IQ2_XXS (which the
+ *     reference only has as float kernels, ggufengine/cudakern.py:315,307,379,432,187; Q5_K is
+ *     Q4_K's sum with a 5-bit unsigned code).  Integer sums do not
  *     depend on how a kernel groups them, so the per-unit sums below are the exact values any
  *     correct kernel must produce from the same Eingang.
  *
  * Sum units (the values that share one weight scale and one activation scale):
- *   Q4_K, Q4_0, Q8_0, TQ2_0, IQ2_XXS: 32 values (n_in/32 units per row); Q6_K: 16 values.
+ *   Q4_K, Q5_K, Q4_0, Q8_0, TQ2_0, IQ2_XXS: 32 values (n_in/32 units per row); Q6_K: 16 values.
  *   Q4_0 and TQ2_0 sums use the unsigned code (the -8 / -1 offset is applied with xs).
  *
  * Parity pins: the dequantisers are pinned to golden vectors generated from the reference's own
@@ -40,7 +41,7 @@
 #include <omp.h>
 #endif
 
-enum { T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q6_K = 14, T_IQ2_XXS = 16, T_TQ2_0 = 35 };
+enum { T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ2_XXS = 16, T_TQ2_0 = 35 };
 
 static const uint16_t IQ2XXS_CODES[256] = {
 #include "../nemicli-terminal_b200/csrc/iq2xxs_grid.inc"
@@ -85,7 +86,7 @@ static uint32_t rd32(const uint8_t* p) {
 int orc_block_values(int fmt) {
     switch (fmt) {
     case T_Q4_0: case T_Q8_0: return 32;
-    case T_Q4_K: case T_Q6_K: case T_IQ2_XXS: case T_TQ2_0: return 256;
+    case T_Q4_K: case T_Q5_K: case T_Q6_K: case T_IQ2_XXS: case T_TQ2_0: return 256;
     }
     return 0;
 }
@@ -95,6 +96,7 @@ int orc_block_bytes(int fmt) {
     case T_Q4_0: return 18;
     case T_Q8_0: return 34;
     case T_Q4_K: return 144;
+    case T_Q5_K: return 176;
     case T_Q6_K: return 210;
     case T_IQ2_XXS: return 66;
     case T_TQ2_0: return 66;
@@ -208,6 +210,21 @@ int orc_dequant(int fmt, const uint8_t* raw, long long n_values, float* out) {
             }
             break;
         }
+        case T_Q5_K: {
+            /* d, dmin, 12 B scales/mins as Q4_K, qh[32] at 16, qs[128] at 48: sub-block j value i is the
+               nibble (j odd: high) of qs[32 (j/2) + i] with bit j of qh[i] as bit 4 (quant.py:123-137) */
+            const float d = f16(b), dmin = f16(b + 2);
+            int sc[8], mn[8];
+            scale_min_k4(b + 4, sc, mn);
+            for (int j = 0; j < 8; ++j) {
+                const float a = d * (float)sc[j], m = dmin * (float)mn[j];
+                for (int i = 0; i < 32; ++i) {
+                    const int q = ((b[48 + 32 * (j >> 1) + i] >> (4 * (j & 1))) & 15) | (((b[16 + i] >> j) & 1) << 4);
+                    o[32 * j + i] = a * (float)q - m;
+                }
+            }
+            break;
+        }
         case T_Q6_K: {
             const uint8_t* ql = b;
             const uint8_t* qh = b + 128;
@@ -254,6 +271,10 @@ static int code_of(int fmt, const uint8_t* b, int v) {
     case T_Q4_0: return v < 16 ? (b[2 + v] & 15) : (b[2 + v - 16] >> 4);
     case T_Q8_0: return (int8_t)b[2 + v];
     case T_Q4_K: { const int j = v >> 5, i = v & 31; return (b[16 + 32 * (j >> 1) + i] >> (4 * (j & 1))) & 15; }
+    case T_Q5_K: {
+        const int j = v >> 5, i = v & 31;
+        return ((b[48 + 32 * (j >> 1) + i] >> (4 * (j & 1))) & 15) | (((b[16 + i] >> j) & 1) << 4);
+    }
     case T_Q6_K: {
         const int n = v >> 7, g = (v >> 5) & 3, l = v & 31;
         const int q = ((b[64 * n + 32 * (g & 1) + l] >> (4 * (g >> 1))) & 15) | (((b[128 + 32 * n + l] >> (2 * g)) & 3) << 4);
@@ -292,7 +313,7 @@ static void unit_scales(int fmt, const uint8_t* b, int u, double* wscale, double
     switch (fmt) {
     case T_Q4_0: *wscale = f16(b); *offs = 8.0 * f16(b); return;
     case T_Q8_0: *wscale = f16(b); *offs = 0.0; return;
-    case T_Q4_K: {
+    case T_Q4_K: case T_Q5_K: {
         int sc[8], mn[8];
         scale_min_k4(b + 4, sc, mn);
         *wscale = (double)f16(b) * sc[u];

@@ -12,7 +12,10 @@ tests/test_gguf_iq.py:81-101, zufallsbloecke).  Extra cases pin the corners:
 * IQ2_XXS blocks whose grid indices run through all 256 codebook entries and whose sign indices
   run through all 128 patterns,
 * TQ2_0 blocks with every 2-bit code, including the never-drawn code 3,
-* Q4_K blocks with 6-bit scales and mins at 0 and 63.
+* Q4_K blocks with 6-bit scales and mins at 0 and 63,
+* Q5_K blocks with scales and mins at 0 and 63 and every fifth bit (qh) set or clear.
+
+Formats added later are generated after the earlier cases, so the earlier arrays stay as they were.
 """
 from __future__ import annotations
 
@@ -23,12 +26,14 @@ import numpy as np
 
 FORMATS = {"Q4_0": (2, 32, 18), "Q8_0": (8, 32, 34), "Q4_K": (12, 256, 144), "Q6_K": (14, 256, 210),
            "IQ2_XXS": (16, 256, 66), "TQ2_0": (35, 256, 66)}
-SCALE_OFFSETS = {"Q4_0": (0,), "Q8_0": (0,), "Q4_K": (0, 2), "Q6_K": (208,), "IQ2_XXS": (0,), "TQ2_0": (64,)}
+LATER = {"Q5_K": (13, 256, 176)}
+SCALE_OFFSETS = {"Q4_0": (0,), "Q8_0": (0,), "Q4_K": (0, 2), "Q6_K": (208,), "IQ2_XXS": (0,), "TQ2_0": (64,),
+                 "Q5_K": (0, 2)}
 ROWS, COLS = 3, 512          # a (3, 512) matrix per format
 
 
 def random_blocks(name: str, n_blocks: int, rng: np.random.Generator) -> np.ndarray:
-    _, _, size = FORMATS[name]
+    _, _, size = {**FORMATS, **LATER}[name]
     raw = rng.integers(0, 256, (n_blocks, size), dtype=np.uint8)
     for o in SCALE_OFFSETS[name]:
         d = (rng.random(n_blocks) * 0.01 + 0.001).astype(np.float16)
@@ -64,6 +69,15 @@ def q4k_cover(rng: np.random.Generator) -> np.ndarray:
     return raw
 
 
+def q5k_cover(rng: np.random.Generator) -> np.ndarray:
+    raw = random_blocks("Q5_K", 2, rng)
+    raw[0, 4:16] = 0xFF        # every 6-bit scale and min = 63
+    raw[0, 16:48] = 0xFF       # every fifth bit set: codes 16..31
+    raw[1, 4:16] = 0x00        # every 6-bit scale and min = 0
+    raw[1, 16:48] = 0x00       # every fifth bit clear
+    return raw
+
+
 def main(ref_root: str) -> None:
     sys.path.insert(0, ref_root)
     import torch
@@ -73,7 +87,7 @@ def main(ref_root: str) -> None:
     out = {}
 
     def add(key: str, name: str, raw: np.ndarray, rows: int, cols: int) -> None:
-        t, bv, bb = FORMATS[name]
+        t, bv, bb = {**FORMATS, **LATER}[name]
         flat = np.ascontiguousarray(raw.reshape(-1))
         assert flat.size == rows * cols // bv * bb
         deq = dequantize(torch.from_numpy(flat.copy()), t, rows * cols, torch.float32).numpy()
@@ -83,13 +97,16 @@ def main(ref_root: str) -> None:
         out[f"{key}__deq"] = deq.astype(np.float32)
         out[f"{key}__x"] = x
         out[f"{key}__y"] = y
-        out[f"{key}__shape"] = np.array([FORMATS[name][0], rows, cols], dtype=np.int64)
+        out[f"{key}__shape"] = np.array([t, rows, cols], dtype=np.int64)
 
     for name, (_, bv, _) in FORMATS.items():
         add(name, name, random_blocks(name, ROWS * COLS // bv, rng), ROWS, COLS)
     add("IQ2_XXS_cover", "IQ2_XXS", iq2xxs_cover(rng), 8, 256)
     add("TQ2_0_cover", "TQ2_0", tq2_cover(rng), 2, 256)
     add("Q4_K_cover", "Q4_K", q4k_cover(rng), 2, 256)
+    for name, (_, bv, _) in LATER.items():
+        add(name, name, random_blocks(name, ROWS * COLS // bv, rng), ROWS, COLS)
+    add("Q5_K_cover", "Q5_K", q5k_cover(rng), 2, 256)
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "dequant_golden.npz")
     np.savez_compressed(path, **out)
     print(f"wrote {path}: {len(out)} arrays")
