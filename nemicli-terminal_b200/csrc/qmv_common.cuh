@@ -6,8 +6,8 @@
 
 namespace qmv {
 
-// GGML type ids of the seven formats (the GGUF type table; reference ggufengine/gguf.py:64-77)
-enum : int { F_Q4_0 = 2, F_Q8_0 = 8, F_Q4_K = 12, F_Q5_K = 13, F_Q6_K = 14, F_IQ2_XXS = 16, F_TQ2_0 = 35 };
+// GGML type ids of the eight formats (the GGUF type table; reference ggufengine/gguf.py:64-77)
+enum : int { F_Q4_0 = 2, F_Q8_0 = 8, F_Q4_K = 12, F_Q5_K = 13, F_Q6_K = 14, F_IQ2_XXS = 16, F_IQ4_XS = 23, F_TQ2_0 = 35 };
 
 // status codes returned across the C ABI (include/nemicli_qmv.h)
 enum : int {
@@ -33,13 +33,15 @@ __host__ __device__ constexpr int block_values(int f) {
     return (f == F_Q4_0 || f == F_Q8_0) ? 32 : 256;
 }
 __host__ __device__ constexpr int block_bytes(int f) {
-    return f == F_Q4_0 ? 18 : f == F_Q8_0 ? 34 : f == F_Q4_K ? 144 : f == F_Q5_K ? 176 : f == F_Q6_K ? 210 : 66;
+    return f == F_Q4_0 ? 18 : f == F_Q8_0 ? 34 : f == F_Q4_K ? 144 : f == F_Q5_K ? 176 : f == F_Q6_K ? 210
+         : f == F_IQ4_XS ? 136 : 66;
 }
 // values per integer-sum unit (one weight scale and one activation scale)
 __host__ __device__ constexpr int unit_values(int f) { return f == F_Q6_K ? 16 : 32; }
 
 __host__ __device__ inline bool known_format(int f) {
-    return f == F_Q4_0 || f == F_Q8_0 || f == F_Q4_K || f == F_Q5_K || f == F_Q6_K || f == F_IQ2_XXS || f == F_TQ2_0;
+    return f == F_Q4_0 || f == F_Q8_0 || f == F_Q4_K || f == F_Q5_K || f == F_Q6_K || f == F_IQ2_XXS || f == F_IQ4_XS ||
+           f == F_TQ2_0;
 }
 // weight rows and blocks of the K-quant formats with 16-byte header words are read 16 bytes at a time
 __host__ __device__ constexpr int weight_align(int f) { return f == F_Q4_K || f == F_Q5_K ? 16 : 2;
@@ -96,6 +98,23 @@ __device__ __forceinline__ float h2f(uint32_t bits) { return __half2float(__usho
 __device__ __forceinline__ float bf2f(uint16_t bits) { return __uint_as_float(uint32_t(bits) << 16); }
 
 __device__ __forceinline__ int dp4(uint32_t a, int b, int c) { return __dp4a(int(a), b, c); }
+
+// IQ4_XS codebook (the format's 16 signed values, the reference's KVALUES_IQ4NL) as int8 bytes, four
+// entries per word
+__host__ __device__ constexpr uint32_t kv4(int a, int b, int c, int d) {
+    return uint32_t(uint8_t(a)) | (uint32_t(uint8_t(b)) << 8) | (uint32_t(uint8_t(c)) << 16) | (uint32_t(uint8_t(d)) << 24);
+}
+// the codebook values of four indices (one 0..15 index in each byte) as four int8 bytes: two byte
+// permutes over the table's halves, the index's bit 3 picks the half
+__device__ __forceinline__ uint32_t iq4nl_bytes(uint32_t idx) {
+    constexpr uint32_t T0 = kv4(-127, -104, -83, -65), T1 = kv4(-49, -35, -22, -10);
+    constexpr uint32_t T2 = kv4(1, 13, 25, 38), T3 = kv4(53, 69, 89, 113);
+    const uint32_t t = idx & 0x07070707u, v = t | (t >> 4);
+    const uint32_t sel = (v & 0xFFu) | ((v >> 8) & 0xFF00u);
+    const uint32_t lo = __byte_perm(T0, T1, sel), hi = __byte_perm(T2, T3, sel);
+    const uint32_t m = ((idx >> 3) & 0x01010101u) * 0xFFu;
+    return (lo & ~m) | (hi & m);
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

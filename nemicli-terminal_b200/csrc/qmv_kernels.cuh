@@ -383,6 +383,51 @@ __device__ __forceinline__ void lane_iq2xxs(const uint8_t* const (&rows)[RW], in
     }
 }
 
+// ---- IQ4_XS: 136 B = d (f16), scales_h (u16), scales_l[4], qs[128] (quant.py:378-387).  Lane q takes
+// sub-block q: 6-bit scale = nibble q%2 of scales_l[q/2] | bits 2q..2q+1 of scales_h << 4, weight
+// scale d * (scale - 32); byte j of qs[16q..] holds codebook indices of values j (low) and 16 + j.
+template <int T, int RW, bool SUMS>
+__device__ __forceinline__ void lane_iq4xs(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                           const Tok<T>& tk, float (&acc)[RW][T], int row0) {
+    uint32_t w[RW][8];
+    float sc[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        const uint8_t* b = rows[r] + (long long)sb * 136;
+        const uint32_t sh = ldw2(b + 2), sl = ldw1(b + 4 + (q >> 1));
+        const int ls = int(((sl >> (4 * (q & 1))) & 15u) | (((sh >> (2 * q)) & 3u) << 4));
+        sc[r] = h2f(ldw2(b)) * float(ls - 32);
+        const uint4 v = ldw16_a2(b + 8 + 16 * q);
+        const uint32_t V[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            w[r][i] = iq4nl_bytes(V[i] & 0x0F0F0F0Fu);
+            w[r][4 + i] = iq4nl_bytes((V[i] >> 4) & 0x0F0F0F0Fu);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const long long o = tk.tb[t] + (long long)sb * 256 + 32 * q;
+        const int4 x0 = ldx16(P.xq + o), x1 = ldx16(P.xq + o + 16);
+        const int4 y0 = ldx16(P.xq2 + o), y1 = ldx16(P.xq2 + o + 16);
+        const float dd = __ldg(P.xd + ((tk.tb[t] + (long long)sb * 256) >> 5) + q);
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            int s = dp4(w[r][0], x0.x, 0); s = dp4(w[r][1], x0.y, s); s = dp4(w[r][2], x0.z, s); s = dp4(w[r][3], x0.w, s);
+            s = dp4(w[r][4], x1.x, s); s = dp4(w[r][5], x1.y, s); s = dp4(w[r][6], x1.z, s); s = dp4(w[r][7], x1.w, s);
+            int u = dp4(w[r][0], y0.x, 0); u = dp4(w[r][1], y0.y, u); u = dp4(w[r][2], y0.z, u); u = dp4(w[r][3], y0.w, u);
+            u = dp4(w[r][4], y1.x, u); u = dp4(w[r][5], y1.y, u); u = dp4(w[r][6], y1.z, u); u = dp4(w[r][7], y1.w, u);
+            if constexpr (SUMS) {
+                const long long base = (long long)row0 * (P.n_in / 32) + sb * 8 + q;
+                atomicAdd(P.s + base, s);
+                atomicAdd(P.s2 + base, u);
+            } else {
+                acc[r][t] += sc[r] * dd * (float(s) + float(u) * kInv254);
+            }
+        }
+    }
+}
+
 // IQ2_XXS codebook, 2 bits per magnitude (index into {8, 25, 43}); expanded per block at launch
 __device__ const uint16_t kIq2xxsCodes[256] = {
 #include "iq2xxs_grid.inc"
@@ -468,6 +513,7 @@ __global__ void __launch_bounds__(256) mv_kernel(const MvParams P) {
             else if constexpr (FMT == F_Q4_0) lane_q4_0<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (FMT == F_Q8_0) lane_q8_0<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (FMT == F_TQ2_0) lane_tq2_0<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+            else if constexpr (FMT == F_IQ4_XS) lane_iq4xs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else lane_iq2xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, grid);
         }
         if constexpr (!SUMS) {

@@ -11,20 +11,21 @@
  *     restatement uses IEEE-rounded division and an explicit fused multiply-add so that it is
  *     reproducible bit for bit on the GPU (the kernels do the same).  Against the reference's
  *     fast-math build a quantised value can differ by one unit on a rounding tie.
- *   - the block dequantisers of ggufengine/quant.py for the seven in-scope formats:
+ *   - the block dequantisers of ggufengine/quant.py for the eight in-scope formats:
  *     deq_q4_0 :60, deq_q8_0 :46, deq_q4_k :111 (+ _scale_min_k4 :99), deq_q5_k :123, deq_q6_k :140,
+ *     deq_iq4_xs :378 (codebook KVALUES_IQ4NL, ggufengine/iqtabellen.py:7),
  *     deq_tq2_0 :417, deq_iq2_xxs :235 (codebook ggufengine/iqtabellen.py:11).  The operation
  *     order of each fp32 expression follows quant.py, so results are bit-identical.
  *   - the integer dot products of the reference's int8 path (ggufengine/mmvq.py:341-419 for
  *     Q4_K: per lane S = sum nibble*xq and S2 = sum nibble*xq2; :421-482 for Q6_K with signed
- *     q-32), and the same formula family for Q4_0, Q8_0, Q5_K, TQ2_0 and IQ2_XXS (which the
- *     reference only has as float kernels, ggufengine/cudakern.py:315,307,379,432,187; Q5_K is
- *     Q4_K's sum with a 5-bit unsigned code).  Integer sums do not
+ *     q-32), and the same formula family for Q4_0, Q8_0, Q5_K, TQ2_0, IQ2_XXS and IQ4_XS (which
+ *     the reference only has as float kernels, ggufengine/cudakern.py:315,307,379,432,187; Q5_K is
+ *     Q4_K's sum with a 5-bit unsigned code, IQ4_XS sums the int8 codebook values).  Integer sums do not
  *     depend on how a kernel groups them, so the per-unit sums below are the exact values any
  *     correct kernel must produce from the same Eingang.
  *
  * Sum units (the values that share one weight scale and one activation scale):
- *   Q4_K, Q5_K, Q4_0, Q8_0, TQ2_0, IQ2_XXS: 32 values (n_in/32 units per row); Q6_K: 16 values.
+ *   Q4_K, Q5_K, Q4_0, Q8_0, TQ2_0, IQ2_XXS, IQ4_XS: 32 values (n_in/32 units per row); Q6_K: 16.
  *   Q4_0 and TQ2_0 sums use the unsigned code (the -8 / -1 offset is applied with xs).
  *
  * Parity pins: the dequantisers are pinned to golden vectors generated from the reference's own
@@ -41,7 +42,10 @@
 #include <omp.h>
 #endif
 
-enum { T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ2_XXS = 16, T_TQ2_0 = 35 };
+enum { T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ2_XXS = 16, T_IQ4_XS = 23, T_TQ2_0 = 35 };
+
+/* IQ4_XS codebook (part of the format: the reference's KVALUES_IQ4NL) */
+static const int8_t IQ4NL_VALUES[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
 
 static const uint16_t IQ2XXS_CODES[256] = {
 #include "../nemicli-terminal_b200/csrc/iq2xxs_grid.inc"
@@ -86,7 +90,7 @@ static uint32_t rd32(const uint8_t* p) {
 int orc_block_values(int fmt) {
     switch (fmt) {
     case T_Q4_0: case T_Q8_0: return 32;
-    case T_Q4_K: case T_Q5_K: case T_Q6_K: case T_IQ2_XXS: case T_TQ2_0: return 256;
+    case T_Q4_K: case T_Q5_K: case T_Q6_K: case T_IQ2_XXS: case T_IQ4_XS: case T_TQ2_0: return 256;
     }
     return 0;
 }
@@ -99,6 +103,7 @@ int orc_block_bytes(int fmt) {
     case T_Q5_K: return 176;
     case T_Q6_K: return 210;
     case T_IQ2_XXS: return 66;
+    case T_IQ4_XS: return 136;
     case T_TQ2_0: return 66;
     }
     return 0;
@@ -239,6 +244,22 @@ int orc_dequant(int fmt, const uint8_t* raw, long long n_values, float* out) {
                     }
             break;
         }
+        case T_IQ4_XS: {
+            /* d (f16), scales_h (u16) at 2, scales_l[4] at 4, qs[128] at 8: sub-block ib's 6-bit scale is
+               nibble ib%2 of scales_l[ib/2] with bits 2ib..2ib+1 of scales_h on top; qs[16 ib + j] holds
+               values j (low nibble) and 16 + j (high) as codebook indices (quant.py:378-387) */
+            const float d = f16(b);
+            const int sh = b[2] | (b[3] << 8);
+            for (int ib = 0; ib < 8; ++ib) {
+                const int ls = ((b[4 + ib / 2] >> (4 * (ib & 1))) & 15) | (((sh >> (2 * ib)) & 3) << 4);
+                const float dl = d * (float)(ls - 32);
+                for (int j = 0; j < 16; ++j) {
+                    o[32 * ib + j] = (float)IQ4NL_VALUES[b[8 + 16 * ib + j] & 15] * dl;
+                    o[32 * ib + 16 + j] = (float)IQ4NL_VALUES[b[8 + 16 * ib + j] >> 4] * dl;
+                }
+            }
+            break;
+        }
         case T_TQ2_0: {
             const float d = f16(b + 64);
             for (int n = 0; n < 2; ++n)
@@ -282,6 +303,10 @@ static int code_of(int fmt, const uint8_t* b, int v) {
     }
     case T_TQ2_0: { const int n = v >> 7, g = (v >> 5) & 3, m = v & 31; return (b[32 * n + m] >> (2 * g)) & 3; }
     case T_IQ2_XXS: return iq2xxs_value(b, v >> 5, v & 31);
+    case T_IQ4_XS: {
+        const int ib = v >> 5, j = v & 31;
+        return IQ4NL_VALUES[(b[8 + 16 * ib + (j & 15)] >> (4 * (j >> 4))) & 15];
+    }
     }
     return 0;
 }
@@ -325,6 +350,13 @@ static void unit_scales(int fmt, const uint8_t* b, int u, double* wscale, double
     case T_IQ2_XXS: {
         const uint32_t aux1 = rd32(b + 2 + 8 * u + 4);
         *wscale = (double)f16(b) * (0.125 + 0.25 * (double)(aux1 >> 28));
+        *offs = 0.0;
+        return;
+    }
+    case T_IQ4_XS: {
+        const int sh = b[2] | (b[3] << 8);
+        const int ls = ((b[4 + u / 2] >> (4 * (u & 1))) & 15) | (((sh >> (2 * u)) & 3) << 4);
+        *wscale = (double)f16(b) * (double)(ls - 32);
         *offs = 0.0;
         return;
     }

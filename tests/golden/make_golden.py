@@ -13,7 +13,9 @@ tests/test_gguf_iq.py:81-101, zufallsbloecke).  Extra cases pin the corners:
   run through all 128 patterns,
 * TQ2_0 blocks with every 2-bit code, including the never-drawn code 3,
 * Q4_K blocks with 6-bit scales and mins at 0 and 63,
-* Q5_K blocks with scales and mins at 0 and 63 and every fifth bit (qh) set or clear.
+* Q5_K blocks with scales and mins at 0 and 63 and every fifth bit (qh) set or clear,
+* IQ4_XS blocks whose sub-block scales run through all 64 values and whose nibbles run through all 16
+  codebook entries.
 
 Formats added later are generated after the earlier cases, so the earlier arrays stay as they were.
 """
@@ -27,13 +29,14 @@ import numpy as np
 FORMATS = {"Q4_0": (2, 32, 18), "Q8_0": (8, 32, 34), "Q4_K": (12, 256, 144), "Q6_K": (14, 256, 210),
            "IQ2_XXS": (16, 256, 66), "TQ2_0": (35, 256, 66)}
 LATER = {"Q5_K": (13, 256, 176)}
+LATER2 = {"IQ4_XS": (23, 256, 136)}
 SCALE_OFFSETS = {"Q4_0": (0,), "Q8_0": (0,), "Q4_K": (0, 2), "Q6_K": (208,), "IQ2_XXS": (0,), "TQ2_0": (64,),
-                 "Q5_K": (0, 2)}
+                 "Q5_K": (0, 2), "IQ4_XS": (0,)}
 ROWS, COLS = 3, 512          # a (3, 512) matrix per format
 
 
 def random_blocks(name: str, n_blocks: int, rng: np.random.Generator) -> np.ndarray:
-    _, _, size = {**FORMATS, **LATER}[name]
+    _, _, size = {**FORMATS, **LATER, **LATER2}[name]
     raw = rng.integers(0, 256, (n_blocks, size), dtype=np.uint8)
     for o in SCALE_OFFSETS[name]:
         d = (rng.random(n_blocks) * 0.01 + 0.001).astype(np.float16)
@@ -78,6 +81,22 @@ def q5k_cover(rng: np.random.Generator) -> np.ndarray:
     return raw
 
 
+def iq4xs_cover(rng: np.random.Generator) -> np.ndarray:
+    """8 blocks = 64 sub-blocks: sub-block k has 6-bit scale k; byte j of a sub-block holds nibbles
+    j and 15 - j."""
+    raw = random_blocks("IQ4_XS", 8, rng)
+    for blk in range(8):
+        sh, sl = 0, [0, 0, 0, 0]
+        for ib in range(8):
+            ls = 8 * blk + ib
+            sl[ib // 2] |= (ls & 15) << (4 * (ib & 1))
+            sh |= (ls >> 4) << (2 * ib)
+            raw[blk, 8 + 16 * ib:8 + 16 * ib + 16] = [j | ((15 - j) << 4) for j in range(16)]
+        raw[blk, 2:4] = [sh & 0xFF, sh >> 8]
+        raw[blk, 4:8] = sl
+    return raw
+
+
 def main(ref_root: str) -> None:
     sys.path.insert(0, ref_root)
     import torch
@@ -87,7 +106,7 @@ def main(ref_root: str) -> None:
     out = {}
 
     def add(key: str, name: str, raw: np.ndarray, rows: int, cols: int) -> None:
-        t, bv, bb = {**FORMATS, **LATER}[name]
+        t, bv, bb = {**FORMATS, **LATER, **LATER2}[name]
         flat = np.ascontiguousarray(raw.reshape(-1))
         assert flat.size == rows * cols // bv * bb
         deq = dequantize(torch.from_numpy(flat.copy()), t, rows * cols, torch.float32).numpy()
@@ -107,6 +126,9 @@ def main(ref_root: str) -> None:
     for name, (_, bv, _) in LATER.items():
         add(name, name, random_blocks(name, ROWS * COLS // bv, rng), ROWS, COLS)
     add("Q5_K_cover", "Q5_K", q5k_cover(rng), 2, 256)
+    for name, (_, bv, _) in LATER2.items():
+        add(name, name, random_blocks(name, ROWS * COLS // bv, rng), ROWS, COLS)
+    add("IQ4_XS_cover", "IQ4_XS", iq4xs_cover(rng), 8, 256)
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "dequant_golden.npz")
     np.savez_compressed(path, **out)
     print(f"wrote {path}: {len(out)} arrays")
