@@ -6,8 +6,11 @@
 
 namespace qmv {
 
-// GGML type ids of the eight formats (the GGUF type table; reference ggufengine/gguf.py:64-77)
-enum : int { F_Q4_0 = 2, F_Q8_0 = 8, F_Q4_K = 12, F_Q5_K = 13, F_Q6_K = 14, F_IQ2_XXS = 16, F_IQ4_XS = 23, F_TQ2_0 = 35 };
+// GGML type ids of the nine formats (the GGUF type table; reference ggufengine/gguf.py:64-77)
+enum : int {
+    F_Q4_0 = 2, F_Q8_0 = 8, F_Q4_K = 12, F_Q5_K = 13, F_Q6_K = 14, F_IQ2_XXS = 16, F_IQ4_XS = 23, F_TQ2_0 = 35,
+    F_MXFP4 = 39
+};
 
 // status codes returned across the C ABI (include/nemicli_qmv.h)
 enum : int {
@@ -30,21 +33,23 @@ constexpr int kMaxTokens = 8;           // tokens per launch of the dp4a kernels
 constexpr float kInv254 = 1.0f / 254.0f;
 
 __host__ __device__ constexpr int block_values(int f) {
-    return (f == F_Q4_0 || f == F_Q8_0) ? 32 : 256;
+    return (f == F_Q4_0 || f == F_Q8_0 || f == F_MXFP4) ? 32 : 256;
 }
 __host__ __device__ constexpr int block_bytes(int f) {
     return f == F_Q4_0 ? 18 : f == F_Q8_0 ? 34 : f == F_Q4_K ? 144 : f == F_Q5_K ? 176 : f == F_Q6_K ? 210
-         : f == F_IQ4_XS ? 136 : 66;
+         : f == F_IQ4_XS ? 136 : f == F_MXFP4 ? 17 : 66;
 }
 // values per integer-sum unit (one weight scale and one activation scale)
 __host__ __device__ constexpr int unit_values(int f) { return f == F_Q6_K ? 16 : 32; }
 
 __host__ __device__ inline bool known_format(int f) {
     return f == F_Q4_0 || f == F_Q8_0 || f == F_Q4_K || f == F_Q5_K || f == F_Q6_K || f == F_IQ2_XXS || f == F_IQ4_XS ||
-           f == F_TQ2_0;
+           f == F_TQ2_0 || f == F_MXFP4;
 }
-// weight rows and blocks of the K-quant formats with 16-byte header words are read 16 bytes at a time
-__host__ __device__ constexpr int weight_align(int f) { return f == F_Q4_K || f == F_Q5_K ? 16 : 2;
+// weight rows and blocks of the K-quant formats with 16-byte header words are read 16 bytes at a time;
+// MXFP4's 17-byte blocks start at any byte, and their loads stay inside the tensor when it starts on a
+// 4-byte boundary
+__host__ __device__ constexpr int weight_align(int f) { return f == F_Q4_K || f == F_Q5_K ? 16 : f == F_MXFP4 ? 4 : 2;
 }
 
 // ---- loads --------------------------------------------------------------------------------------
@@ -82,6 +87,15 @@ __device__ __forceinline__ uint4 ldw16_a2(const uint8_t* p) {
     return make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh),
                       __funnelshift_r(w2, w3, sh), __funnelshift_r(w3, w4, sh));
 }
+// 16 bytes at any address p, reading nothing outside [p & ~3, p + 16) (even p) or [p - 1, p + 16) (odd
+// p: the byte before p is read, e.g. an MXFP4 block's scale before its 16 code bytes)
+__device__ __forceinline__ uint4 ldw16_a1(const uint8_t* p) {
+    if ((reinterpret_cast<uintptr_t>(p) & 1) == 0) return ldw16_a2(p);
+    const uint4 a = ldw16_a2(p - 1);
+    const uint32_t last = ldw1(p + 15);
+    return make_uint4(__funnelshift_r(a.x, a.y, 8), __funnelshift_r(a.y, a.z, 8), __funnelshift_r(a.z, a.w, 8),
+                      __funnelshift_r(a.w, last, 8));
+}
 __device__ __forceinline__ uint2 ldw8_a2(const uint8_t* p) {
     const uintptr_t a = reinterpret_cast<uintptr_t>(p);
     const uint8_t* b = reinterpret_cast<const uint8_t*>(a & ~uintptr_t(3));
@@ -99,21 +113,30 @@ __device__ __forceinline__ float bf2f(uint16_t bits) { return __uint_as_float(ui
 
 __device__ __forceinline__ int dp4(uint32_t a, int b, int c) { return __dp4a(int(a), b, c); }
 
-// IQ4_XS codebook (the format's 16 signed values, the reference's KVALUES_IQ4NL) as int8 bytes, four
-// entries per word
+// 16-entry int8 codebooks of the formats, four entries per word: IQ4_XS (the reference's
+// KVALUES_IQ4NL) and MXFP4 (e2m1 values doubled, KVALUES_MXFP4)
 __host__ __device__ constexpr uint32_t kv4(int a, int b, int c, int d) {
     return uint32_t(uint8_t(a)) | (uint32_t(uint8_t(b)) << 8) | (uint32_t(uint8_t(c)) << 16) | (uint32_t(uint8_t(d)) << 24);
 }
 // the codebook values of four indices (one 0..15 index in each byte) as four int8 bytes: two byte
 // permutes over the table's halves, the index's bit 3 picks the half
-__device__ __forceinline__ uint32_t iq4nl_bytes(uint32_t idx) {
-    constexpr uint32_t T0 = kv4(-127, -104, -83, -65), T1 = kv4(-49, -35, -22, -10);
-    constexpr uint32_t T2 = kv4(1, 13, 25, 38), T3 = kv4(53, 69, 89, 113);
+template <uint32_t T0, uint32_t T1, uint32_t T2, uint32_t T3>
+__device__ __forceinline__ uint32_t lut16_bytes(uint32_t idx) {
     const uint32_t t = idx & 0x07070707u, v = t | (t >> 4);
     const uint32_t sel = (v & 0xFFu) | ((v >> 8) & 0xFF00u);
     const uint32_t lo = __byte_perm(T0, T1, sel), hi = __byte_perm(T2, T3, sel);
     const uint32_t m = ((idx >> 3) & 0x01010101u) * 0xFFu;
     return (lo & ~m) | (hi & m);
+}
+__device__ __forceinline__ uint32_t iq4nl_bytes(uint32_t idx) {
+    return lut16_bytes<kv4(-127, -104, -83, -65), kv4(-49, -35, -22, -10), kv4(1, 13, 25, 38), kv4(53, 69, 89, 113)>(idx);
+}
+__device__ __forceinline__ uint32_t mxfp4_bytes(uint32_t idx) {
+    return lut16_bytes<kv4(0, 1, 2, 3), kv4(4, 6, 8, 12), kv4(0, -1, -2, -3), kv4(-4, -6, -8, -12)>(idx);
+}
+// MXFP4 block scale 2^(e-128) from its float bits (subnormal for e < 2), as the reference builds it
+__device__ __forceinline__ float mxfp4_scale(uint32_t e) {
+    return __uint_as_float(e < 2 ? (0x00200000u << e) : ((e - 1) << 23));
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

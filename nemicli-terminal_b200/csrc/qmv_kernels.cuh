@@ -428,6 +428,50 @@ __device__ __forceinline__ void lane_iq4xs(const uint8_t* const (&rows)[RW], int
     }
 }
 
+// ---- MXFP4: 17 B = e (E8M0 scale 2^(e-128)), 16 B: byte j holds codebook indices of values j (low
+// nibble) and 16 + j (quant.py:390-401).  Lane q takes block 8*sb + q of the row; blocks start at any byte.
+template <int T, int RW, bool SUMS>
+__device__ __forceinline__ void lane_mxfp4(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                           const Tok<T>& tk, float (&acc)[RW][T], int row0) {
+    const int blk = sb * 8 + q;
+    if (blk >= P.n_in / 32) return;
+    uint32_t lo[RW][4], hi[RW][4];
+    float d[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        const uint8_t* b = rows[r] + (long long)blk * 17;
+        d[r] = mxfp4_scale(ldw1(b));
+        const uint4 v = ldw16_a1(b + 1);
+        const uint32_t V[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            lo[r][i] = mxfp4_bytes(V[i] & 0x0F0F0F0Fu);
+            hi[r][i] = mxfp4_bytes((V[i] >> 4) & 0x0F0F0F0Fu);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const long long o = tk.tb[t] + (long long)blk * 32;
+        const int4 xa = ldx16(P.xq + o), xb = ldx16(P.xq + o + 16);
+        const int4 ya = ldx16(P.xq2 + o), yb = ldx16(P.xq2 + o + 16);
+        const float dd = __ldg(P.xd + (tk.tb[t] >> 5) + blk);
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            int s = dp4(lo[r][0], xa.x, 0); s = dp4(lo[r][1], xa.y, s); s = dp4(lo[r][2], xa.z, s); s = dp4(lo[r][3], xa.w, s);
+            s = dp4(hi[r][0], xb.x, s); s = dp4(hi[r][1], xb.y, s); s = dp4(hi[r][2], xb.z, s); s = dp4(hi[r][3], xb.w, s);
+            int u = dp4(lo[r][0], ya.x, 0); u = dp4(lo[r][1], ya.y, u); u = dp4(lo[r][2], ya.z, u); u = dp4(lo[r][3], ya.w, u);
+            u = dp4(hi[r][0], yb.x, u); u = dp4(hi[r][1], yb.y, u); u = dp4(hi[r][2], yb.z, u); u = dp4(hi[r][3], yb.w, u);
+            if constexpr (SUMS) {
+                const long long base = (long long)row0 * (P.n_in / 32) + blk;
+                atomicAdd(P.s + base, s);
+                atomicAdd(P.s2 + base, u);
+            } else {
+                acc[r][t] += d[r] * dd * (float(s) + float(u) * kInv254);
+            }
+        }
+    }
+}
+
 // IQ2_XXS codebook, 2 bits per magnitude (index into {8, 25, 43}); expanded per block at launch
 __device__ const uint16_t kIq2xxsCodes[256] = {
 #include "iq2xxs_grid.inc"
@@ -514,6 +558,7 @@ __global__ void __launch_bounds__(256) mv_kernel(const MvParams P) {
             else if constexpr (FMT == F_Q8_0) lane_q8_0<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (FMT == F_TQ2_0) lane_tq2_0<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (FMT == F_IQ4_XS) lane_iq4xs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+            else if constexpr (FMT == F_MXFP4) lane_mxfp4<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else lane_iq2xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, grid);
         }
         if constexpr (!SUMS) {

@@ -213,7 +213,7 @@ __device__ __forceinline__ void load_act(Act<FMT>& a, int u, const int8_t* xq, c
     constexpr int NS = UnitTraits<FMT>::NS;
 #pragma unroll
     for (int i = 0; i < NS; ++i) a.d[i] = a.s[i] = 0.f;
-    if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0 || FMT == F_IQ2_XXS || FMT == F_IQ4_XS) {
+    if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0 || FMT == F_IQ2_XXS || FMT == F_IQ4_XS || FMT == F_MXFP4) {
         const int o = 32 * u;
         a.q[0] = ldq16<GLOBAL>(xq + o); a.q[1] = ldq16<GLOBAL>(xq + o + 16);
         a.r[0] = ldq16<GLOBAL>(xq2 + o); a.r[1] = ldq16<GLOBAL>(xq2 + o + 16);
@@ -427,6 +427,20 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
             o.wsc[g] = d;
             o.off[g] = d;
         }
+    } else if constexpr (FMT == F_MXFP4) {
+        const uint32_t bl = rs + u * 17;
+        const uint4 v = lds16_a2(bl + 1);           // any byte offset: aligned words + funnel shifts
+        const uint32_t V[4] = {v.x, v.y, v.z, v.w};
+        uint32_t w0[4], w1[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            w0[i] = mxfp4_bytes(V[i] & 0x0F0F0F0Fu);
+            w1[i] = mxfp4_bytes((V[i] >> 4) & 0x0F0F0F0Fu);
+        }
+        o.s[0] = dot4(w1, a.q[1]) + dot4(w0, a.q[0]);
+        o.u[0] = dot4(w1, a.r[1]) + dot4(w0, a.r[0]);
+        o.wsc[0] = mxfp4_scale(lds8u(bl));
+        o.off[0] = 0.f;
     } else if constexpr (FMT == F_IQ4_XS) {
         const int b = u >> 3, q = u & 7;
         const uint32_t sb = rs + b * 136;
@@ -470,7 +484,7 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
 // sum-unit index (values sharing both scales: 16 for Q6_K, 32 otherwise) of scale group k of unit u
 template <int FMT>
 __device__ __forceinline__ int sum_unit(int u, int k) {
-    if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0 || FMT == F_IQ2_XXS || FMT == F_IQ4_XS) return u;
+    if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0 || FMT == F_IQ2_XXS || FMT == F_IQ4_XS || FMT == F_MXFP4) return u;
     if constexpr (FMT == F_Q4_K || FMT == F_Q5_K) return 2 * u + k;   // unit u = sub-blocks 2u, 2u + 1 of the row
     const int b = u >> 3, q = u & 7;
     if constexpr (FMT == F_Q6_K) {

@@ -11,21 +11,23 @@
  *     restatement uses IEEE-rounded division and an explicit fused multiply-add so that it is
  *     reproducible bit for bit on the GPU (the kernels do the same).  Against the reference's
  *     fast-math build a quantised value can differ by one unit on a rounding tie.
- *   - the block dequantisers of ggufengine/quant.py for the eight in-scope formats:
+ *   - the block dequantisers of ggufengine/quant.py for the nine in-scope formats:
  *     deq_q4_0 :60, deq_q8_0 :46, deq_q4_k :111 (+ _scale_min_k4 :99), deq_q5_k :123, deq_q6_k :140,
- *     deq_iq4_xs :378 (codebook KVALUES_IQ4NL, ggufengine/iqtabellen.py:7),
+ *     deq_iq4_xs :378 (codebook KVALUES_IQ4NL, ggufengine/iqtabellen.py:7), deq_mxfp4 :394
+ *     (KVALUES_MXFP4 :391, scale 2^(e-128) as the reference builds its float bits),
  *     deq_tq2_0 :417, deq_iq2_xxs :235 (codebook ggufengine/iqtabellen.py:11).  The operation
  *     order of each fp32 expression follows quant.py, so results are bit-identical.
  *   - the integer dot products of the reference's int8 path (ggufengine/mmvq.py:341-419 for
  *     Q4_K: per lane S = sum nibble*xq and S2 = sum nibble*xq2; :421-482 for Q6_K with signed
- *     q-32), and the same formula family for Q4_0, Q8_0, Q5_K, TQ2_0, IQ2_XXS and IQ4_XS (which
- *     the reference only has as float kernels, ggufengine/cudakern.py:315,307,379,432,187; Q5_K is
- *     Q4_K's sum with a 5-bit unsigned code, IQ4_XS sums the int8 codebook values).  Integer sums do not
+ *     q-32), and the same formula family for Q4_0, Q8_0, Q5_K, TQ2_0, IQ2_XXS, IQ4_XS and MXFP4
+ *     (which the reference only has as float kernels, ggufengine/cudakern.py:315,307,379,432,187;
+ *     Q5_K is Q4_K's sum with a 5-bit unsigned code, IQ4_XS and MXFP4 sum int8 codebook values).  Integer sums do not
  *     depend on how a kernel groups them, so the per-unit sums below are the exact values any
  *     correct kernel must produce from the same Eingang.
  *
  * Sum units (the values that share one weight scale and one activation scale):
- *   Q4_K, Q5_K, Q4_0, Q8_0, TQ2_0, IQ2_XXS, IQ4_XS: 32 values (n_in/32 units per row); Q6_K: 16.
+ *   Q4_K, Q5_K, Q4_0, Q8_0, TQ2_0, IQ2_XXS, IQ4_XS, MXFP4: 32 values (n_in/32 units per row);
+ *   Q6_K: 16.
  *   Q4_0 and TQ2_0 sums use the unsigned code (the -8 / -1 offset is applied with xs).
  *
  * Parity pins: the dequantisers are pinned to golden vectors generated from the reference's own
@@ -42,10 +44,20 @@
 #include <omp.h>
 #endif
 
-enum { T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ2_XXS = 16, T_IQ4_XS = 23, T_TQ2_0 = 35 };
+enum { T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ2_XXS = 16, T_IQ4_XS = 23, T_TQ2_0 = 35, T_MXFP4 = 39 };
 
 /* IQ4_XS codebook (part of the format: the reference's KVALUES_IQ4NL) */
 static const int8_t IQ4NL_VALUES[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+/* MXFP4 codebook: e2m1 values doubled (the reference's KVALUES_MXFP4), so the scale is 2^(e-128) */
+static const int8_t MXFP4_VALUES[16] = {0, 1, 2, 3, 4, 6, 8, 12, 0, -1, -2, -3, -4, -6, -8, -12};
+
+/* 2^(e-128) from its float bits, subnormal for e < 2 (ggufengine/quant.py:397-399) */
+static float mxfp4_scale(uint8_t e) {
+    const uint32_t bits = e < 2 ? (0x00200000u << e) : ((uint32_t)(e - 1) << 23);
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
 
 static const uint16_t IQ2XXS_CODES[256] = {
 #include "../nemicli-terminal_b200/csrc/iq2xxs_grid.inc"
@@ -89,7 +101,7 @@ static uint32_t rd32(const uint8_t* p) {
 
 int orc_block_values(int fmt) {
     switch (fmt) {
-    case T_Q4_0: case T_Q8_0: return 32;
+    case T_Q4_0: case T_Q8_0: case T_MXFP4: return 32;
     case T_Q4_K: case T_Q5_K: case T_Q6_K: case T_IQ2_XXS: case T_IQ4_XS: case T_TQ2_0: return 256;
     }
     return 0;
@@ -105,6 +117,7 @@ int orc_block_bytes(int fmt) {
     case T_IQ2_XXS: return 66;
     case T_IQ4_XS: return 136;
     case T_TQ2_0: return 66;
+    case T_MXFP4: return 17;
     }
     return 0;
 }
@@ -260,6 +273,15 @@ int orc_dequant(int fmt, const uint8_t* raw, long long n_values, float* out) {
             }
             break;
         }
+        case T_MXFP4: {
+            /* e (E8M0) then 16 bytes: byte j holds values j (low nibble) and 16 + j (high) */
+            const float d = mxfp4_scale(b[0]);
+            for (int j = 0; j < 16; ++j) {
+                o[j] = (float)MXFP4_VALUES[b[1 + j] & 15] * d;
+                o[16 + j] = (float)MXFP4_VALUES[b[1 + j] >> 4] * d;
+            }
+            break;
+        }
         case T_TQ2_0: {
             const float d = f16(b + 64);
             for (int n = 0; n < 2; ++n)
@@ -303,6 +325,7 @@ static int code_of(int fmt, const uint8_t* b, int v) {
     }
     case T_TQ2_0: { const int n = v >> 7, g = (v >> 5) & 3, m = v & 31; return (b[32 * n + m] >> (2 * g)) & 3; }
     case T_IQ2_XXS: return iq2xxs_value(b, v >> 5, v & 31);
+    case T_MXFP4: return MXFP4_VALUES[(b[1 + (v & 15)] >> (4 * (v >> 4))) & 15];
     case T_IQ4_XS: {
         const int ib = v >> 5, j = v & 31;
         return IQ4NL_VALUES[(b[8 + 16 * ib + (j & 15)] >> (4 * (j >> 4))) & 15];
@@ -353,6 +376,7 @@ static void unit_scales(int fmt, const uint8_t* b, int u, double* wscale, double
         *offs = 0.0;
         return;
     }
+    case T_MXFP4: *wscale = mxfp4_scale(b[0]); *offs = 0.0; return;
     case T_IQ4_XS: {
         const int sh = b[2] | (b[3] << 8);
         const int ls = ((b[4 + u / 2] >> (4 * (u & 1))) & 15) | (((sh >> (2 * u)) & 3) << 4);

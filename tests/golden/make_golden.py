@@ -15,7 +15,8 @@ tests/test_gguf_iq.py:81-101, zufallsbloecke).  Extra cases pin the corners:
 * Q4_K blocks with 6-bit scales and mins at 0 and 63,
 * Q5_K blocks with scales and mins at 0 and 63 and every fifth bit (qh) set or clear,
 * IQ4_XS blocks whose sub-block scales run through all 64 values and whose nibbles run through all 16
-  codebook entries.
+  codebook entries,
+* MXFP4 blocks with every nibble and scale exponents from the subnormal range (0, 1) up to 200.
 
 Formats added later are generated after the earlier cases, so the earlier arrays stay as they were.
 """
@@ -30,14 +31,17 @@ FORMATS = {"Q4_0": (2, 32, 18), "Q8_0": (8, 32, 34), "Q4_K": (12, 256, 144), "Q6
            "IQ2_XXS": (16, 256, 66), "TQ2_0": (35, 256, 66)}
 LATER = {"Q5_K": (13, 256, 176)}
 LATER2 = {"IQ4_XS": (23, 256, 136)}
+LATER3 = {"MXFP4": (39, 32, 17)}
 SCALE_OFFSETS = {"Q4_0": (0,), "Q8_0": (0,), "Q4_K": (0, 2), "Q6_K": (208,), "IQ2_XXS": (0,), "TQ2_0": (64,),
-                 "Q5_K": (0, 2), "IQ4_XS": (0,)}
+                 "Q5_K": (0, 2), "IQ4_XS": (0,), "MXFP4": ()}
 ROWS, COLS = 3, 512          # a (3, 512) matrix per format
 
 
 def random_blocks(name: str, n_blocks: int, rng: np.random.Generator) -> np.ndarray:
-    _, _, size = {**FORMATS, **LATER, **LATER2}[name]
+    _, _, size = {**FORMATS, **LATER, **LATER2, **LATER3}[name]
     raw = rng.integers(0, 256, (n_blocks, size), dtype=np.uint8)
+    if name == "MXFP4":
+        raw[:, 0] = rng.integers(118, 125, n_blocks)       # scale exponents 2^-10 .. 2^-4
     for o in SCALE_OFFSETS[name]:
         d = (rng.random(n_blocks) * 0.01 + 0.001).astype(np.float16)
         raw[:, o:o + 2] = d.view(np.uint8).reshape(n_blocks, 2)
@@ -97,6 +101,14 @@ def iq4xs_cover(rng: np.random.Generator) -> np.ndarray:
     return raw
 
 
+def mxfp4_cover(rng: np.random.Generator) -> np.ndarray:
+    """16 blocks: byte j of every block holds nibbles j and 15 - j; exponents 0..3, 100, 126..130, 200."""
+    raw = random_blocks("MXFP4", 16, rng)
+    raw[:, 0] = [0, 1, 2, 3, 100, 126, 127, 128, 129, 130, 200, 120, 121, 122, 123, 124]
+    raw[:, 1:17] = [j | ((15 - j) << 4) for j in range(16)]
+    return raw
+
+
 def main(ref_root: str) -> None:
     sys.path.insert(0, ref_root)
     import torch
@@ -106,7 +118,7 @@ def main(ref_root: str) -> None:
     out = {}
 
     def add(key: str, name: str, raw: np.ndarray, rows: int, cols: int) -> None:
-        t, bv, bb = {**FORMATS, **LATER, **LATER2}[name]
+        t, bv, bb = {**FORMATS, **LATER, **LATER2, **LATER3}[name]
         flat = np.ascontiguousarray(raw.reshape(-1))
         assert flat.size == rows * cols // bv * bb
         deq = dequantize(torch.from_numpy(flat.copy()), t, rows * cols, torch.float32).numpy()
@@ -129,6 +141,9 @@ def main(ref_root: str) -> None:
     for name, (_, bv, _) in LATER2.items():
         add(name, name, random_blocks(name, ROWS * COLS // bv, rng), ROWS, COLS)
     add("IQ4_XS_cover", "IQ4_XS", iq4xs_cover(rng), 8, 256)
+    for name, (_, bv, _) in LATER3.items():
+        add(name, name, random_blocks(name, ROWS * COLS // bv, rng), ROWS, COLS)
+    add("MXFP4_cover", "MXFP4", mxfp4_cover(rng), 2, 256)
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "dequant_golden.npz")
     np.savez_compressed(path, **out)
     print(f"wrote {path}: {len(out)} arrays")
