@@ -312,10 +312,11 @@ bool tma_dense(int fmt, int n_jobs, const uint8_t* const* w, const int* n_out, f
 }  // namespace
 
 namespace {
-// Few-token Q4_K matvec on the tensor cores; false when the shape or alignment does not qualify.
-bool mma_q4k(const uint8_t* w, int n_out, int n_in, long long row_bytes, const int8_t* xq, const int8_t* xq2,
-             const float* xd, const float* xs, int T, float* y, int fmt, cudaStream_t st, int* status) {
-    if (fmt != F_Q4_K || T < 2 || T > kMmaMaxTok || n_in % 256 || n_in > kMmaMaxIn || !knobs().enabled) return false;
+// Few-token Q4_K / Q8_0 matvec on the tensor cores; false when the shape or alignment does not qualify.
+template <int FMT>
+bool mma_dense_k(const uint8_t* w, int n_out, int n_in, long long row_bytes, const int8_t* xq, const int8_t* xq2,
+                 const float* xd, const float* xs, int T, float* y, cudaStream_t st, int* status) {
+    if (T < 2 || T > kMmaMaxTok || n_in % block_values(FMT) || n_in > kMmaMaxIn || !knobs().enabled) return false;
     if (!aligned(w, 16) || !aligned(xq, 16) || !aligned(xq2, 16) || row_bytes % 16) return false;
     constexpr int NCW = 16;
     const long long other = mma_act_bytes(n_in) + mma_red_bytes(NCW) + 2 * 8 * 32;
@@ -331,7 +332,7 @@ bool mma_q4k(const uint8_t* w, int n_out, int n_in, long long row_bytes, const i
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        if (cudaFuncSetAttribute(mv_mma_q4k_kernel<NCW>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap) != cudaSuccess) {
+        if (cudaFuncSetAttribute(mv_mma_kernel<FMT, NCW>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap) != cudaSuccess) {
             *status = launched();
             return true;
         }
@@ -339,9 +340,15 @@ bool mma_q4k(const uint8_t* w, int n_out, int n_in, long long row_bytes, const i
     }
     const int tiles = (n_out + kMmaRows - 1) / kMmaRows;
     const int grid = std::min(tiles, sm_count());
-    mv_mma_q4k_kernel<NCW><<<grid, 32 * (NCW + 1), int(S * slot + other), st>>>(P);
+    mv_mma_kernel<FMT, NCW><<<grid, 32 * (NCW + 1), int(S * slot + other), st>>>(P);
     *status = launched();
     return true;
+}
+bool mma_q4k(const uint8_t* w, int n_out, int n_in, long long row_bytes, const int8_t* xq, const int8_t* xq2,
+             const float* xd, const float* xs, int T, float* y, int fmt, cudaStream_t st, int* status) {
+    if (fmt == F_Q4_K) return mma_dense_k<F_Q4_K>(w, n_out, n_in, row_bytes, xq, xq2, xd, xs, T, y, st, status);
+    if (fmt == F_Q8_0) return mma_dense_k<F_Q8_0>(w, n_out, n_in, row_bytes, xq, xq2, xd, xs, T, y, st, status);
+    return false;
 }
 
 // Few-token Q6_K matvec on the tensor cores (rows of a multiple of 2048 values).
@@ -444,7 +451,7 @@ int qmv_mv(int ggml_type, const uint8_t* w, int n_out, int n_in, const int8_t* x
     for (int c0 = 0; c0 < n_tok; c0 += kMaxTokens) {
         const int T = n_tok - c0 < kMaxTokens ? n_tok - c0 : kMaxTokens;
         const long long off = (long long)c0 * n_in;
-        // 2..8 tokens of Q4_K rows up to kMmaMaxIn values: the tensor-core kernel
+        // 2..8 tokens of Q4_K / Q8_0 rows up to kMmaMaxIn values, or of Q6_K rows: the tensor-core kernels
         if (T >= 2 && (mma_q4k(w, n_out, n_in, P.row_bytes, xq + off, xq2 + off, xd + off / 32, xs + off / 32, T,
                                y + (long long)c0 * n_out, ggml_type, static_cast<cudaStream_t>(stream), &st) ||
                        mma_q6k(w, n_out, n_in, P.row_bytes, xq + off, xq2 + off, xd + off / 32, T,

@@ -1,4 +1,4 @@
-// Few-token matvec (2..8 tokens) for Q4_K rows on the tensor cores: y[t] = W x_t.
+// Few-token matvec (2..8 tokens) for Q4_K and Q8_0 rows on the tensor cores: y[t] = W x_t.
 //
 // The weights stream through the same bulk-copy ring as the single-token kernel, in tiles of 16 rows
 // (one MMA row block), one copy per row into rows padded by 16 bytes: the eight rows of an A fragment
@@ -12,6 +12,9 @@
 // token).  Per-sub-block scales are why the accumulators live in registers: a tensor-memory
 // accumulator would have to be read back after every K = 32 step.  Warps' partial sums meet in shared
 // memory and are added in a fixed order.  Every mbarrier wait is bounded.
+// Q8_0 (34-byte blocks: d, 32 int8): each warp takes whole blocks; A = the int8 codes (2-byte aligned
+// in shared memory: aligned words and funnel shifts), two mma.sync.m16n8k32 s8 x s8 per block and
+//     y[r][t] += d_r * (xd_t / 254) * (254 S + S2).
 #pragma once
 #include "qmv_tma.cuh"
 
@@ -41,6 +44,21 @@ __host__ __device__ constexpr long long mma_act_bytes(int n_in) {
 }
 __host__ __device__ constexpr int mma_red_bytes(int ncw) { return ncw * kMmaRows * kMmaMaxTok * 4; }
 
+// 4 bytes at a 2-byte aligned shared address
+__device__ __forceinline__ uint32_t lds32_a2(uint32_t a) {
+    const uint32_t b = a & ~3u, sh = (a & 3u) * 8u;
+    return __funnelshift_r(lds32(b), lds32(b + 4), sh);
+}
+
+// D = A (16x32 s8) * B (32x8 s8) + D, int32
+__device__ __forceinline__ void mma_s8s8_k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                             uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+                 "{%0, %1, %2, %3};"
+                 : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // D = A (16x32 u8) * B (32x8 s8) + D, int32
 __device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1) {
@@ -58,8 +76,9 @@ __device__ __forceinline__ void q4k_scale_words(uint4 hd, uint32_t& sc_lo, uint3
     m_hi = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
 }
 
-template <int NCW>
-__global__ void __launch_bounds__(32 * (NCW + 1), 1) mv_mma_q4k_kernel(const MmaParams P) {
+template <int FMT, int NCW>
+__global__ void __launch_bounds__(32 * (NCW + 1), 1) mv_mma_kernel(const MmaParams P) {
+    static_assert(FMT == F_Q4_K || FMT == F_Q8_0, "few-token tensor-core formats");
     extern __shared__ __align__(128) uint8_t smem[];
     const int S = P.stages;
     const uint32_t rstride = uint32_t(mma_row_stride(P.row_bytes));
@@ -142,7 +161,29 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) mv_mma_q4k_kernel(const Mma
         const uint32_t tile = stage0 + uint32_t(s) * slot_bytes;
         // rows gid and gid + 8 of the tile x tokens 2 tig, 2 tig + 1
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        if (got) {
+        if (got && FMT == F_Q8_0) {
+            const uint32_t rg = tile + uint32_t(gid) * rstride, rh = tile + uint32_t(gid + 8) * rstride;
+            for (int blk = warp; blk < ng; blk += NCW) {
+                const uint32_t bg = rg + blk * 34, bh = rh + blk * 34;
+                // k = 4 tig .. and 16 + 4 tig .. of the block's 32 codes (rows gid, gid + 8)
+                const uint32_t a0 = lds32_a2(bg + 2 + 4 * tig), a1 = lds32_a2(bh + 2 + 4 * tig);
+                const uint32_t a2 = lds32_a2(bg + 18 + 4 * tig), a3 = lds32_a2(bh + 18 + 4 * tig);
+                const int k0 = 32 * blk + 4 * tig;
+                const uint32_t b0 = *reinterpret_cast<const uint32_t*>(aq + gid * stride + k0);
+                const uint32_t b1 = *reinterpret_cast<const uint32_t*>(aq + gid * stride + k0 + 16);
+                const uint32_t c0 = *reinterpret_cast<const uint32_t*>(aq2 + gid * stride + k0);
+                const uint32_t c1 = *reinterpret_cast<const uint32_t*>(aq2 + gid * stride + k0 + 16);
+                int s1[4] = {0, 0, 0, 0}, s2[4] = {0, 0, 0, 0};
+                mma_s8s8_k32(s1, a0, a1, a2, a3, b0, b1);
+                mma_s8s8_k32(s2, a0, a1, a2, a3, c0, c1);
+                const float dg = h2f(lds16u(bg)), dh = h2f(lds16u(bh));
+                const float xd0 = ad[(2 * tig) * gs + blk], xd1 = ad[(2 * tig + 1) * gs + blk];
+                acc[0] += dg * xd0 * float(254 * s1[0] + s2[0]);
+                acc[1] += dg * xd1 * float(254 * s1[1] + s2[1]);
+                acc[2] += dh * xd0 * float(254 * s1[2] + s2[2]);
+                acc[3] += dh * xd1 * float(254 * s1[3] + s2[3]);
+            }
+        } else if (got) {
             const uint32_t rg = tile + uint32_t(gid) * rstride, rh = tile + uint32_t(gid + 8) * rstride;
             for (int sb = warp; sb < n_sb; sb += NCW) {
                 const uint32_t bg = rg + sb * 144, bh = rh + sb * 144;
@@ -235,11 +276,6 @@ __device__ __forceinline__ void mma_s8s8_k16(int (&d)[4], uint32_t a0, uint32_t 
 // four unsigned 6-bit codes -> code - 32 as signed bytes (no carries between bytes)
 __device__ __forceinline__ uint32_t q6_signed(uint32_t c) {
     return ((c | 0x80808080u) - 0x20202020u) ^ 0x80808080u;
-}
-// 4 bytes at a 2-byte aligned shared address
-__device__ __forceinline__ uint32_t lds32_a2(uint32_t a) {
-    const uint32_t b = a & ~3u, sh = (a & 3u) * 8u;
-    return __funnelshift_r(lds32(b), lds32(b + 4), sh);
 }
 
 template <int NCW>
