@@ -512,7 +512,8 @@ def run_moe(args):
 
 def run_vocab(args):
     """Config 3: the vocabulary projection (128256 x 4096, Q8_0 or Q6_K) row-sharded over the N ranks
-    (shard.RowShardedLinear: local matvec + one NCCL all-gather of the fp32 logits), batch 1.  Each rank
+    (shard.RowShardedLinear: local matvec + one NCCL all-gather of the fp32 logits), batch --tokens (the
+    config names 1 and 8; 2..8 tokens run the tensor-core few-token kernels).  Each rank
     rotates over enough copies of its shard to read more than twice its L2 between repeats.  value:
     whole-matrix weight bytes per second of the sharded call (strong scaling: the matrix is fixed)."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -536,7 +537,9 @@ def run_vocab(args):
     copies = max(1, -(-2 * l2 // local_bytes))
     lins = [shard.RowShardedLinear(fmt, synth.blocks(fmt, hi - lo, VOCAB_IN, seed=500 + 17 * rank + c, device=device),
                                    VOCAB_ROWS, VOCAB_IN) for c in range(copies)]
-    x = synth.activations(1, VOCAB_IN, seed=501, device=device)[0].contiguous()
+    T = args.tokens
+    x = synth.activations(T, VOCAB_IN, seed=501, device=device)
+    x = x[0].contiguous() if T == 1 else x.contiguous()
     g_local, _ = capture(lambda: [lin.local(x) for lin in lins])
     g_full, outs = capture(lambda: [lin(x) for lin in lins])
     with Clocks(local) as clk:
@@ -553,14 +556,15 @@ def run_vocab(args):
                 "warmup": args.warmup, "ms_per_step": t_full * 1e3, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "int8",
                 "data": "synthetic (seeded, config-3 distributions)",
-                "config": {"workload": f"config3: {VOCAB_ROWS}x{VOCAB_IN} {fmt} vocabulary projection, batch 1, "
+                "config": {"workload": f"config3: {VOCAB_ROWS}x{VOCAB_IN} {fmt} vocabulary projection, batch {T}, "
                                        f"rows split over {world} GPU(s), NCCL all-gather of fp32 logits",
                            "weight_bytes": total, "shard_bytes": local_bytes, "copies_rotated": copies,
                            "l2": "each rank rotates over copies of its shard totalling > 2x L2"},
                 "compute_only": {"value": total / t_local / 1e9, "unit": "GB/s", "us": t_local * 1e6,
                                  "hbm_frac_per_gpu": local_bytes / t_local / 1e9 / peak},
                 "gather_us": (t_full - t_local) * 1e6, "peak": peak, "peak_kind": peak_kind,
-                "gpu_launches": copies * args.steps * (1 if world == 1 else 2), "clocks": clocks}
+                "gpu_launches": copies * args.steps * ((1 if T == 1 else 2) + (0 if world == 1 else 1)),
+                "clocks": clocks}
         print(json.dumps(line), flush=True)
     del g_local, g_full
     if dist is not None:
@@ -584,6 +588,7 @@ def main():
                     help="stack: config 2 (the headline); vocab: config 3 row-sharded over the GPUs; "
                          "moe: config 4; cfg1 / cfg5: the single-matrix configs")
     ap.add_argument("--vocab-format", choices=["Q8_0", "Q6_K"], default="Q8_0")
+    ap.add_argument("--tokens", type=int, default=1, help="vocab workload: tokens per call (config 3: 1 and 8)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

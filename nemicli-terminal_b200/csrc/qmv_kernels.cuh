@@ -472,6 +472,69 @@ __device__ __forceinline__ void lane_mxfp4(const uint8_t* const (&rows)[RW], int
     }
 }
 
+// ---- IQ3_S: 110 B = d (f16), qs[64], qh[8], signs[32], scales[4] (quant.py:334-346).  Lane q takes
+// sub-block q: group l (4 values) has codebook index qs[8q + l] | bit l of qh[q] << 8 and the signs in
+// bits 4l..4l+3 of the sub-block's four sign bytes; weight scale d * (1 + 2 * 4-bit scale).  The 512
+// entries sit in shared memory as four magnitude bytes each.
+template <int T, int RW, bool SUMS>
+__device__ __forceinline__ void lane_iq3s(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                          const Tok<T>& tk, float (&acc)[RW][T], int row0,
+                                          const uint32_t* __restrict__ grid) {
+    uint32_t w[RW][8];
+    float sc[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        const uint8_t* b = rows[r] + (long long)sb * 110;
+        const uint2 qs = ldw8_a2(b + 2 + 8 * q);
+        const uint32_t qh = ldw1(b + 66 + q);
+        const uint32_t sg = ldw2(b + 74 + 4 * q) | (ldw2(b + 76 + 4 * q) << 16);
+        const uint32_t ls = (ldw1(b + 106 + (q >> 1)) >> (4 * (q & 1))) & 15u;
+        sc[r] = h2f(ldw2(b)) * float(1 + 2 * int(ls));
+#pragma unroll
+        for (int l = 0; l < 8; ++l) {
+            const uint32_t idx = (((l < 4 ? qs.x : qs.y) >> (8 * (l & 3))) & 0xFFu) | (((qh >> l) & 1u) << 8);
+            const uint32_t m = sign4_mask(sg >> (4 * l));
+            w[r][l] = __vsub4(grid[idx] ^ m, m);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const long long o = tk.tb[t] + (long long)sb * 256 + 32 * q;
+        const int4 x0 = ldx16(P.xq + o), x1 = ldx16(P.xq + o + 16);
+        const int4 y0 = ldx16(P.xq2 + o), y1 = ldx16(P.xq2 + o + 16);
+        const float dd = __ldg(P.xd + ((tk.tb[t] + (long long)sb * 256) >> 5) + q);
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            int s = dp4(w[r][0], x0.x, 0); s = dp4(w[r][1], x0.y, s); s = dp4(w[r][2], x0.z, s); s = dp4(w[r][3], x0.w, s);
+            s = dp4(w[r][4], x1.x, s); s = dp4(w[r][5], x1.y, s); s = dp4(w[r][6], x1.z, s); s = dp4(w[r][7], x1.w, s);
+            int u = dp4(w[r][0], y0.x, 0); u = dp4(w[r][1], y0.y, u); u = dp4(w[r][2], y0.z, u); u = dp4(w[r][3], y0.w, u);
+            u = dp4(w[r][4], y1.x, u); u = dp4(w[r][5], y1.y, u); u = dp4(w[r][6], y1.z, u); u = dp4(w[r][7], y1.w, u);
+            if constexpr (SUMS) {
+                const long long base = (long long)row0 * (P.n_in / 32) + sb * 8 + q;
+                atomicAdd(P.s + base, s);
+                atomicAdd(P.s2 + base, u);
+            } else {
+                acc[r][t] += sc[r] * dd * (float(s) + float(u) * kInv254);
+            }
+        }
+    }
+}
+
+// IQ3_S codebook, 3 bits per magnitude ((m - 1) / 2); expanded per block at launch
+__device__ const uint16_t kIq3sCodes[512] = {
+#include "iq3s_grid.inc"
+};
+
+__device__ __forceinline__ void load_iq3s_grid(uint32_t* grid) {
+    for (int i = threadIdx.x; i < 512; i += blockDim.x) {
+        const uint32_t c = kIq3sCodes[i];
+        uint32_t w = 0u;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) w |= (2u * ((c >> (3 * k)) & 7u) + 1u) << (8 * k);
+        grid[i] = w;
+    }
+}
+
 // IQ2_XXS codebook, 2 bits per magnitude (index into {8, 25, 43}); expanded per block at launch
 __device__ const uint16_t kIq2xxsCodes[256] = {
 #include "iq2xxs_grid.inc"
@@ -518,9 +581,12 @@ __device__ __forceinline__ const uint8_t* slot_base(const MvParams& P, int slot)
 // sums of one token into P.s / P.s2 (T = RW = 1).
 template <int FMT, int T, int RW, bool SUMS>
 __global__ void __launch_bounds__(256) mv_kernel(const MvParams P) {
-    __shared__ uint2 grid[FMT == F_IQ2_XXS ? 256 : 1];
+    __shared__ uint2 grid[FMT == F_IQ2_XXS || FMT == F_IQ3_S ? 256 : 1];   // 2 KB: either codebook
     if constexpr (FMT == F_IQ2_XXS) {
         load_iq2xxs_grid(grid);
+        __syncthreads();
+    } else if constexpr (FMT == F_IQ3_S) {
+        load_iq3s_grid(reinterpret_cast<uint32_t*>(grid));
         __syncthreads();
     }
     const int lane = threadIdx.x & 31, q = lane & 7, sb0 = lane >> 3;
@@ -559,6 +625,8 @@ __global__ void __launch_bounds__(256) mv_kernel(const MvParams P) {
             else if constexpr (FMT == F_TQ2_0) lane_tq2_0<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (FMT == F_IQ4_XS) lane_iq4xs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (FMT == F_MXFP4) lane_mxfp4<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+            else if constexpr (FMT == F_IQ3_S)
+                lane_iq3s<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, reinterpret_cast<const uint32_t*>(grid));
             else lane_iq2xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, grid);
         }
         if constexpr (!SUMS) {

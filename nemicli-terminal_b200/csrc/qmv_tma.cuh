@@ -213,7 +213,8 @@ __device__ __forceinline__ void load_act(Act<FMT>& a, int u, const int8_t* xq, c
     constexpr int NS = UnitTraits<FMT>::NS;
 #pragma unroll
     for (int i = 0; i < NS; ++i) a.d[i] = a.s[i] = 0.f;
-    if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0 || FMT == F_IQ2_XXS || FMT == F_IQ4_XS || FMT == F_MXFP4) {
+    if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0 || FMT == F_IQ2_XXS || FMT == F_IQ4_XS || FMT == F_MXFP4 ||
+                  FMT == F_IQ3_S) {
         const int o = 32 * u;
         a.q[0] = ldq16<GLOBAL>(xq + o); a.q[1] = ldq16<GLOBAL>(xq + o + 16);
         a.r[0] = ldq16<GLOBAL>(xq2 + o); a.r[1] = ldq16<GLOBAL>(xq2 + o + 16);
@@ -427,6 +428,26 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
             o.wsc[g] = d;
             o.off[g] = d;
         }
+    } else if constexpr (FMT == F_IQ3_S) {
+        const int b = u >> 3, q = u & 7;
+        const uint32_t sb = rs + b * 110;
+        const uint2 qs = lds8_a2(sb + 2 + 8 * q);
+        const uint32_t qh = lds8u(sb + 66 + q);
+        const uint32_t sg = lds16u(sb + 74 + 4 * q) | (lds16u(sb + 76 + 4 * q) << 16);
+        const uint32_t* g3 = reinterpret_cast<const uint32_t*>(grid);
+        uint32_t w0[4], w1[4];
+#pragma unroll
+        for (int l = 0; l < 8; ++l) {
+            const uint32_t idx = (((l < 4 ? qs.x : qs.y) >> (8 * (l & 3))) & 0xFFu) | (((qh >> l) & 1u) << 8);
+            const uint32_t m = sign4_mask(sg >> (4 * l));
+            const uint32_t v = __vsub4(g3[idx] ^ m, m);
+            if (l < 4) w0[l] = v; else w1[l - 4] = v;
+        }
+        o.s[0] = dot4(w1, a.q[1]) + dot4(w0, a.q[0]);
+        o.u[0] = dot4(w1, a.r[1]) + dot4(w0, a.r[0]);
+        const uint32_t ls = (lds8u(sb + 106 + (q >> 1)) >> (4 * (q & 1))) & 15u;
+        o.wsc[0] = h2f(lds16u(sb)) * float(1 + 2 * int(ls));
+        o.off[0] = 0.f;
     } else if constexpr (FMT == F_MXFP4) {
         const uint32_t bl = rs + u * 17;
         const uint4 v = lds16_a2(bl + 1);           // any byte offset: aligned words + funnel shifts
@@ -484,7 +505,9 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
 // sum-unit index (values sharing both scales: 16 for Q6_K, 32 otherwise) of scale group k of unit u
 template <int FMT>
 __device__ __forceinline__ int sum_unit(int u, int k) {
-    if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0 || FMT == F_IQ2_XXS || FMT == F_IQ4_XS || FMT == F_MXFP4) return u;
+    if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0 || FMT == F_IQ2_XXS || FMT == F_IQ4_XS || FMT == F_MXFP4 ||
+                  FMT == F_IQ3_S)
+        return u;
     if constexpr (FMT == F_Q4_K || FMT == F_Q5_K) return 2 * u + k;   // unit u = sub-blocks 2u, 2u + 1 of the row
     const int b = u >> 3, q = u & 7;
     if constexpr (FMT == F_Q6_K) {
@@ -617,6 +640,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), NCW <= 8 ? 2 : 1) mv_tma_kerne
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if constexpr (FMT == F_IQ2_XXS) load_iq2xxs_grid(grid);
+    if constexpr (FMT == F_IQ3_S) load_iq3s_grid(reinterpret_cast<uint32_t*>(grid));     // same 2 KB
     __syncthreads();
 
     if (warp == NCW) {

@@ -16,7 +16,9 @@ tests/test_gguf_iq.py:81-101, zufallsbloecke).  Extra cases pin the corners:
 * Q5_K blocks with scales and mins at 0 and 63 and every fifth bit (qh) set or clear,
 * IQ4_XS blocks whose sub-block scales run through all 64 values and whose nibbles run through all 16
   codebook entries,
-* MXFP4 blocks with every nibble and scale exponents from the subnormal range (0, 1) up to 200.
+* MXFP4 blocks with every nibble and scale exponents from the subnormal range (0, 1) up to 200,
+* IQ3_S blocks whose grid indices run through all 512 codebook entries, whose sign bytes run through
+  all 256 patterns and whose scales run through all 16 values.
 
 Formats added later are generated after the earlier cases, so the earlier arrays stay as they were.
 """
@@ -32,13 +34,14 @@ FORMATS = {"Q4_0": (2, 32, 18), "Q8_0": (8, 32, 34), "Q4_K": (12, 256, 144), "Q6
 LATER = {"Q5_K": (13, 256, 176)}
 LATER2 = {"IQ4_XS": (23, 256, 136)}
 LATER3 = {"MXFP4": (39, 32, 17)}
+LATER4 = {"IQ3_S": (21, 256, 110)}
 SCALE_OFFSETS = {"Q4_0": (0,), "Q8_0": (0,), "Q4_K": (0, 2), "Q6_K": (208,), "IQ2_XXS": (0,), "TQ2_0": (64,),
-                 "Q5_K": (0, 2), "IQ4_XS": (0,), "MXFP4": ()}
+                 "Q5_K": (0, 2), "IQ4_XS": (0,), "MXFP4": (), "IQ3_S": (0,)}
 ROWS, COLS = 3, 512          # a (3, 512) matrix per format
 
 
 def random_blocks(name: str, n_blocks: int, rng: np.random.Generator) -> np.ndarray:
-    _, _, size = {**FORMATS, **LATER, **LATER2, **LATER3}[name]
+    _, _, size = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4}[name]
     raw = rng.integers(0, 256, (n_blocks, size), dtype=np.uint8)
     if name == "MXFP4":
         raw[:, 0] = rng.integers(118, 125, n_blocks)       # scale exponents 2^-10 .. 2^-4
@@ -109,6 +112,18 @@ def mxfp4_cover(rng: np.random.Generator) -> np.ndarray:
     return raw
 
 
+def iq3s_cover(rng: np.random.Generator) -> np.ndarray:
+    """8 blocks = 512 grid slots: grid index k at slot k; sign byte k % 256; scale k % 16 per sub-block."""
+    raw = random_blocks("IQ3_S", 8, rng)
+    for blk in range(8):
+        idx = [64 * blk + g for g in range(64)]
+        raw[blk, 2:66] = [i & 0xFF for i in idx]
+        raw[blk, 66:74] = [sum(((idx[8 * i + j] >> 8) & 1) << j for j in range(8)) for i in range(8)]
+        raw[blk, 74:106] = [(32 * blk + j) % 256 for j in range(32)]
+        raw[blk, 106:110] = [((8 * blk + 2 * i) % 16) | (((8 * blk + 2 * i + 1) % 16) << 4) for i in range(4)]
+    return raw
+
+
 def main(ref_root: str) -> None:
     sys.path.insert(0, ref_root)
     import torch
@@ -118,7 +133,7 @@ def main(ref_root: str) -> None:
     out = {}
 
     def add(key: str, name: str, raw: np.ndarray, rows: int, cols: int) -> None:
-        t, bv, bb = {**FORMATS, **LATER, **LATER2, **LATER3}[name]
+        t, bv, bb = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4}[name]
         flat = np.ascontiguousarray(raw.reshape(-1))
         assert flat.size == rows * cols // bv * bb
         deq = dequantize(torch.from_numpy(flat.copy()), t, rows * cols, torch.float32).numpy()
@@ -144,6 +159,9 @@ def main(ref_root: str) -> None:
     for name, (_, bv, _) in LATER3.items():
         add(name, name, random_blocks(name, ROWS * COLS // bv, rng), ROWS, COLS)
     add("MXFP4_cover", "MXFP4", mxfp4_cover(rng), 2, 256)
+    for name, (_, bv, _) in LATER4.items():
+        add(name, name, random_blocks(name, ROWS * COLS // bv, rng), ROWS, COLS)
+    add("IQ3_S_cover", "IQ3_S", iq3s_cover(rng), 8, 256)
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "dequant_golden.npz")
     np.savez_compressed(path, **out)
     print(f"wrote {path}: {len(out)} arrays")
