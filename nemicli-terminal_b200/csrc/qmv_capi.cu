@@ -126,6 +126,7 @@ int launch(int fmt, const MvParams& P, int T, cudaStream_t st) {
     case F_IQ4_XS: return launch_fmt<F_IQ4_XS>(P, T, st);
     case F_MXFP4: return launch_fmt<F_MXFP4>(P, T, st);
     case F_IQ3_S: return launch_fmt<F_IQ3_S>(P, T, st);
+    case F_IQ3_XXS: return launch_fmt<F_IQ3_XXS>(P, T, st);
     }
     return ST_BAD_FORMAT;
 }
@@ -143,6 +144,7 @@ int launch_sums(int fmt, const MvParams& P, cudaStream_t st) {
     case F_IQ4_XS: return launch_t<F_IQ4_XS, 1, true>(P, st);
     case F_MXFP4: return launch_t<F_MXFP4, 1, true>(P, st);
     case F_IQ3_S: return launch_t<F_IQ3_S, 1, true>(P, st);
+    case F_IQ3_XXS: return launch_t<F_IQ3_XXS, 1, true>(P, st);
     }
     return ST_BAD_FORMAT;
 }
@@ -273,6 +275,7 @@ int launch_tma(int fmt, TmaParams& P, const TmaPlan& pl, cudaStream_t st) {
     case F_IQ4_XS: return launch_tma_fmt<F_IQ4_XS, XF, SUMS>(P, pl, int(grid), st);
     case F_MXFP4: return launch_tma_fmt<F_MXFP4, XF, SUMS>(P, pl, int(grid), st);
     case F_IQ3_S: return launch_tma_fmt<F_IQ3_S, XF, SUMS>(P, pl, int(grid), st);
+    case F_IQ3_XXS: return launch_tma_fmt<F_IQ3_XXS, XF, SUMS>(P, pl, int(grid), st);
     }
     return ST_BAD_FORMAT;
 }

@@ -6,10 +6,10 @@
 
 namespace qmv {
 
-// GGML type ids of the ten formats (the GGUF type table; reference ggufengine/gguf.py:64-77)
+// GGML type ids of the eleven formats (the GGUF type table; reference ggufengine/gguf.py:64-77)
 enum : int {
     F_Q4_0 = 2, F_Q8_0 = 8, F_Q4_K = 12, F_Q5_K = 13, F_Q6_K = 14, F_IQ2_XXS = 16, F_IQ4_XS = 23, F_TQ2_0 = 35,
-    F_MXFP4 = 39, F_IQ3_S = 21
+    F_MXFP4 = 39, F_IQ3_S = 21, F_IQ3_XXS = 18
 };
 
 // status codes returned across the C ABI (include/nemicli_qmv.h)
@@ -37,14 +37,15 @@ __host__ __device__ constexpr int block_values(int f) {
 }
 __host__ __device__ constexpr int block_bytes(int f) {
     return f == F_Q4_0 ? 18 : f == F_Q8_0 ? 34 : f == F_Q4_K ? 144 : f == F_Q5_K ? 176 : f == F_Q6_K ? 210
-         : f == F_IQ4_XS ? 136 : f == F_MXFP4 ? 17 : f == F_IQ3_S ? 110 : 66;
+         : f == F_IQ4_XS ? 136 : f == F_MXFP4 ? 17 : f == F_IQ3_S ? 110
+         : f == F_IQ3_XXS ? 98 : 66;
 }
 // values per integer-sum unit (one weight scale and one activation scale)
 __host__ __device__ constexpr int unit_values(int f) { return f == F_Q6_K ? 16 : 32; }
 
 __host__ __device__ inline bool known_format(int f) {
     return f == F_Q4_0 || f == F_Q8_0 || f == F_Q4_K || f == F_Q5_K || f == F_Q6_K || f == F_IQ2_XXS || f == F_IQ4_XS ||
-           f == F_TQ2_0 || f == F_MXFP4 || f == F_IQ3_S;
+           f == F_TQ2_0 || f == F_MXFP4 || f == F_IQ3_S || f == F_IQ3_XXS;
 }
 // weight rows and blocks of the K-quant formats with 16-byte header words are read 16 bytes at a time;
 // MXFP4's 17-byte blocks start at any byte, and their loads stay inside the tensor when it starts on a

@@ -520,6 +520,72 @@ __device__ __forceinline__ void lane_iq3s(const uint8_t* const (&rows)[RW], int 
     }
 }
 
+// ---- IQ3_XXS: 98 B = d (f16), qs[64], aux u32[8] (quant.py:322-331).  Lane q takes sub-block q: values
+// 4k..4k+3 are codebook entry qs[8q + k]; aux[q] holds four 7-bit sign groups of 8 values (parity gives
+// the 8th sign) and the 4-bit scale s in bits 28..31: weight scale d * (0.25 + 0.5 s).
+template <int T, int RW, bool SUMS>
+__device__ __forceinline__ void lane_iq3xxs(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                            const Tok<T>& tk, float (&acc)[RW][T], int row0,
+                                            const uint32_t* __restrict__ grid) {
+    uint32_t w[RW][8];
+    float sc[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        const uint8_t* b = rows[r] + (long long)sb * 98;
+        const uint2 qs = ldw8_a2(b + 2 + 8 * q);
+        const uint32_t aux = ldw2(b + 66 + 4 * q) | (ldw2(b + 68 + 4 * q) << 16);
+        sc[r] = h2f(ldw2(b)) * (0.25f + 0.5f * float(aux >> 28));
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            const uint32_t s7 = (aux >> (7 * l)) & 127u;
+            const uint32_t s8 = s7 | (uint32_t(__popc(s7) & 1) << 7);
+            const uint32_t mlo = sign4_mask(s8), mhi = sign4_mask(s8 >> 4);
+            const uint32_t word = l < 2 ? qs.x : qs.y;
+            w[r][2 * l] = __vsub4(grid[(word >> (16 * (l & 1))) & 0xFFu] ^ mlo, mlo);
+            w[r][2 * l + 1] = __vsub4(grid[(word >> (16 * (l & 1) + 8)) & 0xFFu] ^ mhi, mhi);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const long long o = tk.tb[t] + (long long)sb * 256 + 32 * q;
+        const int4 x0 = ldx16(P.xq + o), x1 = ldx16(P.xq + o + 16);
+        const int4 y0 = ldx16(P.xq2 + o), y1 = ldx16(P.xq2 + o + 16);
+        const float dd = __ldg(P.xd + ((tk.tb[t] + (long long)sb * 256) >> 5) + q);
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            int s = dp4(w[r][0], x0.x, 0); s = dp4(w[r][1], x0.y, s); s = dp4(w[r][2], x0.z, s); s = dp4(w[r][3], x0.w, s);
+            s = dp4(w[r][4], x1.x, s); s = dp4(w[r][5], x1.y, s); s = dp4(w[r][6], x1.z, s); s = dp4(w[r][7], x1.w, s);
+            int u = dp4(w[r][0], y0.x, 0); u = dp4(w[r][1], y0.y, u); u = dp4(w[r][2], y0.z, u); u = dp4(w[r][3], y0.w, u);
+            u = dp4(w[r][4], y1.x, u); u = dp4(w[r][5], y1.y, u); u = dp4(w[r][6], y1.z, u); u = dp4(w[r][7], y1.w, u);
+            if constexpr (SUMS) {
+                const long long base = (long long)row0 * (P.n_in / 32) + sb * 8 + q;
+                atomicAdd(P.s + base, s);
+                atomicAdd(P.s2 + base, u);
+            } else {
+                acc[r][t] += sc[r] * dd * (float(s) + float(u) * kInv254);
+            }
+        }
+    }
+}
+
+// IQ3_XXS codebook, 3 bits per magnitude (index into {4, 12, 20, 28, 36, 44, 52, 62})
+__device__ const uint16_t kIq3xxsCodes[256] = {
+#include "iq3xxs_grid.inc"
+};
+
+__device__ __forceinline__ void load_iq3xxs_grid(uint32_t* grid) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+        const uint32_t c = kIq3xxsCodes[i];
+        uint32_t w = 0u;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t lv = (c >> (3 * k)) & 7u;
+            w |= (lv == 7u ? 62u : 4u + 8u * lv) << (8 * k);
+        }
+        grid[i] = w;
+    }
+}
+
 // IQ3_S codebook, 3 bits per magnitude ((m - 1) / 2); expanded per block at launch
 __device__ const uint16_t kIq3sCodes[512] = {
 #include "iq3s_grid.inc"
@@ -581,12 +647,15 @@ __device__ __forceinline__ const uint8_t* slot_base(const MvParams& P, int slot)
 // sums of one token into P.s / P.s2 (T = RW = 1).
 template <int FMT, int T, int RW, bool SUMS>
 __global__ void __launch_bounds__(256) mv_kernel(const MvParams P) {
-    __shared__ uint2 grid[FMT == F_IQ2_XXS || FMT == F_IQ3_S ? 256 : 1];   // 2 KB: either codebook
+    __shared__ uint2 grid[FMT == F_IQ2_XXS || FMT == F_IQ3_S || FMT == F_IQ3_XXS ? 256 : 1];   // 2 KB: a codebook
     if constexpr (FMT == F_IQ2_XXS) {
         load_iq2xxs_grid(grid);
         __syncthreads();
     } else if constexpr (FMT == F_IQ3_S) {
         load_iq3s_grid(reinterpret_cast<uint32_t*>(grid));
+        __syncthreads();
+    } else if constexpr (FMT == F_IQ3_XXS) {
+        load_iq3xxs_grid(reinterpret_cast<uint32_t*>(grid));
         __syncthreads();
     }
     const int lane = threadIdx.x & 31, q = lane & 7, sb0 = lane >> 3;
@@ -627,6 +696,8 @@ __global__ void __launch_bounds__(256) mv_kernel(const MvParams P) {
             else if constexpr (FMT == F_MXFP4) lane_mxfp4<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (FMT == F_IQ3_S)
                 lane_iq3s<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, reinterpret_cast<const uint32_t*>(grid));
+            else if constexpr (FMT == F_IQ3_XXS)
+                lane_iq3xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, reinterpret_cast<const uint32_t*>(grid));
             else lane_iq2xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, grid);
         }
         if constexpr (!SUMS) {

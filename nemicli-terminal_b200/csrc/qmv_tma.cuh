@@ -214,7 +214,7 @@ __device__ __forceinline__ void load_act(Act<FMT>& a, int u, const int8_t* xq, c
 #pragma unroll
     for (int i = 0; i < NS; ++i) a.d[i] = a.s[i] = 0.f;
     if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0 || FMT == F_IQ2_XXS || FMT == F_IQ4_XS || FMT == F_MXFP4 ||
-                  FMT == F_IQ3_S) {
+                  FMT == F_IQ3_S || FMT == F_IQ3_XXS) {
         const int o = 32 * u;
         a.q[0] = ldq16<GLOBAL>(xq + o); a.q[1] = ldq16<GLOBAL>(xq + o + 16);
         a.r[0] = ldq16<GLOBAL>(xq2 + o); a.r[1] = ldq16<GLOBAL>(xq2 + o + 16);
@@ -428,6 +428,27 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
             o.wsc[g] = d;
             o.off[g] = d;
         }
+    } else if constexpr (FMT == F_IQ3_XXS) {
+        const int b = u >> 3, q = u & 7;
+        const uint32_t sb = rs + b * 98;
+        const uint2 qs = lds8_a2(sb + 2 + 8 * q);
+        const uint32_t aux = lds16u(sb + 66 + 4 * q) | (lds16u(sb + 68 + 4 * q) << 16);
+        const uint32_t* g3 = reinterpret_cast<const uint32_t*>(grid);
+        uint32_t w[8];
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+            const uint32_t s7 = (aux >> (7 * l)) & 127u;
+            const uint32_t s8 = s7 | (uint32_t(__popc(s7) & 1) << 7);
+            const uint32_t mlo = sign4_mask(s8), mhi = sign4_mask(s8 >> 4);
+            const uint32_t word = l < 2 ? qs.x : qs.y;
+            w[2 * l] = __vsub4(g3[(word >> (16 * (l & 1))) & 0xFFu] ^ mlo, mlo);
+            w[2 * l + 1] = __vsub4(g3[(word >> (16 * (l & 1) + 8)) & 0xFFu] ^ mhi, mhi);
+        }
+        const uint32_t w0[4] = {w[0], w[1], w[2], w[3]}, w1[4] = {w[4], w[5], w[6], w[7]};
+        o.s[0] = dot4(w1, a.q[1]) + dot4(w0, a.q[0]);
+        o.u[0] = dot4(w1, a.r[1]) + dot4(w0, a.r[0]);
+        o.wsc[0] = h2f(lds16u(sb)) * (0.25f + 0.5f * float(aux >> 28));
+        o.off[0] = 0.f;
     } else if constexpr (FMT == F_IQ3_S) {
         const int b = u >> 3, q = u & 7;
         const uint32_t sb = rs + b * 110;
@@ -506,7 +527,7 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
 template <int FMT>
 __device__ __forceinline__ int sum_unit(int u, int k) {
     if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0 || FMT == F_IQ2_XXS || FMT == F_IQ4_XS || FMT == F_MXFP4 ||
-                  FMT == F_IQ3_S)
+                  FMT == F_IQ3_S || FMT == F_IQ3_XXS)
         return u;
     if constexpr (FMT == F_Q4_K || FMT == F_Q5_K) return 2 * u + k;   // unit u = sub-blocks 2u, 2u + 1 of the row
     const int b = u >> 3, q = u & 7;
@@ -641,6 +662,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), NCW <= 8 ? 2 : 1) mv_tma_kerne
     }
     if constexpr (FMT == F_IQ2_XXS) load_iq2xxs_grid(grid);
     if constexpr (FMT == F_IQ3_S) load_iq3s_grid(reinterpret_cast<uint32_t*>(grid));     // same 2 KB
+    if constexpr (FMT == F_IQ3_XXS) load_iq3xxs_grid(reinterpret_cast<uint32_t*>(grid));
     __syncthreads();
 
     if (warp == NCW) {

@@ -2,7 +2,7 @@
 
 The reference names no dataset or public benchmark for this path; its configs are synthetic.  The
 generators below follow each config's stated distributions and write the exact GGUF block layouts
-(ggufengine/quant.py documents them: Q4_0 :60, Q8_0 :46, Q4_K :111, Q5_K :123, Q6_K :140, IQ3_S :334, IQ4_XS :378, MXFP4 :394, TQ2_0 :417,
+(ggufengine/quant.py documents them: Q4_0 :60, Q8_0 :46, Q4_K :111, Q5_K :123, Q6_K :140, IQ3_XXS :322, IQ3_S :334, IQ4_XS :378, MXFP4 :394, TQ2_0 :417,
 IQ2_XXS :235).  Everything is torch, so it runs on the CPU (tests) or on the GPU (bench, where the
 largest stacks are several GB).
 """
@@ -94,6 +94,9 @@ def blocks(fmt: str, n_rows: int, n_in: int, seed: int = 0, device="cpu",
     elif fmt == "IQ4_XS":                   # d = |N| * 0.01 / 32; 6-bit sub-block scales and nibbles uniform
         d = _f16_bytes(_abs_normal(nb, 0.01 / 32, g, device))
         out = torch.cat([d, _bytes(nb, 134, g, device)], 1)
+    elif fmt == "IQ3_XXS":                  # d = |N| * 0.01 / 32; grid indices, sign groups, scales uniform
+        d = _f16_bytes(_abs_normal(nb, 0.01 / 32, g, device))
+        out = torch.cat([d, _bytes(nb, 96, g, device)], 1)
     elif fmt == "IQ3_S":                    # d = |N| * 0.01 / 16; grid indices, signs and 4-bit scales uniform
         d = _f16_bytes(_abs_normal(nb, 0.01 / 16, g, device))
         out = torch.cat([d, _bytes(nb, 108, g, device)], 1)

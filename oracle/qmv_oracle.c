@@ -11,23 +11,24 @@
  *     restatement uses IEEE-rounded division and an explicit fused multiply-add so that it is
  *     reproducible bit for bit on the GPU (the kernels do the same).  Against the reference's
  *     fast-math build a quantised value can differ by one unit on a rounding tie.
- *   - the block dequantisers of ggufengine/quant.py for the ten in-scope formats:
+ *   - the block dequantisers of ggufengine/quant.py for the eleven in-scope formats:
  *     deq_q4_0 :60, deq_q8_0 :46, deq_q4_k :111 (+ _scale_min_k4 :99), deq_q5_k :123, deq_q6_k :140,
  *     deq_iq4_xs :378 (codebook KVALUES_IQ4NL, ggufengine/iqtabellen.py:7), deq_mxfp4 :394
  *     (KVALUES_MXFP4 :391, scale 2^(e-128) as the reference builds its float bits), deq_iq3_s :334
- *     (codebook ggufengine/iqtabellen.py IQ3S_GRID, kept compact in csrc/iq3s_grid.inc),
+ *     (codebook ggufengine/iqtabellen.py IQ3S_GRID, kept compact in csrc/iq3s_grid.inc), deq_iq3_xxs
+ *     :322 (IQ3XXS_GRID, compact in csrc/iq3xxs_grid.inc),
  *     deq_tq2_0 :417, deq_iq2_xxs :235 (codebook ggufengine/iqtabellen.py:11).  The operation
  *     order of each fp32 expression follows quant.py, so results are bit-identical.
  *   - the integer dot products of the reference's int8 path (ggufengine/mmvq.py:341-419 for
  *     Q4_K: per lane S = sum nibble*xq and S2 = sum nibble*xq2; :421-482 for Q6_K with signed
- *     q-32), and the same formula family for Q4_0, Q8_0, Q5_K, TQ2_0, IQ2_XXS, IQ3_S, IQ4_XS, MXFP4
+ *     q-32), and the same formula family for Q4_0, Q8_0, Q5_K, TQ2_0, IQ2_XXS, IQ3_XXS, IQ3_S, IQ4_XS, MXFP4
  *     (which the reference only has as float kernels, ggufengine/cudakern.py:315,307,379,432,187;
  *     Q5_K is Q4_K's sum with a 5-bit unsigned code, IQ4_XS and MXFP4 sum int8 codebook values).  Integer sums do not
  *     depend on how a kernel groups them, so the per-unit sums below are the exact values any
  *     correct kernel must produce from the same Eingang.
  *
  * Sum units (the values that share one weight scale and one activation scale):
- *   Q4_K, Q5_K, Q4_0, Q8_0, TQ2_0, IQ2_XXS, IQ3_S, IQ4_XS, MXFP4: 32 values (n_in/32 units per row);
+ *   Q4_K, Q5_K, Q4_0, Q8_0, TQ2_0, IQ2_XXS, IQ3_XXS, IQ3_S, IQ4_XS, MXFP4: 32 values (n_in/32 units);
  *   Q6_K: 16.
  *   Q4_0 and TQ2_0 sums use the unsigned code (the -8 / -1 offset is applied with xs).
  *
@@ -46,7 +47,7 @@
 #endif
 
 enum { T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ2_XXS = 16, T_IQ4_XS = 23, T_TQ2_0 = 35, T_MXFP4 = 39,
-       T_IQ3_S = 21 };
+       T_IQ3_S = 21, T_IQ3_XXS = 18 };
 
 /* IQ4_XS codebook (part of the format: the reference's KVALUES_IQ4NL) */
 static const int8_t IQ4NL_VALUES[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
@@ -82,6 +83,11 @@ static int iq3s_value(const uint8_t* b, int ib, int t) {
     return ((b[74 + 4 * ib + t / 8] >> (t % 8)) & 1) ? -g : g;
 }
 static int iq3s_scale(const uint8_t* b, int ib) { return (b[106 + ib / 2] >> (4 * (ib & 1))) & 15; }
+
+static const uint16_t IQ3XXS_CODES[256] = {
+#include "../nemicli-terminal_b200/csrc/iq3xxs_grid.inc"
+};
+static const uint8_t IQ3XXS_LEVELS[8] = {4, 12, 20, 28, 36, 44, 52, 62};
 
 /* ---- scalars -------------------------------------------------------------------------------- */
 
@@ -121,7 +127,8 @@ static uint32_t rd32(const uint8_t* p) {
 int orc_block_values(int fmt) {
     switch (fmt) {
     case T_Q4_0: case T_Q8_0: case T_MXFP4: return 32;
-    case T_Q4_K: case T_Q5_K: case T_Q6_K: case T_IQ2_XXS: case T_IQ3_S: case T_IQ4_XS: case T_TQ2_0: return 256;
+    case T_Q4_K: case T_Q5_K: case T_Q6_K: case T_IQ2_XXS: case T_IQ3_XXS: case T_IQ3_S: case T_IQ4_XS:
+    case T_TQ2_0: return 256;
     }
     return 0;
 }
@@ -136,6 +143,7 @@ int orc_block_bytes(int fmt) {
     case T_IQ2_XXS: return 66;
     case T_IQ4_XS: return 136;
     case T_IQ3_S: return 110;
+    case T_IQ3_XXS: return 98;
     case T_TQ2_0: return 66;
     case T_MXFP4: return 17;
     }
@@ -213,6 +221,16 @@ static int iq2xxs_value(const uint8_t* b, int ib, int e) {
     iq2xxs_entry(q[l], g);
     const uint32_t s = ksign8((aux1 >> (7 * l)) & 127);
     return (s >> j) & 1 ? -(int)g[j] : (int)g[j];
+}
+
+/* signed value t (0..31) of sub-block ib of an IQ3_XXS block: d (f16), qs[64] at 2 (codebook index of
+   values 4k..4k+3 of the sub-block at qs[8 ib + k]), aux u32[8] at 66: four 7-bit sign groups of 8 values
+   (parity gives the 8th sign) and a 4-bit scale in bits 28..31 (quant.py:322-331) */
+static int iq3xxs_value(const uint8_t* b, int ib, int t) {
+    const uint32_t aux = rd32(b + 66 + 4 * ib);
+    const int g = IQ3XXS_LEVELS[(IQ3XXS_CODES[b[2 + 8 * ib + t / 4]] >> (3 * (t % 4))) & 7];
+    const uint32_t s = ksign8((aux >> (7 * (t / 8))) & 127);
+    return (s >> (t % 8)) & 1 ? -g : g;
 }
 
 int orc_dequant(int fmt, const uint8_t* raw, long long n_values, float* out) {
@@ -293,6 +311,14 @@ int orc_dequant(int fmt, const uint8_t* raw, long long n_values, float* out) {
             }
             break;
         }
+        case T_IQ3_XXS: {
+            const float d = f16(b);
+            for (int ib = 0; ib < 8; ++ib) {
+                const float db = d * (0.25f + 0.5f * (float)(rd32(b + 66 + 4 * ib) >> 28));
+                for (int t = 0; t < 32; ++t) o[32 * ib + t] = (float)iq3xxs_value(b, ib, t) * db;
+            }
+            break;
+        }
         case T_IQ3_S: {
             const float d = f16(b);
             for (int ib = 0; ib < 8; ++ib) {
@@ -355,6 +381,7 @@ static int code_of(int fmt, const uint8_t* b, int v) {
     case T_IQ2_XXS: return iq2xxs_value(b, v >> 5, v & 31);
     case T_MXFP4: return MXFP4_VALUES[(b[1 + (v & 15)] >> (4 * (v >> 4))) & 15];
     case T_IQ3_S: return iq3s_value(b, v >> 5, v & 31);
+    case T_IQ3_XXS: return iq3xxs_value(b, v >> 5, v & 31);
     case T_IQ4_XS: {
         const int ib = v >> 5, j = v & 31;
         return IQ4NL_VALUES[(b[8 + 16 * ib + (j & 15)] >> (4 * (j >> 4))) & 15];
@@ -407,6 +434,7 @@ static void unit_scales(int fmt, const uint8_t* b, int u, double* wscale, double
     }
     case T_MXFP4: *wscale = mxfp4_scale(b[0]); *offs = 0.0; return;
     case T_IQ3_S: *wscale = (double)f16(b) * (double)(1 + 2 * iq3s_scale(b, u)); *offs = 0.0; return;
+    case T_IQ3_XXS: *wscale = (double)f16(b) * (0.25 + 0.5 * (double)(rd32(b + 66 + 4 * u) >> 28)); *offs = 0.0; return;
     case T_IQ4_XS: {
         const int sh = b[2] | (b[3] << 8);
         const int ls = ((b[4 + u / 2] >> (4 * (u & 1))) & 15) | (((sh >> (2 * u)) & 3) << 4);

@@ -18,7 +18,9 @@ tests/test_gguf_iq.py:81-101, zufallsbloecke).  Extra cases pin the corners:
   codebook entries,
 * MXFP4 blocks with every nibble and scale exponents from the subnormal range (0, 1) up to 200,
 * IQ3_S blocks whose grid indices run through all 512 codebook entries, whose sign bytes run through
-  all 256 patterns and whose scales run through all 16 values.
+  all 256 patterns and whose scales run through all 16 values,
+* IQ3_XXS blocks whose grid indices run through all 256 codebook entries, whose sign groups run through
+  all 128 patterns and whose scales run through all 16 values.
 
 Formats added later are generated after the earlier cases, so the earlier arrays stay as they were.
 """
@@ -35,13 +37,14 @@ LATER = {"Q5_K": (13, 256, 176)}
 LATER2 = {"IQ4_XS": (23, 256, 136)}
 LATER3 = {"MXFP4": (39, 32, 17)}
 LATER4 = {"IQ3_S": (21, 256, 110)}
+LATER5 = {"IQ3_XXS": (18, 256, 98)}
 SCALE_OFFSETS = {"Q4_0": (0,), "Q8_0": (0,), "Q4_K": (0, 2), "Q6_K": (208,), "IQ2_XXS": (0,), "TQ2_0": (64,),
-                 "Q5_K": (0, 2), "IQ4_XS": (0,), "MXFP4": (), "IQ3_S": (0,)}
+                 "Q5_K": (0, 2), "IQ4_XS": (0,), "MXFP4": (), "IQ3_S": (0,), "IQ3_XXS": (0,)}
 ROWS, COLS = 3, 512          # a (3, 512) matrix per format
 
 
 def random_blocks(name: str, n_blocks: int, rng: np.random.Generator) -> np.ndarray:
-    _, _, size = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4}[name]
+    _, _, size = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4, **LATER5}[name]
     raw = rng.integers(0, 256, (n_blocks, size), dtype=np.uint8)
     if name == "MXFP4":
         raw[:, 0] = rng.integers(118, 125, n_blocks)       # scale exponents 2^-10 .. 2^-4
@@ -124,6 +127,18 @@ def iq3s_cover(rng: np.random.Generator) -> np.ndarray:
     return raw
 
 
+def iq3xxs_cover(rng: np.random.Generator) -> np.ndarray:
+    """4 blocks = 256 grid slots: grid index k at slot k; sign group k % 128; scale per sub-block."""
+    raw = random_blocks("IQ3_XXS", 4, rng)
+    for blk in range(4):
+        raw[blk, 2:66] = [64 * blk + k for k in range(64)]
+        for ib in range(8):
+            signs = [(32 * blk + 4 * ib + l) % 128 for l in range(4)]
+            aux = signs[0] | (signs[1] << 7) | (signs[2] << 14) | (signs[3] << 21) | (((8 * blk + ib) % 16) << 28)
+            raw[blk, 66 + 4 * ib:70 + 4 * ib] = np.frombuffer(np.uint32(aux).tobytes(), dtype=np.uint8)
+    return raw
+
+
 def main(ref_root: str) -> None:
     sys.path.insert(0, ref_root)
     import torch
@@ -133,7 +148,7 @@ def main(ref_root: str) -> None:
     out = {}
 
     def add(key: str, name: str, raw: np.ndarray, rows: int, cols: int) -> None:
-        t, bv, bb = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4}[name]
+        t, bv, bb = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4, **LATER5}[name]
         flat = np.ascontiguousarray(raw.reshape(-1))
         assert flat.size == rows * cols // bv * bb
         deq = dequantize(torch.from_numpy(flat.copy()), t, rows * cols, torch.float32).numpy()
@@ -162,6 +177,9 @@ def main(ref_root: str) -> None:
     for name, (_, bv, _) in LATER4.items():
         add(name, name, random_blocks(name, ROWS * COLS // bv, rng), ROWS, COLS)
     add("IQ3_S_cover", "IQ3_S", iq3s_cover(rng), 8, 256)
+    for name, (_, bv, _) in LATER5.items():
+        add(name, name, random_blocks(name, ROWS * COLS // bv, rng), ROWS, COLS)
+    add("IQ3_XXS_cover", "IQ3_XXS", iq3xxs_cover(rng), 4, 256)
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "dequant_golden.npz")
     np.savez_compressed(path, **out)
     print(f"wrote {path}: {len(out)} arrays")
