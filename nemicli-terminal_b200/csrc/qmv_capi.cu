@@ -127,6 +127,10 @@ int launch(int fmt, const MvParams& P, int T, cudaStream_t st) {
     case F_MXFP4: return launch_fmt<F_MXFP4>(P, T, st);
     case F_IQ3_S: return launch_fmt<F_IQ3_S>(P, T, st);
     case F_IQ3_XXS: return launch_fmt<F_IQ3_XXS>(P, T, st);
+    case F_Q4_1: return launch_fmt<F_Q4_1>(P, T, st);
+    case F_Q5_0: return launch_fmt<F_Q5_0>(P, T, st);
+    case F_Q5_1: return launch_fmt<F_Q5_1>(P, T, st);
+    case F_IQ4_NL: return launch_fmt<F_IQ4_NL>(P, T, st);
     }
     return ST_BAD_FORMAT;
 }
@@ -145,6 +149,10 @@ int launch_sums(int fmt, const MvParams& P, cudaStream_t st) {
     case F_MXFP4: return launch_t<F_MXFP4, 1, true>(P, st);
     case F_IQ3_S: return launch_t<F_IQ3_S, 1, true>(P, st);
     case F_IQ3_XXS: return launch_t<F_IQ3_XXS, 1, true>(P, st);
+    case F_Q4_1: return launch_t<F_Q4_1, 1, true>(P, st);
+    case F_Q5_0: return launch_t<F_Q5_0, 1, true>(P, st);
+    case F_Q5_1: return launch_t<F_Q5_1, 1, true>(P, st);
+    case F_IQ4_NL: return launch_t<F_IQ4_NL, 1, true>(P, st);
     }
     return ST_BAD_FORMAT;
 }
@@ -276,6 +284,10 @@ int launch_tma(int fmt, TmaParams& P, const TmaPlan& pl, cudaStream_t st) {
     case F_MXFP4: return launch_tma_fmt<F_MXFP4, XF, SUMS>(P, pl, int(grid), st);
     case F_IQ3_S: return launch_tma_fmt<F_IQ3_S, XF, SUMS>(P, pl, int(grid), st);
     case F_IQ3_XXS: return launch_tma_fmt<F_IQ3_XXS, XF, SUMS>(P, pl, int(grid), st);
+    case F_Q4_1: return launch_tma_fmt<F_Q4_1, XF, SUMS>(P, pl, int(grid), st);
+    case F_Q5_0: return launch_tma_fmt<F_Q5_0, XF, SUMS>(P, pl, int(grid), st);
+    case F_Q5_1: return launch_tma_fmt<F_Q5_1, XF, SUMS>(P, pl, int(grid), st);
+    case F_IQ4_NL: return launch_tma_fmt<F_IQ4_NL, XF, SUMS>(P, pl, int(grid), st);
     }
     return ST_BAD_FORMAT;
 }

@@ -6,11 +6,15 @@
 
 namespace qmv {
 
-// GGML type ids of the eleven formats (the GGUF type table; reference ggufengine/gguf.py:64-77)
+// GGML type ids of the fifteen formats (the GGUF type table; reference ggufengine/gguf.py:64-77)
 enum : int {
     F_Q4_0 = 2, F_Q8_0 = 8, F_Q4_K = 12, F_Q5_K = 13, F_Q6_K = 14, F_IQ2_XXS = 16, F_IQ4_XS = 23, F_TQ2_0 = 35,
-    F_MXFP4 = 39, F_IQ3_S = 21, F_IQ3_XXS = 18
+    F_MXFP4 = 39, F_IQ3_S = 21, F_IQ3_XXS = 18, F_Q4_1 = 3, F_Q5_0 = 6, F_Q5_1 = 7, F_IQ4_NL = 20
 };
+// the 32-value block formats (one block per integer-sum unit)
+__host__ __device__ constexpr bool b32_format(int f) {
+    return f == F_Q4_0 || f == F_Q8_0 || f == F_MXFP4 || f == F_Q4_1 || f == F_Q5_0 || f == F_Q5_1 || f == F_IQ4_NL;
+}
 
 // status codes returned across the C ABI (include/nemicli_qmv.h)
 enum : int {
@@ -33,10 +37,10 @@ constexpr int kMaxTokens = 8;           // tokens per launch of the dp4a kernels
 constexpr float kInv254 = 1.0f / 254.0f;
 
 __host__ __device__ constexpr int block_values(int f) {
-    return (f == F_Q4_0 || f == F_Q8_0 || f == F_MXFP4) ? 32 : 256;
+    return b32_format(f) ? 32 : 256;
 }
 __host__ __device__ constexpr int block_bytes(int f) {
-    return f == F_Q4_0 ? 18 : f == F_Q8_0 ? 34 : f == F_Q4_K ? 144 : f == F_Q5_K ? 176 : f == F_Q6_K ? 210
+    return f == F_Q4_0 || f == F_IQ4_NL ? 18 : f == F_Q4_1 ? 20 : f == F_Q5_0 ? 22 : f == F_Q5_1 ? 24 : f == F_Q8_0 ? 34 : f == F_Q4_K ? 144 : f == F_Q5_K ? 176 : f == F_Q6_K ? 210
          : f == F_IQ4_XS ? 136 : f == F_MXFP4 ? 17 : f == F_IQ3_S ? 110
          : f == F_IQ3_XXS ? 98 : 66;
 }
@@ -45,7 +49,8 @@ __host__ __device__ constexpr int unit_values(int f) { return f == F_Q6_K ? 16 :
 
 __host__ __device__ inline bool known_format(int f) {
     return f == F_Q4_0 || f == F_Q8_0 || f == F_Q4_K || f == F_Q5_K || f == F_Q6_K || f == F_IQ2_XXS || f == F_IQ4_XS ||
-           f == F_TQ2_0 || f == F_MXFP4 || f == F_IQ3_S || f == F_IQ3_XXS;
+           f == F_TQ2_0 || f == F_MXFP4 || f == F_IQ3_S || f == F_IQ3_XXS || f == F_Q4_1 || f == F_Q5_0 ||
+           f == F_Q5_1 || f == F_IQ4_NL;
 }
 // weight rows and blocks of the K-quant formats with 16-byte header words are read 16 bytes at a time;
 // MXFP4's 17-byte blocks start at any byte, and their loads stay inside the tensor when it starts on a
@@ -135,8 +140,10 @@ __device__ __forceinline__ uint32_t iq4nl_bytes(uint32_t idx) {
 __device__ __forceinline__ uint32_t mxfp4_bytes(uint32_t idx) {
     return lut16_bytes<kv4(0, 1, 2, 3), kv4(4, 6, 8, 12), kv4(0, -1, -2, -3), kv4(-4, -6, -8, -12)>(idx);
 }
-// byte masks of four sign bits (bit j set -> byte j = 0xFF): bit j moves to bit 8 j
-__device__ __forceinline__ uint32_t sign4_mask(uint32_t s4) { return (((s4 & 15u) * 0x00204081u) & 0x01010101u) * 0xFFu; }
+// four bits to four bytes: bit j -> bit 0 of byte j
+__device__ __forceinline__ uint32_t spread4(uint32_t s4) { return ((s4 & 15u) * 0x00204081u) & 0x01010101u; }
+// byte masks of four sign bits (bit j set -> byte j = 0xFF)
+__device__ __forceinline__ uint32_t sign4_mask(uint32_t s4) { return spread4(s4) * 0xFFu; }
 // MXFP4 block scale 2^(e-128) from its float bits (subnormal for e < 2), as the reference builds it
 __device__ __forceinline__ float mxfp4_scale(uint32_t e) {
     return __uint_as_float(e < 2 ? (0x00200000u << e) : ((e - 1) << 23));

@@ -246,6 +246,65 @@ __device__ __forceinline__ void lane_q4_0(const uint8_t* const (&rows)[RW], int 
     }
 }
 
+// ---- Q4_1 (20 B: d, m, 16 B nibbles), Q5_0 (22 B: d, qh u32, nibbles), Q5_1 (24 B: d, m, qh, nibbles),
+// IQ4_NL (18 B: d, 16 B codebook indices); byte j holds values j (low nibble) and 16 + j, bit j of qh is
+// bit 4 of value j (quant.py:67-95, 264-270).  Lane q takes block 8*sb + q.  Unsigned codes for the
+// Q4_1 / Q5_x formats: y = d xd (S + S2/254) - off xs with off = -m (Q4_1, Q5_1) or 16 d (Q5_0).
+template <int FMT>
+__device__ __forceinline__ void b32_codes(const uint8_t* b, uint32_t (&lo)[4], uint32_t (&hi)[4], float& d, float& off) {
+    d = h2f(ldw2(b));
+    constexpr int qo = FMT == F_Q4_1 ? 4 : FMT == F_Q5_0 ? 6 : FMT == F_Q5_1 ? 8 : 2;
+    const uint4 v = ldw16_a2(b + qo);
+    const uint32_t V[4] = {v.x, v.y, v.z, v.w};
+    uint32_t qh = 0u;
+    if constexpr (FMT == F_Q5_0) qh = ldw2(b + 2) | (ldw2(b + 4) << 16);
+    if constexpr (FMT == F_Q5_1) qh = ldw2(b + 4) | (ldw2(b + 6) << 16);
+    off = FMT == F_Q5_0 ? 16.0f * d : (FMT == F_Q4_1 || FMT == F_Q5_1) ? -h2f(ldw2(b + 2)) : 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if constexpr (FMT == F_IQ4_NL) {
+            lo[i] = iq4nl_bytes(V[i] & 0x0F0F0F0Fu);
+            hi[i] = iq4nl_bytes((V[i] >> 4) & 0x0F0F0F0Fu);
+        } else {
+            lo[i] = (V[i] & 0x0F0F0F0Fu) | (spread4(qh >> (4 * i)) << 4);
+            hi[i] = ((V[i] >> 4) & 0x0F0F0F0Fu) | (spread4(qh >> (16 + 4 * i)) << 4);
+        }
+    }
+}
+
+template <int FMT, int T, int RW, bool SUMS>
+__device__ __forceinline__ void lane_b32(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                         const Tok<T>& tk, float (&acc)[RW][T], int row0) {
+    const int blk = sb * 8 + q;
+    if (blk >= P.n_in / 32) return;
+    uint32_t lo[RW][4], hi[RW][4];
+    float d[RW], off[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) b32_codes<FMT>(rows[r] + (long long)blk * block_bytes(FMT), lo[r], hi[r], d[r], off[r]);
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const long long o = tk.tb[t] + (long long)blk * 32;
+        const int4 xa = ldx16(P.xq + o), xb = ldx16(P.xq + o + 16);
+        const int4 ya = ldx16(P.xq2 + o), yb = ldx16(P.xq2 + o + 16);
+        const long long g = (tk.tb[t] >> 5) + blk;
+        const float dd = __ldg(P.xd + g), ss = __ldg(P.xs + g);
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            int s = dp4(lo[r][0], xa.x, 0); s = dp4(lo[r][1], xa.y, s); s = dp4(lo[r][2], xa.z, s); s = dp4(lo[r][3], xa.w, s);
+            s = dp4(hi[r][0], xb.x, s); s = dp4(hi[r][1], xb.y, s); s = dp4(hi[r][2], xb.z, s); s = dp4(hi[r][3], xb.w, s);
+            int u = dp4(lo[r][0], ya.x, 0); u = dp4(lo[r][1], ya.y, u); u = dp4(lo[r][2], ya.z, u); u = dp4(lo[r][3], ya.w, u);
+            u = dp4(hi[r][0], yb.x, u); u = dp4(hi[r][1], yb.y, u); u = dp4(hi[r][2], yb.z, u); u = dp4(hi[r][3], yb.w, u);
+            if constexpr (SUMS) {
+                const long long base = (long long)row0 * (P.n_in / 32) + blk;
+                atomicAdd(P.s + base, s);
+                atomicAdd(P.s2 + base, u);
+            } else {
+                acc[r][t] += d[r] * dd * (float(s) + float(u) * kInv254) - off[r] * ss;
+            }
+        }
+    }
+}
+
 // ---- Q8_0: 34 B = d (f16), int8[32] (quant.py:46-50).  Lane q takes block 8*sb + q.
 template <int T, int RW, bool SUMS>
 __device__ __forceinline__ void lane_q8_0(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
@@ -698,6 +757,8 @@ __global__ void __launch_bounds__(256) mv_kernel(const MvParams P) {
                 lane_iq3s<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, reinterpret_cast<const uint32_t*>(grid));
             else if constexpr (FMT == F_IQ3_XXS)
                 lane_iq3xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, reinterpret_cast<const uint32_t*>(grid));
+            else if constexpr (FMT == F_Q4_1 || FMT == F_Q5_0 || FMT == F_Q5_1 || FMT == F_IQ4_NL)
+                lane_b32<FMT, T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else lane_iq2xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, grid);
         }
         if constexpr (!SUMS) {

@@ -214,12 +214,13 @@ __device__ __forceinline__ void load_act(Act<FMT>& a, int u, const int8_t* xq, c
 #pragma unroll
     for (int i = 0; i < NS; ++i) a.d[i] = a.s[i] = 0.f;
     if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0 || FMT == F_IQ2_XXS || FMT == F_IQ4_XS || FMT == F_MXFP4 ||
-                  FMT == F_IQ3_S || FMT == F_IQ3_XXS) {
+                  FMT == F_IQ3_S || FMT == F_IQ3_XXS || FMT == F_Q4_1 || FMT == F_Q5_0 || FMT == F_Q5_1 ||
+                  FMT == F_IQ4_NL) {
         const int o = 32 * u;
         a.q[0] = ldq16<GLOBAL>(xq + o); a.q[1] = ldq16<GLOBAL>(xq + o + 16);
         a.r[0] = ldq16<GLOBAL>(xq2 + o); a.r[1] = ldq16<GLOBAL>(xq2 + o + 16);
         a.d[0] = ldf<GLOBAL, SCALES>(xd, u) * kInv254;
-        if (FMT == F_Q4_0) a.s[0] = ldf<GLOBAL, SCALES>(xs, u);
+        if (FMT == F_Q4_0 || FMT == F_Q4_1 || FMT == F_Q5_0 || FMT == F_Q5_1) a.s[0] = ldf<GLOBAL, SCALES>(xs, u);
     } else if constexpr (FMT == F_Q4_K || FMT == F_Q5_K) {
         const int b = u >> 2, p = u & 3, o = b * 256 + 64 * p;
         a.q[0] = ldq16<GLOBAL>(xq + o); a.q[1] = ldq16<GLOBAL>(xq + o + 16);
@@ -428,6 +429,30 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
             o.wsc[g] = d;
             o.off[g] = d;
         }
+    } else if constexpr (FMT == F_Q4_1 || FMT == F_Q5_0 || FMT == F_Q5_1 || FMT == F_IQ4_NL) {
+        constexpr int qo = FMT == F_Q4_1 ? 4 : FMT == F_Q5_0 ? 6 : FMT == F_Q5_1 ? 8 : 2;
+        const uint32_t bl = rs + u * block_bytes(FMT);
+        const uint4 v = lds16_a2(bl + qo);
+        const uint32_t V[4] = {v.x, v.y, v.z, v.w};
+        uint32_t qh = 0u;
+        if constexpr (FMT == F_Q5_0) qh = lds16u(bl + 2) | (lds16u(bl + 4) << 16);
+        if constexpr (FMT == F_Q5_1) qh = lds16u(bl + 4) | (lds16u(bl + 6) << 16);
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if constexpr (FMT == F_IQ4_NL) {
+                lo[i] = iq4nl_bytes(V[i] & 0x0F0F0F0Fu);
+                hi[i] = iq4nl_bytes((V[i] >> 4) & 0x0F0F0F0Fu);
+            } else {
+                lo[i] = (V[i] & 0x0F0F0F0Fu) | (spread4(qh >> (4 * i)) << 4);
+                hi[i] = ((V[i] >> 4) & 0x0F0F0F0Fu) | (spread4(qh >> (16 + 4 * i)) << 4);
+            }
+        }
+        o.s[0] = dot4(hi, a.q[1]) + dot4(lo, a.q[0]);
+        o.u[0] = dot4(hi, a.r[1]) + dot4(lo, a.r[0]);
+        const float d = h2f(lds16u(bl));
+        o.wsc[0] = d;
+        o.off[0] = FMT == F_Q5_0 ? 16.0f * d : (FMT == F_Q4_1 || FMT == F_Q5_1) ? -h2f(lds16u(bl + 2)) : 0.f;
     } else if constexpr (FMT == F_IQ3_XXS) {
         const int b = u >> 3, q = u & 7;
         const uint32_t sb = rs + b * 98;
@@ -527,7 +552,8 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
 template <int FMT>
 __device__ __forceinline__ int sum_unit(int u, int k) {
     if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0 || FMT == F_IQ2_XXS || FMT == F_IQ4_XS || FMT == F_MXFP4 ||
-                  FMT == F_IQ3_S || FMT == F_IQ3_XXS)
+                  FMT == F_IQ3_S || FMT == F_IQ3_XXS || FMT == F_Q4_1 || FMT == F_Q5_0 || FMT == F_Q5_1 ||
+                  FMT == F_IQ4_NL)
         return u;
     if constexpr (FMT == F_Q4_K || FMT == F_Q5_K) return 2 * u + k;   // unit u = sub-blocks 2u, 2u + 1 of the row
     const int b = u >> 3, q = u & 7;

@@ -2,7 +2,7 @@
 
 The reference names no dataset or public benchmark for this path; its configs are synthetic.  The
 generators below follow each config's stated distributions and write the exact GGUF block layouts
-(ggufengine/quant.py documents them: Q4_0 :60, Q8_0 :46, Q4_K :111, Q5_K :123, Q6_K :140, IQ3_XXS :322, IQ3_S :334, IQ4_XS :378, MXFP4 :394, TQ2_0 :417,
+(ggufengine/quant.py documents them: Q4_0 :60, Q4_1 :67, Q5_0 :83, Q5_1 :90, IQ4_NL :264, Q8_0 :46, Q4_K :111, Q5_K :123, Q6_K :140, IQ3_XXS :322, IQ3_S :334, IQ4_XS :378, MXFP4 :394, TQ2_0 :417,
 IQ2_XXS :235).  Everything is torch, so it runs on the CPU (tests) or on the GPU (bench, where the
 largest stacks are several GB).
 """
@@ -57,6 +57,16 @@ def blocks(fmt: str, n_rows: int, n_in: int, seed: int = 0, device="cpu",
     nb = n_rows * n_in // bv
     if fmt == "Q4_0":                       # d = |N(0,1)| * 0.01, nibbles uniform 0..15
         out = torch.cat([_f16_bytes(_abs_normal(nb, 0.01, g, device)), _bytes(nb, 16, g, device)], 1)
+    elif fmt == "Q4_1":                     # d = |N| * 0.01, m = -|N| * 0.08, nibbles uniform
+        out = torch.cat([_f16_bytes(_abs_normal(nb, 0.01, g, device)), _f16_bytes(-_abs_normal(nb, 0.08, g, device)),
+                         _bytes(nb, 16, g, device)], 1)
+    elif fmt == "Q5_0":                     # d = |N| * 0.005; qh and nibbles uniform
+        out = torch.cat([_f16_bytes(_abs_normal(nb, 0.005, g, device)), _bytes(nb, 20, g, device)], 1)
+    elif fmt == "Q5_1":                     # d = |N| * 0.005, m = -|N| * 0.08; qh and nibbles uniform
+        out = torch.cat([_f16_bytes(_abs_normal(nb, 0.005, g, device)), _f16_bytes(-_abs_normal(nb, 0.08, g, device)),
+                         _bytes(nb, 20, g, device)], 1)
+    elif fmt == "IQ4_NL":                   # d = |N| * 0.01 / 127; codebook indices uniform
+        out = torch.cat([_f16_bytes(_abs_normal(nb, 0.01 / 127, g, device)), _bytes(nb, 16, g, device)], 1)
     elif fmt == "Q8_0":                     # d = |N| * 0.002, q uniform -127..127
         q = torch.randint(-127, 128, (nb, 32), generator=g, device=device, dtype=torch.int16).to(torch.int8)
         out = torch.cat([_f16_bytes(_abs_normal(nb, 0.002, g, device)), q.view(torch.uint8)], 1)

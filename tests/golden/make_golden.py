@@ -20,7 +20,8 @@ tests/test_gguf_iq.py:81-101, zufallsbloecke).  Extra cases pin the corners:
 * IQ3_S blocks whose grid indices run through all 512 codebook entries, whose sign bytes run through
   all 256 patterns and whose scales run through all 16 values,
 * IQ3_XXS blocks whose grid indices run through all 256 codebook entries, whose sign groups run through
-  all 128 patterns and whose scales run through all 16 values.
+  all 128 patterns and whose scales run through all 16 values,
+* Q5_0 / Q5_1 blocks with every fifth bit set and with every fifth bit clear.
 
 Formats added later are generated after the earlier cases, so the earlier arrays stay as they were.
 """
@@ -38,13 +39,15 @@ LATER2 = {"IQ4_XS": (23, 256, 136)}
 LATER3 = {"MXFP4": (39, 32, 17)}
 LATER4 = {"IQ3_S": (21, 256, 110)}
 LATER5 = {"IQ3_XXS": (18, 256, 98)}
+LATER6 = {"Q4_1": (3, 32, 20), "Q5_0": (6, 32, 22), "Q5_1": (7, 32, 24), "IQ4_NL": (20, 32, 18)}
 SCALE_OFFSETS = {"Q4_0": (0,), "Q8_0": (0,), "Q4_K": (0, 2), "Q6_K": (208,), "IQ2_XXS": (0,), "TQ2_0": (64,),
-                 "Q5_K": (0, 2), "IQ4_XS": (0,), "MXFP4": (), "IQ3_S": (0,), "IQ3_XXS": (0,)}
+                 "Q5_K": (0, 2), "IQ4_XS": (0,), "MXFP4": (), "IQ3_S": (0,), "IQ3_XXS": (0,),
+                 "Q4_1": (0, 2), "Q5_0": (0,), "Q5_1": (0, 2), "IQ4_NL": (0,)}
 ROWS, COLS = 3, 512          # a (3, 512) matrix per format
 
 
 def random_blocks(name: str, n_blocks: int, rng: np.random.Generator) -> np.ndarray:
-    _, _, size = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4, **LATER5}[name]
+    _, _, size = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4, **LATER5, **LATER6}[name]
     raw = rng.integers(0, 256, (n_blocks, size), dtype=np.uint8)
     if name == "MXFP4":
         raw[:, 0] = rng.integers(118, 125, n_blocks)       # scale exponents 2^-10 .. 2^-4
@@ -139,6 +142,14 @@ def iq3xxs_cover(rng: np.random.Generator) -> np.ndarray:
     return raw
 
 
+def q5_cover(name: str, rng: np.random.Generator) -> np.ndarray:
+    raw = random_blocks(name, 16, rng)
+    o = 4 if name == "Q5_1" else 2
+    raw[:8, o:o + 4] = 0xFF
+    raw[8:, o:o + 4] = 0x00
+    return raw
+
+
 def main(ref_root: str) -> None:
     sys.path.insert(0, ref_root)
     import torch
@@ -148,7 +159,7 @@ def main(ref_root: str) -> None:
     out = {}
 
     def add(key: str, name: str, raw: np.ndarray, rows: int, cols: int) -> None:
-        t, bv, bb = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4, **LATER5}[name]
+        t, bv, bb = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4, **LATER5, **LATER6}[name]
         flat = np.ascontiguousarray(raw.reshape(-1))
         assert flat.size == rows * cols // bv * bb
         deq = dequantize(torch.from_numpy(flat.copy()), t, rows * cols, torch.float32).numpy()
@@ -180,6 +191,10 @@ def main(ref_root: str) -> None:
     for name, (_, bv, _) in LATER5.items():
         add(name, name, random_blocks(name, ROWS * COLS // bv, rng), ROWS, COLS)
     add("IQ3_XXS_cover", "IQ3_XXS", iq3xxs_cover(rng), 4, 256)
+    for name, (_, bv, _) in LATER6.items():
+        add(name, name, random_blocks(name, ROWS * COLS // bv, rng), ROWS, COLS)
+    add("Q5_0_cover", "Q5_0", q5_cover("Q5_0", rng), 2, 256)
+    add("Q5_1_cover", "Q5_1", q5_cover("Q5_1", rng), 2, 256)
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "dequant_golden.npz")
     np.savez_compressed(path, **out)
     print(f"wrote {path}: {len(out)} arrays")
