@@ -131,6 +131,9 @@ int launch(int fmt, const MvParams& P, int T, cudaStream_t st) {
     case F_Q5_0: return launch_fmt<F_Q5_0>(P, T, st);
     case F_Q5_1: return launch_fmt<F_Q5_1>(P, T, st);
     case F_IQ4_NL: return launch_fmt<F_IQ4_NL>(P, T, st);
+    case F_Q1_0: return launch_fmt<F_Q1_0>(P, T, st);
+    case F_Q2_0: return launch_fmt<F_Q2_0>(P, T, st);
+    case F_PQ2_0: return launch_fmt<F_PQ2_0>(P, T, st);
     }
     return ST_BAD_FORMAT;
 }
@@ -153,6 +156,9 @@ int launch_sums(int fmt, const MvParams& P, cudaStream_t st) {
     case F_Q5_0: return launch_t<F_Q5_0, 1, true>(P, st);
     case F_Q5_1: return launch_t<F_Q5_1, 1, true>(P, st);
     case F_IQ4_NL: return launch_t<F_IQ4_NL, 1, true>(P, st);
+    case F_Q1_0: return launch_t<F_Q1_0, 1, true>(P, st);
+    case F_Q2_0: return launch_t<F_Q2_0, 1, true>(P, st);
+    case F_PQ2_0: return launch_t<F_PQ2_0, 1, true>(P, st);
     }
     return ST_BAD_FORMAT;
 }
@@ -288,6 +294,9 @@ int launch_tma(int fmt, TmaParams& P, const TmaPlan& pl, cudaStream_t st) {
     case F_Q5_0: return launch_tma_fmt<F_Q5_0, XF, SUMS>(P, pl, int(grid), st);
     case F_Q5_1: return launch_tma_fmt<F_Q5_1, XF, SUMS>(P, pl, int(grid), st);
     case F_IQ4_NL: return launch_tma_fmt<F_IQ4_NL, XF, SUMS>(P, pl, int(grid), st);
+    case F_Q1_0: return launch_tma_fmt<F_Q1_0, XF, SUMS>(P, pl, int(grid), st);
+    case F_Q2_0: return launch_tma_fmt<F_Q2_0, XF, SUMS>(P, pl, int(grid), st);
+    case F_PQ2_0: return launch_tma_fmt<F_PQ2_0, XF, SUMS>(P, pl, int(grid), st);
     }
     return ST_BAD_FORMAT;
 }

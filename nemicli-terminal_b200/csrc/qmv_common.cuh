@@ -6,11 +6,14 @@
 
 namespace qmv {
 
-// GGML type ids of the fifteen formats (the GGUF type table; reference ggufengine/gguf.py:64-77)
+// GGML type ids of the eighteen formats (PQ2_0 = 142: the reference's id for the 128-value Q2_0 variant) (the GGUF type table; reference ggufengine/gguf.py:64-77)
 enum : int {
     F_Q4_0 = 2, F_Q8_0 = 8, F_Q4_K = 12, F_Q5_K = 13, F_Q6_K = 14, F_IQ2_XXS = 16, F_IQ4_XS = 23, F_TQ2_0 = 35,
-    F_MXFP4 = 39, F_IQ3_S = 21, F_IQ3_XXS = 18, F_Q4_1 = 3, F_Q5_0 = 6, F_Q5_1 = 7, F_IQ4_NL = 20
+    F_MXFP4 = 39, F_IQ3_S = 21, F_IQ3_XXS = 18, F_Q4_1 = 3, F_Q5_0 = 6, F_Q5_1 = 7, F_IQ4_NL = 20,
+    F_Q1_0 = 41, F_Q2_0 = 42, F_PQ2_0 = 142
 };
+// the ternary / 1-bit formats with one scale per 64 or 128 values, taken in 32-value units
+__host__ __device__ constexpr bool bits_format(int f) { return f == F_Q1_0 || f == F_Q2_0 || f == F_PQ2_0; }
 // the 32-value block formats (one block per integer-sum unit)
 __host__ __device__ constexpr bool b32_format(int f) {
     return f == F_Q4_0 || f == F_Q8_0 || f == F_MXFP4 || f == F_Q4_1 || f == F_Q5_0 || f == F_Q5_1 || f == F_IQ4_NL;
@@ -37,10 +40,10 @@ constexpr int kMaxTokens = 8;           // tokens per launch of the dp4a kernels
 constexpr float kInv254 = 1.0f / 254.0f;
 
 __host__ __device__ constexpr int block_values(int f) {
-    return b32_format(f) ? 32 : 256;
+    return b32_format(f) ? 32 : f == F_Q2_0 ? 64 : (f == F_Q1_0 || f == F_PQ2_0) ? 128 : 256;
 }
 __host__ __device__ constexpr int block_bytes(int f) {
-    return f == F_Q4_0 || f == F_IQ4_NL ? 18 : f == F_Q4_1 ? 20 : f == F_Q5_0 ? 22 : f == F_Q5_1 ? 24 : f == F_Q8_0 ? 34 : f == F_Q4_K ? 144 : f == F_Q5_K ? 176 : f == F_Q6_K ? 210
+    return f == F_Q4_0 || f == F_IQ4_NL || f == F_Q1_0 || f == F_Q2_0 ? 18 : f == F_PQ2_0 ? 34 : f == F_Q4_1 ? 20 : f == F_Q5_0 ? 22 : f == F_Q5_1 ? 24 : f == F_Q8_0 ? 34 : f == F_Q4_K ? 144 : f == F_Q5_K ? 176 : f == F_Q6_K ? 210
          : f == F_IQ4_XS ? 136 : f == F_MXFP4 ? 17 : f == F_IQ3_S ? 110
          : f == F_IQ3_XXS ? 98 : 66;
 }
@@ -50,7 +53,7 @@ __host__ __device__ constexpr int unit_values(int f) { return f == F_Q6_K ? 16 :
 __host__ __device__ inline bool known_format(int f) {
     return f == F_Q4_0 || f == F_Q8_0 || f == F_Q4_K || f == F_Q5_K || f == F_Q6_K || f == F_IQ2_XXS || f == F_IQ4_XS ||
            f == F_TQ2_0 || f == F_MXFP4 || f == F_IQ3_S || f == F_IQ3_XXS || f == F_Q4_1 || f == F_Q5_0 ||
-           f == F_Q5_1 || f == F_IQ4_NL;
+           f == F_Q5_1 || f == F_IQ4_NL || bits_format(f);
 }
 // weight rows and blocks of the K-quant formats with 16-byte header words are read 16 bytes at a time;
 // MXFP4's 17-byte blocks start at any byte, and their loads stay inside the tensor when it starts on a
@@ -139,6 +142,14 @@ __device__ __forceinline__ uint32_t iq4nl_bytes(uint32_t idx) {
 }
 __device__ __forceinline__ uint32_t mxfp4_bytes(uint32_t idx) {
     return lut16_bytes<kv4(0, 1, 2, 3), kv4(4, 6, 8, 12), kv4(0, -1, -2, -3), kv4(-4, -6, -8, -12)>(idx);
+}
+// 4x4 byte transpose of 16 activation bytes: word s of the result holds values s, 4 + s, 8 + s, 12 + s
+// (the order of Q2_0's 2-bit codes shifted by 2 s)
+__device__ __forceinline__ int4 byte_transpose(int4 x) {
+    const uint32_t t01 = __byte_perm(uint32_t(x.x), uint32_t(x.y), 0x5140), t23 = __byte_perm(uint32_t(x.z), uint32_t(x.w), 0x5140);
+    const uint32_t u01 = __byte_perm(uint32_t(x.x), uint32_t(x.y), 0x7362), u23 = __byte_perm(uint32_t(x.z), uint32_t(x.w), 0x7362);
+    return make_int4(int(__byte_perm(t01, t23, 0x5410)), int(__byte_perm(t01, t23, 0x7632)),
+                     int(__byte_perm(u01, u23, 0x5410)), int(__byte_perm(u01, u23, 0x7632)));
 }
 // four bits to four bytes: bit j -> bit 0 of byte j
 __device__ __forceinline__ uint32_t spread4(uint32_t s4) { return ((s4 & 15u) * 0x00204081u) & 0x01010101u; }

@@ -305,6 +305,73 @@ __device__ __forceinline__ void lane_b32(const uint8_t* const (&rows)[RW], int s
     }
 }
 
+// ---- Q1_0 (128 values: d, 16 B of bits, value j = bit j % 8 of byte j / 8: d (2 b - 1)), Q2_0 (64 values:
+// d, 16 B) and PQ2_0 (128 values: d, 32 B) with value j at bits 2 (j % 4) of byte j / 4: d (q - 1)
+// (quant.py:406-428).  Lane q takes the 32-value unit 8*sb + q.  Q1_0 codes are the bits (weight scale
+// 2 d, offset d xs); Q2_0 codes q (offset d xs) meet the activation bytes transposed 4 x 4.
+template <int FMT>
+__device__ __forceinline__ const uint8_t* bits_unit(const uint8_t* row, int u, int& sub) {
+    constexpr int upb = block_values(FMT) / 32;
+    sub = u % upb;
+    return row + (long long)(u / upb) * block_bytes(FMT);
+}
+template <int T, int RW, bool SUMS, int FMT>
+__device__ __forceinline__ void lane_bits(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                          const Tok<T>& tk, float (&acc)[RW][T], int row0) {
+    const int u = sb * 8 + q;
+    if (u >= P.n_in / 32) return;
+    uint32_t w[RW][8];
+    float d[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        int sub;
+        const uint8_t* b = bits_unit<FMT>(rows[r], u, sub);
+        d[r] = h2f(ldw2(b));
+        if constexpr (FMT == F_Q1_0) {
+            const uint32_t bits = ldw2(b + 2 + 4 * sub) | (ldw2(b + 4 + 4 * sub) << 16);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                w[r][2 * k] = spread4(bits >> (8 * k));
+                w[r][2 * k + 1] = spread4(bits >> (8 * k + 4));
+            }
+        } else {
+            const uint2 c = ldw8_a2(b + 2 + 8 * sub);
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                w[r][s] = (c.x >> (2 * s)) & 0x03030303u;
+                w[r][4 + s] = (c.y >> (2 * s)) & 0x03030303u;
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const long long o = tk.tb[t] + (long long)u * 32;
+        int4 xa = ldx16(P.xq + o), xb = ldx16(P.xq + o + 16);
+        int4 ya = ldx16(P.xq2 + o), yb = ldx16(P.xq2 + o + 16);
+        if constexpr (FMT != F_Q1_0) {
+            xa = byte_transpose(xa); xb = byte_transpose(xb);
+            ya = byte_transpose(ya); yb = byte_transpose(yb);
+        }
+        const long long g = (tk.tb[t] >> 5) + u;
+        const float dd = __ldg(P.xd + g), ss = __ldg(P.xs + g);
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            int s = dp4(w[r][0], xa.x, 0); s = dp4(w[r][1], xa.y, s); s = dp4(w[r][2], xa.z, s); s = dp4(w[r][3], xa.w, s);
+            s = dp4(w[r][4], xb.x, s); s = dp4(w[r][5], xb.y, s); s = dp4(w[r][6], xb.z, s); s = dp4(w[r][7], xb.w, s);
+            int v = dp4(w[r][0], ya.x, 0); v = dp4(w[r][1], ya.y, v); v = dp4(w[r][2], ya.z, v); v = dp4(w[r][3], ya.w, v);
+            v = dp4(w[r][4], yb.x, v); v = dp4(w[r][5], yb.y, v); v = dp4(w[r][6], yb.z, v); v = dp4(w[r][7], yb.w, v);
+            if constexpr (SUMS) {
+                const long long base = (long long)row0 * (P.n_in / 32) + u;
+                atomicAdd(P.s + base, s);
+                atomicAdd(P.s2 + base, v);
+            } else {
+                const float wsc = FMT == F_Q1_0 ? 2.0f * d[r] : d[r];
+                acc[r][t] += wsc * dd * (float(s) + float(v) * kInv254) - d[r] * ss;
+            }
+        }
+    }
+}
+
 // ---- Q8_0: 34 B = d (f16), int8[32] (quant.py:46-50).  Lane q takes block 8*sb + q.
 template <int T, int RW, bool SUMS>
 __device__ __forceinline__ void lane_q8_0(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
@@ -759,6 +826,7 @@ __global__ void __launch_bounds__(256) mv_kernel(const MvParams P) {
                 lane_iq3xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, reinterpret_cast<const uint32_t*>(grid));
             else if constexpr (FMT == F_Q4_1 || FMT == F_Q5_0 || FMT == F_Q5_1 || FMT == F_IQ4_NL)
                 lane_b32<FMT, T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+            else if constexpr (bits_format(FMT)) lane_bits<T, RW, SUMS, FMT>(rows, sb, q, P, tk, acc, row0);
             else lane_iq2xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, grid);
         }
         if constexpr (!SUMS) {

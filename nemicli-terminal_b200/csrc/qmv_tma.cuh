@@ -215,12 +215,16 @@ __device__ __forceinline__ void load_act(Act<FMT>& a, int u, const int8_t* xq, c
     for (int i = 0; i < NS; ++i) a.d[i] = a.s[i] = 0.f;
     if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0 || FMT == F_IQ2_XXS || FMT == F_IQ4_XS || FMT == F_MXFP4 ||
                   FMT == F_IQ3_S || FMT == F_IQ3_XXS || FMT == F_Q4_1 || FMT == F_Q5_0 || FMT == F_Q5_1 ||
-                  FMT == F_IQ4_NL) {
+                  FMT == F_IQ4_NL || bits_format(FMT)) {
         const int o = 32 * u;
         a.q[0] = ldq16<GLOBAL>(xq + o); a.q[1] = ldq16<GLOBAL>(xq + o + 16);
         a.r[0] = ldq16<GLOBAL>(xq2 + o); a.r[1] = ldq16<GLOBAL>(xq2 + o + 16);
         a.d[0] = ldf<GLOBAL, SCALES>(xd, u) * kInv254;
-        if (FMT == F_Q4_0 || FMT == F_Q4_1 || FMT == F_Q5_0 || FMT == F_Q5_1) a.s[0] = ldf<GLOBAL, SCALES>(xs, u);
+        if (FMT == F_Q4_0 || FMT == F_Q4_1 || FMT == F_Q5_0 || FMT == F_Q5_1 || bits_format(FMT)) a.s[0] = ldf<GLOBAL, SCALES>(xs, u);
+        if constexpr (FMT == F_Q2_0 || FMT == F_PQ2_0) {       // the order of the 2-bit codes
+            a.q[0] = byte_transpose(a.q[0]); a.q[1] = byte_transpose(a.q[1]);
+            a.r[0] = byte_transpose(a.r[0]); a.r[1] = byte_transpose(a.r[1]);
+        }
     } else if constexpr (FMT == F_Q4_K || FMT == F_Q5_K) {
         const int b = u >> 2, p = u & 3, o = b * 256 + 64 * p;
         a.q[0] = ldq16<GLOBAL>(xq + o); a.q[1] = ldq16<GLOBAL>(xq + o + 16);
@@ -453,6 +457,33 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
         const float d = h2f(lds16u(bl));
         o.wsc[0] = d;
         o.off[0] = FMT == F_Q5_0 ? 16.0f * d : (FMT == F_Q4_1 || FMT == F_Q5_1) ? -h2f(lds16u(bl + 2)) : 0.f;
+    } else if constexpr (bits_format(FMT)) {
+        constexpr int upb = block_values(FMT) / 32;
+        const int sub = u % upb;
+        const uint32_t bl = rs + uint32_t(u / upb) * block_bytes(FMT);
+        uint32_t w0[4], w1[4];
+        if constexpr (FMT == F_Q1_0) {
+            const uint32_t bits = lds16u(bl + 2 + 4 * sub) | (lds16u(bl + 4 + 4 * sub) << 16);
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                w0[2 * k] = spread4(bits >> (8 * k));
+                w0[2 * k + 1] = spread4(bits >> (8 * k + 4));
+                w1[2 * k] = spread4(bits >> (8 * k + 16));
+                w1[2 * k + 1] = spread4(bits >> (8 * k + 20));
+            }
+        } else {
+            const uint2 c = lds8_a2(bl + 2 + 8 * sub);
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                w0[s] = (c.x >> (2 * s)) & 0x03030303u;
+                w1[s] = (c.y >> (2 * s)) & 0x03030303u;
+            }
+        }
+        o.s[0] = dot4(w1, a.q[1]) + dot4(w0, a.q[0]);
+        o.u[0] = dot4(w1, a.r[1]) + dot4(w0, a.r[0]);
+        const float d = h2f(lds16u(bl));
+        o.wsc[0] = FMT == F_Q1_0 ? 2.0f * d : d;
+        o.off[0] = d;
     } else if constexpr (FMT == F_IQ3_XXS) {
         const int b = u >> 3, q = u & 7;
         const uint32_t sb = rs + b * 98;
@@ -553,7 +584,7 @@ template <int FMT>
 __device__ __forceinline__ int sum_unit(int u, int k) {
     if constexpr (FMT == F_Q4_0 || FMT == F_Q8_0 || FMT == F_IQ2_XXS || FMT == F_IQ4_XS || FMT == F_MXFP4 ||
                   FMT == F_IQ3_S || FMT == F_IQ3_XXS || FMT == F_Q4_1 || FMT == F_Q5_0 || FMT == F_Q5_1 ||
-                  FMT == F_IQ4_NL)
+                  FMT == F_IQ4_NL || bits_format(FMT))
         return u;
     if constexpr (FMT == F_Q4_K || FMT == F_Q5_K) return 2 * u + k;   // unit u = sub-blocks 2u, 2u + 1 of the row
     const int b = u >> 3, q = u & 7;
