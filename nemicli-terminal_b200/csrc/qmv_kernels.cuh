@@ -372,6 +372,55 @@ __device__ __forceinline__ void lane_bits(const uint8_t* const (&rows)[RW], int 
     }
 }
 
+// ---- Q3_K: 110 B = hmask[32], qs[64], scales[12], d (f16) (quant.py:295-306).  Lane q takes values
+// 32q..32q+31 of the superblock: half n = q/4, 2-bit field s = q%4 of qs[32n + l], high bit q of hmask[l];
+// scale group 2q (values 0..15) and 2q + 1 (16..31): 6-bit scale (nibble of scales[i % 8], 2 bits of
+// scales[8 + i % 4]) - 32.
+template <int T, int RW, bool SUMS>
+__device__ __forceinline__ void lane_q3k(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                         const Tok<T>& tk, float (&acc)[RW][T], int row0) {
+    const int n = q >> 2, s2 = 2 * (q & 3);
+    uint32_t w[RW][8];
+    float sc0[RW], sc1[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        const uint8_t* b = rows[r] + (long long)sb * 110;
+        const uint4 q0 = ldw16_a2(b + 32 + 32 * n), q1 = ldw16_a2(b + 48 + 32 * n);
+        const uint4 h0 = ldw16_a2(b), h1 = ldw16_a2(b + 16);
+        const uint32_t Q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        const uint32_t H[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[r][i] = q3k_word((Q[i] >> s2) & 0x03030303u, (H[i] >> q) & 0x01010101u);
+        const float d = h2f(ldw2(b + 108));
+        const int i0 = 2 * q, i1 = 2 * q + 1;
+        const int l0 = int(ldw1(b + 96 + i0 % 8) >> (4 * (i0 / 8))) & 15, g0 = int(ldw1(b + 104 + i0 % 4) >> (2 * (i0 / 4))) & 3;
+        const int l1 = int(ldw1(b + 96 + i1 % 8) >> (4 * (i1 / 8))) & 15, g1 = int(ldw1(b + 104 + i1 % 4) >> (2 * (i1 / 4))) & 3;
+        sc0[r] = d * float((l0 | (g0 << 4)) - 32);
+        sc1[r] = d * float((l1 | (g1 << 4)) - 32);
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const long long o = tk.tb[t] + (long long)sb * 256 + 32 * q;
+        const int4 x0 = ldx16(P.xq + o), x1 = ldx16(P.xq + o + 16);
+        const int4 y0 = ldx16(P.xq2 + o), y1 = ldx16(P.xq2 + o + 16);
+        const float dd = __ldg(P.xd + ((tk.tb[t] + (long long)sb * 256) >> 5) + q);
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            int sa = dp4(w[r][0], x0.x, 0); sa = dp4(w[r][1], x0.y, sa); sa = dp4(w[r][2], x0.z, sa); sa = dp4(w[r][3], x0.w, sa);
+            int sb2 = dp4(w[r][4], x1.x, 0); sb2 = dp4(w[r][5], x1.y, sb2); sb2 = dp4(w[r][6], x1.z, sb2); sb2 = dp4(w[r][7], x1.w, sb2);
+            int ua = dp4(w[r][0], y0.x, 0); ua = dp4(w[r][1], y0.y, ua); ua = dp4(w[r][2], y0.z, ua); ua = dp4(w[r][3], y0.w, ua);
+            int ub = dp4(w[r][4], y1.x, 0); ub = dp4(w[r][5], y1.y, ub); ub = dp4(w[r][6], y1.z, ub); ub = dp4(w[r][7], y1.w, ub);
+            if constexpr (SUMS) {
+                const long long base = (long long)row0 * (P.n_in / 16) + sb * 16 + 2 * q;
+                atomicAdd(P.s + base, sa); atomicAdd(P.s + base + 1, sb2);
+                atomicAdd(P.s2 + base, ua); atomicAdd(P.s2 + base + 1, ub);
+            } else {
+                acc[r][t] += dd * (sc0[r] * (float(sa) + float(ua) * kInv254) + sc1[r] * (float(sb2) + float(ub) * kInv254));
+            }
+        }
+    }
+}
+
 // ---- Q8_0: 34 B = d (f16), int8[32] (quant.py:46-50).  Lane q takes block 8*sb + q.
 template <int T, int RW, bool SUMS>
 __device__ __forceinline__ void lane_q8_0(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
@@ -827,6 +876,7 @@ __global__ void __launch_bounds__(256) mv_kernel(const MvParams P) {
             else if constexpr (FMT == F_Q4_1 || FMT == F_Q5_0 || FMT == F_Q5_1 || FMT == F_IQ4_NL)
                 lane_b32<FMT, T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (bits_format(FMT)) lane_bits<T, RW, SUMS, FMT>(rows, sb, q, P, tk, acc, row0);
+            else if constexpr (FMT == F_Q3_K) lane_q3k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else lane_iq2xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, grid);
         }
         if constexpr (!SUMS) {

@@ -164,6 +164,7 @@ __device__ __forceinline__ int dot4us(const uint32_t (&w)[4], const int4& x) {
 template <int FMT> struct UnitTraits { static constexpr int VPU = 32, NS = 1, NQ = 2; };
 template <> struct UnitTraits<F_Q4_K> { static constexpr int VPU = 64, NS = 2, NQ = 4; };
 template <> struct UnitTraits<F_Q5_K> { static constexpr int VPU = 64, NS = 2, NQ = 4; };
+template <> struct UnitTraits<F_Q3_K> { static constexpr int VPU = 32, NS = 2, NQ = 2; };   // two 16-value scales
 template <> struct UnitTraits<F_Q6_K> { static constexpr int VPU = 64, NS = 4, NQ = 4; };
 // Q6_K with 32-value units (ql bytes 64n+16j..+15 of superblock b: 16 values of group j/2 and of j/2 + 2):
 // a smaller activation footprint, for the decode chain's register budget.  Internal tag only.
@@ -235,6 +236,11 @@ __device__ __forceinline__ void load_act(Act<FMT>& a, int u, const int8_t* xq, c
         a.d[1] = ldf<GLOBAL, SCALES>(xd, b * 8 + 2 * p + 1) * kInv254;
         a.s[0] = ldf<GLOBAL, SCALES>(xs, b * 8 + 2 * p);
         a.s[1] = ldf<GLOBAL, SCALES>(xs, b * 8 + 2 * p + 1);
+    } else if constexpr (FMT == F_Q3_K) {
+        const int o = 32 * u;
+        a.q[0] = ldq16<GLOBAL>(xq + o); a.q[1] = ldq16<GLOBAL>(xq + o + 16);
+        a.r[0] = ldq16<GLOBAL>(xq2 + o); a.r[1] = ldq16<GLOBAL>(xq2 + o + 16);
+        a.d[0] = a.d[1] = ldf<GLOBAL, SCALES>(xd, u) * kInv254;
     } else if constexpr (FMT == F_Q6_K_U32) {
         const int b = u >> 3, q = u & 7, n = q >> 2, j = q & 3, A = j >> 1, B = A + 2, o = b * 256 + 128 * n + 16 * (j & 1);
         a.q[0] = ldq16<GLOBAL>(xq + o + 32 * A); a.q[1] = ldq16<GLOBAL>(xq + o + 32 * B);
@@ -457,6 +463,31 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
         const float d = h2f(lds16u(bl));
         o.wsc[0] = d;
         o.off[0] = FMT == F_Q5_0 ? 16.0f * d : (FMT == F_Q4_1 || FMT == F_Q5_1) ? -h2f(lds16u(bl + 2)) : 0.f;
+    } else if constexpr (FMT == F_Q3_K) {
+        const int b = u >> 3, q = u & 7, n = q >> 2, s2 = 2 * (q & 3);
+        const uint32_t sb = rs + b * 110;
+        const uint4 q0 = lds16_a2(sb + 32 + 32 * n), q1 = lds16_a2(sb + 48 + 32 * n);
+        const uint4 h0 = lds16_a2(sb), h1 = lds16_a2(sb + 16);
+        const uint32_t Q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        const uint32_t H[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+        uint32_t w0[4], w1[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            w0[i] = q3k_word((Q[i] >> s2) & 0x03030303u, (H[i] >> q) & 0x01010101u);
+            w1[i] = q3k_word((Q[4 + i] >> s2) & 0x03030303u, (H[4 + i] >> q) & 0x01010101u);
+        }
+        o.s[0] = dot4(w0, a.q[0]);
+        o.u[0] = dot4(w0, a.r[0]);
+        o.s[1] = dot4(w1, a.q[1]);
+        o.u[1] = dot4(w1, a.r[1]);
+        const float d = h2f(lds16u(sb + 108));
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int i = 2 * q + k;
+            const int lo = int(lds8u(sb + 96 + i % 8) >> (4 * (i / 8))) & 15, hi = int(lds8u(sb + 104 + i % 4) >> (2 * (i / 4))) & 3;
+            o.wsc[k] = d * float((lo | (hi << 4)) - 32);
+            o.off[k] = 0.f;
+        }
     } else if constexpr (bits_format(FMT)) {
         constexpr int upb = block_values(FMT) / 32;
         const int sub = u % upb;
@@ -587,6 +618,7 @@ __device__ __forceinline__ int sum_unit(int u, int k) {
                   FMT == F_IQ4_NL || bits_format(FMT))
         return u;
     if constexpr (FMT == F_Q4_K || FMT == F_Q5_K) return 2 * u + k;   // unit u = sub-blocks 2u, 2u + 1 of the row
+    if constexpr (FMT == F_Q3_K) return 2 * u + k;                    // the two 16-value scale groups of unit u
     const int b = u >> 3, q = u & 7;
     if constexpr (FMT == F_Q6_K) {
         const int b6 = u >> 2, n = (u >> 1) & 1, h = u & 1;     // group k: values 128n + 32k + 16h.. of b6

@@ -22,7 +22,8 @@ tests/test_gguf_iq.py:81-101, zufallsbloecke).  Extra cases pin the corners:
 * IQ3_XXS blocks whose grid indices run through all 256 codebook entries, whose sign groups run through
   all 128 patterns and whose scales run through all 16 values,
 * Q5_0 / Q5_1 blocks with every fifth bit set and with every fifth bit clear,
-* Q2_0 / PQ2_0 blocks with every 2-bit code (3, never written by the quantiser, included).
+* Q2_0 / PQ2_0 blocks with every 2-bit code (3, never written by the quantiser, included),
+* Q3_K blocks with every 6-bit scale (-32..31) and every high bit set or clear.
 
 Formats added later are generated after the earlier cases, so the earlier arrays stay as they were.
 """
@@ -42,15 +43,16 @@ LATER4 = {"IQ3_S": (21, 256, 110)}
 LATER5 = {"IQ3_XXS": (18, 256, 98)}
 LATER6 = {"Q4_1": (3, 32, 20), "Q5_0": (6, 32, 22), "Q5_1": (7, 32, 24), "IQ4_NL": (20, 32, 18)}
 LATER7 = {"Q1_0": (41, 128, 18), "Q2_0": (42, 64, 18), "PQ2_0": (142, 128, 34)}
+LATER8 = {"Q3_K": (11, 256, 110)}
 SCALE_OFFSETS = {"Q4_0": (0,), "Q8_0": (0,), "Q4_K": (0, 2), "Q6_K": (208,), "IQ2_XXS": (0,), "TQ2_0": (64,),
                  "Q5_K": (0, 2), "IQ4_XS": (0,), "MXFP4": (), "IQ3_S": (0,), "IQ3_XXS": (0,),
                  "Q4_1": (0, 2), "Q5_0": (0,), "Q5_1": (0, 2), "IQ4_NL": (0,), "Q1_0": (0,), "Q2_0": (0,),
-                 "PQ2_0": (0,)}
+                 "PQ2_0": (0,), "Q3_K": (108,)}
 ROWS, COLS = 3, 512          # a (3, 512) matrix per format
 
 
 def random_blocks(name: str, n_blocks: int, rng: np.random.Generator) -> np.ndarray:
-    _, _, size = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4, **LATER5, **LATER6, **LATER7}[name]
+    _, _, size = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4, **LATER5, **LATER6, **LATER7, **LATER8}[name]
     raw = rng.integers(0, 256, (n_blocks, size), dtype=np.uint8)
     if name == "MXFP4":
         raw[:, 0] = rng.integers(118, 125, n_blocks)       # scale exponents 2^-10 .. 2^-4
@@ -162,7 +164,7 @@ def main(ref_root: str) -> None:
     out = {}
 
     def add(key: str, name: str, raw: np.ndarray, rows: int, cols: int) -> None:
-        t, bv, bb = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4, **LATER5, **LATER6, **LATER7}[name]
+        t, bv, bb = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4, **LATER5, **LATER6, **LATER7, **LATER8}[name]
         flat = np.ascontiguousarray(raw.reshape(-1))
         assert flat.size == rows * cols // bv * bb
         deq = dequantize(torch.from_numpy(flat.copy()), t, rows * cols, torch.float32).numpy()
@@ -204,6 +206,16 @@ def main(ref_root: str) -> None:
         raw = random_blocks(name, per, rng)
         raw[:, 2:] = np.arange(raw[:, 2:].size, dtype=np.uint32).reshape(raw[:, 2:].shape) % 256
         add(name + "_cover", name, raw, 1, 256)
+    for name, (_, bv, _) in LATER8.items():
+        add(name, name, random_blocks(name, ROWS * COLS // bv, rng), ROWS, COLS)
+    raw = random_blocks("Q3_K", 4, rng)                      # 64 scale groups: every 6-bit scale once
+    for blk in range(4):
+        sc = [16 * blk + i for i in range(16)]
+        raw[blk, 96:104] = [(sc[i] & 15) | ((sc[i + 8] & 15) << 4) for i in range(8)]
+        raw[blk, 104:108] = [sum(((sc[4 * s + i] >> 4) & 3) << (2 * s) for s in range(4)) for i in range(4)]
+    raw[0, :32] = 0xFF
+    raw[1, :32] = 0x00
+    add("Q3_K_cover", "Q3_K", raw, 4, 256)
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "dequant_golden.npz")
     np.savez_compressed(path, **out)
     print(f"wrote {path}: {len(out)} arrays")
