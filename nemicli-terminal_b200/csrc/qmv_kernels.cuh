@@ -421,6 +421,89 @@ __device__ __forceinline__ void lane_q3k(const uint8_t* const (&rows)[RW], int s
     }
 }
 
+// ---- IQ2_XS (74 B = d, u16 qs[32], scales[8]) and IQ2_S (82 B = d, qs[32], signs[32], qh[8], scales[8])
+// (quant.py:248-260, 310-318).  Entry k (8 values): IQ2_XS index bits 0..8 of qs[k] with a 7-bit sign
+// index in bits 9..15 (parity gives the 8th sign); IQ2_S index qs[k] | bits 2 (k % 4).. of qh[k / 4] << 8
+// with sign byte signs[k].  The 16-value scale group i has weight scale d (0.125 + 0.25 s), s = nibble
+// i % 2 of scales[i / 2].  Codebooks compact (2 bits per magnitude) in global memory, read through L1.
+__device__ const uint16_t kIq2xsCodes[512] = {
+#include "iq2xs_grid.inc"
+};
+__device__ const uint16_t kIq2sCodes[1024] = {
+#include "iq2s_grid.inc"
+};
+
+// the signed bytes of sub-block q (entries 4q..4q+3) of an IQ2_XS / IQ2_S block at b (global or shared
+// through the loader L), and the two scale nibbles
+template <int FMT>
+__device__ __forceinline__ void iq2x_words(uint32_t q0, uint32_t q1, uint32_t sg, uint32_t qh, uint32_t (&w)[8]) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        uint32_t idx, s8;
+        if constexpr (FMT == F_IQ2_XS) {
+            const uint32_t q16 = ((e < 2 ? q0 : q1) >> (16 * (e & 1))) & 0xFFFFu;
+            idx = q16 & 511u;
+            const uint32_t s7 = q16 >> 9;
+            s8 = s7 | (uint32_t(__popc(s7) & 1) << 7);
+        } else {
+            idx = ((q0 >> (8 * e)) & 0xFFu) | (((qh >> (2 * e)) & 3u) << 8);
+            s8 = (sg >> (8 * e)) & 0xFFu;
+        }
+        const uint32_t code = FMT == F_IQ2_XS ? uint32_t(__ldg(kIq2xsCodes + idx)) : uint32_t(__ldg(kIq2sCodes + idx));
+        const uint32_t mlo = sign4_mask(s8), mhi = sign4_mask(s8 >> 4);
+        w[2 * e] = __vsub4(iq2_mag4(code & 0xFFu) ^ mlo, mlo);
+        w[2 * e + 1] = __vsub4(iq2_mag4(code >> 8) ^ mhi, mhi);
+    }
+}
+
+template <int T, int RW, bool SUMS, int FMT>
+__device__ __forceinline__ void lane_iq2x(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                          const Tok<T>& tk, float (&acc)[RW][T], int row0) {
+    uint32_t w[RW][8];
+    float sc0[RW], sc1[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        const uint8_t* b = rows[r] + (long long)sb * block_bytes(FMT);
+        uint32_t q0, q1 = 0u, sg = 0u, qh = 0u, scb;
+        if constexpr (FMT == F_IQ2_XS) {
+            const uint2 c = ldw8_a2(b + 2 + 8 * q);
+            q0 = c.x;
+            q1 = c.y;
+            scb = ldw1(b + 66 + q);
+        } else {
+            q0 = ldw2(b + 2 + 4 * q) | (ldw2(b + 4 + 4 * q) << 16);
+            sg = ldw2(b + 34 + 4 * q) | (ldw2(b + 36 + 4 * q) << 16);
+            qh = ldw1(b + 66 + q);
+            scb = ldw1(b + 74 + q);
+        }
+        iq2x_words<FMT>(q0, q1, sg, qh, w[r]);
+        const float d = h2f(ldw2(b));
+        sc0[r] = d * (0.125f + 0.25f * float(scb & 15u));
+        sc1[r] = d * (0.125f + 0.25f * float(scb >> 4));
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const long long o = tk.tb[t] + (long long)sb * 256 + 32 * q;
+        const int4 x0 = ldx16(P.xq + o), x1 = ldx16(P.xq + o + 16);
+        const int4 y0 = ldx16(P.xq2 + o), y1 = ldx16(P.xq2 + o + 16);
+        const float dd = __ldg(P.xd + ((tk.tb[t] + (long long)sb * 256) >> 5) + q);
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            int sa = dp4(w[r][0], x0.x, 0); sa = dp4(w[r][1], x0.y, sa); sa = dp4(w[r][2], x0.z, sa); sa = dp4(w[r][3], x0.w, sa);
+            int sb2 = dp4(w[r][4], x1.x, 0); sb2 = dp4(w[r][5], x1.y, sb2); sb2 = dp4(w[r][6], x1.z, sb2); sb2 = dp4(w[r][7], x1.w, sb2);
+            int ua = dp4(w[r][0], y0.x, 0); ua = dp4(w[r][1], y0.y, ua); ua = dp4(w[r][2], y0.z, ua); ua = dp4(w[r][3], y0.w, ua);
+            int ub = dp4(w[r][4], y1.x, 0); ub = dp4(w[r][5], y1.y, ub); ub = dp4(w[r][6], y1.z, ub); ub = dp4(w[r][7], y1.w, ub);
+            if constexpr (SUMS) {
+                const long long base = (long long)row0 * (P.n_in / 16) + sb * 16 + 2 * q;
+                atomicAdd(P.s + base, sa); atomicAdd(P.s + base + 1, sb2);
+                atomicAdd(P.s2 + base, ua); atomicAdd(P.s2 + base + 1, ub);
+            } else {
+                acc[r][t] += dd * (sc0[r] * (float(sa) + float(ua) * kInv254) + sc1[r] * (float(sb2) + float(ub) * kInv254));
+            }
+        }
+    }
+}
+
 // ---- Q8_0: 34 B = d (f16), int8[32] (quant.py:46-50).  Lane q takes block 8*sb + q.
 template <int T, int RW, bool SUMS>
 __device__ __forceinline__ void lane_q8_0(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
@@ -877,6 +960,7 @@ __global__ void __launch_bounds__(256) mv_kernel(const MvParams P) {
                 lane_b32<FMT, T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (bits_format(FMT)) lane_bits<T, RW, SUMS, FMT>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (FMT == F_Q3_K) lane_q3k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+            else if constexpr (iq2x_format(FMT)) lane_iq2x<T, RW, SUMS, FMT>(rows, sb, q, P, tk, acc, row0);
             else lane_iq2xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, grid);
         }
         if constexpr (!SUMS) {

@@ -165,6 +165,8 @@ template <int FMT> struct UnitTraits { static constexpr int VPU = 32, NS = 1, NQ
 template <> struct UnitTraits<F_Q4_K> { static constexpr int VPU = 64, NS = 2, NQ = 4; };
 template <> struct UnitTraits<F_Q5_K> { static constexpr int VPU = 64, NS = 2, NQ = 4; };
 template <> struct UnitTraits<F_Q3_K> { static constexpr int VPU = 32, NS = 2, NQ = 2; };   // two 16-value scales
+template <> struct UnitTraits<F_IQ2_XS> { static constexpr int VPU = 32, NS = 2, NQ = 2; };
+template <> struct UnitTraits<F_IQ2_S> { static constexpr int VPU = 32, NS = 2, NQ = 2; };
 template <> struct UnitTraits<F_Q6_K> { static constexpr int VPU = 64, NS = 4, NQ = 4; };
 // Q6_K with 32-value units (ql bytes 64n+16j..+15 of superblock b: 16 values of group j/2 and of j/2 + 2):
 // a smaller activation footprint, for the decode chain's register budget.  Internal tag only.
@@ -236,7 +238,7 @@ __device__ __forceinline__ void load_act(Act<FMT>& a, int u, const int8_t* xq, c
         a.d[1] = ldf<GLOBAL, SCALES>(xd, b * 8 + 2 * p + 1) * kInv254;
         a.s[0] = ldf<GLOBAL, SCALES>(xs, b * 8 + 2 * p);
         a.s[1] = ldf<GLOBAL, SCALES>(xs, b * 8 + 2 * p + 1);
-    } else if constexpr (FMT == F_Q3_K) {
+    } else if constexpr (FMT == F_Q3_K || iq2x_format(FMT)) {
         const int o = 32 * u;
         a.q[0] = ldq16<GLOBAL>(xq + o); a.q[1] = ldq16<GLOBAL>(xq + o + 16);
         a.r[0] = ldq16<GLOBAL>(xq2 + o); a.r[1] = ldq16<GLOBAL>(xq2 + o + 16);
@@ -463,6 +465,32 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
         const float d = h2f(lds16u(bl));
         o.wsc[0] = d;
         o.off[0] = FMT == F_Q5_0 ? 16.0f * d : (FMT == F_Q4_1 || FMT == F_Q5_1) ? -h2f(lds16u(bl + 2)) : 0.f;
+    } else if constexpr (iq2x_format(FMT)) {
+        const int b = u >> 3, q = u & 7;
+        const uint32_t sb = rs + b * block_bytes(FMT);
+        uint32_t q0, q1 = 0u, sg = 0u, qh = 0u, scb;
+        if constexpr (FMT == F_IQ2_XS) {
+            const uint2 c = lds8_a2(sb + 2 + 8 * q);
+            q0 = c.x;
+            q1 = c.y;
+            scb = lds8u(sb + 66 + q);
+        } else {
+            q0 = lds16u(sb + 2 + 4 * q) | (lds16u(sb + 4 + 4 * q) << 16);
+            sg = lds16u(sb + 34 + 4 * q) | (lds16u(sb + 36 + 4 * q) << 16);
+            qh = lds8u(sb + 66 + q);
+            scb = lds8u(sb + 74 + q);
+        }
+        uint32_t w[8];
+        iq2x_words<FMT>(q0, q1, sg, qh, w);
+        const uint32_t w0[4] = {w[0], w[1], w[2], w[3]}, w1[4] = {w[4], w[5], w[6], w[7]};
+        o.s[0] = dot4(w0, a.q[0]);
+        o.u[0] = dot4(w0, a.r[0]);
+        o.s[1] = dot4(w1, a.q[1]);
+        o.u[1] = dot4(w1, a.r[1]);
+        const float d = h2f(lds16u(sb));
+        o.wsc[0] = d * (0.125f + 0.25f * float(scb & 15u));
+        o.wsc[1] = d * (0.125f + 0.25f * float(scb >> 4));
+        o.off[0] = o.off[1] = 0.f;
     } else if constexpr (FMT == F_Q3_K) {
         const int b = u >> 3, q = u & 7, n = q >> 2, s2 = 2 * (q & 3);
         const uint32_t sb = rs + b * 110;
@@ -618,7 +646,7 @@ __device__ __forceinline__ int sum_unit(int u, int k) {
                   FMT == F_IQ4_NL || bits_format(FMT))
         return u;
     if constexpr (FMT == F_Q4_K || FMT == F_Q5_K) return 2 * u + k;   // unit u = sub-blocks 2u, 2u + 1 of the row
-    if constexpr (FMT == F_Q3_K) return 2 * u + k;                    // the two 16-value scale groups of unit u
+    if constexpr (FMT == F_Q3_K || iq2x_format(FMT)) return 2 * u + k;   // the two 16-value scale groups of unit u
     const int b = u >> 3, q = u & 7;
     if constexpr (FMT == F_Q6_K) {
         const int b6 = u >> 2, n = (u >> 1) & 1, h = u & 1;     // group k: values 128n + 32k + 16h.. of b6

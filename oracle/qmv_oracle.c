@@ -11,10 +11,11 @@
  *     restatement uses IEEE-rounded division and an explicit fused multiply-add so that it is
  *     reproducible bit for bit on the GPU (the kernels do the same).  Against the reference's
  *     fast-math build a quantised value can differ by one unit on a rounding tie.
- *   - the block dequantisers of ggufengine/quant.py for the nineteen in-scope formats:
+ *   - the block dequantisers of ggufengine/quant.py for the twenty-one in-scope formats:
  *     deq_q4_0 :60, deq_q4_1 :67, deq_q5_0 :83, deq_q5_1 :90 (+ _q5_high_bits :74), deq_iq4_nl :264,
  *     deq_q1_0 :424, deq_q2_0 :410 (and PQ2_0, the same codes in 34-byte blocks of 128 values),
- *     deq_q3_k :295, deq_q8_0 :46, deq_q4_k :111 (+ _scale_min_k4 :99), deq_q5_k :123, deq_q6_k :140,
+ *     deq_q3_k :295, deq_iq2_xs :310 and deq_iq2_s :248 (IQ2XS_GRID, IQ2S_GRID, compact in
+ *     csrc/iq2xs_grid.inc, csrc/iq2s_grid.inc), deq_q8_0 :46, deq_q4_k :111 (+ _scale_min_k4 :99), deq_q5_k :123, deq_q6_k :140,
  *     deq_iq4_xs :378 (codebook KVALUES_IQ4NL, ggufengine/iqtabellen.py:7), deq_mxfp4 :394
  *     (KVALUES_MXFP4 :391, scale 2^(e-128) as the reference builds its float bits), deq_iq3_s :334
  *     (codebook ggufengine/iqtabellen.py IQ3S_GRID, kept compact in csrc/iq3s_grid.inc), deq_iq3_xxs
@@ -32,7 +33,7 @@
  * Sum units (the values that share one weight scale and one activation scale):
  *   Q4_K, Q5_K, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, TQ2_0, IQ2_XXS, IQ3_XXS, IQ3_S, IQ4_NL, IQ4_XS, MXFP4: 32
  *   values (n_in/32 units).  Q4_1 and Q5_1 take their +m offset and Q5_0 its -16 d offset with xs.
- *   Q3_K: 16 values (its scale groups; codes q2 - 4 (1 - hbit), signed).
+ *   Q3_K, IQ2_XS, IQ2_S: 16 values (their scale groups; Q3_K codes q2 - 4 (1 - hbit), signed).
  *   Q1_0, Q2_0, PQ2_0: 32-value units inside 128 / 64 / 128-value blocks; codes bit (weight 2 d, offset
  *   d: d (2 b - 1)) and q (offset d: d (q - 1)).
  *   Q6_K: 16.
@@ -54,7 +55,14 @@
 
 enum { T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ2_XXS = 16, T_IQ4_XS = 23, T_TQ2_0 = 35, T_MXFP4 = 39,
        T_IQ3_S = 21, T_IQ3_XXS = 18, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_IQ4_NL = 20,
-       T_Q1_0 = 41, T_Q2_0 = 42, T_PQ2_0 = 142, T_Q3_K = 11 };
+       T_Q1_0 = 41, T_Q2_0 = 42, T_PQ2_0 = 142, T_Q3_K = 11, T_IQ2_XS = 17, T_IQ2_S = 22 };
+
+static const uint16_t IQ2XS_CODES[512] = {
+#include "../nemicli-terminal_b200/csrc/iq2xs_grid.inc"
+};
+static const uint16_t IQ2S_CODES[1024] = {
+#include "../nemicli-terminal_b200/csrc/iq2s_grid.inc"
+};
 
 /* IQ4_XS codebook (part of the format: the reference's KVALUES_IQ4NL) */
 static const int8_t IQ4NL_VALUES[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
@@ -137,7 +145,7 @@ int orc_block_values(int fmt) {
     case T_Q2_0: return 64;
     case T_Q1_0: case T_PQ2_0: return 128;
     case T_Q4_K: case T_Q5_K: case T_Q6_K: case T_IQ2_XXS: case T_IQ3_XXS: case T_IQ3_S: case T_IQ4_XS:
-    case T_TQ2_0: case T_Q3_K: return 256;
+    case T_TQ2_0: case T_Q3_K: case T_IQ2_XS: case T_IQ2_S: return 256;
     }
     return 0;
 }
@@ -160,6 +168,8 @@ int orc_block_bytes(int fmt) {
     case T_IQ3_S: return 110;
     case T_IQ3_XXS: return 98;
     case T_Q3_K: return 110;
+    case T_IQ2_XS: return 74;
+    case T_IQ2_S: return 82;
     case T_TQ2_0: return 66;
     case T_MXFP4: return 17;
     }
@@ -167,13 +177,37 @@ int orc_block_bytes(int fmt) {
 }
 
 /* values per integer-sum unit */
-int orc_unit_values(int fmt) { return fmt == T_Q6_K || fmt == T_Q3_K ? 16 : 32; }
+int orc_unit_values(int fmt) { return fmt == T_Q6_K || fmt == T_Q3_K || fmt == T_IQ2_XS || fmt == T_IQ2_S ? 16 : 32; }
 
 /* Q3_K (110 B = hmask[32], qs[64], scales[12], d; quant.py:295-306): scale group i (16 values) and the
    signed code of value v (0..255) */
 static int q3k_scale(const uint8_t* b, int i) {
     const int lo = (b[96 + i % 8] >> (4 * (i / 8))) & 15, hi = (b[104 + i % 4] >> (2 * (i / 4))) & 3;
     return (lo | (hi << 4)) - 32;
+}
+/* IQ2_XS (74 B = d, u16 qs[32], scales[8]; quant.py:310-318): entry k (8 values) has codebook index
+   bits 0..8 and a 7-bit sign index (parity gives the 8th sign) in bits 9..15.  IQ2_S (82 B = d, qs[32],
+   signs[32], qh[8], scales[8]; quant.py:248-260): entry k has index qs[k] | bits 2 (k % 4).. of qh[k / 4]
+   << 8 and sign byte signs[k].  Both: 4-bit scale of 16-value group i = nibble i % 2 of scales[i / 2],
+   weight scale d (0.125 + 0.25 s). */
+static uint32_t ksign8(uint32_t s7);
+static int iq2xs_value(const uint8_t* b, int fmt, int v) {
+    const int k = v / 8, j = v % 8;
+    int idx, s8;
+    if (fmt == T_IQ2_XS) {
+        const int q = b[2 + 2 * k] | (b[3 + 2 * k] << 8);
+        idx = q & 511;
+        s8 = (int)ksign8((uint32_t)(q >> 9));
+    } else {
+        idx = b[2 + k] | (((b[66 + k / 4] >> (2 * (k % 4))) & 3) << 8);
+        s8 = b[34 + k];
+    }
+    const int code = fmt == T_IQ2_XS ? IQ2XS_CODES[idx] : IQ2S_CODES[idx];
+    const int g = IQ2XXS_LEVELS[(code >> (2 * j)) & 3];
+    return (s8 >> j) & 1 ? -g : g;
+}
+static int iq2xs_scale(const uint8_t* b, int fmt, int i) {
+    return (b[(fmt == T_IQ2_XS ? 66 : 74) + i / 2] >> (4 * (i % 2))) & 15;
 }
 static int q3k_code(const uint8_t* b, int v) {
     const int n = v / 128, s = (v % 128) / 32, l = v % 32;
@@ -304,6 +338,14 @@ int orc_dequant(int fmt, const uint8_t* raw, long long n_values, float* out) {
                     o[i] = d * ((float)lo - 16.0f);
                     o[i + 16] = d * ((float)hi - 16.0f);
                 }
+            }
+            break;
+        }
+        case T_IQ2_XS: case T_IQ2_S: {
+            const float d = f16(b);
+            for (int i = 0; i < 16; ++i) {
+                const float db = d * (0.125f + 0.25f * (float)iq2xs_scale(b, fmt, i));
+                for (int l = 0; l < 16; ++l) o[16 * i + l] = (float)iq2xs_value(b, fmt, 16 * i + l) * db;
             }
             break;
         }
@@ -458,6 +500,7 @@ static int code_of(int fmt, const uint8_t* b, int v) {
     case T_Q2_0: case T_PQ2_0: return (b[2 + v / 4] >> (2 * (v % 4))) & 3;
     case T_Q1_0: return (b[2 + v / 8] >> (v % 8)) & 1;
     case T_Q3_K: return q3k_code(b, v);
+    case T_IQ2_XS: case T_IQ2_S: return iq2xs_value(b, fmt, v);
     case T_Q4_K: { const int j = v >> 5, i = v & 31; return (b[16 + 32 * (j >> 1) + i] >> (4 * (j & 1))) & 15; }
     case T_Q5_K: {
         const int j = v >> 5, i = v & 31;
@@ -514,6 +557,10 @@ static void unit_scales(int fmt, const uint8_t* b, int u, double* wscale, double
     case T_Q2_0: case T_PQ2_0: *wscale = f16(b); *offs = f16(b); return;
     case T_Q1_0: *wscale = 2.0 * f16(b); *offs = f16(b); return;
     case T_Q3_K: *wscale = (double)f16(b + 108) * (double)q3k_scale(b, u); *offs = 0.0; return;
+    case T_IQ2_XS: case T_IQ2_S:
+        *wscale = (double)f16(b) * (0.125 + 0.25 * (double)iq2xs_scale(b, fmt, u));
+        *offs = 0.0;
+        return;
     case T_Q4_K: case T_Q5_K: {
         int sc[8], mn[8];
         scale_min_k4(b + 4, sc, mn);

@@ -23,7 +23,9 @@ tests/test_gguf_iq.py:81-101, zufallsbloecke).  Extra cases pin the corners:
   all 128 patterns and whose scales run through all 16 values,
 * Q5_0 / Q5_1 blocks with every fifth bit set and with every fifth bit clear,
 * Q2_0 / PQ2_0 blocks with every 2-bit code (3, never written by the quantiser, included),
-* Q3_K blocks with every 6-bit scale (-32..31) and every high bit set or clear.
+* Q3_K blocks with every 6-bit scale (-32..31) and every high bit set or clear,
+* IQ2_XS / IQ2_S blocks whose codebook indices run through all 512 / 1024 entries, with every sign
+  pattern and every 4-bit scale.
 
 Formats added later are generated after the earlier cases, so the earlier arrays stay as they were.
 """
@@ -44,15 +46,17 @@ LATER5 = {"IQ3_XXS": (18, 256, 98)}
 LATER6 = {"Q4_1": (3, 32, 20), "Q5_0": (6, 32, 22), "Q5_1": (7, 32, 24), "IQ4_NL": (20, 32, 18)}
 LATER7 = {"Q1_0": (41, 128, 18), "Q2_0": (42, 64, 18), "PQ2_0": (142, 128, 34)}
 LATER8 = {"Q3_K": (11, 256, 110)}
+LATER9 = {"IQ2_XS": (17, 256, 74), "IQ2_S": (22, 256, 82)}
 SCALE_OFFSETS = {"Q4_0": (0,), "Q8_0": (0,), "Q4_K": (0, 2), "Q6_K": (208,), "IQ2_XXS": (0,), "TQ2_0": (64,),
                  "Q5_K": (0, 2), "IQ4_XS": (0,), "MXFP4": (), "IQ3_S": (0,), "IQ3_XXS": (0,),
                  "Q4_1": (0, 2), "Q5_0": (0,), "Q5_1": (0, 2), "IQ4_NL": (0,), "Q1_0": (0,), "Q2_0": (0,),
-                 "PQ2_0": (0,), "Q3_K": (108,)}
+                 "PQ2_0": (0,), "Q3_K": (108,), "IQ2_XS": (0,), "IQ2_S": (0,)}
 ROWS, COLS = 3, 512          # a (3, 512) matrix per format
 
 
 def random_blocks(name: str, n_blocks: int, rng: np.random.Generator) -> np.ndarray:
-    _, _, size = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4, **LATER5, **LATER6, **LATER7, **LATER8}[name]
+    _, _, size = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4, **LATER5, **LATER6, **LATER7, **LATER8,
+                  **LATER9}[name]
     raw = rng.integers(0, 256, (n_blocks, size), dtype=np.uint8)
     if name == "MXFP4":
         raw[:, 0] = rng.integers(118, 125, n_blocks)       # scale exponents 2^-10 .. 2^-4
@@ -164,7 +168,8 @@ def main(ref_root: str) -> None:
     out = {}
 
     def add(key: str, name: str, raw: np.ndarray, rows: int, cols: int) -> None:
-        t, bv, bb = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4, **LATER5, **LATER6, **LATER7, **LATER8}[name]
+        t, bv, bb = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4, **LATER5, **LATER6, **LATER7, **LATER8,
+                     **LATER9}[name]
         flat = np.ascontiguousarray(raw.reshape(-1))
         assert flat.size == rows * cols // bv * bb
         deq = dequantize(torch.from_numpy(flat.copy()), t, rows * cols, torch.float32).numpy()
@@ -216,6 +221,24 @@ def main(ref_root: str) -> None:
     raw[0, :32] = 0xFF
     raw[1, :32] = 0x00
     add("Q3_K_cover", "Q3_K", raw, 4, 256)
+    for name, (_, bv, _) in LATER9.items():
+        add(name, name, random_blocks(name, ROWS * COLS // bv, rng), ROWS, COLS)
+    raw = random_blocks("IQ2_XS", 16, rng)                   # 512 entries: index k, sign index k % 128
+    for blk in range(16):
+        for e in range(32):
+            k = 32 * blk + e
+            q = (k & 511) | ((k % 128) << 9)
+            raw[blk, 2 + 2 * e:4 + 2 * e] = [q & 0xFF, q >> 8]
+        raw[blk, 66:74] = [(blk + 2 * i) % 16 | (((blk + 2 * i + 1) % 16) << 4) for i in range(8)]
+    add("IQ2_XS_cover", "IQ2_XS", raw, 16, 256)
+    raw = random_blocks("IQ2_S", 32, rng)                    # 1024 entries: index k, sign byte k % 256
+    for blk in range(32):
+        idx = [32 * blk + e for e in range(32)]
+        raw[blk, 2:34] = [i & 0xFF for i in idx]
+        raw[blk, 34:66] = [i % 256 for i in idx]
+        raw[blk, 66:74] = [sum(((idx[4 * g + j] >> 8) & 3) << (2 * j) for j in range(4)) for g in range(8)]
+        raw[blk, 74:82] = [(blk + 2 * i) % 16 | (((blk + 2 * i + 1) % 16) << 4) for i in range(8)]
+    add("IQ2_S_cover", "IQ2_S", raw, 32, 256)
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "dequant_golden.npz")
     np.savez_compressed(path, **out)
     print(f"wrote {path}: {len(out)} arrays")
