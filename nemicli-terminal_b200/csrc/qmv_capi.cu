@@ -135,6 +135,7 @@ int launch(int fmt, const MvParams& P, int T, cudaStream_t st) {
     case F_Q2_0: return launch_fmt<F_Q2_0>(P, T, st);
     case F_PQ2_0: return launch_fmt<F_PQ2_0>(P, T, st);
     case F_Q3_K: return launch_fmt<F_Q3_K>(P, T, st);
+    case F_Q2_K: return launch_fmt<F_Q2_K>(P, T, st);
     case F_IQ2_XS: return launch_fmt<F_IQ2_XS>(P, T, st);
     case F_IQ2_S: return launch_fmt<F_IQ2_S>(P, T, st);
     }
@@ -163,6 +164,7 @@ int launch_sums(int fmt, const MvParams& P, cudaStream_t st) {
     case F_Q2_0: return launch_t<F_Q2_0, 1, true>(P, st);
     case F_PQ2_0: return launch_t<F_PQ2_0, 1, true>(P, st);
     case F_Q3_K: return launch_t<F_Q3_K, 1, true>(P, st);
+    case F_Q2_K: return launch_t<F_Q2_K, 1, true>(P, st);
     case F_IQ2_XS: return launch_t<F_IQ2_XS, 1, true>(P, st);
     case F_IQ2_S: return launch_t<F_IQ2_S, 1, true>(P, st);
     }
@@ -304,6 +306,7 @@ int launch_tma(int fmt, TmaParams& P, const TmaPlan& pl, cudaStream_t st) {
     case F_Q2_0: return launch_tma_fmt<F_Q2_0, XF, SUMS>(P, pl, int(grid), st);
     case F_PQ2_0: return launch_tma_fmt<F_PQ2_0, XF, SUMS>(P, pl, int(grid), st);
     case F_Q3_K: return launch_tma_fmt<F_Q3_K, XF, SUMS>(P, pl, int(grid), st);
+    case F_Q2_K: return launch_tma_fmt<F_Q2_K, XF, SUMS>(P, pl, int(grid), st);
     case F_IQ2_XS: return launch_tma_fmt<F_IQ2_XS, XF, SUMS>(P, pl, int(grid), st);
     case F_IQ2_S: return launch_tma_fmt<F_IQ2_S, XF, SUMS>(P, pl, int(grid), st);
     }

@@ -504,6 +504,57 @@ __device__ __forceinline__ void lane_iq2x(const uint8_t* const (&rows)[RW], int 
     }
 }
 
+// ---- Q2_K: 84 B = scales[16] (low nibble: scale, high: min), qs[64], d, dmin (quant.py:284-292).  Lane q
+// takes values 32q..32q+31: 2-bit field 2 (q % 4) of qs[32 (q / 4) + l]; 16-value groups 2q, 2q + 1 with
+// weight scale d sc and minimum dmin m.  The minimum multiplies the quantised input's own 16-value sum,
+// xd (sum xq + sum xq2 / 254): xs covers 32 values, the minimum only 16.
+template <int T, int RW, bool SUMS>
+__device__ __forceinline__ void lane_q2k(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                         const Tok<T>& tk, float (&acc)[RW][T], int row0) {
+    const int n = q >> 2, s2 = 2 * (q & 3);
+    uint32_t w[RW][8];
+    float dl0[RW], dl1[RW], ml0[RW], ml1[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        const uint8_t* b = rows[r] + (long long)sb * 84;
+        const uint4 q0 = ldw16_a2(b + 16 + 32 * n), q1 = ldw16_a2(b + 32 + 32 * n);
+        const uint32_t Q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[r][i] = (Q[i] >> s2) & 0x03030303u;
+        const float d = h2f(ldw2(b + 80)), dm = h2f(ldw2(b + 82));
+        const uint32_t sc0 = ldw1(b + 2 * q), sc1 = ldw1(b + 2 * q + 1);
+        dl0[r] = d * float(sc0 & 15u); ml0[r] = dm * float(sc0 >> 4);
+        dl1[r] = d * float(sc1 & 15u); ml1[r] = dm * float(sc1 >> 4);
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const long long o = tk.tb[t] + (long long)sb * 256 + 32 * q;
+        const int4 x0 = ldx16(P.xq + o), x1 = ldx16(P.xq + o + 16);
+        const int4 y0 = ldx16(P.xq2 + o), y1 = ldx16(P.xq2 + o + 16);
+        const float dd = __ldg(P.xd + ((tk.tb[t] + (long long)sb * 256) >> 5) + q);
+        constexpr uint32_t one = 0x01010101u;
+        const int qa = dp4(one, x0.w, dp4(one, x0.z, dp4(one, x0.y, dp4(one, x0.x, 0))));
+        const int qb = dp4(one, x1.w, dp4(one, x1.z, dp4(one, x1.y, dp4(one, x1.x, 0))));
+        const int ra = dp4(one, y0.w, dp4(one, y0.z, dp4(one, y0.y, dp4(one, y0.x, 0))));
+        const int rb = dp4(one, y1.w, dp4(one, y1.z, dp4(one, y1.y, dp4(one, y1.x, 0))));
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            int sa = dp4(w[r][0], x0.x, 0); sa = dp4(w[r][1], x0.y, sa); sa = dp4(w[r][2], x0.z, sa); sa = dp4(w[r][3], x0.w, sa);
+            int sb2 = dp4(w[r][4], x1.x, 0); sb2 = dp4(w[r][5], x1.y, sb2); sb2 = dp4(w[r][6], x1.z, sb2); sb2 = dp4(w[r][7], x1.w, sb2);
+            int ua = dp4(w[r][0], y0.x, 0); ua = dp4(w[r][1], y0.y, ua); ua = dp4(w[r][2], y0.z, ua); ua = dp4(w[r][3], y0.w, ua);
+            int ub = dp4(w[r][4], y1.x, 0); ub = dp4(w[r][5], y1.y, ub); ub = dp4(w[r][6], y1.z, ub); ub = dp4(w[r][7], y1.w, ub);
+            if constexpr (SUMS) {
+                const long long base = (long long)row0 * (P.n_in / 16) + sb * 16 + 2 * q;
+                atomicAdd(P.s + base, sa); atomicAdd(P.s + base + 1, sb2);
+                atomicAdd(P.s2 + base, ua); atomicAdd(P.s2 + base + 1, ub);
+            } else {
+                acc[r][t] += dd * (dl0[r] * (float(sa) + float(ua) * kInv254) + dl1[r] * (float(sb2) + float(ub) * kInv254)
+                                   - ml0[r] * (float(qa) + float(ra) * kInv254) - ml1[r] * (float(qb) + float(rb) * kInv254));
+            }
+        }
+    }
+}
+
 // ---- Q8_0: 34 B = d (f16), int8[32] (quant.py:46-50).  Lane q takes block 8*sb + q.
 template <int T, int RW, bool SUMS>
 __device__ __forceinline__ void lane_q8_0(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
@@ -961,6 +1012,7 @@ __global__ void __launch_bounds__(256) mv_kernel(const MvParams P) {
             else if constexpr (bits_format(FMT)) lane_bits<T, RW, SUMS, FMT>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (FMT == F_Q3_K) lane_q3k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (iq2x_format(FMT)) lane_iq2x<T, RW, SUMS, FMT>(rows, sb, q, P, tk, acc, row0);
+            else if constexpr (FMT == F_Q2_K) lane_q2k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else lane_iq2xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, grid);
         }
         if constexpr (!SUMS) {

@@ -167,6 +167,7 @@ template <> struct UnitTraits<F_Q5_K> { static constexpr int VPU = 64, NS = 2, N
 template <> struct UnitTraits<F_Q3_K> { static constexpr int VPU = 32, NS = 2, NQ = 2; };   // two 16-value scales
 template <> struct UnitTraits<F_IQ2_XS> { static constexpr int VPU = 32, NS = 2, NQ = 2; };
 template <> struct UnitTraits<F_IQ2_S> { static constexpr int VPU = 32, NS = 2, NQ = 2; };
+template <> struct UnitTraits<F_Q2_K> { static constexpr int VPU = 32, NS = 2, NQ = 2; };
 template <> struct UnitTraits<F_Q6_K> { static constexpr int VPU = 64, NS = 4, NQ = 4; };
 // Q6_K with 32-value units (ql bytes 64n+16j..+15 of superblock b: 16 values of group j/2 and of j/2 + 2):
 // a smaller activation footprint, for the decode chain's register budget.  Internal tag only.
@@ -238,11 +239,21 @@ __device__ __forceinline__ void load_act(Act<FMT>& a, int u, const int8_t* xq, c
         a.d[1] = ldf<GLOBAL, SCALES>(xd, b * 8 + 2 * p + 1) * kInv254;
         a.s[0] = ldf<GLOBAL, SCALES>(xs, b * 8 + 2 * p);
         a.s[1] = ldf<GLOBAL, SCALES>(xs, b * 8 + 2 * p + 1);
-    } else if constexpr (FMT == F_Q3_K || iq2x_format(FMT)) {
+    } else if constexpr (FMT == F_Q3_K || iq2x_format(FMT) || FMT == F_Q2_K) {
         const int o = 32 * u;
         a.q[0] = ldq16<GLOBAL>(xq + o); a.q[1] = ldq16<GLOBAL>(xq + o + 16);
         a.r[0] = ldq16<GLOBAL>(xq2 + o); a.r[1] = ldq16<GLOBAL>(xq2 + o + 16);
         a.d[0] = a.d[1] = ldf<GLOBAL, SCALES>(xd, u) * kInv254;
+        if constexpr (FMT == F_Q2_K) {
+            // the minimum's activation: (xd / 254) (254 sum xq + sum xq2) of each 16-value half
+#pragma unroll
+            for (int g = 0; g < 2; ++g) {
+                const int4 x = a.q[g], y = a.r[g];
+                const int sq = dp4(0x01010101u, x.w, dp4(0x01010101u, x.z, dp4(0x01010101u, x.y, dp4(0x01010101u, x.x, 0))));
+                const int sr = dp4(0x01010101u, y.w, dp4(0x01010101u, y.z, dp4(0x01010101u, y.y, dp4(0x01010101u, y.x, 0))));
+                a.s[g] = a.d[g] * float(254 * sq + sr);
+            }
+        }
     } else if constexpr (FMT == F_Q6_K_U32) {
         const int b = u >> 3, q = u & 7, n = q >> 2, j = q & 3, A = j >> 1, B = A + 2, o = b * 256 + 128 * n + 16 * (j & 1);
         a.q[0] = ldq16<GLOBAL>(xq + o + 32 * A); a.q[1] = ldq16<GLOBAL>(xq + o + 32 * B);
@@ -491,6 +502,24 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
         o.wsc[0] = d * (0.125f + 0.25f * float(scb & 15u));
         o.wsc[1] = d * (0.125f + 0.25f * float(scb >> 4));
         o.off[0] = o.off[1] = 0.f;
+    } else if constexpr (FMT == F_Q2_K) {
+        const int b = u >> 3, q = u & 7, n = q >> 2, s2 = 2 * (q & 3);
+        const uint32_t sb = rs + b * 84;
+        const uint4 q0 = lds16_a2(sb + 16 + 32 * n), q1 = lds16_a2(sb + 32 + 32 * n);
+        const uint32_t w0[4] = {(q0.x >> s2) & 0x03030303u, (q0.y >> s2) & 0x03030303u, (q0.z >> s2) & 0x03030303u,
+                                (q0.w >> s2) & 0x03030303u};
+        const uint32_t w1[4] = {(q1.x >> s2) & 0x03030303u, (q1.y >> s2) & 0x03030303u, (q1.z >> s2) & 0x03030303u,
+                                (q1.w >> s2) & 0x03030303u};
+        o.s[0] = dot4(w0, a.q[0]);
+        o.u[0] = dot4(w0, a.r[0]);
+        o.s[1] = dot4(w1, a.q[1]);
+        o.u[1] = dot4(w1, a.r[1]);
+        const float d = h2f(lds16u(sb + 80)), dm = h2f(lds16u(sb + 82));
+        const uint32_t sc0 = lds8u(sb + 2 * q), sc1 = lds8u(sb + 2 * q + 1);
+        o.wsc[0] = d * float(sc0 & 15u);
+        o.wsc[1] = d * float(sc1 & 15u);
+        o.off[0] = dm * float(sc0 >> 4);
+        o.off[1] = dm * float(sc1 >> 4);
     } else if constexpr (FMT == F_Q3_K) {
         const int b = u >> 3, q = u & 7, n = q >> 2, s2 = 2 * (q & 3);
         const uint32_t sb = rs + b * 110;
@@ -646,7 +675,7 @@ __device__ __forceinline__ int sum_unit(int u, int k) {
                   FMT == F_IQ4_NL || bits_format(FMT))
         return u;
     if constexpr (FMT == F_Q4_K || FMT == F_Q5_K) return 2 * u + k;   // unit u = sub-blocks 2u, 2u + 1 of the row
-    if constexpr (FMT == F_Q3_K || iq2x_format(FMT)) return 2 * u + k;   // the two 16-value scale groups of unit u
+    if constexpr (FMT == F_Q3_K || iq2x_format(FMT) || FMT == F_Q2_K) return 2 * u + k;   // 16-value groups of unit u
     const int b = u >> 3, q = u & 7;
     if constexpr (FMT == F_Q6_K) {
         const int b6 = u >> 2, n = (u >> 1) & 1, h = u & 1;     // group k: values 128n + 32k + 16h.. of b6

@@ -8,7 +8,7 @@ meaning and return shapes, computed by this package's sm_100a kernels through th
 * `mm` — the reference's 17..112-token entry (mmvq.py:902-918); here the same int8 kernels in groups
   of SPALTEN tokens (the tensor-core tile path for long inputs is a separate, later kernel).
 
-Where the reference takes Q4_K and Q6_K only, these kernels take all twenty-one block formats of the path
+Where the reference takes Q4_K and Q6_K only, these kernels take all twenty-two block formats of the path
 (`FORMATE`: the classic, K-quant, IQ, MXFP4, ternary and 1-bit formats).  Everything runs on torch's current stream and is CUDA-graph
 safe (no host reads, no synchronisation).  Non-CUDA tensors or unsupported formats raise; nothing
 falls back to another implementation.
@@ -210,7 +210,7 @@ def mm(fmt: str, raw: torch.Tensor, x: torch.Tensor, n_out: int, n_in: int) -> t
 def block_sums(fmt: str, raw: torch.Tensor, e: Eingang, n_out: int, n_in: int):
     """Test hook: the int32 sums (code*xq, code*xq2) per row and unit of one token (include/nemicli_qmv.h)."""
     _check_raw(fmt, raw, n_out, n_in)
-    unit = 16 if fmt in ("Q6_K", "Q3_K", "IQ2_XS", "IQ2_S") else 32
+    unit = 16 if fmt in ("Q6_K", "Q3_K", "IQ2_XS", "IQ2_S", "Q2_K") else 32
     s = torch.empty(n_out, n_in // unit, dtype=torch.int32, device=raw.device)
     s2 = torch.empty_like(s)
     _lib.check(_lib.load().qmv_block_sums(TYPE_ID[fmt], _lib.ptr(raw), n_out, n_in, _lib.ptr(e.xq), _lib.ptr(e.xq2),

@@ -11,10 +11,10 @@
  *     restatement uses IEEE-rounded division and an explicit fused multiply-add so that it is
  *     reproducible bit for bit on the GPU (the kernels do the same).  Against the reference's
  *     fast-math build a quantised value can differ by one unit on a rounding tie.
- *   - the block dequantisers of ggufengine/quant.py for the twenty-one in-scope formats:
+ *   - the block dequantisers of ggufengine/quant.py for the twenty-two in-scope formats:
  *     deq_q4_0 :60, deq_q4_1 :67, deq_q5_0 :83, deq_q5_1 :90 (+ _q5_high_bits :74), deq_iq4_nl :264,
  *     deq_q1_0 :424, deq_q2_0 :410 (and PQ2_0, the same codes in 34-byte blocks of 128 values),
- *     deq_q3_k :295, deq_iq2_xs :310 and deq_iq2_s :248 (IQ2XS_GRID, IQ2S_GRID, compact in
+ *     deq_q2_k :284, deq_q3_k :295, deq_iq2_xs :310 and deq_iq2_s :248 (IQ2XS_GRID, IQ2S_GRID, compact in
  *     csrc/iq2xs_grid.inc, csrc/iq2s_grid.inc), deq_q8_0 :46, deq_q4_k :111 (+ _scale_min_k4 :99), deq_q5_k :123, deq_q6_k :140,
  *     deq_iq4_xs :378 (codebook KVALUES_IQ4NL, ggufengine/iqtabellen.py:7), deq_mxfp4 :394
  *     (KVALUES_MXFP4 :391, scale 2^(e-128) as the reference builds its float bits), deq_iq3_s :334
@@ -33,7 +33,9 @@
  * Sum units (the values that share one weight scale and one activation scale):
  *   Q4_K, Q5_K, Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, TQ2_0, IQ2_XXS, IQ3_XXS, IQ3_S, IQ4_NL, IQ4_XS, MXFP4: 32
  *   values (n_in/32 units).  Q4_1 and Q5_1 take their +m offset and Q5_0 its -16 d offset with xs.
- *   Q3_K, IQ2_XS, IQ2_S: 16 values (their scale groups; Q3_K codes q2 - 4 (1 - hbit), signed).
+ *   Q3_K, IQ2_XS, IQ2_S, Q2_K: 16 values (their scale groups; Q3_K codes q2 - 4 (1 - hbit), signed).
+ *   Q2_K's minimum applies per 16 values, finer than xs: its offset multiplies the quantised input's own
+ *   16-value sum, xd (sum xq + sum xq2 / 254), the same activation the code sums see.
  *   Q1_0, Q2_0, PQ2_0: 32-value units inside 128 / 64 / 128-value blocks; codes bit (weight 2 d, offset
  *   d: d (2 b - 1)) and q (offset d: d (q - 1)).
  *   Q6_K: 16.
@@ -55,7 +57,7 @@
 
 enum { T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ2_XXS = 16, T_IQ4_XS = 23, T_TQ2_0 = 35, T_MXFP4 = 39,
        T_IQ3_S = 21, T_IQ3_XXS = 18, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_IQ4_NL = 20,
-       T_Q1_0 = 41, T_Q2_0 = 42, T_PQ2_0 = 142, T_Q3_K = 11, T_IQ2_XS = 17, T_IQ2_S = 22 };
+       T_Q1_0 = 41, T_Q2_0 = 42, T_PQ2_0 = 142, T_Q3_K = 11, T_IQ2_XS = 17, T_IQ2_S = 22, T_Q2_K = 10 };
 
 static const uint16_t IQ2XS_CODES[512] = {
 #include "../nemicli-terminal_b200/csrc/iq2xs_grid.inc"
@@ -145,7 +147,7 @@ int orc_block_values(int fmt) {
     case T_Q2_0: return 64;
     case T_Q1_0: case T_PQ2_0: return 128;
     case T_Q4_K: case T_Q5_K: case T_Q6_K: case T_IQ2_XXS: case T_IQ3_XXS: case T_IQ3_S: case T_IQ4_XS:
-    case T_TQ2_0: case T_Q3_K: case T_IQ2_XS: case T_IQ2_S: return 256;
+    case T_TQ2_0: case T_Q3_K: case T_IQ2_XS: case T_IQ2_S: case T_Q2_K: return 256;
     }
     return 0;
 }
@@ -170,6 +172,7 @@ int orc_block_bytes(int fmt) {
     case T_Q3_K: return 110;
     case T_IQ2_XS: return 74;
     case T_IQ2_S: return 82;
+    case T_Q2_K: return 84;
     case T_TQ2_0: return 66;
     case T_MXFP4: return 17;
     }
@@ -177,7 +180,11 @@ int orc_block_bytes(int fmt) {
 }
 
 /* values per integer-sum unit */
-int orc_unit_values(int fmt) { return fmt == T_Q6_K || fmt == T_Q3_K || fmt == T_IQ2_XS || fmt == T_IQ2_S ? 16 : 32; }
+int orc_unit_values(int fmt) {
+    return fmt == T_Q6_K || fmt == T_Q3_K || fmt == T_IQ2_XS || fmt == T_IQ2_S || fmt == T_Q2_K ? 16 : 32;
+}
+/* Q2_K (84 B = scales[16] (scale nibble, min nibble), qs[64], d, dmin; quant.py:284-292): code of value v */
+static int q2k_code(const uint8_t* b, int v) { return (b[16 + 32 * (v / 128) + v % 32] >> (2 * ((v % 128) / 32))) & 3; }
 
 /* Q3_K (110 B = hmask[32], qs[64], scales[12], d; quant.py:295-306): scale group i (16 values) and the
    signed code of value v (0..255) */
@@ -341,6 +348,14 @@ int orc_dequant(int fmt, const uint8_t* raw, long long n_values, float* out) {
             }
             break;
         }
+        case T_Q2_K: {
+            const float d = f16(b + 80), dmin = f16(b + 82);
+            for (int i = 0; i < 16; ++i) {
+                const float dl = d * (float)(b[i] & 15), ml = dmin * (float)(b[i] >> 4);
+                for (int l = 0; l < 16; ++l) o[16 * i + l] = dl * (float)q2k_code(b, 16 * i + l) - ml;
+            }
+            break;
+        }
         case T_IQ2_XS: case T_IQ2_S: {
             const float d = f16(b);
             for (int i = 0; i < 16; ++i) {
@@ -500,6 +515,7 @@ static int code_of(int fmt, const uint8_t* b, int v) {
     case T_Q2_0: case T_PQ2_0: return (b[2 + v / 4] >> (2 * (v % 4))) & 3;
     case T_Q1_0: return (b[2 + v / 8] >> (v % 8)) & 1;
     case T_Q3_K: return q3k_code(b, v);
+    case T_Q2_K: return q2k_code(b, v);
     case T_IQ2_XS: case T_IQ2_S: return iq2xs_value(b, fmt, v);
     case T_Q4_K: { const int j = v >> 5, i = v & 31; return (b[16 + 32 * (j >> 1) + i] >> (4 * (j & 1))) & 15; }
     case T_Q5_K: {
@@ -557,6 +573,7 @@ static void unit_scales(int fmt, const uint8_t* b, int u, double* wscale, double
     case T_Q2_0: case T_PQ2_0: *wscale = f16(b); *offs = f16(b); return;
     case T_Q1_0: *wscale = 2.0 * f16(b); *offs = f16(b); return;
     case T_Q3_K: *wscale = (double)f16(b + 108) * (double)q3k_scale(b, u); *offs = 0.0; return;
+    case T_Q2_K: *wscale = (double)f16(b + 80) * (double)(b[u] & 15); *offs = (double)f16(b + 82) * (double)(b[u] >> 4); return;
     case T_IQ2_XS: case T_IQ2_S:
         *wscale = (double)f16(b) * (0.125 + 0.25 * (double)iq2xs_scale(b, fmt, u));
         *offs = 0.0;
@@ -616,18 +633,21 @@ int orc_mv(int fmt, const uint8_t* w, int n_out, int n_in, const int8_t* xq, con
             for (int blk = 0; blk < n_in / bv; ++blk) {
                 const uint8_t* b = w + r * row_bytes + (long long)blk * bb;
                 for (int ub = 0; ub < upb; ++ub) {
-                    int32_t a = 0, a2 = 0;
+                    int32_t a = 0, a2 = 0, qa = 0, qa2 = 0;
                     const int v0 = blk * bv + ub * uv;
                     for (int i = 0; i < uv; ++i) {
                         const int c = code_of(fmt, b, ub * uv + i);
                         a += c * q[v0 + i];
                         a2 += c * q2[v0 + i];
+                        qa += q[v0 + i];
+                        qa2 += q2[v0 + i];
                     }
                     double wscale, offs;
                     unit_scales(fmt, b, ub, &wscale, &offs);
                     const int g = v0 / 32;
                     acc += wscale * (double)dd[g] * ((double)a + (double)a2 / 254.0);
-                    if (v0 % 32 == 0) acc -= offs * (double)ss[g];
+                    if (fmt == T_Q2_K) acc -= offs * (double)dd[g] * ((double)qa + (double)qa2 / 254.0);
+                    else if (v0 % 32 == 0) acc -= offs * (double)ss[g];
                 }
             }
             y[(long long)t * n_out + r] = acc;
