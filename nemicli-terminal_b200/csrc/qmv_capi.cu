@@ -136,6 +136,7 @@ int launch(int fmt, const MvParams& P, int T, cudaStream_t st) {
     case F_PQ2_0: return launch_fmt<F_PQ2_0>(P, T, st);
     case F_Q3_K: return launch_fmt<F_Q3_K>(P, T, st);
     case F_Q2_K: return launch_fmt<F_Q2_K>(P, T, st);
+    case F_TQ1_0: return launch_fmt<F_TQ1_0>(P, T, st);
     case F_IQ2_XS: return launch_fmt<F_IQ2_XS>(P, T, st);
     case F_IQ2_S: return launch_fmt<F_IQ2_S>(P, T, st);
     }
@@ -165,6 +166,7 @@ int launch_sums(int fmt, const MvParams& P, cudaStream_t st) {
     case F_PQ2_0: return launch_t<F_PQ2_0, 1, true>(P, st);
     case F_Q3_K: return launch_t<F_Q3_K, 1, true>(P, st);
     case F_Q2_K: return launch_t<F_Q2_K, 1, true>(P, st);
+    case F_TQ1_0: return launch_t<F_TQ1_0, 1, true>(P, st);
     case F_IQ2_XS: return launch_t<F_IQ2_XS, 1, true>(P, st);
     case F_IQ2_S: return launch_t<F_IQ2_S, 1, true>(P, st);
     }
@@ -204,6 +206,7 @@ const TmaKnobs& knobs() {
 // when a team of <= 512 lanes covers the row; fused quantisation reserves 2.25 * n_in bytes.
 bool tma_plan(int fmt, int n_in, long long row_bytes, bool fused, TmaPlan& pl) {
     if (!knobs().enabled || row_bytes % 16 || n_in % unit_vals(fmt)) return false;
+    if (fmt == F_TQ1_0) return false;          // TQ1_0 runs on the warp-per-row kernel only
     const int ncw = knobs().ncw;
     const int cap = ncw <= 8 ? kSmemHalf : kSmemCap;
     const int U = n_in / unit_vals(fmt);

@@ -6,11 +6,11 @@
 
 namespace qmv {
 
-// GGML type ids of the twenty-two formats (PQ2_0 = 142: the reference's id for the 128-value Q2_0 variant) (the GGUF type table; reference ggufengine/gguf.py:64-77)
+// GGML type ids of the twenty-three formats (PQ2_0 = 142: the reference's id for the 128-value Q2_0 variant) (the GGUF type table; reference ggufengine/gguf.py:64-77)
 enum : int {
     F_Q4_0 = 2, F_Q8_0 = 8, F_Q4_K = 12, F_Q5_K = 13, F_Q6_K = 14, F_IQ2_XXS = 16, F_IQ4_XS = 23, F_TQ2_0 = 35,
     F_MXFP4 = 39, F_IQ3_S = 21, F_IQ3_XXS = 18, F_Q4_1 = 3, F_Q5_0 = 6, F_Q5_1 = 7, F_IQ4_NL = 20,
-    F_Q1_0 = 41, F_Q2_0 = 42, F_PQ2_0 = 142, F_Q3_K = 11, F_IQ2_XS = 17, F_IQ2_S = 22, F_Q2_K = 10
+    F_Q1_0 = 41, F_Q2_0 = 42, F_PQ2_0 = 142, F_Q3_K = 11, F_IQ2_XS = 17, F_IQ2_S = 22, F_Q2_K = 10, F_TQ1_0 = 34
 };
 // IQ2_XS / IQ2_S: 16-value scale groups, eight-magnitude codebook entries
 __host__ __device__ constexpr bool iq2x_format(int f) { return f == F_IQ2_XS || f == F_IQ2_S; }
@@ -45,7 +45,7 @@ __host__ __device__ constexpr int block_values(int f) {
     return b32_format(f) ? 32 : f == F_Q2_0 ? 64 : (f == F_Q1_0 || f == F_PQ2_0) ? 128 : 256;
 }
 __host__ __device__ constexpr int block_bytes(int f) {
-    return f == F_Q4_0 || f == F_IQ4_NL || f == F_Q1_0 || f == F_Q2_0 ? 18 : f == F_PQ2_0 ? 34 : f == F_Q3_K ? 110 : f == F_Q2_K ? 84 : f == F_IQ2_XS ? 74 : f == F_IQ2_S ? 82 : f == F_Q4_1 ? 20 : f == F_Q5_0 ? 22 : f == F_Q5_1 ? 24 : f == F_Q8_0 ? 34 : f == F_Q4_K ? 144 : f == F_Q5_K ? 176 : f == F_Q6_K ? 210
+    return f == F_Q4_0 || f == F_IQ4_NL || f == F_Q1_0 || f == F_Q2_0 ? 18 : f == F_PQ2_0 ? 34 : f == F_Q3_K ? 110 : f == F_Q2_K ? 84 : f == F_TQ1_0 ? 54 : f == F_IQ2_XS ? 74 : f == F_IQ2_S ? 82 : f == F_Q4_1 ? 20 : f == F_Q5_0 ? 22 : f == F_Q5_1 ? 24 : f == F_Q8_0 ? 34 : f == F_Q4_K ? 144 : f == F_Q5_K ? 176 : f == F_Q6_K ? 210
          : f == F_IQ4_XS ? 136 : f == F_MXFP4 ? 17 : f == F_IQ3_S ? 110
          : f == F_IQ3_XXS ? 98 : 66;
 }
@@ -60,7 +60,7 @@ __device__ __forceinline__ uint32_t q3k_word(uint32_t q2, uint32_t h1) { return 
 __host__ __device__ inline bool known_format(int f) {
     return f == F_Q4_0 || f == F_Q8_0 || f == F_Q4_K || f == F_Q5_K || f == F_Q6_K || f == F_IQ2_XXS || f == F_IQ4_XS ||
            f == F_TQ2_0 || f == F_MXFP4 || f == F_IQ3_S || f == F_IQ3_XXS || f == F_Q4_1 || f == F_Q5_0 ||
-           f == F_Q5_1 || f == F_IQ4_NL || bits_format(f) || f == F_Q3_K || iq2x_format(f) || f == F_Q2_K;
+           f == F_Q5_1 || f == F_IQ4_NL || bits_format(f) || f == F_Q3_K || iq2x_format(f) || f == F_Q2_K || f == F_TQ1_0;
 }
 // weight rows and blocks of the K-quant formats with 16-byte header words are read 16 bytes at a time;
 // MXFP4's 17-byte blocks start at any byte, and their loads stay inside the tensor when it starts on a

@@ -555,6 +555,69 @@ __device__ __forceinline__ void lane_q2k(const uint8_t* const (&rows)[RW], int s
     }
 }
 
+// ---- TQ1_0: 54 B = qs[48], qh[4], d (quant.py:405-458).  Five trits per byte as a fixed-point fraction:
+// trit n of byte v = ((v 3^n) mod 256) 3 >> 8.  Values 0..159: byte j % 32, n = j / 32; 160..239: byte
+// 32 + (j - 160) % 16, n = (j - 160) / 16; 240..255: byte 48 + (j - 240) % 4, n = (j - 240) / 4.  Lane q
+// takes values 32q..32q+31; every four consecutive values share one power, so the trits of a word come
+// out together (bytes multiplied in 16-bit lanes).  The code is the trit, value d (trit - 1): offset d xs.
+__device__ __forceinline__ uint32_t trits4(uint32_t w, uint32_t pw) {
+    const uint32_t lo = ((w & 0x00FF00FFu) * pw) & 0x00FF00FFu, hi = (((w >> 8) & 0x00FF00FFu) * pw) & 0x00FF00FFu;
+    return (((lo * 3u) >> 8) & 0x00030003u) | ((((hi * 3u) >> 8) & 0x00030003u) << 8);
+}
+template <int T, int RW, bool SUMS>
+__device__ __forceinline__ void lane_tq1(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                         const Tok<T>& tk, float (&acc)[RW][T], int row0) {
+    uint32_t w[RW][8];
+    float d[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        const uint8_t* b = rows[r] + (long long)sb * 54;
+        d[r] = h2f(ldw2(b + 52));
+        if (q < 5) {
+            const uint32_t pw = q == 0 ? 1u : q == 1 ? 3u : q == 2 ? 9u : q == 3 ? 27u : 81u;
+            const uint4 a0 = ldw16_a2(b), a1 = ldw16_a2(b + 16);
+            const uint32_t V[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) w[r][i] = trits4(V[i], pw);
+        } else {
+            const uint4 a = ldw16_a2(b + 32);
+            const uint32_t V[4] = {a.x, a.y, a.z, a.w};
+            const uint32_t p0 = q == 5 ? 1u : q == 6 ? 9u : 81u, p1 = q == 5 ? 3u : 27u;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) w[r][i] = trits4(V[i], p0);
+            if (q < 7) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) w[r][4 + i] = trits4(V[i], p1);
+            } else {
+                const uint32_t h = ldw2(b + 48) | (ldw2(b + 50) << 16);
+                w[r][4] = trits4(h, 1u); w[r][5] = trits4(h, 3u); w[r][6] = trits4(h, 9u); w[r][7] = trits4(h, 27u);
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const long long o = tk.tb[t] + (long long)sb * 256 + 32 * q;
+        const int4 x0 = ldx16(P.xq + o), x1 = ldx16(P.xq + o + 16);
+        const int4 y0 = ldx16(P.xq2 + o), y1 = ldx16(P.xq2 + o + 16);
+        const long long g = ((tk.tb[t] + (long long)sb * 256) >> 5) + q;
+        const float dd = __ldg(P.xd + g), ss = __ldg(P.xs + g);
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            int s = dp4(w[r][0], x0.x, 0); s = dp4(w[r][1], x0.y, s); s = dp4(w[r][2], x0.z, s); s = dp4(w[r][3], x0.w, s);
+            s = dp4(w[r][4], x1.x, s); s = dp4(w[r][5], x1.y, s); s = dp4(w[r][6], x1.z, s); s = dp4(w[r][7], x1.w, s);
+            int u = dp4(w[r][0], y0.x, 0); u = dp4(w[r][1], y0.y, u); u = dp4(w[r][2], y0.z, u); u = dp4(w[r][3], y0.w, u);
+            u = dp4(w[r][4], y1.x, u); u = dp4(w[r][5], y1.y, u); u = dp4(w[r][6], y1.z, u); u = dp4(w[r][7], y1.w, u);
+            if constexpr (SUMS) {
+                const long long base = (long long)row0 * (P.n_in / 32) + sb * 8 + q;
+                atomicAdd(P.s + base, s);
+                atomicAdd(P.s2 + base, u);
+            } else {
+                acc[r][t] += d[r] * (dd * (float(s) + float(u) * kInv254) - ss);
+            }
+        }
+    }
+}
+
 // ---- Q8_0: 34 B = d (f16), int8[32] (quant.py:46-50).  Lane q takes block 8*sb + q.
 template <int T, int RW, bool SUMS>
 __device__ __forceinline__ void lane_q8_0(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
@@ -1013,6 +1076,7 @@ __global__ void __launch_bounds__(256) mv_kernel(const MvParams P) {
             else if constexpr (FMT == F_Q3_K) lane_q3k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (iq2x_format(FMT)) lane_iq2x<T, RW, SUMS, FMT>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (FMT == F_Q2_K) lane_q2k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+            else if constexpr (FMT == F_TQ1_0) lane_tq1<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else lane_iq2xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, grid);
         }
         if constexpr (!SUMS) {

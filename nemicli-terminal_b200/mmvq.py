@@ -8,7 +8,7 @@ meaning and return shapes, computed by this package's sm_100a kernels through th
 * `mm` — the reference's 17..112-token entry (mmvq.py:902-918); here the same int8 kernels in groups
   of SPALTEN tokens (the tensor-core tile path for long inputs is a separate, later kernel).
 
-Where the reference takes Q4_K and Q6_K only, these kernels take all twenty-two block formats of the path
+Where the reference takes Q4_K and Q6_K only, these kernels take all twenty-three block formats of the path
 (`FORMATE`: the classic, K-quant, IQ, MXFP4, ternary and 1-bit formats).  Everything runs on torch's current stream and is CUDA-graph
 safe (no host reads, no synchronisation).  Non-CUDA tensors or unsupported formats raise; nothing
 falls back to another implementation.

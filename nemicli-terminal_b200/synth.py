@@ -3,7 +3,7 @@
 The reference names no dataset or public benchmark for this path; its configs are synthetic.  The
 generators below follow each config's stated distributions and write the exact GGUF block layouts
 (ggufengine/quant.py documents them: Q4_0 :60, Q4_1 :67, Q5_0 :83, Q5_1 :90, IQ4_NL :264, Q1_0 :424,
-Q2_0 :410, Q2_K :284, Q3_K :295, IQ2_XS :310, IQ2_S :248, Q8_0 :46, Q4_K :111, Q5_K :123, Q6_K :140, IQ3_XXS :322, IQ3_S :334, IQ4_XS :378, MXFP4 :394, TQ2_0 :417,
+Q2_0 :410, Q2_K :284, Q3_K :295, TQ1_0 :449, IQ2_XS :310, IQ2_S :248, Q8_0 :46, Q4_K :111, Q5_K :123, Q6_K :140, IQ3_XXS :322, IQ3_S :334, IQ4_XS :378, MXFP4 :394, TQ2_0 :417,
 IQ2_XXS :235).  Everything is torch, so it runs on the CPU (tests) or on the GPU (bench, where the
 largest stacks are several GB).
 """
@@ -70,6 +70,8 @@ def blocks(fmt: str, n_rows: int, n_in: int, seed: int = 0, device="cpu",
         out = torch.cat([_f16_bytes(_abs_normal(nb, 0.01 / 127, g, device)), _bytes(nb, 16, g, device)], 1)
     elif fmt in ("IQ2_XS", "IQ2_S"):        # d = |N| * 0.01; indices, signs, scales uniform
         out = torch.cat([_f16_bytes(_abs_normal(nb, 0.01, g, device)), _bytes(nb, bb - 2, g, device)], 1)
+    elif fmt == "TQ1_0":                    # trit bytes uniform; d = |N| * 0.01
+        out = torch.cat([_bytes(nb, 52, g, device), _f16_bytes(_abs_normal(nb, 0.01, g, device))], 1)
     elif fmt == "Q2_K":                     # scale/min bytes and codes uniform; d, dmin = |N| * 0.005
         out = torch.cat([_bytes(nb, 80, g, device), _f16_bytes(_abs_normal(nb, 0.005, g, device)),
                          _f16_bytes(_abs_normal(nb, 0.005, g, device))], 1)

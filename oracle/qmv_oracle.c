@@ -11,10 +11,10 @@
  *     restatement uses IEEE-rounded division and an explicit fused multiply-add so that it is
  *     reproducible bit for bit on the GPU (the kernels do the same).  Against the reference's
  *     fast-math build a quantised value can differ by one unit on a rounding tie.
- *   - the block dequantisers of ggufengine/quant.py for the twenty-two in-scope formats:
+ *   - the block dequantisers of ggufengine/quant.py for the twenty-three in-scope formats:
  *     deq_q4_0 :60, deq_q4_1 :67, deq_q5_0 :83, deq_q5_1 :90 (+ _q5_high_bits :74), deq_iq4_nl :264,
  *     deq_q1_0 :424, deq_q2_0 :410 (and PQ2_0, the same codes in 34-byte blocks of 128 values),
- *     deq_q2_k :284, deq_q3_k :295, deq_iq2_xs :310 and deq_iq2_s :248 (IQ2XS_GRID, IQ2S_GRID, compact in
+ *     deq_q2_k :284, deq_q3_k :295, TQ1_0 (_deq_trits :449 with trit_plan :430), deq_iq2_xs :310 and deq_iq2_s :248 (IQ2XS_GRID, IQ2S_GRID, compact in
  *     csrc/iq2xs_grid.inc, csrc/iq2s_grid.inc), deq_q8_0 :46, deq_q4_k :111 (+ _scale_min_k4 :99), deq_q5_k :123, deq_q6_k :140,
  *     deq_iq4_xs :378 (codebook KVALUES_IQ4NL, ggufengine/iqtabellen.py:7), deq_mxfp4 :394
  *     (KVALUES_MXFP4 :391, scale 2^(e-128) as the reference builds its float bits), deq_iq3_s :334
@@ -57,7 +57,7 @@
 
 enum { T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ2_XXS = 16, T_IQ4_XS = 23, T_TQ2_0 = 35, T_MXFP4 = 39,
        T_IQ3_S = 21, T_IQ3_XXS = 18, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_IQ4_NL = 20,
-       T_Q1_0 = 41, T_Q2_0 = 42, T_PQ2_0 = 142, T_Q3_K = 11, T_IQ2_XS = 17, T_IQ2_S = 22, T_Q2_K = 10 };
+       T_Q1_0 = 41, T_Q2_0 = 42, T_PQ2_0 = 142, T_Q3_K = 11, T_IQ2_XS = 17, T_IQ2_S = 22, T_Q2_K = 10, T_TQ1_0 = 34 };
 
 static const uint16_t IQ2XS_CODES[512] = {
 #include "../nemicli-terminal_b200/csrc/iq2xs_grid.inc"
@@ -147,7 +147,7 @@ int orc_block_values(int fmt) {
     case T_Q2_0: return 64;
     case T_Q1_0: case T_PQ2_0: return 128;
     case T_Q4_K: case T_Q5_K: case T_Q6_K: case T_IQ2_XXS: case T_IQ3_XXS: case T_IQ3_S: case T_IQ4_XS:
-    case T_TQ2_0: case T_Q3_K: case T_IQ2_XS: case T_IQ2_S: case T_Q2_K: return 256;
+    case T_TQ2_0: case T_Q3_K: case T_IQ2_XS: case T_IQ2_S: case T_Q2_K: case T_TQ1_0: return 256;
     }
     return 0;
 }
@@ -173,6 +173,7 @@ int orc_block_bytes(int fmt) {
     case T_IQ2_XS: return 74;
     case T_IQ2_S: return 82;
     case T_Q2_K: return 84;
+    case T_TQ1_0: return 54;
     case T_TQ2_0: return 66;
     case T_MXFP4: return 17;
     }
@@ -182,6 +183,17 @@ int orc_block_bytes(int fmt) {
 /* values per integer-sum unit */
 int orc_unit_values(int fmt) {
     return fmt == T_Q6_K || fmt == T_Q3_K || fmt == T_IQ2_XS || fmt == T_IQ2_S || fmt == T_Q2_K ? 16 : 32;
+}
+/* TQ1_0 (54 B = qs[48], qh[4], d; quant.py:405-458): five trits per byte as a fixed-point fraction, trit n of
+   byte v = ((v 3^n) mod 256) 3 >> 8.  Value j < 160: byte j % 32, n = j / 32; j < 240: byte 32 + (j - 160) % 16,
+   n = (j - 160) / 16; else byte 48 + (j - 240) % 4, n = (j - 240) / 4.  The code is the trit (offset d xs). */
+static int tq1_trit(const uint8_t* b, int v) {
+    static const int pw[5] = {1, 3, 9, 27, 81};
+    int byte, n;
+    if (v < 160) { byte = v % 32; n = v / 32; }
+    else if (v < 240) { byte = 32 + (v - 160) % 16; n = (v - 160) / 16; }
+    else { byte = 48 + (v - 240) % 4; n = (v - 240) / 4; }
+    return (((b[byte] * pw[n]) & 255) * 3) >> 8;
 }
 /* Q2_K (84 B = scales[16] (scale nibble, min nibble), qs[64], d, dmin; quant.py:284-292): code of value v */
 static int q2k_code(const uint8_t* b, int v) { return (b[16 + 32 * (v / 128) + v % 32] >> (2 * ((v % 128) / 32))) & 3; }
@@ -346,6 +358,11 @@ int orc_dequant(int fmt, const uint8_t* raw, long long n_values, float* out) {
                     o[i + 16] = d * ((float)hi - 16.0f);
                 }
             }
+            break;
+        }
+        case T_TQ1_0: {
+            const float d = f16(b + 52);
+            for (int j = 0; j < 256; ++j) o[j] = d * ((float)tq1_trit(b, j) - 1.0f);
             break;
         }
         case T_Q2_K: {
@@ -516,6 +533,7 @@ static int code_of(int fmt, const uint8_t* b, int v) {
     case T_Q1_0: return (b[2 + v / 8] >> (v % 8)) & 1;
     case T_Q3_K: return q3k_code(b, v);
     case T_Q2_K: return q2k_code(b, v);
+    case T_TQ1_0: return tq1_trit(b, v);
     case T_IQ2_XS: case T_IQ2_S: return iq2xs_value(b, fmt, v);
     case T_Q4_K: { const int j = v >> 5, i = v & 31; return (b[16 + 32 * (j >> 1) + i] >> (4 * (j & 1))) & 15; }
     case T_Q5_K: {
@@ -573,6 +591,7 @@ static void unit_scales(int fmt, const uint8_t* b, int u, double* wscale, double
     case T_Q2_0: case T_PQ2_0: *wscale = f16(b); *offs = f16(b); return;
     case T_Q1_0: *wscale = 2.0 * f16(b); *offs = f16(b); return;
     case T_Q3_K: *wscale = (double)f16(b + 108) * (double)q3k_scale(b, u); *offs = 0.0; return;
+    case T_TQ1_0: *wscale = f16(b + 52); *offs = f16(b + 52); return;
     case T_Q2_K: *wscale = (double)f16(b + 80) * (double)(b[u] & 15); *offs = (double)f16(b + 82) * (double)(b[u] >> 4); return;
     case T_IQ2_XS: case T_IQ2_S:
         *wscale = (double)f16(b) * (0.125 + 0.25 * (double)iq2xs_scale(b, fmt, u));

@@ -26,7 +26,8 @@ tests/test_gguf_iq.py:81-101, zufallsbloecke).  Extra cases pin the corners:
 * Q3_K blocks with every 6-bit scale (-32..31) and every high bit set or clear,
 * IQ2_XS / IQ2_S blocks whose codebook indices run through all 512 / 1024 entries, with every sign
   pattern and every 4-bit scale,
-* Q2_K blocks with every scale/min byte.
+* Q2_K blocks with every scale/min byte,
+* TQ1_0 blocks with every byte value in every trit position.
 
 Formats added later are generated after the earlier cases, so the earlier arrays stay as they were.
 """
@@ -49,16 +50,17 @@ LATER7 = {"Q1_0": (41, 128, 18), "Q2_0": (42, 64, 18), "PQ2_0": (142, 128, 34)}
 LATER8 = {"Q3_K": (11, 256, 110)}
 LATER9 = {"IQ2_XS": (17, 256, 74), "IQ2_S": (22, 256, 82)}
 LATER10 = {"Q2_K": (10, 256, 84)}
+LATER11 = {"TQ1_0": (34, 256, 54)}
 SCALE_OFFSETS = {"Q4_0": (0,), "Q8_0": (0,), "Q4_K": (0, 2), "Q6_K": (208,), "IQ2_XXS": (0,), "TQ2_0": (64,),
                  "Q5_K": (0, 2), "IQ4_XS": (0,), "MXFP4": (), "IQ3_S": (0,), "IQ3_XXS": (0,),
                  "Q4_1": (0, 2), "Q5_0": (0,), "Q5_1": (0, 2), "IQ4_NL": (0,), "Q1_0": (0,), "Q2_0": (0,),
-                 "PQ2_0": (0,), "Q3_K": (108,), "IQ2_XS": (0,), "IQ2_S": (0,), "Q2_K": (80, 82)}
+                 "PQ2_0": (0,), "Q3_K": (108,), "IQ2_XS": (0,), "IQ2_S": (0,), "Q2_K": (80, 82), "TQ1_0": (52,)}
 ROWS, COLS = 3, 512          # a (3, 512) matrix per format
 
 
 def random_blocks(name: str, n_blocks: int, rng: np.random.Generator) -> np.ndarray:
     _, _, size = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4, **LATER5, **LATER6, **LATER7, **LATER8,
-                  **LATER9, **LATER10}[name]
+                  **LATER9, **LATER10, **LATER11}[name]
     raw = rng.integers(0, 256, (n_blocks, size), dtype=np.uint8)
     if name == "MXFP4":
         raw[:, 0] = rng.integers(118, 125, n_blocks)       # scale exponents 2^-10 .. 2^-4
@@ -171,7 +173,7 @@ def main(ref_root: str) -> None:
 
     def add(key: str, name: str, raw: np.ndarray, rows: int, cols: int) -> None:
         t, bv, bb = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4, **LATER5, **LATER6, **LATER7, **LATER8,
-                     **LATER9, **LATER10}[name]
+                     **LATER9, **LATER10, **LATER11}[name]
         flat = np.ascontiguousarray(raw.reshape(-1))
         assert flat.size == rows * cols // bv * bb
         deq = dequantize(torch.from_numpy(flat.copy()), t, rows * cols, torch.float32).numpy()
@@ -246,6 +248,12 @@ def main(ref_root: str) -> None:
     raw = random_blocks("Q2_K", 16, rng)                     # every scale/min byte once
     raw[:, :16] = np.arange(256, dtype=np.uint8).reshape(16, 16)
     add("Q2_K_cover", "Q2_K", raw, 16, 256)
+    for name, (_, bv, _) in LATER11.items():
+        add(name, name, random_blocks(name, ROWS * COLS // bv, rng), ROWS, COLS)
+    raw = random_blocks("TQ1_0", 6, rng)                     # every byte value in qs and in qh positions
+    vals = np.arange(6 * 52, dtype=np.uint32) % 256
+    raw[:, :52] = vals.reshape(6, 52)
+    add("TQ1_0_cover", "TQ1_0", raw, 6, 256)
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "dequant_golden.npz")
     np.savez_compressed(path, **out)
     print(f"wrote {path}: {len(out)} arrays")
