@@ -2,11 +2,14 @@
 
     python -m nemicli_terminal_b200.build        (or __graft_entry__.build())
 
-nvcc cross-compiles without a GPU.  The library links the CUDA runtime statically, so it loads
-beside torch without depending on where torch keeps its own runtime.
+nvcc cross-compiles without a GPU.  The sources compile to separate objects in parallel: qmv_fmt.cu once
+per block format (-DQMV_FMT_ID=<GGML type id>), every other .cu once; an object is rebuilt only when its
+source or a header is newer.  The library links the CUDA runtime statically, so it loads beside torch
+without depending on where torch keeps its own runtime.
 """
 from __future__ import annotations
 
+import concurrent.futures as cf
 import glob
 import os
 import shutil
@@ -17,7 +20,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB_NAME = "libnemiqmv.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
+OBJ_DIR = os.path.join(HERE, "_build")
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+PER_FORMAT = "qmv_fmt.cu"
 
 
 def nvcc() -> str:
@@ -36,27 +41,85 @@ def headers() -> list:
                   + glob.glob(os.path.join(HERE, "..", "include", "*.h")))
 
 
-def up_to_date() -> bool:
-    if not os.path.exists(LIB_PATH):
+def format_ids() -> list:
+    """GGML type ids of the formats with kernels (formats.py is the one list)."""
+    sys.path.insert(0, HERE)
+    try:
+        import importlib.util
+        spec = importlib.util.spec_from_file_location("_qmv_formats", os.path.join(HERE, "formats.py"))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+    finally:
+        sys.path.pop(0)
+    return sorted(mod.TYPE_ID.values())
+
+
+def units(obj_dir: str) -> list:
+    """(source, object, extra defines) of every object of the library."""
+    out = []
+    for src in sources():
+        base = os.path.splitext(os.path.basename(src))[0]
+        if os.path.basename(src) == PER_FORMAT:
+            for fid in format_ids():
+                out.append((src, os.path.join(obj_dir, f"{base}_{fid}.o"), [f"-DQMV_FMT_ID={fid}"]))
+        else:
+            out.append((src, os.path.join(obj_dir, f"{base}.o"), []))
+    return out
+
+
+def _stale(src: str, obj: str, newest_header: float) -> bool:
+    if not os.path.exists(obj):
+        return True
+    t = os.path.getmtime(obj)
+    return os.path.getmtime(src) > t or newest_header > t
+
+
+def up_to_date(out: str = LIB_PATH, obj_dir: str = OBJ_DIR) -> bool:
+    if not os.path.exists(out):
         return False
-    t = os.path.getmtime(LIB_PATH)
+    t = os.path.getmtime(out)
     return all(os.path.getmtime(p) <= t for p in sources() + headers())
 
 
-def build(force: bool = False, verbose: bool = False, extra: tuple = ()) -> str:
-    if not force and up_to_date():
-        return LIB_PATH
-    cmd = [nvcc(), *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "--shared", "-Xcompiler", "-fPIC",
-           "-cudart", "static", "-o", LIB_PATH + ".tmp", *extra, *sources()]
-    if verbose:
-        print(" ".join(cmd), file=sys.stderr)
+def build(force: bool = False, verbose: bool = False, extra: tuple = (), out: str = LIB_PATH,
+          obj_dir: str = OBJ_DIR, jobs: int = 0) -> str:
+    """Compile the stale objects in parallel and link `out`.  extra: more nvcc flags (e.g. -D...)."""
+    if not force and up_to_date(out, obj_dir):
+        return out
+    os.makedirs(obj_dir, exist_ok=True)
+    stamp = os.path.join(obj_dir, "flags.txt")
+    flags = " ".join(extra)
+    if not os.path.exists(stamp) or open(stamp).read() != flags:
+        force = True                                   # other flags: every object is stale
+    newest = max(os.path.getmtime(p) for p in headers())
+    todo = [u for u in units(obj_dir) if force or _stale(u[0], u[1], newest)]
+    base = [nvcc(), *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", *extra]
+
+    def compile_one(u):
+        src, obj, defs = u
+        cmd = [*base, *defs, "-c", "-o", obj + ".tmp", src]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr, flush=True)
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"nvcc failed on {os.path.basename(src)} {defs} ({res.returncode}):\n"
+                               f"{res.stderr[-4000:]}")
+        if verbose and res.stderr:
+            print(res.stderr, file=sys.stderr, flush=True)
+        os.replace(obj + ".tmp", obj)
+
+    with cf.ThreadPoolExecutor(max_workers=jobs or os.cpu_count() or 4) as ex:
+        for f in [ex.submit(compile_one, u) for u in todo]:
+            f.result()
+    with open(stamp, "w") as f:
+        f.write(flags)
+    objs = [u[1] for u in units(obj_dir)]
+    cmd = [nvcc(), *ARCH_FLAGS, "--shared", "-Xcompiler", "-fPIC", "-cudart", "static", "-o", out + ".tmp", *objs]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stderr[-4000:]}")
-    if verbose and res.stderr:
-        print(res.stderr, file=sys.stderr)
-    os.replace(LIB_PATH + ".tmp", LIB_PATH)
-    return LIB_PATH
+        raise RuntimeError(f"link failed ({res.returncode}):\n{res.stderr[-4000:]}")
+    os.replace(out + ".tmp", out)
+    return out
 
 
 if __name__ == "__main__":

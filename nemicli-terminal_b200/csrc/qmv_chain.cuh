@@ -65,7 +65,10 @@ struct ChainParams {
     ChainStage st[kChainMaxStages];
     int n_stages;
     int S;                 // ring slots
+    int F;                 // most copies in flight (1..S): the ring may hold more landed tiles than that
+    int PF;                // tiles ahead of the copies that are prefetched into L2 (0: none)
     int slot_bytes;
+    unsigned long long* trace;   // per (stage, CTA) timestamps (sweep builds; null otherwise)
     int* bar;              // grid-barrier counters: stage k done at [k], its input ready at [kChainMaxStages + k]
     int* cnt;              // group counters [buffer][group]
     int8_t* xq[2];
@@ -114,6 +117,14 @@ __device__ __forceinline__ int chain_job_of(const ChainStage& st, int g) {
     int j = 0;
     while (j + 1 < st.n_jobs && g >= int(st.row_start[j + 1])) ++j;
     return j;
+}
+
+// trace points of a sweep build: per (stage, CTA) four %globaltimer stamps
+enum : int { TR_ENTER = 0, TR_READY = 1, TR_DONE = 2, TR_FED = 3 };
+__device__ __forceinline__ void chain_trace(const ChainParams& P, int k, int field) {
+#ifdef QMV_TRACE
+    if (P.trace && threadIdx.x == 0) P.trace[((long long)k * gridDim.x + blockIdx.x) * 4 + field] = global_ns();
+#endif
 }
 
 __device__ __forceinline__ int ld_acquire(const int* p) {
@@ -252,6 +263,7 @@ __device__ __noinline__ int chain_consume(const ChainParams& P, const ChainStage
             }
         }
     }
+    chain_trace(P, k_stage, TR_READY);
     int w_g0 = 0, w_rows = 0;                              // window: rows [w_g0, w_g0 + w_rows)
     auto flush = [&]() {                                    // every consumer thread, uniformly
         named_sync(kConsumerBarrier, 32 * NCW);
@@ -329,6 +341,41 @@ __device__ __noinline__ int chain_consume(const ChainParams& P, const ChainStage
     return it;
 }
 
+// ---- the producer's walk over every stage's tiles ---------------------------------------------------
+
+// Position in the walk: stage k, tile i of this CTA's rows [lo, lo + n) of that stage.
+struct ChainCursor {
+    int k, i, lo, n;
+};
+__device__ __forceinline__ void chain_cursor_settle(const ChainParams& P, ChainCursor& c) {
+    while (c.k < P.n_stages) {
+        const ChainStage& st = P.st[c.k];
+        c.lo = chain_row_begin(st, blockIdx.x);
+        c.n = chain_row_begin(st, blockIdx.x + 1) - c.lo;
+        if (c.i * st.R < c.n) return;
+        ++c.k;
+        c.i = 0;
+    }
+}
+__device__ __forceinline__ void chain_cursor_next(const ChainParams& P, ChainCursor& c) {
+    ++c.i;
+    chain_cursor_settle(P, c);
+}
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(p), "r"(bytes) : "memory");
+}
+// L2 prefetch of the tile at cursor c (every job segment; bulk sizes are multiples of 16 bytes)
+__device__ __forceinline__ void chain_prefetch_tile(const ChainParams& P, const ChainCursor& c) {
+    const ChainStage& st = P.st[c.k];
+    const int t0 = c.lo + c.i * st.R, t1 = min(c.lo + c.n, t0 + st.R);
+    for (int j = 0; j < st.n_jobs; ++j) {
+        const int js = int(st.row_start[j]);
+        const int a0 = max(t0, js), a1 = min(t1, int(st.row_start[j + 1]));
+        if (a1 > a0) prefetch_l2(st.w[j] + (long long)(a0 - js) * st.row_bytes, uint32_t((a1 - a0) * st.row_bytes));
+    }
+}
+
+
 // ---- the kernel ---------------------------------------------------------------------------------------
 // shared memory: [S slots x slot_bytes][partial sums kChainPartFloats floats]
 //                [staged activation kChainActSmem][scale 16 B][mbarriers 2 S]
@@ -359,31 +406,50 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) chain_kernel(const __grid_c
 
     if (warp == NCW) {
         // ---------------- producer: every stage's weight tiles, in order ----------------
+        // At most F copies are in flight: a copy is issued once its slot is free AND the copy F tiles
+        // back has landed.  The ring can then hold up to S landed tiles (while the consumers wait at a
+        // stage boundary) without every slot's bytes queueing in the memory system at once, which
+        // would delay the boundary's own small loads behind them.
         if (lane != 0) return;
-        int it = 0;
         bool ok = true;
-        for (int k = 0; k < P.n_stages && ok; ++k) {
-            const ChainStage& st = P.st[k];
-            const int lo = chain_row_begin(st, blockIdx.x), n = chain_row_begin(st, blockIdx.x + 1) - lo;
-            const int R = st.R, tiles = (n + R - 1) / R;
-            const long long row_bytes = st.row_bytes;
-            for (int i = 0; i < tiles; ++i, ++it) {
-                const int s = it % S;
-                if (it >= S && !mbar_wait(empty0 + 8 * s, ((it / S) & 1) ^ 1)) {
+        ChainCursor c{0, 0, 0}, pf{0, 0, 0};
+        chain_cursor_settle(P, c);
+        chain_cursor_settle(P, pf);
+        for (int a = 0; a < P.PF && pf.k < P.n_stages; ++a) {   // the prefetch cursor starts PF tiles ahead
+            chain_prefetch_tile(P, pf);
+            chain_cursor_next(P, pf);
+        }
+        int it = 0;
+        for (; c.k < P.n_stages; ++it) {
+            const int s = it % S;
+            if (it >= S && !mbar_wait(empty0 + 8 * s, ((it / S) & 1) ^ 1)) {
+                ok = false;
+                break;
+            }
+            if (P.F < S && it >= P.F) {
+                const int j = it - P.F;
+                if (!mbar_wait(full0 + 8 * (j % S), (j / S) & 1)) {
                     ok = false;
                     break;
                 }
-                const int t0 = lo + i * R, t1 = min(lo + n, t0 + R);
-                mbar_arrive_tx(full0 + 8 * s, uint32_t((t1 - t0) * row_bytes));
-                // one copy per job segment of the tile, into consecutive rows of the slot
-                for (int j = 0; j < st.n_jobs; ++j) {
-                    const int js = int(st.row_start[j]);
-                    const int a0 = max(t0, js), a1 = min(t1, int(st.row_start[j + 1]));
-                    if (a1 <= a0) continue;
-                    bulk_g2s(stage0 + uint32_t(s) * uint32_t(P.slot_bytes) + uint32_t((a0 - t0) * row_bytes),
-                             st.w[j] + (long long)(a0 - js) * row_bytes, uint32_t((a1 - a0) * row_bytes),
-                             full0 + 8 * s);
-                }
+            }
+            const ChainStage& st = P.st[c.k];
+            const int t0 = c.lo + c.i * st.R, t1 = min(c.lo + c.n, t0 + st.R);
+            const long long row_bytes = st.row_bytes;
+            mbar_arrive_tx(full0 + 8 * s, uint32_t((t1 - t0) * row_bytes));
+            // one copy per job segment of the tile, into consecutive rows of the slot
+            for (int j = 0; j < st.n_jobs; ++j) {
+                const int js = int(st.row_start[j]);
+                const int a0 = max(t0, js), a1 = min(t1, int(st.row_start[j + 1]));
+                if (a1 <= a0) continue;
+                bulk_g2s(stage0 + uint32_t(s) * uint32_t(P.slot_bytes) + uint32_t((a0 - t0) * row_bytes),
+                         st.w[j] + (long long)(a0 - js) * row_bytes, uint32_t((a1 - a0) * row_bytes),
+                         full0 + 8 * s);
+            }
+            chain_cursor_next(P, c);
+            if (P.PF > 0 && pf.k < P.n_stages) {
+                chain_prefetch_tile(P, pf);
+                chain_cursor_next(P, pf);
             }
         }
         if (!ok) {
@@ -399,6 +465,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) chain_kernel(const __grid_c
     for (int k = 0; k < P.n_stages; ++k) {
         const ChainStage& st = P.st[k];
         const int buf = k & 1;
+        chain_trace(P, k, TR_ENTER);
         if (st.wait && k > 0) grid_wait<NCW>(P.bar + (k - 1), dead, P.status);
         if (!st.fed) {
             // this stage quantises its own input: groups split over the CTAs, then a grid barrier
@@ -416,6 +483,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) chain_kernel(const __grid_c
             it = chain_consume<CB, NCW>(P, st, k, it, &dead_io, part, act_smem, stage0, full0, empty0);
         dead = dead_io != 0;
         named_sync(kConsumerBarrier, 32 * NCW);            // this CTA's rows of stage k are written
+        chain_trace(P, k, TR_DONE);
         if (k + 1 < P.n_stages && P.st[k + 1].fed) {
             // quantise every group of the next stage's input whose last rows this CTA wrote
             const ChainStage& ns = P.st[k + 1];
@@ -446,6 +514,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) chain_kernel(const __grid_c
             }
             named_sync(kConsumerBarrier, 32 * NCW);
         }
+        chain_trace(P, k, TR_FED);
         grid_arrive(P.bar + k);
     }
 }

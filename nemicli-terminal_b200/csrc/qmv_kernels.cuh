@@ -38,7 +38,7 @@ __device__ __forceinline__ void quantize_group(float v, long long i, int8_t* __r
     }
 }
 
-__global__ void __launch_bounds__(256) quant_q8_kernel(const void* __restrict__ x, int x_f32,
+static __global__ void __launch_bounds__(256) quant_q8_kernel(const void* __restrict__ x, int x_f32,
                                                        int8_t* __restrict__ xq, int8_t* __restrict__ xq2,
                                                        float* __restrict__ xd, float* __restrict__ xs,
                                                        long long n) {
