@@ -97,6 +97,32 @@ int qmv_mv_multi(int ggml_type, int n_jobs, const uint8_t* const* w, const int* 
 int qmv_mv_x(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
              const void* x, int x_is_f32, void* stream);
 
+/* ---- fused producers of the activation input (one token) and unpacking --------------------------- */
+
+/* RMS norm of one row and its activation input: v = h (+ rs * r, written to h_out when r is given),
+ * xn = v * rsqrt(mean(v^2) + eps) * w (n fp32 values, n % 32 == 0), quantised into xq, xq2, xd, xs.
+ * One launch.  Replaces: ggufengine/mmvq.py:946-956 (norm_q8) and its kernel (:100-118). */
+int qmv_norm_q8(const float* h, const float* r, float rs, float* h_out, const float* w, float eps, float* xn,
+                int8_t* xq, int8_t* xq2, float* xd, float* xs, int n, void* stream);
+
+/* a = act(g) * u (u == NULL: act(g)), act = SiLU, or GELU in its tanh form when gelu != 0; n fp32 values
+ * (n % 32 == 0) and their activation input.  Replaces: ggufengine/mmvq.py:959-966 (akt_q8) and its kernel
+ * (:120-131). */
+int qmv_act_q8(const float* g, const float* u, int gelu, float* a, int8_t* xq, int8_t* xq2, float* xd, float* xs,
+               int n, void* stream);
+
+#define QMV_OUT_F32 0
+#define QMV_OUT_BF16 1
+#define QMV_OUT_F16 2
+
+/* Unpack n_values (a multiple of the block size) of block-format weights to dense values (out_dtype one of
+ * QMV_OUT_*; out 16-byte aligned): the fp32 values of the reference's dequantiser bit for bit (the same
+ * products and sums, each rounded), bf16 / fp16 rounded to nearest even from them.  Replaces:
+ * ggufengine/mmvq.py:931-940 (entpacken, kernels aus_Q4_K / aus_Q6_K :496-534) for every format here, and
+ * ggufengine/quant.py:484 (dequantize) on the GPU (the reference's PackedExperts.weights,
+ * models/common.py:456-460, and QuantLinear.bf16_weight, qlinear.py:217). */
+int qmv_unpack(int ggml_type, const uint8_t* w, long long n_values, void* out, int out_dtype, void* stream);
+
 /* Programmatic dependent launch for the staged single-token kernels (default off): when on, each such
  * kernel lets the next kernel of the stream start early and streams its weights before the previous
  * kernel has finished; its inputs are read only after the previous kernel completed.  Turn it on only

@@ -36,6 +36,9 @@ _SIGNATURES = {
     "qmv_chain_noalloc": ([P, I, P], I),
     "qmv_chain_workspace_bytes": ([], LL),
     "qmv_device_status": ([I, P, P], I),
+    "qmv_norm_q8": ([P, P, ctypes.c_float, P, P, ctypes.c_float, P, P, P, P, P, I, P], I),
+    "qmv_act_q8": ([P, P, I, P, P, P, P, P, I, P], I),
+    "qmv_unpack": ([I, P, LL, P, I, P], I),
 }
 
 ABI_VERSION = 2
@@ -76,6 +79,13 @@ def check(status: int, what: str) -> None:
         msg = L.qmv_status_string(status).decode()
         extra = f" (cudaError {L.qmv_last_cuda_error()})" if status == 5 else ""
         raise RuntimeError(f"{what}: {msg}{extra}")
+
+
+def on_gpu(x) -> bool:
+    """A CUDA tensor or CUDA device: the one device question the mirrors ask before calling the library."""
+    if isinstance(x, torch.Tensor):
+        return x.is_cuda
+    return torch.device(x).type == "cuda"
 
 
 def ptr(t) -> ctypes.c_void_p:

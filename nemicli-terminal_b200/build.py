@@ -67,11 +67,26 @@ def units(obj_dir: str) -> list:
     return out
 
 
+def _deps(obj: str):
+    """Headers the object was compiled from (nvcc -MD writes them next to it), or None if unknown."""
+    try:
+        text = open(obj + ".d").read().replace("\\\n", " ")
+    except OSError:
+        return None
+    parts = text.split(":", 1)
+    return [p for p in parts[1].split()] if len(parts) == 2 else None
+
+
 def _stale(src: str, obj: str, newest_header: float) -> bool:
     if not os.path.exists(obj):
         return True
     t = os.path.getmtime(obj)
-    return os.path.getmtime(src) > t or newest_header > t
+    if os.path.getmtime(src) > t:
+        return True
+    deps = _deps(obj)
+    if deps is None:
+        return newest_header > t
+    return any(not os.path.exists(d) or os.path.getmtime(d) > t for d in deps)
 
 
 def up_to_date(out: str = LIB_PATH, obj_dir: str = OBJ_DIR) -> bool:
@@ -97,7 +112,7 @@ def build(force: bool = False, verbose: bool = False, extra: tuple = (), out: st
 
     def compile_one(u):
         src, obj, defs = u
-        cmd = [*base, *defs, "-c", "-o", obj + ".tmp", src]
+        cmd = [*base, *defs, "-MD", "-MF", obj + ".d", "-c", "-o", obj + ".tmp", src]
         if verbose:
             print(" ".join(cmd), file=sys.stderr, flush=True)
         res = subprocess.run(cmd, capture_output=True, text=True)

@@ -119,11 +119,18 @@ __device__ __forceinline__ int chain_job_of(const ChainStage& st, int g) {
     return j;
 }
 
-// trace points of a sweep build: per (stage, CTA) four %globaltimer stamps
-enum : int { TR_ENTER = 0, TR_READY = 1, TR_DONE = 2, TR_FED = 3 };
+// trace points of a sweep build: per (stage, CTA) kChainTraceFields words: four %globaltimer stamps, the
+// ns thread 0 spent waiting for tile data in the stage, and the stage's tile count
+enum : int { TR_ENTER = 0, TR_READY = 1, TR_DONE = 2, TR_FED = 3, TR_DATAWAIT = 4, TR_TILES = 5 };
+constexpr int kChainTraceFields = 6;
+__device__ __forceinline__ void chain_trace_set(const ChainParams& P, int k, int field, unsigned long long v) {
+#ifdef QMV_TRACE
+    if (P.trace && threadIdx.x == 0) P.trace[((long long)k * gridDim.x + blockIdx.x) * kChainTraceFields + field] = v;
+#endif
+}
 __device__ __forceinline__ void chain_trace(const ChainParams& P, int k, int field) {
 #ifdef QMV_TRACE
-    if (P.trace && threadIdx.x == 0) P.trace[((long long)k * gridDim.x + blockIdx.x) * 4 + field] = global_ns();
+    chain_trace_set(P, k, field, global_ns());
 #endif
 }
 
@@ -282,10 +289,19 @@ __device__ __noinline__ int chain_consume(const ChainParams& P, const ChainStage
     const int lo = chain_row_begin(st, blockIdx.x), n = chain_row_begin(st, blockIdx.x + 1) - lo;
     const int R = st.R, tiles = (n + R - 1) / R;
     const uint32_t row_bytes = uint32_t(st.row_bytes);
+#ifdef QMV_TRACE
+    unsigned long long wait_ns = 0;
+#endif
     for (int i = 0; i < tiles; ++i, ++it) {
         const int t0 = lo + i * R, nrows = min(R, n - i * R);
         const int s = it % S;
+#ifdef QMV_TRACE
+        const unsigned long long tw = threadIdx.x == 0 ? global_ns() : 0;
+#endif
         const bool got = !dead && mbar_wait(full0 + 8 * s, (it / S) & 1);
+#ifdef QMV_TRACE
+        if (threadIdx.x == 0) wait_ns += global_ns() - tw;
+#endif
         if (!got && !dead) {
             dead = true;
             if (lane == 0 && P.status) atomicOr(P.status, DEV_TIMEOUT);
@@ -337,6 +353,10 @@ __device__ __noinline__ int chain_consume(const ChainParams& P, const ChainStage
     if constexpr (G > 32) {
         if (w_rows > 0) flush();
     }
+#ifdef QMV_TRACE
+    chain_trace_set(P, k_stage, TR_DATAWAIT, wait_ns);
+    chain_trace_set(P, k_stage, TR_TILES, (unsigned long long)tiles);
+#endif
     *dead_io = dead;
     return it;
 }

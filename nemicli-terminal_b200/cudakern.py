@@ -18,21 +18,49 @@ from .formats import FORMATS, TYPE_ID
 from .mmvq import Eingang
 
 FORMATE = dict(FORMATS)
-IMMER_GEPACKT = frozenset(("IQ2_XXS", "TQ2_0"))   # formats without an int4 QuantLinear route (cudakern.py:52-54)
+# Formats that always stay in block format (cudakern.py:52-54).  The reference lists those without an int4
+# QuantLinear route; here no format is repacked, so every format of this path is listed, and the reference's
+# loader keeps expert tensors of any of them as PackedExperts (models/common.py:280-282, 220-224).
+IMMER_GEPACKT = frozenset(FORMATE)
 MM_ZEILEN = 16                                    # rows of one `mm` call (cudakern.py:31)
+
+
+_cu = None
+
+
+def _treiber():
+    """The CUDA driver library (reference cudakern.py:586-596; hostmem.py maps pinned memory through it)."""
+    global _cu
+    if _cu is None:
+        import ctypes
+        cu = ctypes.CDLL("libcuda.so.1")
+        cu.cuLaunchKernel.argtypes = [ctypes.c_void_p] + [ctypes.c_uint] * 6 + [
+            ctypes.c_uint, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        _cu = cu
+    return _cu
+
+
+def _nvrtc_pfad():
+    """Where the kernels come from (reference cudakern.py:580-583 returns the NVRTC library, whose presence
+    tells schichten.int8_weg_da that the int8 path exists): here the prebuilt kernel library, or None."""
+    try:
+        _lib.load()
+    except RuntimeError:
+        return None
+    return _lib.lib_path()
 
 
 def verfuegbar(device, fmt: str, n_in: int) -> bool:
     """Kernel for this format and row length on this device (cudakern.py:733-739)."""
     device = torch.device(device)
-    if device.type != "cuda" or fmt not in FORMATE:
+    if not _lib.on_gpu(device) or fmt not in FORMATE:
         return False
     return bool(_lib.load().qmv_supported(TYPE_ID[fmt], int(n_in)))
 
 
 def mm_bis(device) -> int:
     """Most input rows of one `mm` call on this device (cudakern.py:742-745)."""
-    return MM_ZEILEN if torch.device(device).type == "cuda" else 1
+    return MM_ZEILEN if _lib.on_gpu(device) else 1
 
 
 def _eingang(x: torch.Tensor) -> Eingang:
@@ -46,7 +74,7 @@ def mv(fmt: str, raw: torch.Tensor, ids: torch.Tensor, x: torch.Tensor, n_out: i
     where each expert's bytes lie (then raw is not read).  -> (k, n_out) float32."""
     if fmt not in FORMATE:
         raise RuntimeError(f"format {fmt} has no kernel in this path")
-    if not x.is_cuda:
+    if not _lib.on_gpu(x):
         raise RuntimeError("cudakern.mv: x must be on the GPU (no CPU fallback)")
     geraet = x.device
     ids = ids.to(geraet, torch.int64).contiguous()
@@ -58,7 +86,7 @@ def mv(fmt: str, raw: torch.Tensor, ids: torch.Tensor, x: torch.Tensor, n_out: i
     y = torch.empty(k, n_out, dtype=torch.float32, device=geraet)
     if adressen is None:
         raw2 = raw.reshape(raw.shape[0], -1) if raw.dim() > 1 else raw.view(1, -1)
-        if not raw2.is_cuda:
+        if not _lib.on_gpu(raw2):
             raise RuntimeError("cudakern.mv: expert bytes must be device-addressable (GPU memory)")
         quelle, per, n_exp = raw2, raw2.shape[1], raw2.shape[0]
     else:
@@ -77,7 +105,7 @@ def mm(fmt: str, raw: torch.Tensor, x: torch.Tensor, n_out: int, n_in: int) -> t
         raise ValueError(f"mm: {M} rows (2..{mm_bis(x.device)})")
     if fmt not in FORMATE:
         raise RuntimeError(f"format {fmt} has no kernel in this path")
-    if not (raw.is_cuda and x.is_cuda):
+    if not (_lib.on_gpu(raw) and _lib.on_gpu(x)):
         raise RuntimeError("cudakern.mm: tensors must be on the GPU (no CPU fallback)")
     e = _eingang(x.reshape(-1))
     y = torch.empty(M, n_out, dtype=torch.float32, device=x.device)

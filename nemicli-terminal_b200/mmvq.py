@@ -6,7 +6,15 @@ meaning and return shapes, computed by this package's sm_100a kernels through th
 * `mv` — y = W x for up to MMVQ_BIS tokens per call (mmvq.py:852-865), in launches of SPALTEN tokens,
   each weight byte read once per launch.
 * `mm` — the reference's 17..112-token entry (mmvq.py:902-918); here the same int8 kernels in groups
-  of SPALTEN tokens (the tensor-core tile path for long inputs is a separate, later kernel).
+  of SPALTEN tokens.
+* `entpacken` — a block-format matrix unpacked to bf16 for long inputs (mmvq.py:931-940), every format.
+* `norm_q8`, `akt_q8` — the fused one-token producers of an Eingang (mmvq.py:946-966): RMS norm with the
+  residual add, and the gated activation, each one launch that also quantises its output.
+* `rope_kv`, `attention1`, `schritt_moeglich` — the attention steps of the reference's fused one-token
+  layer (mmvq.py:969-1014) are not part of this package (the matvec path ends where attention begins).
+  They are forwarded to an attention provider registered with `set_attention` (the reference's own
+  module, for instance); without one `schritt_moeglich` is False and the reference's layer takes its
+  general path, whose projections still run here through PackedLinear / mv.
 
 Where the reference takes Q4_K and Q6_K only, these kernels take all twenty-three block formats of the path
 (`FORMATE`: the classic, K-quant, IQ, MXFP4, ternary and 1-bit formats).  Everything runs on torch's current stream and is CUDA-graph
@@ -29,18 +37,19 @@ FORMATE = dict(FORMATS)                 # name -> (values per block, bytes per b
 SPALTEN = 8                             # tokens per kernel launch (weights read once for all of them)
 MMVQ_BIS = {f: 16 for f in FORMATE}     # up to this many tokens: mv (reference mmvq.py:32)
 MMQ_BIS = {f: 112 for f in FORMATE}     # up to this many tokens: mm (reference mmvq.py:33)
+SCHRITT_KERNE = ("quant_q8", "norm_q8", "akt_q8")   # fused one-token kernels of this package (mmvq.py:34)
 
 
 def verfuegbar(device, fmt: str, n_in: int) -> bool:
     """Kernels for this format and row length on this device (reference mmvq.py:808-810)."""
     device = torch.device(device)
-    if device.type != "cuda" or fmt not in FORMATE:
+    if not _lib.on_gpu(device) or fmt not in FORMATE:
         return False
     return bool(_lib.load().qmv_supported(TYPE_ID[fmt], int(n_in)))
 
 
 def _need_cuda(t: torch.Tensor, what: str) -> None:
-    if not t.is_cuda:
+    if not _lib.on_gpu(t):
         raise RuntimeError(f"{what}: tensor on {t.device}; the quantized matvec path runs on CUDA only")
 
 
@@ -73,6 +82,12 @@ class Eingang:
             return [_lib.ptr(self.xq), _lib.ptr(self.xq2), _lib.ptr(self.xd), _lib.ptr(self.xs)]
         return [_lib.ptr(self.xq[ab:]), _lib.ptr(self.xq2[ab:]), _lib.ptr(self.xd[ab // 32:]),
                 _lib.ptr(self.xs[ab // 32:])]
+
+
+def _ist_eingang(x) -> bool:
+    """An activation input: this module's Eingang or any object with its buffers (the reference's own
+    Eingang, as its attention kernels return it, mmvq.py:987-1007)."""
+    return isinstance(x, Eingang) or all(hasattr(x, a) for a in ("n", "xq", "xq2", "xd", "xs", "zeiger"))
 
 
 def _check_raw(fmt: str, raw: torch.Tensor, n_out: int, n_in: int) -> None:
@@ -128,18 +143,19 @@ def mv(fmt: str, raw: torch.Tensor, x, n_out: int, n_in: int) -> torch.Tensor:
     Eingang with M rows -> (M, n_out) float32, or (n_out,) for a vector.  One token given as a tensor
     is quantised inside the matvec kernel (no separate Eingang)."""
     _check_raw(fmt, raw, n_out, n_in)
-    if not isinstance(x, Eingang) and x.numel() == n_in:
+    ist_eingang = _ist_eingang(x)
+    if not ist_eingang and x.numel() == n_in:
         ys = _fused(fmt, [(raw, n_out)], x, n_in)
         if ys is not None:
             return ys[0] if x.dim() == 1 else ys[0].view(1, n_out)
-    e = x if isinstance(x, Eingang) else Eingang(x)
+    e = x if ist_eingang else Eingang(x)
     if e.n % n_in:
         raise RuntimeError(f"mv: input of {e.n} values is not a whole number of rows of {n_in}")
     M = e.n // n_in
     y = torch.empty(M, n_out, dtype=torch.float32, device=raw.device)
     _lib.check(_lib.load().qmv_mv(TYPE_ID[fmt], _lib.ptr(raw), n_out, n_in, *e.zeiger(), M, _lib.ptr(y),
                                   _lib.stream_ptr(raw.device)), f"qmv_mv {fmt}")
-    vektor = M == 1 if isinstance(x, Eingang) else x.dim() == 1
+    vektor = M == 1 if ist_eingang else x.dim() == 1
     return y[0] if vektor else y
 
 
@@ -151,11 +167,11 @@ def mv_geteilt(fmt: str, mats, x, n_in: int) -> list:
         raise RuntimeError("mv_geteilt: 1 to 4 matrices")
     for raw, n_out in mats:
         _check_raw(fmt, raw, n_out, n_in)
-    if not isinstance(x, Eingang):
+    if not _ist_eingang(x):
         ys = _fused(fmt, mats, x, n_in)
         if ys is not None:
             return ys
-    e = x if isinstance(x, Eingang) else Eingang(x)
+    e = x if _ist_eingang(x) else Eingang(x)
     if e.n != n_in:
         raise RuntimeError(f"mv_geteilt: one token of {n_in} values expected, got {e.n}")
     dev = mats[0][0].device
@@ -217,3 +233,89 @@ def block_sums(fmt: str, raw: torch.Tensor, e: Eingang, n_out: int, n_in: int):
                                           _lib.ptr(s), _lib.ptr(s2), _lib.stream_ptr(raw.device)),
                f"qmv_block_sums {fmt}")
     return s, s2
+
+
+_OUT = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+
+
+def entpacken(fmt: str, raw: torch.Tensor, n_out: int, n_in: int, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """raw: (n_out, n_in) in block format on the GPU -> (n_out, n_in) bf16 (reference mmvq.py:931-940), the
+    reference's dequantised values rounded to nearest even (fp32 / fp16 with `dtype`)."""
+    _check_raw(fmt, raw, n_out, n_in)
+    if dtype not in _OUT:
+        raise RuntimeError(f"entpacken: output dtype {dtype} (float32, bfloat16 or float16)")
+    out = torch.empty(n_out, n_in, dtype=dtype, device=raw.device)
+    _lib.check(_lib.load().qmv_unpack(TYPE_ID[fmt], _lib.ptr(raw), n_out * n_in, _lib.ptr(out), _OUT[dtype],
+                                      _lib.stream_ptr(raw.device)), f"qmv_unpack {fmt}")
+    return out
+
+
+def _vektor(t: torch.Tensor, what: str) -> torch.Tensor:
+    _need_cuda(t, what)
+    if t.dtype != torch.float32 or not t.is_contiguous():
+        raise RuntimeError(f"{what}: contiguous float32 vectors expected")
+    return t.reshape(-1)
+
+
+def norm_q8(h: torch.Tensor, w: torch.Tensor, eps: float, rest: Optional[torch.Tensor] = None, rs: float = 1.0):
+    """RMS norm of one row; with `rest` first h = h + rs * rest.  -> (normalised float32, Eingang, new h)
+    (reference mmvq.py:946-956).  One launch."""
+    h_in = h
+    h, w = _vektor(h, "norm_q8"), _vektor(w, "norm_q8")
+    n = h.numel()
+    e = Eingang(n=n, device=h.device)
+    xn = torch.empty(n, dtype=torch.float32, device=h.device)
+    hn = None
+    if rest is not None:
+        rest = _vektor(rest, "norm_q8")
+        hn = torch.empty(n, dtype=torch.float32, device=h.device)
+    _lib.check(_lib.load().qmv_norm_q8(_lib.ptr(h), _lib.ptr(rest), ctypes.c_float(rs), _lib.ptr(hn), _lib.ptr(w),
+                                       ctypes.c_float(eps), _lib.ptr(xn), *e.zeiger(), n, _lib.stream_ptr(h.device)),
+               "qmv_norm_q8")
+    return xn, e, (h_in if hn is None else hn)
+
+
+def akt_q8(g: torch.Tensor, u: Optional[torch.Tensor], gelu: bool):
+    """act(g) * u (without u: act(g)), act = SiLU or GELU (tanh form) -> (float32, Eingang)
+    (reference mmvq.py:959-966).  One launch."""
+    g = _vektor(g, "akt_q8")
+    n = g.numel()
+    if u is not None:
+        u = _vektor(u, "akt_q8")
+    e = Eingang(n=n, device=g.device)
+    a = torch.empty(n, dtype=torch.float32, device=g.device)
+    _lib.check(_lib.load().qmv_act_q8(_lib.ptr(g), _lib.ptr(u), int(bool(gelu)), _lib.ptr(a), *e.zeiger(), n,
+                                      _lib.stream_ptr(g.device)), "qmv_act_q8")
+    return a, e
+
+
+_ATTENTION = None
+
+
+def set_attention(provider) -> None:
+    """Registers the provider of the one-token attention steps (an object with rope_kv, attention1 and
+    schritt_moeglich of the reference's signatures, e.g. the reference's own mmvq module); None removes it."""
+    global _ATTENTION
+    _ATTENTION = provider
+
+
+def schritt_moeglich(device, H: int, Hkv: int, D: int) -> bool:
+    """Can the reference's fused one-token layer step run (mmvq.py:1010-1014)?  Only with an attention
+    provider that takes these head shapes; otherwise the layer takes its general path."""
+    if _ATTENTION is None or not _lib.on_gpu(device):
+        return False
+    return bool(_ATTENTION.schritt_moeglich(device, H, Hkv, D))
+
+
+def rope_kv(*args, **kwargs):
+    """The provider's rope_kv (reference mmvq.py:969-984)."""
+    if _ATTENTION is None:
+        raise RuntimeError("rope_kv: no attention provider registered (mmvq.set_attention)")
+    return _ATTENTION.rope_kv(*args, **kwargs)
+
+
+def attention1(*args, **kwargs):
+    """The provider's attention1 (reference mmvq.py:987-1007); its Eingang is read by mv directly."""
+    if _ATTENTION is None:
+        raise RuntimeError("attention1: no attention provider registered (mmvq.set_attention)")
+    return _ATTENTION.attention1(*args, **kwargs)

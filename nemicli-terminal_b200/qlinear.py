@@ -13,11 +13,11 @@ from typing import Optional
 
 import torch
 
-from . import mmvq
+from . import _lib, mmvq
 from .formats import FORMATS, GGML_TYPES
 
 G = 32                                     # group size along K (reference qlinear.py:33)
-UNPACK_FROM = 256                          # reference qlinear.py:36 (kept for callers that read it)
+UNPACK_FROM = 256                          # from this many rows: unpack to bf16 + cuBLAS (reference qlinear.py:36)
 _QUANT = ("Q4_0", "Q8_0", "Q4_K", "Q6_K")  # formats this QuantLinear takes
 
 
@@ -27,10 +27,10 @@ class GGUFError(ValueError):
 
 def kernel_available(device: torch.device) -> bool:
     """The kernels run on this device (reference qlinear.py:42-43)."""
-    if torch.device(device).type != "cuda":
+    from . import _lib
+    if not _lib.on_gpu(device):
         return False
     try:
-        from . import _lib
         _lib.load()
         return True
     except RuntimeError:
@@ -60,11 +60,31 @@ class QuantLinear:
     def dtype(self):
         return torch.bfloat16
 
+    @property
+    def mats(self):
+        """The reference keeps tinygemm int4 tiles here (qlinear.py:200), which only its stacked-expert path
+        reads (models/moe.py:56-80, torch._weight_int4pack_mm).  This QuantLinear keeps the GGUF bytes and has
+        no int4 tiles: expert tensors load as PackedExperts instead (cudakern.IMMER_GEPACKT lists every
+        format, so WeightLoader.experts takes that route), and asking for the tiles is an error."""
+        raise RuntimeError("QuantLinear.mats: no int4 tile layout in this package (GGUF blocks are kept as they "
+                           "are); expert tensors are PackedExperts here (cudakern.IMMER_GEPACKT)")
+
+    def bf16_weight(self) -> torch.Tensor:
+        """The matrix as (n_out, n_in) bf16 (reference qlinear.py:217-227), unpacked on the GPU."""
+        return mmvq.entpacken(self.type_name, self.raw, self.n_out, self.n_in)
+
+    def _mm(self, x2: torch.Tensor) -> torch.Tensor:
+        return mmvq.mm(self.type_name, self.raw, x2, self.n_out, self.n_in)
+
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         x2 = x.reshape(-1, self.n_in)
-        if x2.dtype != torch.float32:
-            x2 = x2.to(torch.bfloat16)
-        y = mmvq.mm(self.type_name, self.raw, x2, self.n_out, self.n_in).to(torch.bfloat16)
+        M = x2.shape[0]
+        if M >= UNPACK_FROM:                     # long inputs: one unpack, one cuBLAS matmul (qlinear.py:232)
+            y = x2.to(torch.bfloat16) @ self.bf16_weight().t()
+        else:
+            if x2.dtype != torch.float32:
+                x2 = x2.to(torch.bfloat16)
+            y = self._mm(x2).to(torch.bfloat16)
         if self.b is not None:
             y = y + self.b
         return y.reshape(*x.shape[:-1], self.n_out)
@@ -79,6 +99,6 @@ def build_quant_linear(raw: torch.Tensor, ggml_type: int, n_out: int, n_in: int,
         raise GGUFError(f"{name} has no QuantLinear route in this path")
     if raw.numel() != n_out * n_in // block_size * type_size:
         raise GGUFError("byte count mismatch in build_quant_linear")
-    if not raw.is_cuda:
+    if not _lib.on_gpu(raw):
         raise GGUFError("build_quant_linear: raw bytes must already be on the CUDA device")
     return QuantLinear(raw.reshape(-1).contiguous(), n_out, n_in, bias, name)

@@ -1,0 +1,137 @@
+"""The kernels around the matvecs on the GPU: unpacking (qmv_unpack: mmvq.entpacken, PackedExperts.weights,
+QuantLinear.bf16_weight, PackedLinear's long-input path) and the fused one-token producers (qmv_norm_q8,
+qmv_act_q8: mmvq.norm_q8, mmvq.akt_q8).
+
+Unpacking is bit-exact: its fp32 values against the reference's own dequantised golden vectors
+(tests/golden, every format and every codebook entry), bf16 / fp16 against torch's round-to-nearest-even
+of those.  The producers against torch fp32 (1e-6), and their activation input bit-exact against the
+oracle's quantisation of the kernel's own normalised / activated output."""
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from nemicli_terminal_b200 import layers, mmvq, qlinear, synth
+from nemicli_terminal_b200.formats import FORMATS, TYPE_ID
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = np.load(os.path.join(os.path.dirname(__file__), "golden", "dequant_golden.npz"))
+KEYS = sorted({k.split("__")[0] for k in GOLDEN.files})
+NAME = {v: k for k, v in O.TYPES.items()}
+
+
+@pytest.mark.parametrize("key", KEYS)
+def test_unpack_bit_exact_with_reference_golden(cuda, key):
+    t, rows, cols = (int(v) for v in GOLDEN[key + "__shape"])
+    fmt = NAME[t]
+    raw = torch.from_numpy(GOLDEN[key + "__raw"].copy()).to(cuda)
+    deq = torch.from_numpy(GOLDEN[key + "__deq"].copy()).view(rows, cols)
+    y32 = mmvq.entpacken(fmt, raw, rows, cols, torch.float32).cpu()
+    assert torch.equal(y32.view(torch.int32), deq.view(torch.int32)), fmt
+    for dt in (torch.bfloat16, torch.float16):
+        y = mmvq.entpacken(fmt, raw, rows, cols, dt).cpu()
+        assert torch.equal(y.view(torch.int16), deq.to(dt).view(torch.int16)), (fmt, dt)
+
+
+@pytest.mark.parametrize("fmt", sorted(FORMATS))
+def test_unpack_large_matches_oracle(cuda, fmt):
+    n_out, n_in = 1024, 4096
+    raw = synth.blocks(fmt, n_out, n_in, seed=5)
+    ref = torch.from_numpy(O.dequant(fmt, raw.numpy(), n_out * n_in)).view(n_out, n_in)
+    y = mmvq.entpacken(fmt, raw.to(cuda), n_out, n_in).cpu()
+    assert torch.equal(y.view(torch.int16), ref.to(torch.bfloat16).view(torch.int16))
+
+
+def test_unpack_refusals(cuda):
+    from nemicli_terminal_b200 import _lib
+    L = _lib.load()
+    raw = synth.blocks("Q4_K", 4, 256, seed=1).to(cuda)
+    out = torch.empty(4, 256, device=cuda)
+    assert L.qmv_unpack(99, _lib.ptr(raw), 1024, _lib.ptr(out), 0, None) == 1          # unknown format
+    assert L.qmv_unpack(TYPE_ID["Q4_K"], _lib.ptr(raw), 1000, _lib.ptr(out), 0, None) == 2   # not whole blocks
+    assert L.qmv_unpack(TYPE_ID["Q4_K"], _lib.ptr(raw), 1024, _lib.ptr(out), 7, None) == 2   # no such dtype
+    assert L.qmv_unpack(TYPE_ID["Q4_K"], _lib.ptr(raw), 1024, _lib.ptr(out[0, 1:]), 0, None) == 3  # misaligned
+
+
+def test_packed_experts_weights_and_items(cuda):
+    n_exp, n_out, n_in = 6, 64, 512
+    raw = synth.blocks("IQ2_XXS", n_exp * n_out, n_in, seed=7)
+    ex = layers.PackedExperts(raw.to(cuda), TYPE_ID["IQ2_XXS"], n_exp, n_out, n_in, torch.bfloat16)
+    ids = torch.tensor([4, 1, 4], device=cuda)
+    w = ex.weights(ids)
+    assert w.shape == (3, n_out, n_in) and w.dtype == torch.bfloat16
+    for j, e in enumerate((4, 1, 4)):
+        ref = torch.from_numpy(O.dequant("IQ2_XXS", raw.view(n_exp, -1)[e].numpy(), n_out * n_in)).view(n_out, n_in)
+        assert torch.equal(w[j].cpu().view(torch.int16), ref.to(torch.bfloat16).view(torch.int16))
+    x = synth.activations(3, n_in, seed=1, device=cuda).to(torch.bfloat16)
+    y = ex[1](x)
+    assert torch.allclose(y.float(), (x @ w[1].t()).float())
+    with pytest.raises(IndexError):
+        ex[n_exp]
+
+
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q6_K", "IQ3_S"])
+def test_packed_linear_long_inputs_unpack(cuda, fmt):
+    """M > MMQ_BIS: the unpack + cuBLAS route of PackedLinear._rechnen (reference common.py:414-428)."""
+    n_out, n_in, M = 512, 1024, 200
+    raw = synth.blocks(fmt, n_out, n_in, seed=9)
+    pl = layers.PackedLinear(raw.to(cuda), TYPE_ID[fmt], n_out, n_in, None, torch.bfloat16)
+    x = synth.activations(M, n_in, seed=2, device=cuda)
+    y = pl(x).float().cpu()
+    w = torch.from_numpy(O.dequant(fmt, raw.numpy(), n_out * n_in)).view(n_out, n_in).to(torch.bfloat16)
+    ref = (x.cpu().to(torch.bfloat16).double() @ w.double().t())
+    assert O.max_rel(y.numpy(), ref.numpy()) < 1e-2           # bf16 output, as the reference
+
+
+def test_quant_linear_bf16_weight(cuda):
+    raw = synth.blocks("Q8_0", 256, 512, seed=4)
+    ql = qlinear.build_quant_linear(raw.to(cuda), TYPE_ID["Q8_0"], 256, 512)
+    w = ql.bf16_weight().cpu()
+    ref = torch.from_numpy(O.dequant("Q8_0", raw.numpy(), 256 * 512)).view(256, 512).to(torch.bfloat16)
+    assert torch.equal(w.view(torch.int16), ref.view(torch.int16))
+    x = synth.activations(300, 512, seed=3, device=cuda)       # M >= UNPACK_FROM: unpack + cuBLAS
+    y = ql(x).float().cpu()
+    assert O.max_rel(y.numpy(), (x.cpu().to(torch.bfloat16).double() @ ref.double().t()).numpy()) < 1e-2
+
+
+def _eingang_matches_oracle(e, v):
+    q, q2, d, s = O.quant_q8(v.cpu().numpy())
+    assert np.array_equal(e.xq.cpu().numpy(), q) and np.array_equal(e.xq2.cpu().numpy(), q2)
+    assert np.array_equal(e.xd.cpu().numpy(), d) and np.array_equal(e.xs.cpu().numpy(), s)
+
+
+@pytest.mark.parametrize("n", [512, 4096, 14336])
+@pytest.mark.parametrize("rest", [False, True])
+def test_norm_q8(cuda, n, rest):
+    h = synth.activations(1, n, seed=n, device=cuda)[0]
+    w = torch.rand(n, device=cuda) + 0.5
+    r = synth.activations(1, n, seed=n + 1, device=cuda)[0] if rest else None
+    xn, e, h2 = mmvq.norm_q8(h, w, 1e-5, rest=r, rs=0.5 if rest else 1.0)
+    v = h + 0.5 * r if rest else h
+    if rest:
+        assert torch.equal(h2, v)
+    else:
+        assert h2 is h
+    ref = v * torch.rsqrt(v.pow(2).mean() + 1e-5) * w
+    assert float((xn - ref).abs().max() / ref.abs().max()) < 1e-6
+    _eingang_matches_oracle(e, xn)
+    y = mmvq.mv("Q4_K", synth.blocks("Q4_K", 64, n, seed=3, device=cuda), e, 64, n)
+    assert y.shape == (64,)
+
+
+@pytest.mark.parametrize("gelu", [False, True])
+@pytest.mark.parametrize("with_u", [False, True])
+def test_akt_q8(cuda, gelu, with_u):
+    n = 14336
+    g = synth.activations(1, n, seed=1, device=cuda)[0] * 3
+    u = synth.activations(1, n, seed=2, device=cuda)[0] if with_u else None
+    a, e = mmvq.akt_q8(g, u, gelu)
+    ref = F.gelu(g, approximate="tanh") if gelu else F.silu(g)
+    if with_u:
+        ref = ref * u
+    assert float((a - ref).abs().max() / ref.abs().max()) < 1e-6
+    _eingang_matches_oracle(e, a)
