@@ -234,6 +234,93 @@ def cpu_baseline(budget_s: float = 12.0):
             "tok_s_32_layers": 1.0 / (per * LAYERS)}
 
 
+def sharded_suite(world: int, rank: int, dist, device, steps: int, warmup: int) -> dict:
+    """BASELINE configs 3 and 4 sharded over this job's ranks, measured in the same process as the headline:
+    the 128256x4096 vocabulary projection (Q8_0 and Q6_K, 1 and 8 tokens) row-sharded with an all-gather of
+    the logits, and the 128-expert MoE FFN (batch 1, 4, 16) expert-sharded with all-to-all exchanges.  Per
+    case: the time with the collective and without it (compute only), the load imbalance, and parity
+    against the unsharded computation on this rank (max over ranks of max|diff| / max|ref|).  Every rank
+    holds the same weights (same seeds) and the same vocab input; MoE tokens and routings are per rank.
+    Times are CUDA events over graph replays, max over ranks; distinct shard copies rotate so that each
+    replay reads more than twice L2."""
+    from nemicli_terminal_b200 import moe, mmvq, shard, synth
+    from nemicli_terminal_b200.formats import TYPE_ID, row_bytes
+    from nemicli_terminal_b200.layers import PackedExperts
+    peak, _ = peaks()
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+
+    def rel(y, ref):
+        r = float((y.double() - ref.double()).abs().max() / ref.double().abs().max().clamp_min(1e-30))
+        return max_over_ranks(r, dist, device)
+
+    out = {"vocab": {}, "moe": {}}
+    for fmt in ("Q8_0", "Q6_K"):
+        full = synth.blocks(fmt, VOCAB_ROWS, VOCAB_IN, seed=500, device=device)
+        lo, hi = shard.shard_range(VOCAB_ROWS, world, rank)
+        loc = shard.slice_rows(fmt, full, VOCAB_ROWS, VOCAB_IN, lo, hi)
+        copies = max(1, -(-2 * l2 // loc.numel()))
+        lins = [shard.RowShardedLinear(fmt, loc if c == 0 else loc.clone(), VOCAB_ROWS, VOCAB_IN)
+                for c in range(copies)]
+        total = VOCAB_ROWS * row_bytes(fmt, VOCAB_IN)
+        for T in (1, 8):
+            x = synth.activations(T, VOCAB_IN, seed=501 + T, device=device)
+            x = x[0].contiguous() if T == 1 else x.contiguous()
+            par = rel(lins[0](x), mmvq.mv(fmt, full, x, VOCAB_ROWS, VOCAB_IN))
+            g_loc, _ = capture(lambda: [l.local(x) for l in lins])
+            g_full, _ = capture(lambda: [l(x) for l in lins])
+            t_full = max_over_ranks(time_graph(g_full, steps, warmup, dist) / (steps * copies), dist, device)
+            t_loc = max_over_ranks(time_graph(g_loc, steps, warmup, dist) / (steps * copies), dist, device)
+            del g_loc, g_full
+            out["vocab"][f"{fmt} {T}tok"] = {
+                "us": t_full * 1e6, "gbs": total / t_full / 1e9, "compute_only_us": t_loc * 1e6,
+                "compute_only_hbm_frac_per_gpu": loc.numel() / t_loc / 1e9 / peak,
+                "gather_us": (t_full - t_loc) * 1e6, "parity_max_rel": par, "parity": "ok" if par == 0.0 else
+                ("ok" if par < 1e-6 else "FAIL")}
+        del lins, full, loc
+    torch.cuda.empty_cache()
+    shapes = ((MOE_FF, MOE_DIM), (MOE_FF, MOE_DIM), (MOE_DIM, MOE_FF))
+    per_expert = sum(o * row_bytes("Q4_K", i) for o, i in shapes)
+    blobs = [synth.blocks("Q4_K", MOE_EXPERTS * o, i, seed=700 + s_, device=device).view(MOE_EXPERTS, -1)
+             for s_, (o, i) in enumerate(shapes)]
+    elo, ehi = shard.shard_range(MOE_EXPERTS, world, rank)
+    full_ex = [PackedExperts(b, TYPE_ID["Q4_K"], MOE_EXPERTS, o, i, torch.float32) for b, (o, i) in zip(blobs, shapes)]
+    loc_ex = [PackedExperts(b[elo:ehi].reshape(-1), TYPE_ID["Q4_K"], ehi - elo, o, i, torch.float32)
+              for b, (o, i) in zip(blobs, shapes)]
+    layer = shard.ExpertShardedMoE(*loc_ex, MOE_EXPERTS, MOE_DIM)
+    ref_layer = moe.MoeFFN(*full_ex)
+    for B in (1, 4, 16):
+        n_rot = 8
+        xs = [synth.activations(B, MOE_DIM, seed=710 + r + 97 * rank, device=device) for r in range(n_rot)]
+        routes = [moe.route(synth.router_logits(B, MOE_EXPERTS, seed=720 + r + 97 * rank, device=device), MOE_K)
+                  for r in range(n_rot)]
+        par = max(rel(layer(x, ix, w), ref_layer(x, ix, w)) for x, (ix, w) in zip(xs[:2], routes[:2]))
+        recvs = [layer.dispatch(x, ix)[0] for x, (ix, _) in zip(xs, routes)]
+        g_full, _ = capture(lambda: [layer(x, ix, w) for x, (ix, w) in zip(xs, routes)])
+        g_cmp, _ = capture(lambda: [layer.compute(r) for r in recvs])
+        t_full = max_over_ranks(time_graph(g_full, steps, warmup, dist) / (steps * n_rot), dist, device)
+        t_cmp = max_over_ranks(time_graph(g_cmp, steps, warmup, dist) / (steps * n_rot), dist, device)
+        del g_full, g_cmp
+        # load: pairs each owner receives (all ranks' routings), and the experts this rank's owner touches
+        sent = torch.stack([torch.bincount(shard.owner_of(ix.reshape(-1), MOE_EXPERTS, world), minlength=world)
+                            for ix, _ in routes]).sum(0).to(device)
+        if dist is not None:
+            dist.all_reduce(sent)
+        per_rank = sent.tolist()
+        mean = sum(per_rank) / world
+        touched = torch.zeros(MOE_EXPERTS, dtype=torch.int64, device=device)
+        for ix, _ in routes:
+            touched.index_fill_(0, ix.reshape(-1), 1)
+        uniq = float(touched.sum()) / n_rot                 # upper bound per routing: this rank's own tokens
+        out["moe"][f"batch {B}"] = {
+            "us_per_call": t_full * 1e6, "compute_only_us": t_cmp * 1e6, "exchange_us": (t_full - t_cmp) * 1e6,
+            "pairs_per_owner": per_rank, "imbalance_max_over_mean": max(per_rank) / mean if mean else 1.0,
+            "parity_max_rel": par, "parity": "ok" if par < 1e-5 else "FAIL",
+            "touched_expert_gbs_rank0_tokens": uniq * per_expert / t_full / 1e9}
+    del blobs, full_ex, loc_ex, layer, ref_layer
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -365,6 +452,8 @@ def run_ours(args):
     torch.cuda.synchronize()
     te = max_over_ranks(a.elapsed_time(b) / 1e3 / e_steps, dist, device)
 
+    sharded = None if args.no_sharded else sharded_suite(world, rank, dist, device, max(5, args.steps // 10),
+                                                          max(3, args.warmup))
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
     launches_per_step = 1 if args.mode == "chain" else args.layers * 4   # chain: one launch per step
     if rank == 0:
@@ -378,7 +467,9 @@ def run_ours(args):
                                        "o_proj reads q_proj's output in place of attention" if args.mode == "chain" else ""),
                        "layers": args.layers, "batch": 1, "weight_bytes_per_step": step_bytes,
                        "l2": "inputs larger than L2 (4.41 GB distinct weights per step), no flush",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "parallelism": (f"value: replicas x{world} of the config-2 stack (one per GPU, no "
+                                       "collective); configs 3 and 4 sharded over the GPUs in `sharded`")
+                                      if world > 1 else "single GPU",
                        "graph": "whole step captured once in a CUDA graph",
                        "mode": args.mode,
                        "pdl": not args.no_pdl},
@@ -395,6 +486,7 @@ def run_ours(args):
                     "d2h_bytes_per_step": d2h, "ms_per_step": te * 1e3},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
+            "sharded": sharded,
         }
         print(json.dumps(line), flush=True)
     del g1
@@ -581,6 +673,7 @@ def main():
     ap.add_argument("--batches", type=int, nargs="*", default=[1, 4, 8])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-pdl", action="store_true", help="plain stream order between the matvec launches")
+    ap.add_argument("--no-sharded", action="store_true", help="skip configs 3 and 4 (row / expert sharded)")
     ap.add_argument("--mode", choices=["chain", "calls"], default="chain",
                     help="chain: the step as one decode-chain launch; calls: one launch per matrix group")
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers in the stack (profiling runs use fewer)")

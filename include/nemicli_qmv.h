@@ -18,8 +18,9 @@
  *
  * Weights stay in raw GGUF block layout, row-major (n_out rows of n_in / block_values blocks).
  * Formats (GGML type ids): Q4_0 = 2, Q4_1 = 3, Q5_0 = 6, Q5_1 = 7, Q8_0 = 8, Q2_K = 10, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_K = 14, IQ2_XXS = 16, IQ2_XS = 17, IQ3_XXS = 18,
- *          IQ4_NL = 20, IQ3_S = 21, IQ2_S = 22, IQ4_XS = 23, TQ1_0 = 34, TQ2_0 = 35, MXFP4 = 39, Q1_0 = 41, Q2_0 = 42,
- *          PQ2_0 = 142 (the reference's id for Q2_0 codes in 128-value blocks).
+ *          IQ1_S = 19, IQ4_NL = 20, IQ3_S = 21, IQ2_S = 22, IQ4_XS = 23, IQ1_M = 29, TQ1_0 = 34, TQ2_0 = 35, MXFP4 = 39,
+ *          Q1_0 = 41, Q2_0 = 42, PQ2_0 = 142 (the reference's id for Q2_0 codes in 128-value blocks), PTQ1_0 = 143
+ *          (the reference's id for TQ1_0 trits in 128-value blocks).
  * Alignment: Q4_K and Q5_K weights 16 bytes, MXFP4 4 bytes, the other formats 2 bytes.
  */
 #ifndef NEMICLI_QMV_H
@@ -34,7 +35,7 @@ extern "C" {
 #define NEMICLI_QMV_ABI_VERSION 2
 
 #define QMV_OK 0
-#define QMV_ERR_FORMAT 1   /* format not one of the twenty-three above */
+#define QMV_ERR_FORMAT 1   /* format not one of the twenty-six above */
 #define QMV_ERR_SHAPE 2    /* n_in not a positive multiple of the block size, n_out <= 0, ... */
 #define QMV_ERR_ALIGN 3    /* a pointer or stride misses the alignment above */
 #define QMV_ERR_TOKENS 4   /* token / slot count out of range */
@@ -51,7 +52,7 @@ const char* qmv_status_string(int status);
 int qmv_last_cuda_error(void);
 
 /* Values / bytes per block of a format (0 for a format this library does not compute).
- * Replaces: ggufengine/gguf.py:64-77 (GGML_TYPES) for the twenty-three formats. */
+ * Replaces: ggufengine/gguf.py:64-77 (GGML_TYPES) for the twenty-six formats. */
 int qmv_block_values(int ggml_type);
 int qmv_block_bytes(int ggml_type);
 

@@ -73,6 +73,7 @@ int by_format(int fmt, Fn&& f) {
     QMV_CASE(F_MXFP4) QMV_CASE(F_Q1_0) QMV_CASE(F_Q2_0) QMV_CASE(F_PQ2_0) QMV_CASE(F_Q2_K) QMV_CASE(F_Q3_K)
     QMV_CASE(F_Q4_K) QMV_CASE(F_Q5_K) QMV_CASE(F_Q6_K) QMV_CASE(F_IQ2_XXS) QMV_CASE(F_IQ2_XS) QMV_CASE(F_IQ2_S)
     QMV_CASE(F_IQ3_XXS) QMV_CASE(F_IQ3_S) QMV_CASE(F_IQ4_XS) QMV_CASE(F_TQ1_0) QMV_CASE(F_TQ2_0)
+    QMV_CASE(F_IQ1_S) QMV_CASE(F_IQ1_M) QMV_CASE(F_PTQ1_0)
     }
 #undef QMV_CASE
     return ST_BAD_FORMAT;

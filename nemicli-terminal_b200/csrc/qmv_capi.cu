@@ -87,6 +87,7 @@ int by_format(int fmt, Fn&& f) {
     QMV_CASE(F_MXFP4) QMV_CASE(F_Q1_0) QMV_CASE(F_Q2_0) QMV_CASE(F_PQ2_0) QMV_CASE(F_Q2_K) QMV_CASE(F_Q3_K)
     QMV_CASE(F_Q4_K) QMV_CASE(F_Q5_K) QMV_CASE(F_Q6_K) QMV_CASE(F_IQ2_XXS) QMV_CASE(F_IQ2_XS) QMV_CASE(F_IQ2_S)
     QMV_CASE(F_IQ3_XXS) QMV_CASE(F_IQ3_S) QMV_CASE(F_IQ4_XS) QMV_CASE(F_TQ1_0) QMV_CASE(F_TQ2_0)
+    QMV_CASE(F_IQ1_S) QMV_CASE(F_IQ1_M) QMV_CASE(F_PTQ1_0)
     }
 #undef QMV_CASE
     return ST_BAD_FORMAT;
@@ -122,7 +123,7 @@ __host__ __device__ constexpr int unit_vals(int fmt) { return fmt == F_Q4_K || f
 // when a team of <= 512 lanes covers the row; fused quantisation reserves 2.25 * n_in bytes.
 bool tma_plan(int fmt, int n_in, long long row_bytes, bool fused, TmaPlan& pl) {
     if (!knobs().enabled || row_bytes % 16 || n_in % unit_vals(fmt)) return false;
-    if (fmt == F_TQ1_0) return false;          // TQ1_0 runs on the warp-per-row kernel only
+    if (!staged_format(fmt)) return false;     // TQ1_0, IQ1_S, IQ1_M, PTQ1_0 run on the warp-per-row kernel only
     const int ncw = knobs().ncw;
     const int cap = ncw <= 8 ? kSmemHalf : kSmemCap;
     const int U = n_in / unit_vals(fmt);

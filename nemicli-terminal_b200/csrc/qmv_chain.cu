@@ -76,9 +76,10 @@ void* chain_workspace_ptr() {
 // Ring of the decode chain: slots, most copies in flight, tiles prefetched into L2 ahead of the copies.
 // Fixed in the shipped library; a -DQMV_SWEEP build reads NEMICLI_CHAIN_SLOTS / _INFLIGHT / _PF.
 struct ChainRing {
-    int slots = 3, inflight = 0, prefetch = 0;
+    int slots = 3, inflight = 0, prefetch = 0, ncw = kChainNcw;
     ChainRing() {
 #ifdef QMV_SWEEP
+        if (const char* e = std::getenv("NEMICLI_CHAIN_NCW")) ncw = std::atoi(e) == 16 ? 16 : 8;
         if (const char* e = std::getenv("NEMICLI_CHAIN_SLOTS")) slots = std::atoi(e);
         if (const char* e = std::getenv("NEMICLI_CHAIN_INFLIGHT")) inflight = std::atoi(e);
         if (const char* e = std::getenv("NEMICLI_CHAIN_PF")) prefetch = std::atoi(e);
@@ -89,7 +90,22 @@ const ChainRing& chain_ring() {
     static const ChainRing r;
     return r;
 }
-unsigned long long* g_chain_trace = nullptr;   // per (stage, CTA) timestamps: sweep builds only
+unsigned long long* g_chain_trace = nullptr;
+
+// the kernel instance for NCW consumer warps and a pair of configurations (a chain uses at most two)
+template <int NCW>
+void (*chain_kernel_pair(int pair))(const ChainParams) {
+    return pair == 0 ? chain_kernel<NCW, CFG_Q4K_4096, CFG_Q6K_14336>
+         : pair == 1 ? chain_kernel<NCW, CFG_Q4K_4096, CFG_Q4K_14336>
+         : pair == 2 ? chain_kernel<NCW, CFG_Q6K_4096, CFG_Q6K_14336>
+                     : chain_kernel<NCW, CFG_Q8_0_4096, CFG_Q6K_4096>;
+}
+void (*chain_kernel_for(int ncw, int pair))(const ChainParams) {
+#ifdef QMV_SWEEP
+    if (ncw == 16) return chain_kernel_pair<16>(pair);
+#endif
+    return ncw == kChainNcw ? chain_kernel_pair<kChainNcw>(pair) : nullptr;
+}   // per (stage, CTA) timestamps: sweep builds only
 
 }  // namespace
 
@@ -135,7 +151,7 @@ int qmv_chain(const qmv_stage* stages, int n_stages, void* workspace, void* stre
         }
         c.row_start[q.n_jobs] = rows;
         c.total_rows = rows;
-        c.R = chain_cfg_nper(cfg) * (32 * kChainNcw / chain_cfg_g(cfg));
+        c.R = chain_cfg_rows(cfg);
         c.in_kind = q.input;
         c.a = q.a;
         c.b = q.input == QMV_INPUT_RAW ? nullptr : q.b;
@@ -204,21 +220,21 @@ int qmv_chain(const qmv_stage* stages, int n_stages, void* workspace, void* stre
     const int smem = int(S * slot + other);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (cudaMemsetAsync(workspace, 0, kChainCounterBytes, st) != cudaSuccess) return launched();
-    void (*kern)(const ChainParams) = pair == 0 ? chain_kernel<kChainNcw, CFG_Q4K_4096, CFG_Q6K_14336>
-                                    : pair == 1 ? chain_kernel<kChainNcw, CFG_Q4K_4096, CFG_Q4K_14336>
-                                    : pair == 2 ? chain_kernel<kChainNcw, CFG_Q6K_4096, CFG_Q6K_14336>
-                                                : chain_kernel<kChainNcw, CFG_Q8_0_4096, CFG_Q6K_4096>;
-    static int configured[64][4] = {{0}};
+    const int ncw = ring.ncw;
+    void (*kern)(const ChainParams) = chain_kernel_for(ncw, pair);
+    if (!kern) return ST_BAD_SHAPE;
+    static int configured[64][2][4] = {{{0}}};
+    const int wi = ncw == kChainNcw ? 0 : 1;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !configured[dev][pair]) {
+    if (dev >= 0 && dev < 64 && !configured[dev][wi][pair]) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap) != cudaSuccess)
             return launched();
-        configured[dev][pair] = 1;
+        configured[dev][wi][pair] = 1;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(sm_count());
-    cfg.blockDim = dim3(32 * (kChainNcw + 1));
+    cfg.blockDim = dim3(32 * (ncw + 1));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];

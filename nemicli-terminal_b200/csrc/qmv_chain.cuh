@@ -29,7 +29,7 @@ enum : int { CH_RAW = 0, CH_RMSNORM = 1, CH_SILU_MUL = 2 };
 // consumer configurations compiled into the chain kernel (format, row length class)
 enum : int { CFG_Q4K_4096 = 0, CFG_Q6K_14336 = 1, CFG_Q4K_14336 = 2, CFG_Q6K_4096 = 3, CFG_Q8_0_4096 = 4, CFG_COUNT = 5 };
 constexpr int kChainMaxStages = 128;
-constexpr int kChainNcw = 16;
+constexpr int kChainNcw = 8;                        // consumer warps (measured: 8 beat 16, no spills)
 constexpr int kChainMaxIn = 14336;                  // longest input vector a chain stage takes
 constexpr int kChainMaxGroups = kChainMaxIn / 32;
 constexpr int kChainPartFloats = 1024;              // deferred cross-warp partial sums (shared memory)
@@ -79,30 +79,39 @@ struct ChainParams {
     int* status;
 };
 
-template <int CFG> struct ChainCfg;
-// tiles of 27..47 KB (R = NPER * 512 / G rows; 4 Q6_K rows give every CTA the same tile count for
-// a 4096-row down projection).  Q6_K uses 32-value units here (F_Q6_K_U32): the 64-value units of the
-// staged kernel need more registers than this non-inlined loop has without spilling.
-template <> struct ChainCfg<CFG_Q4K_4096> { static constexpr int FMT = F_Q4_K, G = 64, UPL = 1, NPER = 2; };
-template <> struct ChainCfg<CFG_Q6K_14336> { static constexpr int FMT = F_Q6_K_U32, G = 512, UPL = 1, NPER = 4; };
-template <> struct ChainCfg<CFG_Q4K_14336> { static constexpr int FMT = F_Q4_K, G = 256, UPL = 1, NPER = 2; };
-template <> struct ChainCfg<CFG_Q6K_4096> { static constexpr int FMT = F_Q6_K_U32, G = 128, UPL = 1, NPER = 2; };
-template <> struct ChainCfg<CFG_Q8_0_4096> { static constexpr int FMT = F_Q8_0, G = 128, UPL = 1, NPER = 2; };
-
+// Base geometry of each configuration (for 16 consumer warps): team width G (lanes per row) and rows
+// per tile R.  Tiles are 27..47 KB; 4 Q6_K rows give every CTA the same tile count for a 4096-row down
+// projection.  Q6_K uses 32-value units here (F_Q6_K_U32): the 64-value units of the staged kernel need
+// more registers than this non-inlined loop has.
 __host__ __device__ constexpr int chain_cfg_g(int cfg) {
     return cfg == CFG_Q4K_4096 ? 64 : cfg == CFG_Q6K_14336 ? 512 : cfg == CFG_Q4K_14336 ? 256 : 128;
 }
-__host__ __device__ constexpr int chain_cfg_nper(int cfg) { return cfg == CFG_Q6K_14336 ? 4 : 2; }
+__host__ __device__ constexpr int chain_cfg_rows(int cfg) {
+    return cfg == CFG_Q4K_4096 ? 16 : cfg == CFG_Q6K_14336 ? 4 : cfg == CFG_Q4K_14336 ? 4 : 8;
+}
 __host__ __device__ constexpr int chain_cfg_fmt(int cfg) {
     return cfg == CFG_Q4K_4096 || cfg == CFG_Q4K_14336 ? F_Q4_K : cfg == CFG_Q8_0_4096 ? F_Q8_0 : F_Q6_K;
 }
 __host__ __device__ constexpr int chain_cfg_nin(int cfg) {
     return cfg == CFG_Q6K_14336 || cfg == CFG_Q4K_14336 ? 14336 : 4096;
 }
+// The geometry for NCW consumer warps keeps each configuration's tile (R rows): with fewer warps a team
+// is at most 32 NCW lanes wide (each lane then takes UPL units of its row) and takes more of the tile's
+// rows (NPER), so every lane has more independent rows and units in flight.
+template <int CFG, int NCW>
+struct ChainCfg {
+    static constexpr int FMT = chain_cfg_fmt(CFG) == F_Q6_K ? F_Q6_K_U32 : chain_cfg_fmt(CFG);
+    static constexpr int G = chain_cfg_g(CFG) < 32 * NCW ? chain_cfg_g(CFG) : 32 * NCW;
+    static constexpr int UPL = chain_cfg_g(CFG) / G;
+    static constexpr int TEAMS = 32 * NCW / G;
+    static constexpr int NPER = chain_cfg_rows(CFG) / TEAMS;
+    static_assert(NPER * TEAMS == chain_cfg_rows(CFG), "tile rows split over the teams");
+};
 // the activation goes through shared memory when several teams would load the same units (every CTA
 // reading the same few L2 lines many times over is slow); otherwise each lane loads its own units
-__host__ __device__ constexpr bool chain_cfg_staged(int cfg) {
-    return 32 * kChainNcw / chain_cfg_g(cfg) > 1 && chain_cfg_nin(cfg) <= kChainStageIn;
+template <int CFG, int NCW>
+__host__ __device__ constexpr bool chain_cfg_staged() {
+    return ChainCfg<CFG, NCW>::TEAMS > 1 && chain_cfg_nin(CFG) <= kChainStageIn;
 }
 
 // rows [c * total / grid, (c + 1) * total / grid) of a stage belong to CTA c
@@ -198,7 +207,7 @@ __device__ __noinline__ int chain_consume(const ChainParams& P, const ChainStage
                                           uint32_t empty0) {
     bool dead = *dead_io != 0;
     const int buf = k_stage & 1;
-    using C = ChainCfg<CFG>;
+    using C = ChainCfg<CFG, NCW>;
     constexpr int FMT = C::FMT, G = C::G, UPL = C::UPL, NPER = C::NPER;
     constexpr int TEAMS = 32 * NCW / G;
     constexpr int WPT = G >= 32 ? G / 32 : 1;
@@ -209,28 +218,40 @@ __device__ __noinline__ int chain_consume(const ChainParams& P, const ChainStage
     const int lane = threadIdx.x & 31;
     const int cl = threadIdx.x, team = cl / G, li = cl % G;
     const int U = st.n_in / VPU;
-    // the 1/rms factor of an RMSNORM input (warp 0, after its activation loads are out: the groups'
-    // sums of squares in a fixed order)
+    // the 1/rms factor of an RMSNORM input: warp 0 issues the loads of the groups' sums of squares together
+    // with the activation loads (one round trip for both) and adds them in a fixed order afterwards
     float* s_scale = reinterpret_cast<float*>(act_smem + kChainActSmem);
+    float* s_pss = s_scale + 4;                          // kChainMaxGroups floats
+    const bool rms = st.in_kind == CH_RMSNORM;
+    auto pss_issue = [&]() {                             // asynchronous copies: no registers held
+        if (threadIdx.x < 32 && rms) {
+            for (int g = lane; g < st.n_in / 32; g += 32)
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" :: "r"(smem_u32(s_pss + g)), "l"(P.pss[buf] + g)
+                             : "memory");
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        }
+    };
     auto norm_scale = [&]() {
         if (threadIdx.x < 32) {
             float scale = 1.f;
-            if (st.in_kind == CH_RMSNORM) {
-                const int ng = st.n_in / 32;
+            if (rms) {
+                asm volatile("cp.async.wait_all;" ::: "memory");
+                __syncwarp();
                 float ss = 0.f;
-                for (int g = lane; g < ng; g += 32) ss += __ldcg(P.pss[buf] + g);
+                for (int g = lane; g < st.n_in / 32; g += 32) ss += s_pss[g];
                 scale = rsqrtf(warp_sum(ss) / float(st.n_in) + st.eps);
             }
             if (lane == 0) *s_scale = scale;
         }
     };
     Act<FMT> act[UPL];
-    if constexpr (chain_cfg_staged(CFG)) {
+    if constexpr (chain_cfg_staged<CFG, NCW>()) {
         int8_t* sq = reinterpret_cast<int8_t*>(act_smem);
         int8_t* sq2 = sq + kChainStageIn;
         float* sd = reinterpret_cast<float*>(sq2 + kChainStageIn);
         float* ss_ = sd + kChainStageIn / 32;
         const int n16 = st.n_in / 16, ng = st.n_in / 32;
+        pss_issue();
         for (int i = cl; i < n16; i += 32 * NCW) {
             const int4 a = __ldcg(reinterpret_cast<const int4*>(P.xq[buf]) + i);
             const int4 b = __ldcg(reinterpret_cast<const int4*>(P.xq2[buf]) + i);
@@ -251,6 +272,7 @@ __device__ __noinline__ int chain_consume(const ChainParams& P, const ChainStage
             if (u < U) load_act<FMT, true, SRC_SMEM>(act[i], u, sq, sq2, sd, ss_);
         }
     } else {
+        pss_issue();
 #pragma unroll
         for (int i = 0; i < UPL; ++i) {
             const int u = li + G * i;
@@ -400,7 +422,7 @@ __device__ __forceinline__ void chain_prefetch_tile(const ChainParams& P, const 
 // shared memory: [S slots x slot_bytes][partial sums kChainPartFloats floats]
 //                [staged activation kChainActSmem][scale 16 B][mbarriers 2 S]
 
-__host__ __device__ constexpr int chain_red_bytes() { return kChainPartFloats * 4 + kChainActSmem + 16; }
+__host__ __device__ constexpr int chain_red_bytes() { return kChainPartFloats * 4 + kChainActSmem + 16 + 4 * kChainMaxGroups; }
 
 // CA, CB: the two consumer configurations this instance carries (a chain uses at most two; one
 // kernel with all of them would spill registers)

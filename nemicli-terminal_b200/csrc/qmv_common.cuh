@@ -6,12 +6,17 @@
 
 namespace qmv {
 
-// GGML type ids of the twenty-three formats (PQ2_0 = 142: the reference's id for the 128-value Q2_0 variant) (the GGUF type table; reference ggufengine/gguf.py:64-77)
+// GGML type ids of the twenty-six formats (PQ2_0 = 142: the reference's id for the 128-value Q2_0 variant) (the GGUF type table; reference ggufengine/gguf.py:64-77)
 enum : int {
     F_Q4_0 = 2, F_Q8_0 = 8, F_Q4_K = 12, F_Q5_K = 13, F_Q6_K = 14, F_IQ2_XXS = 16, F_IQ4_XS = 23, F_TQ2_0 = 35,
     F_MXFP4 = 39, F_IQ3_S = 21, F_IQ3_XXS = 18, F_Q4_1 = 3, F_Q5_0 = 6, F_Q5_1 = 7, F_IQ4_NL = 20,
-    F_Q1_0 = 41, F_Q2_0 = 42, F_PQ2_0 = 142, F_Q3_K = 11, F_IQ2_XS = 17, F_IQ2_S = 22, F_Q2_K = 10, F_TQ1_0 = 34
+    F_Q1_0 = 41, F_Q2_0 = 42, F_PQ2_0 = 142, F_Q3_K = 11, F_IQ2_XS = 17, F_IQ2_S = 22, F_Q2_K = 10, F_TQ1_0 = 34,
+    F_IQ1_S = 19, F_IQ1_M = 29, F_PTQ1_0 = 143
 };
+// IQ1_S / IQ1_M: codebook entries of values in {-1, 0, +1} plus a +-1/8 delta
+__host__ __device__ constexpr bool iq1_format(int f) { return f == F_IQ1_S || f == F_IQ1_M; }
+// formats the staged single-token kernel takes (the rest run on the warp-per-row kernel)
+__host__ __device__ constexpr bool staged_format(int f) { return f != F_TQ1_0 && !iq1_format(f) && f != F_PTQ1_0; }
 // IQ2_XS / IQ2_S: 16-value scale groups, eight-magnitude codebook entries
 __host__ __device__ constexpr bool iq2x_format(int f) { return f == F_IQ2_XS || f == F_IQ2_S; }
 // the ternary / 1-bit formats with one scale per 64 or 128 values, taken in 32-value units
@@ -42,16 +47,17 @@ constexpr int kMaxTokens = 8;           // tokens per launch of the dp4a kernels
 constexpr float kInv254 = 1.0f / 254.0f;
 
 __host__ __device__ constexpr int block_values(int f) {
-    return b32_format(f) ? 32 : f == F_Q2_0 ? 64 : (f == F_Q1_0 || f == F_PQ2_0) ? 128 : 256;
+    return b32_format(f) ? 32 : f == F_Q2_0 ? 64 : (f == F_Q1_0 || f == F_PQ2_0 || f == F_PTQ1_0) ? 128 : 256;
 }
 __host__ __device__ constexpr int block_bytes(int f) {
-    return f == F_Q4_0 || f == F_IQ4_NL || f == F_Q1_0 || f == F_Q2_0 ? 18 : f == F_PQ2_0 ? 34 : f == F_Q3_K ? 110 : f == F_Q2_K ? 84 : f == F_TQ1_0 ? 54 : f == F_IQ2_XS ? 74 : f == F_IQ2_S ? 82 : f == F_Q4_1 ? 20 : f == F_Q5_0 ? 22 : f == F_Q5_1 ? 24 : f == F_Q8_0 ? 34 : f == F_Q4_K ? 144 : f == F_Q5_K ? 176 : f == F_Q6_K ? 210
+    return f == F_Q4_0 || f == F_IQ4_NL || f == F_Q1_0 || f == F_Q2_0 ? 18 : f == F_PQ2_0 ? 34 : f == F_IQ1_S ? 50 :
+         f == F_IQ1_M ? 56 : f == F_PTQ1_0 ? 28 : f == F_Q3_K ? 110 : f == F_Q2_K ? 84 : f == F_TQ1_0 ? 54 : f == F_IQ2_XS ? 74 : f == F_IQ2_S ? 82 : f == F_Q4_1 ? 20 : f == F_Q5_0 ? 22 : f == F_Q5_1 ? 24 : f == F_Q8_0 ? 34 : f == F_Q4_K ? 144 : f == F_Q5_K ? 176 : f == F_Q6_K ? 210
          : f == F_IQ4_XS ? 136 : f == F_MXFP4 ? 17 : f == F_IQ3_S ? 110
          : f == F_IQ3_XXS ? 98 : 66;
 }
 // values per integer-sum unit (one weight scale and one activation scale)
 __host__ __device__ constexpr int unit_values(int f) {
-    return f == F_Q6_K || f == F_Q3_K || iq2x_format(f) || f == F_Q2_K ? 16 : 32;
+    return f == F_Q6_K || f == F_Q3_K || iq2x_format(f) || f == F_Q2_K || f == F_IQ1_M ? 16 : 32;
 }
 // Q3_K signed codes q2 - 4 (1 - hbit) of four values: 2-bit fields already in place (0x03 bytes), high bits
 // in bit 0 of each byte
@@ -60,7 +66,8 @@ __device__ __forceinline__ uint32_t q3k_word(uint32_t q2, uint32_t h1) { return 
 __host__ __device__ inline bool known_format(int f) {
     return f == F_Q4_0 || f == F_Q8_0 || f == F_Q4_K || f == F_Q5_K || f == F_Q6_K || f == F_IQ2_XXS || f == F_IQ4_XS ||
            f == F_TQ2_0 || f == F_MXFP4 || f == F_IQ3_S || f == F_IQ3_XXS || f == F_Q4_1 || f == F_Q5_0 ||
-           f == F_Q5_1 || f == F_IQ4_NL || bits_format(f) || f == F_Q3_K || iq2x_format(f) || f == F_Q2_K || f == F_TQ1_0;
+           f == F_Q5_1 || f == F_IQ4_NL || bits_format(f) || f == F_Q3_K || iq2x_format(f) || f == F_Q2_K || f == F_TQ1_0 ||
+           iq1_format(f) || f == F_PTQ1_0;
 }
 // weight rows and blocks of the K-quant formats with 16-byte header words are read 16 bytes at a time;
 // MXFP4's 17-byte blocks start at any byte, and their loads stay inside the tensor when it starts on a

@@ -113,6 +113,7 @@ int launch_sums_fmt(const MvParams& P, cudaStream_t st) {
 
 template <int FMT>
 int launch_tma_fmt(int xf, bool sums, const TmaParams& P, const TmaPlan& pl, int grid, cudaStream_t st) {
+    if constexpr (!staged_format(FMT)) return ST_BAD_FORMAT;        // the warp-per-row kernel takes these
     if (sums) return xf == 0 ? launch_tma_x<FMT, 0, true>(P, pl, grid, st) : ST_BAD_SHAPE;
     switch (xf) {
     case 0: return launch_tma_x<FMT, 0, false>(P, pl, grid, st);

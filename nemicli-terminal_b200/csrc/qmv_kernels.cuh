@@ -618,6 +618,159 @@ __device__ __forceinline__ void lane_tq1(const uint8_t* const (&rows)[RW], int s
     }
 }
 
+// ---- IQ1_S (50 B = d, qs[32], qh u16[8]; quant.py:350-360) and IQ1_M (56 B = qs[32], qh[16], scales
+// u16[4]; quant.py:363-375).  Lane q takes sub-block q: codebook entries 4q..4q+3, eight values each in
+// {-1, 0, +1} (kIq1sCodes, two bits a value) plus a delta of +-1/8 per sub-block (IQ1_S) or per entry
+// (IQ1_M).  Value = dl (g + delta) with dl = d (2 s + 1): the code 8 g +- 1 is an exact int8 and the weight
+// scale dl / 8, so the sums need nothing but xq / xq2.  IQ1_M's 3-bit scales cover 16 values (two groups
+// per lane) and its d sits in the top nibbles of the four scale words.
+__device__ const uint16_t kIq1sCodes[2048] = {
+#include "iq1s_grid.inc"
+};
+// eight codes 8 g + (neg ? -1 : +1) of one codebook entry as two words of int8 bytes
+__device__ __forceinline__ void iq1_words(uint32_t idx, uint32_t neg, uint32_t& lo, uint32_t& hi) {
+    const uint32_t c = __ldg(kIq1sCodes + idx);
+    const uint32_t delta = neg ? 0xFFFFFFFFu : 0x01010101u;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint32_t c4 = (c >> (8 * h)) & 0xFFu;
+        const uint32_t f = (c4 | (c4 << 6) | (c4 << 12) | (c4 << 18)) & 0x03030303u;   // 2-bit field per byte
+        const uint32_t g8 = __vsub4((f & 0x01010101u) << 3, (f & 0x02020202u) << 3);   // 8 g: 0, 8 or -8
+        (h ? hi : lo) = __vadd4(g8, delta);
+    }
+}
+__device__ __forceinline__ float iq1m_d(const uint8_t* b) {
+    const uint32_t s01 = ldw2(b + 48) | (ldw2(b + 50) << 16), s23 = ldw2(b + 52) | (ldw2(b + 54) << 16);
+    const uint32_t d16 = ((s01 >> 12) & 0xFu) | ((s01 >> 24) & 0xF0u) | ((s23 >> 4) & 0xF00u) | ((s23 >> 16) & 0xF000u);
+    return h2f(d16);
+}
+template <int T, int RW, bool SUMS, int FMT>
+__device__ __forceinline__ void lane_iq1(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                         const Tok<T>& tk, float (&acc)[RW][T], int row0) {
+    uint32_t w[RW][8];
+    float wsc[RW][2];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        const uint8_t* b = rows[r] + (long long)sb * block_bytes(FMT);
+        if constexpr (FMT == F_IQ1_S) {
+            const uint32_t qh = ldw2(b + 34 + 2 * q);
+            const uint32_t qs = ldw2(b + 2 + 4 * q) | (ldw2(b + 4 + 4 * q) << 16);
+#pragma unroll
+            for (int l = 0; l < 4; ++l)
+                iq1_words(((qs >> (8 * l)) & 0xFFu) | (((qh >> (3 * l)) & 7u) << 8), qh >> 15, w[r][2 * l], w[r][2 * l + 1]);
+            wsc[r][0] = wsc[r][1] = h2f(ldw2(b)) * (float(2 * ((qh >> 12) & 7u) + 1) * 0.125f);
+        } else {
+            const uint32_t qs = ldw2(b + 4 * q) | (ldw2(b + 2 + 4 * q) << 16);
+            const uint32_t nb = ldw2(b + 32 + 2 * q);              // nibbles of entries 4q..4q+3
+#pragma unroll
+            for (int l = 0; l < 4; ++l) {
+                const uint32_t nib = (nb >> (4 * l)) & 15u;
+                iq1_words(((qs >> (8 * l)) & 0xFFu) | ((nib & 7u) << 8), nib >> 3, w[r][2 * l], w[r][2 * l + 1]);
+            }
+            const float d = iq1m_d(b);
+            const uint32_t sw = ldw2(b + 48 + 2 * (q >> 1));       // groups 2q, 2q + 1: fields (2q) % 4, (2q+1) % 4
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+                wsc[r][k] = d * (float(2 * ((sw >> (3 * ((2 * q + k) & 3))) & 7u) + 1) * 0.125f);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const long long o = tk.tb[t] + (long long)sb * 256 + 32 * q;
+        const int4 x0 = ldx16(P.xq + o), x1 = ldx16(P.xq + o + 16);
+        const int4 y0 = ldx16(P.xq2 + o), y1 = ldx16(P.xq2 + o + 16);
+        const float dd = __ldg(P.xd + ((tk.tb[t] + (long long)sb * 256) >> 5) + q);
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            const int s0 = dp4(w[r][3], x0.w, dp4(w[r][2], x0.z, dp4(w[r][1], x0.y, dp4(w[r][0], x0.x, 0))));
+            const int s1 = dp4(w[r][7], x1.w, dp4(w[r][6], x1.z, dp4(w[r][5], x1.y, dp4(w[r][4], x1.x, 0))));
+            const int u0 = dp4(w[r][3], y0.w, dp4(w[r][2], y0.z, dp4(w[r][1], y0.y, dp4(w[r][0], y0.x, 0))));
+            const int u1 = dp4(w[r][7], y1.w, dp4(w[r][6], y1.z, dp4(w[r][5], y1.y, dp4(w[r][4], y1.x, 0))));
+            if constexpr (SUMS) {
+                if constexpr (FMT == F_IQ1_S) {
+                    const long long base = (long long)row0 * (P.n_in / 32) + sb * 8 + q;
+                    atomicAdd(P.s + base, s0 + s1);
+                    atomicAdd(P.s2 + base, u0 + u1);
+                } else {
+                    const long long base = (long long)row0 * (P.n_in / 16) + sb * 16 + 2 * q;
+                    atomicAdd(P.s + base, s0);
+                    atomicAdd(P.s2 + base, u0);
+                    atomicAdd(P.s + base + 1, s1);
+                    atomicAdd(P.s2 + base + 1, u1);
+                }
+            } else {
+                acc[r][t] += dd * (wsc[r][0] * (float(s0) + float(u0) * kInv254) +
+                                   wsc[r][1] * (float(s1) + float(u1) * kInv254));
+            }
+        }
+    }
+}
+
+// ---- PTQ1_0 (28 B = qs[24], qh[2], d; quant.py:431-469, trit_plan(24, 2)): values 0..79 are trit j / 16 of
+// byte j % 16, 80..119 trit (j - 80) / 8 of byte 16 + (j - 80) % 8, 120..127 trit (j - 120) / 2 of qh byte
+// (j - 120) % 2.  Lane q takes the 32-value unit 8 sb + q (unit u % 4 of block u / 4); the code is the trit,
+// value d (trit - 1): offset d xs.
+template <int T, int RW, bool SUMS>
+__device__ __forceinline__ void lane_ptq1(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                          const Tok<T>& tk, float (&acc)[RW][T], int row0) {
+    const int u = sb * 8 + q;
+    if (u >= P.n_in / 32) return;
+    const int sub = u & 3;
+    uint32_t w[RW][8];
+    float d[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        const uint8_t* b = rows[r] + (long long)(u >> 2) * 28;
+        d[r] = h2f(ldw2(b + 26));
+        const uint4 a = ldw16_a2(b);                           // bytes 0..15
+        const uint2 c = ldw8_a2(b + 16);                       // bytes 16..23
+        const uint32_t A[4] = {a.x, a.y, a.z, a.w};
+        if (sub < 2) {                                         // values 32 sub ..: powers 3^(2 sub), 3^(2 sub + 1)
+            const uint32_t p0 = sub == 0 ? 1u : 9u, p1 = sub == 0 ? 3u : 27u;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                w[r][i] = trits4(A[i], p0);
+                w[r][4 + i] = trits4(A[i], p1);
+            }
+        } else if (sub == 2) {                                 // 64..79: 3^4 of bytes 0..15; 80..95: 3^0, 3^1 of 16..23
+#pragma unroll
+            for (int i = 0; i < 4; ++i) w[r][i] = trits4(A[i], 81u);
+            w[r][4] = trits4(c.x, 1u); w[r][5] = trits4(c.y, 1u);
+            w[r][6] = trits4(c.x, 3u); w[r][7] = trits4(c.y, 3u);
+        } else {                                               // 96..119: 3^2..3^4 of 16..23; 120..127: qh
+            w[r][0] = trits4(c.x, 9u); w[r][1] = trits4(c.y, 9u);
+            w[r][2] = trits4(c.x, 27u); w[r][3] = trits4(c.y, 27u);
+            w[r][4] = trits4(c.x, 81u); w[r][5] = trits4(c.y, 81u);
+            const uint32_t h = ldw2(b + 24);
+            const uint32_t hh = h | (h << 16);                 // bytes qh0, qh1, qh0, qh1
+            w[r][6] = (trits4(hh, 1u) & 0x0000FFFFu) | (trits4(hh, 3u) & 0xFFFF0000u);
+            w[r][7] = (trits4(hh, 9u) & 0x0000FFFFu) | (trits4(hh, 27u) & 0xFFFF0000u);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        const long long o = tk.tb[t] + (long long)u * 32;
+        const int4 x0 = ldx16(P.xq + o), x1 = ldx16(P.xq + o + 16);
+        const int4 y0 = ldx16(P.xq2 + o), y1 = ldx16(P.xq2 + o + 16);
+        const long long g = (tk.tb[t] >> 5) + u;
+        const float dd = __ldg(P.xd + g), ss = __ldg(P.xs + g);
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            int s = dp4(w[r][0], x0.x, 0); s = dp4(w[r][1], x0.y, s); s = dp4(w[r][2], x0.z, s); s = dp4(w[r][3], x0.w, s);
+            s = dp4(w[r][4], x1.x, s); s = dp4(w[r][5], x1.y, s); s = dp4(w[r][6], x1.z, s); s = dp4(w[r][7], x1.w, s);
+            int v = dp4(w[r][0], y0.x, 0); v = dp4(w[r][1], y0.y, v); v = dp4(w[r][2], y0.z, v); v = dp4(w[r][3], y0.w, v);
+            v = dp4(w[r][4], y1.x, v); v = dp4(w[r][5], y1.y, v); v = dp4(w[r][6], y1.z, v); v = dp4(w[r][7], y1.w, v);
+            if constexpr (SUMS) {
+                const long long base = (long long)row0 * (P.n_in / 32) + u;
+                atomicAdd(P.s + base, s);
+                atomicAdd(P.s2 + base, v);
+            } else {
+                acc[r][t] += d[r] * (dd * (float(s) + float(v) * kInv254) - ss);
+            }
+        }
+    }
+}
+
 // ---- Q8_0: 34 B = d (f16), int8[32] (quant.py:46-50).  Lane q takes block 8*sb + q.
 template <int T, int RW, bool SUMS>
 __device__ __forceinline__ void lane_q8_0(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
@@ -1077,6 +1230,8 @@ __global__ void __launch_bounds__(256) mv_kernel(const MvParams P) {
             else if constexpr (iq2x_format(FMT)) lane_iq2x<T, RW, SUMS, FMT>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (FMT == F_Q2_K) lane_q2k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else if constexpr (FMT == F_TQ1_0) lane_tq1<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+            else if constexpr (iq1_format(FMT)) lane_iq1<T, RW, SUMS, FMT>(rows, sb, q, P, tk, acc, row0);
+            else if constexpr (FMT == F_PTQ1_0) lane_ptq1<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
             else lane_iq2xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, grid);
         }
         if constexpr (!SUMS) {

@@ -160,6 +160,45 @@ __device__ __forceinline__ void unpack8(const uint8_t* b, int v0, float (&o)[8])
             const int j = j0 + i;
             o[i] = mul(float(kIq4nl[(ub(b + 8 + 16 * ib + (j & 15)) >> (4 * (j >> 4))) & 15]), dl);
         }
+    } else if constexpr (FMT == F_PTQ1_0) {           // quant.py:431-469: trits, d (trit - 1)
+        const float d = hf(b + 26);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int v = v0 + i;
+            int byte, n;
+            if (v < 80) { byte = v % 16; n = v / 16; }
+            else if (v < 120) { byte = 16 + (v - 80) % 8; n = (v - 80) / 8; }
+            else { byte = 24 + (v - 120) % 2; n = (v - 120) / 2; }
+            const int pw = n == 0 ? 1 : n == 1 ? 3 : n == 2 ? 9 : n == 3 ? 27 : 81;
+            const int t = int(((ub(b + byte) * uint32_t(pw)) & 255u) * 3u >> 8);
+            o[i] = mul(d, float(t) - 1.0f);
+        }
+    } else if constexpr (FMT == F_IQ1_S || FMT == F_IQ1_M) {   // quant.py:350-375: (d (2 s + 1)) (g + delta)
+        const int e = v0 / 8;
+        uint32_t idx, neg;
+        float dl;
+        if constexpr (FMT == F_IQ1_S) {
+            const uint32_t qh = u16le(b + 34 + 2 * (e / 4));
+            idx = ub(b + 2 + e) | (((qh >> (3 * (e % 4))) & 7u) << 8);
+            neg = qh >> 15;
+            dl = mul(hf(b), float(2 * int((qh >> 12) & 7u) + 1));
+        } else {
+            const uint32_t nib = (ub(b + 32 + e / 2) >> (4 * (e & 1))) & 15u;
+            idx = ub(b + e) | ((nib & 7u) << 8);
+            neg = nib >> 3;
+            const uint32_t s0 = u16le(b + 48), s1 = u16le(b + 50), s2 = u16le(b + 52), s3 = u16le(b + 54);
+            const uint32_t d16 = (s0 >> 12) | ((s1 >> 8) & 0xF0u) | ((s2 >> 4) & 0xF00u) | (s3 & 0xF000u);
+            const int g = e / 2;
+            const uint32_t sw = u16le(b + 48 + 2 * (g / 4));
+            dl = mul(h2f(d16), float(2 * int((sw >> (3 * (g % 4))) & 7u) + 1));
+        }
+        const uint32_t code = kIq1sCodes[idx];
+        const float delta = neg ? -0.125f : 0.125f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t f = (code >> (2 * i)) & 3u;
+            o[i] = mul(dl, __fadd_rn(float(f == 3u ? -1 : int(f)), delta));
+        }
     } else if constexpr (FMT == F_IQ2_XXS) {          // quant.py:235-245: value x (d (0.125 + 0.25 s))
         const int ib = v0 / 32, l = (v0 & 31) >> 3;
         const uint8_t* q = b + 2 + 8 * ib;

@@ -1,7 +1,7 @@
 """GGUF block formats of the quantized matvec path.
 
 GGML type ids and block geometry follow the GGUF format (the reference's table is
-ggufengine/gguf.py:64-77).  Only the twenty-three formats of the hot path have kernels here; asking for any
+ggufengine/gguf.py:64-77).  Only the twenty-six formats of the hot path have kernels here; asking for any
 other format raises instead of computing elsewhere.
 """
 from __future__ import annotations
@@ -31,10 +31,14 @@ FORMATS = {
     "TQ2_0": (256, 66),
     "TQ1_0": (256, 54),
     "MXFP4": (32, 17),
+    "IQ1_S": (256, 50),
+    "IQ1_M": (256, 56),
+    "PTQ1_0": (128, 28),
 }
 
 # name -> GGML type id
-TYPE_ID = {"Q4_0": 2, "Q4_1": 3, "Q5_0": 6, "Q5_1": 7, "IQ4_NL": 20, "Q1_0": 41, "Q2_0": 42, "PQ2_0": 142, "Q2_K": 10, "Q3_K": 11, "TQ1_0": 34, "IQ2_XS": 17, "IQ2_S": 22, "Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "IQ2_XXS": 16, "IQ3_XXS": 18, "IQ3_S": 21, "IQ4_XS": 23, "TQ2_0": 35, "MXFP4": 39}
+TYPE_ID = {"Q4_0": 2, "Q4_1": 3, "Q5_0": 6, "Q5_1": 7, "IQ4_NL": 20, "Q1_0": 41, "Q2_0": 42, "PQ2_0": 142, "Q2_K": 10, "Q3_K": 11, "TQ1_0": 34, "IQ2_XS": 17, "IQ2_S": 22, "Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "IQ2_XXS": 16, "IQ3_XXS": 18, "IQ3_S": 21, "IQ4_XS": 23, "TQ2_0": 35, "MXFP4": 39,
+           "IQ1_S": 19, "IQ1_M": 29, "PTQ1_0": 143}
 TYPE_NAME = {v: k for k, v in TYPE_ID.items()}
 
 # GGML types the reference knows but this path does not compute (for clear refusals)

@@ -16,7 +16,7 @@ meaning and return shapes, computed by this package's sm_100a kernels through th
   module, for instance); without one `schritt_moeglich` is False and the reference's layer takes its
   general path, whose projections still run here through PackedLinear / mv.
 
-Where the reference takes Q4_K and Q6_K only, these kernels take all twenty-three block formats of the path
+Where the reference takes Q4_K and Q6_K only, these kernels take all twenty-six block formats of the path
 (`FORMATE`: the classic, K-quant, IQ, MXFP4, ternary and 1-bit formats).  Everything runs on torch's current stream and is CUDA-graph
 safe (no host reads, no synchronisation).  Non-CUDA tensors or unsupported formats raise; nothing
 falls back to another implementation.
@@ -118,14 +118,14 @@ def _raw_x(x: torch.Tensor, n_in: int):
     return x.contiguous()
 
 
-def _fused(fmt: str, mats, x: torch.Tensor, n_in: int):
+def _fused(fmt: str, mats, x: torch.Tensor, n_in: int, outs=None):
     """One launch that quantises x itself; None where the staged kernel does not take the shape."""
     xr = _raw_x(x, n_in)
     if xr is None:
         return None
     _need_cuda(xr, f"mv {fmt}")
     dev = mats[0][0].device
-    ys = [torch.empty(n_out, dtype=torch.float32, device=dev) for _, n_out in mats]
+    ys = outs or [torch.empty(n_out, dtype=torch.float32, device=dev) for _, n_out in mats]
     n = len(mats)
     w_arr = (ctypes.c_void_p * n)(*[raw.data_ptr() for raw, _ in mats])
     n_arr = (ctypes.c_int * n)(*[n_out for _, n_out in mats])
@@ -138,21 +138,26 @@ def _fused(fmt: str, mats, x: torch.Tensor, n_in: int):
     return ys
 
 
-def mv(fmt: str, raw: torch.Tensor, x, n_out: int, n_in: int) -> torch.Tensor:
+def mv(fmt: str, raw: torch.Tensor, x, n_out: int, n_in: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """raw: (n_out, n_in) in block format on the GPU; x: (M, n_in) or (n_in,) bf16/float32, or an
     Eingang with M rows -> (M, n_out) float32, or (n_out,) for a vector.  One token given as a tensor
-    is quantised inside the matvec kernel (no separate Eingang)."""
+    is quantised inside the matvec kernel (no separate Eingang).  out: a contiguous float32 tensor of
+    M * n_out values to write into (this package's sharded layers gather from it in place)."""
     _check_raw(fmt, raw, n_out, n_in)
     ist_eingang = _ist_eingang(x)
+    M = (x.n if ist_eingang else x.numel()) // n_in
+    if out is not None and (out.dtype != torch.float32 or not out.is_contiguous() or out.numel() != M * n_out):
+        raise RuntimeError(f"mv: out must be a contiguous float32 tensor of {M * n_out} values")
     if not ist_eingang and x.numel() == n_in:
-        ys = _fused(fmt, [(raw, n_out)], x, n_in)
+        ys = _fused(fmt, [(raw, n_out)], x, n_in, None if out is None else [out.view(n_out)])
         if ys is not None:
-            return ys[0] if x.dim() == 1 else ys[0].view(1, n_out)
+            y = ys[0] if out is None else out
+            return y.view(n_out) if x.dim() == 1 else y.view(1, n_out)
     e = x if ist_eingang else Eingang(x)
     if e.n % n_in:
         raise RuntimeError(f"mv: input of {e.n} values is not a whole number of rows of {n_in}")
     M = e.n // n_in
-    y = torch.empty(M, n_out, dtype=torch.float32, device=raw.device)
+    y = torch.empty(M, n_out, dtype=torch.float32, device=raw.device) if out is None else out.view(M, n_out)
     _lib.check(_lib.load().qmv_mv(TYPE_ID[fmt], _lib.ptr(raw), n_out, n_in, *e.zeiger(), M, _lib.ptr(y),
                                   _lib.stream_ptr(raw.device)), f"qmv_mv {fmt}")
     vektor = M == 1 if ist_eingang else x.dim() == 1

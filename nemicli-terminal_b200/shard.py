@@ -76,7 +76,11 @@ class RowShardedLinear:
             raise ValueError(f"RowShardedLinear: rank {self.rank} needs rows [{self.lo}, {self.hi}) "
                              f"({self.n_local * row_bytes(fmt, n_in)} bytes), got {raw_local.numel()}")
         self.raw = raw_local.reshape(-1)
-        self._mv = matvec or (lambda raw, x: mmvq.mv(self.fmt, raw, x, self.n_local, self.n_in).reshape(-1, self.n_local))
+        self._custom_mv = matvec is not None
+        self._mv = matvec or self._mv_default
+
+    def _mv_default(self, raw: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+        return mmvq.mv(self.fmt, raw, x, self.n_local, self.n_in).reshape(-1, self.n_local)
 
     def local(self, x: torch.Tensor) -> torch.Tensor:
         """This rank's outputs: (M, n_in) -> (M, n_local) float32."""
@@ -86,22 +90,28 @@ class RowShardedLinear:
         return self._mv(self.raw, x2).reshape(x2.shape[0], self.n_local)
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        """(M, n_in) or (n_in,) -> (M, n_rows) or (n_rows,) float32 on every rank."""
+        """(M, n_in) or (n_in,) -> (M, n_rows) or (n_rows,) float32 on every rank.
+
+        The local product is written straight into this rank's block of the gather buffer
+        [rank][token][n_pad] and gathered in place, so nothing is copied around the collective; with equal
+        shards and one token the gathered buffer is the result itself."""
         x2 = x.reshape(-1, self.n_in)
         M = x2.shape[0]
-        y = self.local(x2)
         if self.world == 1:
-            out = y
+            out = self.local(x2)
+            return out.reshape(self.n_rows) if x.dim() == 1 else out
+        buf = torch.empty(self.world, M, self.n_pad, dtype=torch.float32, device=x2.device)
+        mine = buf[self.rank]
+        if self.n_local == self.n_pad and not self._custom_mv:
+            mmvq.mv(self.fmt, self.raw, x2 if M > 1 else x2[0], self.n_local, self.n_in, out=mine)
+        elif self.n_local > 0:
+            mine[:, :self.n_local] = self.local(x2)
+        dist.all_gather_into_tensor(buf.view(-1), mine.reshape(-1), group=self.group)
+        if self.n_rows == self.world * self.n_pad:                    # equal shards: no padding to drop
+            out = buf.permute(1, 0, 2).reshape(M, self.n_rows) if M > 1 else buf.view(1, self.n_rows)
         else:
-            send = torch.zeros(self.n_pad, M, dtype=torch.float32, device=y.device)
-            send[:self.n_local] = y.t()
-            recv = torch.empty(self.world * self.n_pad, M, dtype=torch.float32, device=y.device)
-            dist.all_gather_into_tensor(recv, send, group=self.group)
-            parts = []
-            for r in range(self.world):
-                lo, hi = shard_range(self.n_rows, self.world, r)
-                parts.append(recv[r * self.n_pad:r * self.n_pad + hi - lo])
-            out = torch.cat(parts, 0).t().contiguous()
+            sizes = [shard_range(self.n_rows, self.world, r) for r in range(self.world)]
+            out = torch.cat([buf[r, :, :hi - lo] for r, (lo, hi) in enumerate(sizes)], 1)
         return out.reshape(self.n_rows) if x.dim() == 1 else out
 
 
@@ -137,7 +147,7 @@ class ExpertShardedMoE:
                 raise ValueError("ExpertShardedMoE: gate/up/down shapes do not chain")
         self.gate, self.up, self.down = gate, up, down
         self._ffn = ffn or self._ffn_cuda
-        self.last_load: Optional[torch.Tensor] = None
+        self.last_sent: Optional[torch.Tensor] = None
         self._lo_tab = {}                       # device -> first expert of every rank
 
     def _ffn_cuda(self, ids: torch.Tensor, a: torch.Tensor) -> torch.Tensor:
@@ -152,18 +162,25 @@ class ExpertShardedMoE:
         dist.all_to_all_single(recv, send, group=self.group)      # equal splits: world blocks
         return recv
 
-    def __call__(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-        """x (L, dim) this rank's tokens, idx (L, k) expert ids, w (L, k) weights -> (L, dim) float32.
+    # Every rank sends every rank a block of C = L * k pair slots (the most pairs one owner can receive
+    # from it).  A slot is one row of dim + 4 floats: the pair's activation, then its expert id (local to
+    # the owner; -1 for an unused slot, -2 for an id outside [0, n_exp)) as an exact float.  One all-to-all
+    # carries the pairs to their owners, one brings the results back; all sizes are fixed and nothing is
+    # read on the host, so a whole call can be captured in a CUDA graph.
+    _ID = 4                                      # columns after the activation (the id, then padding)
 
-        Every rank sends every rank a buffer of C = L * k pair slots (the most pairs one owner can
-        receive from it): each pair's activation at its owner's block, in pair order, unused slots
-        with expert id -1.  All sizes are fixed, nothing is read on the host, so the call can be
-        captured in a CUDA graph.  Owners skip unused slots (the kernels write zeros for id -1)."""
+    def dispatch(self, x: torch.Tensor, idx: torch.Tensor):
+        """This rank's pairs to their owners -> (received slots (world * L * k, dim + 4) float32, slot of
+        every local pair in the send buffer (L * k,) int64)."""
         L, k = idx.shape
         dev = x.device
         P = L * k
         pair_e = idx.reshape(-1).to(torch.int64)
-        dest = owner_of(pair_e, self.n_exp, self.world)
+        # an id outside [0, n_exp) goes to rank 0 as local id -2: the owner's kernels refuse it (zero rows and
+        # the device status bit, as the single-GPU path does) and its weight adds nothing
+        valid = (pair_e >= 0) & (pair_e < self.n_exp)
+        dest = torch.where(valid, owner_of(pair_e.clamp(0, self.n_exp - 1), self.n_exp, self.world),
+                           torch.zeros_like(pair_e))
         onehot = (dest[:, None] == torch.arange(self.world, device=dev)[None, :]).to(torch.int64)
         pos = (onehot.cumsum(0) - 1).gather(1, dest[:, None]).squeeze(1)   # rank among pairs to that owner
         slot = dest * P + pos
@@ -172,16 +189,30 @@ class ExpertShardedMoE:
             lo_tab = torch.tensor([shard_range(self.n_exp, self.world, r)[0] for r in range(self.world)],
                                   dtype=torch.int64, device=dev)
             self._lo_tab[dev] = lo_tab
-        send_e = torch.full((self.world * P,), -1, dtype=torch.int64, device=dev)
-        send_e[slot] = pair_e - lo_tab[dest]
-        send_a = torch.zeros(self.world * P, self.dim, dtype=torch.float32, device=dev)
-        send_a[slot] = x.float()[torch.arange(P, device=dev) // k]
-        recv_e = self._a2a(send_e)
-        recv_a = self._a2a(send_a)
-        self.last_load = self._a2a(onehot.sum(0))                   # pairs received from each rank
-        y_recv = self._ffn(recv_e, recv_a).float()
-        y_recv = torch.where(recv_e[:, None] >= 0, y_recv, torch.zeros_like(y_recv))
-        y_back = self._a2a(y_recv.contiguous())
+        send = torch.zeros(self.world * P, self.dim + self._ID, dtype=torch.float32, device=dev)
+        send[:, self.dim] = -1.0
+        rows = torch.cat([x.float()[torch.arange(P, device=dev) // k],
+                          torch.where(valid, pair_e - lo_tab[dest], torch.full_like(pair_e, -2)).float()[:, None],
+                          torch.zeros(P, self._ID - 1, dtype=torch.float32, device=dev)], 1)
+        send[slot] = rows
+        self.last_sent = onehot.sum(0)          # pairs this rank sent to each owner (no collective)
+        return self._a2a(send), slot
+
+    def compute(self, recv: torch.Tensor) -> torch.Tensor:
+        """The owner's part: gate/up -> act -> down for every received slot -> (slots, dim) float32, zero rows
+        for unused slots."""
+        ids = recv[:, self.dim].to(torch.int64)
+        a = recv[:, :self.dim]
+        y = self._ffn(ids, a.contiguous()).float()
+        return torch.where(ids[:, None] >= 0, y, torch.zeros_like(y))
+
+    def __call__(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """x (L, dim) this rank's tokens, idx (L, k) expert ids, w (L, k) weights -> (L, dim) float32: two
+        all-to-alls (pairs out, results back) around the owners' expert FFNs, then the weighted sum in
+        slot order on the home rank."""
+        L, k = idx.shape
+        recv, slot = self.dispatch(x, idx)
+        y_back = self._a2a(self.compute(recv).contiguous())
         return combine(y_back[slot].view(L, k, self.dim), w)
 
 

@@ -122,6 +122,17 @@ def blocks(fmt: str, n_rows: int, n_in: int, seed: int = 0, device="cpu",
     elif fmt == "IQ3_S":                    # d = |N| * 0.01 / 16; grid indices, signs and 4-bit scales uniform
         d = _f16_bytes(_abs_normal(nb, 0.01 / 16, g, device))
         out = torch.cat([d, _bytes(nb, 108, g, device)], 1)
+    elif fmt == "IQ1_S":                    # d = |N| * 0.01 / 8; grid indices, 3-bit scales, delta signs uniform
+        out = torch.cat([_f16_bytes(_abs_normal(nb, 0.01 / 8, g, device)), _bytes(nb, 48, g, device)], 1)
+    elif fmt == "IQ1_M":                    # index bytes and nibbles, 3-bit scales uniform; d = |N| * 0.01 / 8 in
+        body = _bytes(nb, 48, g, device)     # the top nibbles of the four scale words
+        sc = torch.randint(0, 4096, (nb, 4), generator=g, device=device, dtype=torch.int32)
+        d = _abs_normal(nb, 0.01 / 8, g, device).to(torch.float16).view(torch.int16).to(torch.int32) & 0xFFFF
+        sc = sc | (((d.view(nb, 1) >> (4 * torch.arange(4, device=device, dtype=torch.int32))) & 0xF) << 12)
+        sc = (sc - ((sc >> 15) << 16)).to(torch.int16).contiguous().view(torch.uint8).view(nb, 8)
+        out = torch.cat([body, sc], 1)
+    elif fmt == "PTQ1_0":                   # trit bytes uniform; d = |N| * 0.01
+        out = torch.cat([_bytes(nb, 26, g, device), _f16_bytes(_abs_normal(nb, 0.01, g, device))], 1)
     elif fmt == "MXFP4":                    # scale 2^(e-128) with e uniform 118..124; nibbles uniform
         e = torch.randint(118, 125, (nb, 1), generator=g, device=device, dtype=torch.int32).to(torch.uint8)
         out = torch.cat([e, _bytes(nb, 16, g, device)], 1)

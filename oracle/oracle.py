@@ -22,16 +22,16 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libqmv_oracle.so")
 
-# GGML type ids (ggufengine/gguf.py:64-77) of the twenty-three in-scope formats
+# GGML type ids (ggufengine/gguf.py:64-77) of the twenty-six in-scope formats
 TYPES = {"Q4_0": 2, "Q8_0": 8, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "IQ2_XXS": 16, "IQ4_XS": 23, "TQ2_0": 35, "MXFP4": 39, "IQ3_S": 21, "IQ3_XXS": 18,
          "Q4_1": 3, "Q5_0": 6, "Q5_1": 7, "IQ4_NL": 20, "Q1_0": 41, "Q2_0": 42, "PQ2_0": 142,
-         "Q3_K": 11, "IQ2_XS": 17, "IQ2_S": 22, "Q2_K": 10, "TQ1_0": 34}
+         "Q3_K": 11, "IQ2_XS": 17, "IQ2_S": 22, "Q2_K": 10, "TQ1_0": 34, "IQ1_S": 19, "IQ1_M": 29, "PTQ1_0": 143}
 BLOCK = {"Q4_0": (32, 18), "Q8_0": (32, 34), "Q4_K": (256, 144), "Q5_K": (256, 176), "Q6_K": (256, 210),
          "IQ2_XXS": (256, 66), "IQ4_XS": (256, 136), "TQ2_0": (256, 66), "MXFP4": (32, 17),
          "IQ3_S": (256, 110), "IQ3_XXS": (256, 98), "Q4_1": (32, 20), "Q5_0": (32, 22), "Q5_1": (32, 24),
          "IQ4_NL": (32, 18), "Q1_0": (128, 18), "Q2_0": (64, 18), "PQ2_0": (128, 34),
          "Q3_K": (256, 110), "IQ2_XS": (256, 74), "IQ2_S": (256, 82),
-         "Q2_K": (256, 84), "TQ1_0": (256, 54)}
+         "Q2_K": (256, 84), "TQ1_0": (256, 54), "IQ1_S": (256, 50), "IQ1_M": (256, 56), "PTQ1_0": (128, 28)}
 
 _lock = threading.Lock()
 _lib = None
@@ -93,7 +93,8 @@ def dequant(fmt, raw: np.ndarray, n_values: int) -> np.ndarray:
 
 
 def unit_values(fmt) -> int:
-    return 16 if fmt_id(fmt) in (TYPES["Q6_K"], TYPES["Q3_K"], TYPES["IQ2_XS"], TYPES["IQ2_S"], TYPES["Q2_K"]) else 32
+    return 16 if fmt_id(fmt) in (TYPES["Q6_K"], TYPES["Q3_K"], TYPES["IQ2_XS"], TYPES["IQ2_S"], TYPES["Q2_K"],
+                                 TYPES["IQ1_M"]) else 32
 
 
 def block_sums(fmt, w: np.ndarray, n_out: int, n_in: int, xq: np.ndarray, xq2: np.ndarray):

@@ -57,7 +57,18 @@
 
 enum { T_Q4_0 = 2, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ2_XXS = 16, T_IQ4_XS = 23, T_TQ2_0 = 35, T_MXFP4 = 39,
        T_IQ3_S = 21, T_IQ3_XXS = 18, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_IQ4_NL = 20,
-       T_Q1_0 = 41, T_Q2_0 = 42, T_PQ2_0 = 142, T_Q3_K = 11, T_IQ2_XS = 17, T_IQ2_S = 22, T_Q2_K = 10, T_TQ1_0 = 34 };
+       T_Q1_0 = 41, T_Q2_0 = 42, T_PQ2_0 = 142, T_Q3_K = 11, T_IQ2_XS = 17, T_IQ2_S = 22, T_Q2_K = 10, T_TQ1_0 = 34,
+       T_IQ1_S = 19, T_IQ1_M = 29, T_PTQ1_0 = 143 };
+
+/* IQ1_S / IQ1_M codebook (ggufengine/iqtabellen.py:570, IQ1S_GRID): 2048 entries of eight values in
+   {-1, 0, +1}, two bits each (00 = 0, 01 = +1, 11 = -1) */
+static const uint16_t IQ1S_CODES[2048] = {
+#include "../nemicli-terminal_b200/csrc/iq1s_grid.inc"
+};
+static int iq1s_value(int idx, int j) {
+    const int f = (IQ1S_CODES[idx] >> (2 * j)) & 3;
+    return f == 3 ? -1 : f;
+}
 
 static const uint16_t IQ2XS_CODES[512] = {
 #include "../nemicli-terminal_b200/csrc/iq2xs_grid.inc"
@@ -148,6 +159,8 @@ int orc_block_values(int fmt) {
     case T_Q1_0: case T_PQ2_0: return 128;
     case T_Q4_K: case T_Q5_K: case T_Q6_K: case T_IQ2_XXS: case T_IQ3_XXS: case T_IQ3_S: case T_IQ4_XS:
     case T_TQ2_0: case T_Q3_K: case T_IQ2_XS: case T_IQ2_S: case T_Q2_K: case T_TQ1_0: return 256;
+    case T_IQ1_S: case T_IQ1_M: return 256;
+    case T_PTQ1_0: return 128;
     }
     return 0;
 }
@@ -176,13 +189,16 @@ int orc_block_bytes(int fmt) {
     case T_TQ1_0: return 54;
     case T_TQ2_0: return 66;
     case T_MXFP4: return 17;
+    case T_IQ1_S: return 50;
+    case T_IQ1_M: return 56;
+    case T_PTQ1_0: return 28;
     }
     return 0;
 }
 
 /* values per integer-sum unit */
 int orc_unit_values(int fmt) {
-    return fmt == T_Q6_K || fmt == T_Q3_K || fmt == T_IQ2_XS || fmt == T_IQ2_S || fmt == T_Q2_K ? 16 : 32;
+    return fmt == T_Q6_K || fmt == T_Q3_K || fmt == T_IQ2_XS || fmt == T_IQ2_S || fmt == T_Q2_K || fmt == T_IQ1_M ? 16 : 32;
 }
 /* TQ1_0 (54 B = qs[48], qh[4], d; quant.py:405-458): five trits per byte as a fixed-point fraction, trit n of
    byte v = ((v 3^n) mod 256) 3 >> 8.  Value j < 160: byte j % 32, n = j / 32; j < 240: byte 32 + (j - 160) % 16,
@@ -195,6 +211,46 @@ static int tq1_trit(const uint8_t* b, int v) {
     else { byte = 48 + (v - 240) % 4; n = (v - 240) / 4; }
     return (((b[byte] * pw[n]) & 255) * 3) >> 8;
 }
+/* PTQ1_0 (28 B = qs[24], qh[2], d; quant.py:431-469, trit_plan(24, 2)): values 0..79 are trit n = j / 16
+   of byte j % 16, 80..119 trit n = (j - 80) / 8 of byte 16 + (j - 80) % 8, 120..127 trit n = (j - 120) / 2 of
+   qh byte 24 + (j - 120) % 2.  The code is the trit (offset d xs). */
+static int ptq1_trit(const uint8_t* b, int v) {
+    static const int pw[5] = {1, 3, 9, 27, 81};
+    int byte, n;
+    if (v < 80) { byte = v % 16; n = v / 16; }
+    else if (v < 120) { byte = 16 + (v - 80) % 8; n = (v - 80) / 8; }
+    else { byte = 24 + (v - 120) % 2; n = (v - 120) / 2; }
+    return (((b[byte] * pw[n]) & 255) * 3) >> 8;
+}
+/* IQ1_S (50 B = d, qs[32], qh[8] u16; quant.py:350-360): sub-block ib's u16 qh holds three high index bits
+   per entry (bits 3l..3l+2), a 3-bit scale (bits 12..14) and the sign of its delta (bit 15).
+   IQ1_M (56 B = qs[32], qh[16] (a nibble per entry: three high index bits and the delta sign), scales
+   u16[4] (3-bit scale of each 16-value group in bits 0..11, d's four nibbles in bits 12..15);
+   quant.py:363-375).  Value = dl (grid + delta), dl = d (2 s + 1), delta = +-1/8: the integer code is
+   8 grid +- 1 with weight scale dl / 8. */
+static int iq1_entry(const uint8_t* b, int fmt, int e, int* neg) {
+    if (fmt == T_IQ1_S) {
+        const int qh = b[34 + 2 * (e / 4)] | (b[35 + 2 * (e / 4)] << 8);
+        *neg = (qh >> 15) & 1;
+        return b[2 + e] | (((qh >> (3 * (e % 4))) & 7) << 8);
+    }
+    const int nib = (b[32 + e / 2] >> (4 * (e & 1))) & 15;
+    *neg = nib >> 3;
+    return b[e] | ((nib & 7) << 8);
+}
+static float iq1m_d(const uint8_t* b) {
+    int sc[4];
+    for (int i = 0; i < 4; ++i) sc[i] = b[48 + 2 * i] | (b[49 + 2 * i] << 8);
+    const int d16 = (sc[0] >> 12) | ((sc[1] >> 8) & 0xF0) | ((sc[2] >> 4) & 0xF00) | (sc[3] & 0xF000);
+    const uint8_t h[2] = {(uint8_t)(d16 & 0xFF), (uint8_t)(d16 >> 8)};
+    return f16(h);
+}
+static int iq1_scale(const uint8_t* b, int fmt, int g) {   /* 3-bit scale: sub-block g (IQ1_S), 16-value group g (IQ1_M) */
+    if (fmt == T_IQ1_S) return ((b[34 + 2 * g] | (b[35 + 2 * g] << 8)) >> 12) & 7;
+    const int sc = b[48 + 2 * (g / 4)] | (b[49 + 2 * (g / 4)] << 8);
+    return (sc >> (3 * (g % 4))) & 7;
+}
+
 /* Q2_K (84 B = scales[16] (scale nibble, min nibble), qs[64], d, dmin; quant.py:284-292): code of value v */
 static int q2k_code(const uint8_t* b, int v) { return (b[16 + 32 * (v / 128) + v % 32] >> (2 * ((v % 128) / 32))) & 3; }
 
@@ -389,6 +445,33 @@ int orc_dequant(int fmt, const uint8_t* raw, long long n_values, float* out) {
             }
             break;
         }
+        case T_IQ1_S: {
+            const float d = f16(b);
+            for (int ib = 0; ib < 8; ++ib) {
+                const float dl = d * (float)(2 * iq1_scale(b, T_IQ1_S, ib) + 1);
+                for (int l = 0; l < 4; ++l) {
+                    int neg;
+                    const int idx = iq1_entry(b, T_IQ1_S, 4 * ib + l, &neg);
+                    for (int j = 0; j < 8; ++j) o[32 * ib + 8 * l + j] = dl * ((float)iq1s_value(idx, j) + (neg ? -0.125f : 0.125f));
+                }
+            }
+            break;
+        }
+        case T_IQ1_M: {
+            const float d = iq1m_d(b);
+            for (int e = 0; e < 32; ++e) {
+                const float dl = d * (float)(2 * iq1_scale(b, T_IQ1_M, e / 2) + 1);
+                int neg;
+                const int idx = iq1_entry(b, T_IQ1_M, e, &neg);
+                for (int j = 0; j < 8; ++j) o[8 * e + j] = ((float)iq1s_value(idx, j) + (neg ? -0.125f : 0.125f)) * dl;
+            }
+            break;
+        }
+        case T_PTQ1_0: {
+            const float d = f16(b + 26);
+            for (int j = 0; j < 128; ++j) o[j] = d * ((float)ptq1_trit(b, j) - 1.0f);
+            break;
+        }
         case T_Q2_0: case T_PQ2_0: {  /* d, then 2-bit codes: value j at bits 2 (j % 4) of byte j / 4 */
             const float d = f16(b);
             for (int j = 0; j < bv; ++j) o[j] = d * ((float)((b[2 + j / 4] >> (2 * (j % 4))) & 3) - 1.0f);
@@ -534,6 +617,12 @@ static int code_of(int fmt, const uint8_t* b, int v) {
     case T_Q3_K: return q3k_code(b, v);
     case T_Q2_K: return q2k_code(b, v);
     case T_TQ1_0: return tq1_trit(b, v);
+    case T_PTQ1_0: return ptq1_trit(b, v);
+    case T_IQ1_S: case T_IQ1_M: {
+        int neg;
+        const int idx = iq1_entry(b, fmt, v / 8, &neg);
+        return 8 * iq1s_value(idx, v % 8) + (neg ? -1 : 1);
+    }
     case T_IQ2_XS: case T_IQ2_S: return iq2xs_value(b, fmt, v);
     case T_Q4_K: { const int j = v >> 5, i = v & 31; return (b[16 + 32 * (j >> 1) + i] >> (4 * (j & 1))) & 15; }
     case T_Q5_K: {
@@ -592,6 +681,9 @@ static void unit_scales(int fmt, const uint8_t* b, int u, double* wscale, double
     case T_Q1_0: *wscale = 2.0 * f16(b); *offs = f16(b); return;
     case T_Q3_K: *wscale = (double)f16(b + 108) * (double)q3k_scale(b, u); *offs = 0.0; return;
     case T_TQ1_0: *wscale = f16(b + 52); *offs = f16(b + 52); return;
+    case T_PTQ1_0: *wscale = f16(b + 26); *offs = f16(b + 26); return;
+    case T_IQ1_S: *wscale = (double)f16(b) * (double)(2 * iq1_scale(b, T_IQ1_S, u) + 1) / 8.0; *offs = 0.0; return;
+    case T_IQ1_M: *wscale = (double)iq1m_d(b) * (double)(2 * iq1_scale(b, T_IQ1_M, u) + 1) / 8.0; *offs = 0.0; return;
     case T_Q2_K: *wscale = (double)f16(b + 80) * (double)(b[u] & 15); *offs = (double)f16(b + 82) * (double)(b[u] >> 4); return;
     case T_IQ2_XS: case T_IQ2_S:
         *wscale = (double)f16(b) * (0.125 + 0.25 * (double)iq2xs_scale(b, fmt, u));

@@ -57,6 +57,25 @@ def check_rows(rank, world):
     assert y1.shape == (n_rows,) and torch.equal(y1, y[0])
 
 
+def check_bad_ids(rank, world):
+    """Expert ids outside [0, n_exp) (-1, n_exp, a large one) add nothing to their token's sum."""
+    from nemicli_terminal_b200 import shard, synth
+    n_exp, dim, ff, L, k = 8, 64, 48, 4, 3
+    wg, wu, wd = _expert_weights(n_exp, dim, ff)
+    lo, hi = shard.shard_range(n_exp, world, rank)
+    x = synth.activations(L, dim, seed=40 + rank)
+    idx = torch.tensor([[0, -1, 7], [n_exp, 3, 5], [2, 6, 1000], [-1, n_exp, 4]])
+    w = torch.rand(L, k, generator=torch.Generator().manual_seed(41 + rank))
+
+    def ffn(local_ids, a):
+        return _ffn_ref(wg, wu, wd, torch.where(local_ids >= 0, local_ids + lo, local_ids), a)
+
+    y = shard.ExpertShardedMoE(None, None, None, n_exp, dim, ffn=ffn)(x, idx, w)
+    ok = (idx >= 0) & (idx < n_exp)
+    pairs = _ffn_ref(wg, wu, wd, torch.where(ok, idx, -1).reshape(-1), x.repeat_interleave(k, 0)).view(L, k, dim)
+    assert torch.equal(y, shard.combine(pairs, w)), "refused expert ids changed the result"
+
+
 def check_experts(rank, world, skew):
     from nemicli_terminal_b200 import moe, shard, synth
     n_exp, dim, ff, L, k = 8, 64, 48, 5, 2
@@ -76,9 +95,9 @@ def check_experts(rank, world, skew):
     pairs = _ffn_ref(wg, wu, wd, idx.reshape(-1), x.repeat_interleave(k, 0)).view(L, k, dim)
     ref = shard.combine(pairs, w)
     assert torch.equal(y, ref), f"expert shard differs by {float((y - ref).abs().max())}"
-    if skew:                                     # pairs received from each rank: all land on rank 0
-        got = moe_layer.last_load.tolist()
-        assert got == ([L * k] * world if rank == 0 else [0] * world), got
+    if skew:                                     # pairs sent to each owner: all go to rank 0
+        got = moe_layer.last_sent.tolist()
+        assert got == [L * k] + [0] * (world - 1), got
 
 
 def worker(rank, world, port, result_dir):
@@ -91,6 +110,7 @@ def worker(rank, world, port, result_dir):
         check_rows(rank, world)
         check_experts(rank, world, skew=False)
         check_experts(rank, world, skew=True)
+        check_bad_ids(rank, world)
         dist.barrier()
     except Exception:                                                  # reported to the parent test
         status = traceback.format_exc()

@@ -27,7 +27,10 @@ tests/test_gguf_iq.py:81-101, zufallsbloecke).  Extra cases pin the corners:
 * IQ2_XS / IQ2_S blocks whose codebook indices run through all 512 / 1024 entries, with every sign
   pattern and every 4-bit scale,
 * Q2_K blocks with every scale/min byte,
-* TQ1_0 blocks with every byte value in every trit position.
+* TQ1_0 blocks with every byte value in every trit position,
+* IQ1_S / IQ1_M blocks whose grid indices run through all 2048 codebook entries, with every 3-bit scale
+  and both delta signs,
+* PTQ1_0 blocks with every byte value in every qs and qh position.
 
 Formats added later are generated after the earlier cases, so the earlier arrays stay as they were.
 """
@@ -51,17 +54,25 @@ LATER8 = {"Q3_K": (11, 256, 110)}
 LATER9 = {"IQ2_XS": (17, 256, 74), "IQ2_S": (22, 256, 82)}
 LATER10 = {"Q2_K": (10, 256, 84)}
 LATER11 = {"TQ1_0": (34, 256, 54)}
+LATER12 = {"IQ1_S": (19, 256, 50), "IQ1_M": (29, 256, 56), "PTQ1_0": (143, 128, 28)}
 SCALE_OFFSETS = {"Q4_0": (0,), "Q8_0": (0,), "Q4_K": (0, 2), "Q6_K": (208,), "IQ2_XXS": (0,), "TQ2_0": (64,),
                  "Q5_K": (0, 2), "IQ4_XS": (0,), "MXFP4": (), "IQ3_S": (0,), "IQ3_XXS": (0,),
                  "Q4_1": (0, 2), "Q5_0": (0,), "Q5_1": (0, 2), "IQ4_NL": (0,), "Q1_0": (0,), "Q2_0": (0,),
-                 "PQ2_0": (0,), "Q3_K": (108,), "IQ2_XS": (0,), "IQ2_S": (0,), "Q2_K": (80, 82), "TQ1_0": (52,)}
+                 "PQ2_0": (0,), "Q3_K": (108,), "IQ2_XS": (0,), "IQ2_S": (0,), "Q2_K": (80, 82), "TQ1_0": (52,),
+                 "IQ1_S": (0,), "IQ1_M": (), "PTQ1_0": (26,)}
 ROWS, COLS = 3, 512          # a (3, 512) matrix per format
 
 
 def random_blocks(name: str, n_blocks: int, rng: np.random.Generator) -> np.ndarray:
     _, _, size = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4, **LATER5, **LATER6, **LATER7, **LATER8,
-                  **LATER9, **LATER10, **LATER11}[name]
+                  **LATER9, **LATER10, **LATER11, **LATER12}[name]
     raw = rng.integers(0, 256, (n_blocks, size), dtype=np.uint8)
+    if name == "IQ1_M":                                 # d's four nibbles in the top bits of the scale words
+        d = (rng.random(n_blocks) * 0.01 + 0.001).astype(np.float16).view(np.uint16).astype(np.uint32)
+        sc = raw[:, 48:56].copy().view(np.uint16).astype(np.uint32) & 0x0FFF
+        for i in range(4):
+            sc[:, i] |= ((d >> (4 * i)) & 0xF) << 12
+        raw[:, 48:56] = sc.astype(np.uint16).view(np.uint8).reshape(n_blocks, 8)
     if name == "MXFP4":
         raw[:, 0] = rng.integers(118, 125, n_blocks)       # scale exponents 2^-10 .. 2^-4
     for o in SCALE_OFFSETS[name]:
@@ -173,7 +184,7 @@ def main(ref_root: str) -> None:
 
     def add(key: str, name: str, raw: np.ndarray, rows: int, cols: int) -> None:
         t, bv, bb = {**FORMATS, **LATER, **LATER2, **LATER3, **LATER4, **LATER5, **LATER6, **LATER7, **LATER8,
-                     **LATER9, **LATER10, **LATER11}[name]
+                     **LATER9, **LATER10, **LATER11, **LATER12}[name]
         flat = np.ascontiguousarray(raw.reshape(-1))
         assert flat.size == rows * cols // bv * bb
         deq = dequantize(torch.from_numpy(flat.copy()), t, rows * cols, torch.float32).numpy()
@@ -254,6 +265,32 @@ def main(ref_root: str) -> None:
     vals = np.arange(6 * 52, dtype=np.uint32) % 256
     raw[:, :52] = vals.reshape(6, 52)
     add("TQ1_0_cover", "TQ1_0", raw, 6, 256)
+    for name, (_, bv, _) in LATER12.items():
+        add(name, name, random_blocks(name, ROWS * COLS // bv, rng), ROWS, COLS)
+    raw = random_blocks("IQ1_S", 64, rng)          # entry k at slot k; sub-block j: scale j % 8, sign (j // 8) % 2
+    for blk in range(64):
+        for ib in range(8):
+            idx = [32 * blk + 4 * ib + l for l in range(4)]
+            raw[blk, 2 + 4 * ib:6 + 4 * ib] = [i & 0xFF for i in idx]
+            j = 8 * blk + ib
+            qh = sum((i >> 8) << (3 * l) for l, i in enumerate(idx)) | ((j % 8) << 12) | (((j // 8) % 2) << 15)
+            raw[blk, 34 + 2 * ib:36 + 2 * ib] = [qh & 0xFF, qh >> 8]
+    add("IQ1_S_cover", "IQ1_S", raw, 64, 256)
+    raw = random_blocks("IQ1_M", 64, rng)          # entry k at slot k, delta sign k % 2, group scale (blk + g) % 8
+    for blk in range(64):
+        idx = [32 * blk + e for e in range(32)]
+        raw[blk, :32] = [i & 0xFF for i in idx]
+        nib = [(i >> 8) | ((e % 2) << 3) for e, i in enumerate(idx)]
+        raw[blk, 32:48] = [nib[2 * i] | (nib[2 * i + 1] << 4) for i in range(16)]
+        sc = raw[blk, 48:56].copy().view(np.uint16).astype(np.uint32) & 0xF000
+        for g in range(16):
+            sc[g // 4] |= ((blk + g) % 8) << (3 * (g % 4))
+        raw[blk, 48:56] = sc.astype(np.uint16).view(np.uint8)
+    add("IQ1_M_cover", "IQ1_M", raw, 64, 256)
+    raw = random_blocks("PTQ1_0", 128, rng)        # qs: byte values cycling through 0..255; qh: every value
+    raw[:, :24] = (np.arange(128 * 24, dtype=np.uint32) % 256).reshape(128, 24)
+    raw[:, 24:26] = np.arange(256, dtype=np.uint32).reshape(128, 2)
+    add("PTQ1_0_cover", "PTQ1_0", raw, 16, 1024)
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "dequant_golden.npz")
     np.savez_compressed(path, **out)
     print(f"wrote {path}: {len(out)} arrays")

@@ -1,9 +1,15 @@
 """qmv_chain_noalloc (grid-barrier counters in a fixed device array, nothing allocated by the call)
 against qmv_chain with a caller-provided workspace, through the C ABI.
 
-Collected last on purpose: it must pass on a fresh process (the first call looks the array up) and
-after every other GPU test has run in the same process."""
+Collected last on purpose, so that a run stopping at the first failure has run every other test first.
+The first call in a process looks the array's address up; that path is checked in a fresh subprocess,
+and the in-process test checks the calls after every other GPU test has run.  The device's free memory
+is the same before and after a call: nothing is allocated."""
 import ctypes
+import os
+import subprocess
+import sys
+import textwrap
 
 import pytest
 import torch
@@ -56,6 +62,10 @@ def test_noalloc_chain_matches_workspace_chain_on_two_calls(cuda):
         for a, b in zip(outs, ref):
             assert torch.equal(a, b)
     assert _lib.device_status(clear=True, device=cuda) == 0      # no barrier timed out
+    free0 = torch.cuda.mem_get_info(cuda)[0]
+    assert L.qmv_chain_noalloc(ch.arr, len(ch.stages), stream) == 0
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info(cuda)[0] == free0                # the call allocated nothing
 
 
 def test_noalloc_chain_refuses_more_stages_than_its_counters(cuda):
@@ -66,3 +76,31 @@ def test_noalloc_chain_refuses_more_stages_than_its_counters(cuda):
     assert b"no-allocation" in L.qmv_status_string(rc)
     assert L.qmv_chain_noalloc(None, 4, _lib.stream_ptr(cuda)) != 0
     assert L.qmv_chain_noalloc(big, 0, _lib.stream_ptr(cuda)) != 0
+
+
+_FRESH = textwrap.dedent("""
+    import sys, torch
+    sys.path.insert(0, {root!r})
+    from nemicli_terminal_b200 import _lib, chain, synth
+    dev = torch.device("cuda", 0)
+    raw = synth.blocks("Q4_K", 4096, 4096, seed=3, device=dev)
+    x = synth.activations(1, 4096, seed=4, device=dev)[0].contiguous()
+    ch = chain.Chain([chain.Stage("Q4_K", [(raw, 4096)], 4096, chain.RAW, a=x, wait=False)])
+    L = _lib.load()
+    for _ in range(2):                    # the first call in this process looks the array up
+        ch.stages[0].ys[0].fill_(float("nan"))
+        rc = L.qmv_chain_noalloc(ch.arr, 1, _lib.stream_ptr(dev))
+        assert rc == 0, L.qmv_status_string(rc)
+        torch.cuda.synchronize()
+        got = ch.stages[0].ys[0].clone()
+        ch.run()
+        torch.cuda.synchronize()
+        assert torch.equal(got, ch.stages[0].ys[0])
+    print("fresh ok")
+""")
+
+
+def test_noalloc_first_call_in_a_fresh_process(cuda):
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", _FRESH.format(root=root)], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "fresh ok" in r.stdout, r.stderr[-3000:]
