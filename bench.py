@@ -300,6 +300,14 @@ def sharded_suite(world: int, rank: int, dist, device, steps: int, warmup: int) 
         t_full = max_over_ranks(time_graph(g_full, steps, warmup, dist) / (steps * n_rot), dist, device)
         t_cmp = max_over_ranks(time_graph(g_cmp, steps, warmup, dist) / (steps * n_rot), dist, device)
         del g_full, g_cmp
+        single = {}
+        if world == 1:
+            # the unsharded layer: the grouped kernels (3 launches) and the per-(token, slot) expert matvecs
+            per_slot = moe.MoeFFN(*full_ex, act=lambda t: torch.nn.functional.silu(t))
+            for name, fn in (("grouped_us", ref_layer), ("per_slot_us", per_slot)):
+                g1, _ = capture(lambda: [fn(x, ix, w) for x, (ix, w) in zip(xs, routes)])
+                single[name] = time_graph(g1, steps, warmup, dist) / (steps * n_rot) * 1e6
+                del g1
         # load: pairs each owner receives (all ranks' routings), and the experts this rank's owner touches
         sent = torch.stack([torch.bincount(shard.owner_of(ix.reshape(-1), MOE_EXPERTS, world), minlength=world)
                             for ix, _ in routes]).sum(0).to(device)
@@ -315,7 +323,9 @@ def sharded_suite(world: int, rank: int, dist, device, steps: int, warmup: int) 
             "us_per_call": t_full * 1e6, "compute_only_us": t_cmp * 1e6, "exchange_us": (t_full - t_cmp) * 1e6,
             "pairs_per_owner": per_rank, "imbalance_max_over_mean": max(per_rank) / mean if mean else 1.0,
             "parity_max_rel": par, "parity": "ok" if par < 1e-5 else "FAIL",
-            "touched_expert_gbs_rank0_tokens": uniq * per_expert / t_full / 1e9}
+            "touched_expert_gbs_rank0_tokens": uniq * per_expert / t_full / 1e9, **single}
+        if single:
+            out["moe"][f"batch {B}"]["grouped_touched_gbs"] = uniq * per_expert / (single["grouped_us"] * 1e-6) / 1e9
     del blobs, full_ex, loc_ex, layer, ref_layer
     torch.cuda.empty_cache()
     return out

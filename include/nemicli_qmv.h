@@ -83,6 +83,27 @@ int qmv_mv_experts(int ggml_type, const void* raw, long long per_expert, long lo
                    int k, const int8_t* xq, const int8_t* xq2, const float* xd, const float* xs,
                    int x_group, float* y, int n_out, int n_in, void* stream);
 
+/* Bytes of the workspace qmv_moe_ffn needs for n_tok tokens of k slots (0 for an invalid shape). */
+int64_t qmv_moe_workspace_bytes(int n_tok, int k, int dim, int ff);
+
+/* Whole mixture-of-experts FFN of n_tok tokens with k slots each (n_tok * k at most 1024, n_exp at most
+ * 1024) in three launches:
+ *     out[t][:] = sum_j wts[t][j] * down_e(silu(gate_e x_t) * up_e x_t),   e = ids[t][j]
+ * x: n_tok rows of dim values, x_stride values apart (fp32 if x_is_f32, else bf16), quantised once;
+ * gate and up share one format (n_exp experts of gate_up_per_expert bytes, ff rows of dim values);
+ * down has its own (dim rows of ff values).  Every expert the call touches is read once whatever
+ * number of tokens chose it; silu and the product are formed and quantised in the gate/up kernel, and
+ * the weighted sum over the slots (in slot order) in the down kernel, which writes out (n_tok x dim
+ * fp32).  Ids: -1 marks an unused slot (adds nothing); other ids outside [0, n_exp) add nothing and
+ * set QMV_DEV_BAD_ADDRESS.  dim and ff multiples of 32 and of their formats' block; workspace 256-byte
+ * aligned, qmv_moe_workspace_bytes long.  Replaces: ggufengine/models/moe.py:264-321
+ * (Experten.__call__ over PackedExperts with the SiLU gate, models/common.py:462-475) and its
+ * cudakern.py:756-774 expert matvecs. */
+int qmv_moe_ffn(int gate_up_type, const void* gate, const void* up, long long gate_up_per_expert, int down_type,
+                const void* down, long long down_per_expert, long long n_exp, const long long* ids, const float* wts,
+                int n_tok, int k, const void* x, int x_is_f32, long long x_stride, int dim, int ff, void* workspace,
+                float* out, void* stream);
+
 /* Several matrices reading the same single-token input in one launch (q/k/v, gate/up): for j < n_jobs
  * (at most 4), y[j][r] = W_j[r, :] . x.  w, n_out, y: host arrays of n_jobs entries (device pointers).
  * Replaces: the separate mmvq.mv calls the reference makes for matrices sharing an Eingang
@@ -190,9 +211,12 @@ int64_t qmv_chain_workspace_bytes(void);
 #define QMV_CHAIN_NOALLOC_MAX_STAGES 128
 int qmv_chain_noalloc(const qmv_stage* stages, int n_stages, void* stream);
 
+/* Values per unit of qmv_block_sums for a format (16 or 32; 0 for an unknown format). */
+int qmv_unit_values(int ggml_type);
+
 /* Test hook: the int32 sums of one token per (row, unit), unit = the values sharing one weight scale
- * and one activation scale (16 for Q6_K, else 32): s = sum code * xq, s2 = sum code * xq2, from the
- * same device code as qmv_mv.  s, s2: int32[n_out][n_in / unit], overwritten.
+ * and one activation scale (qmv_unit_values): s = sum code * xq, s2 = sum code * xq2, from the same
+ * device code as qmv_mv.  s, s2: int32[n_out][n_in / unit], overwritten.
  * Replaces: nothing callable — it exposes the dp4a sums of ggufengine/mmvq.py:389-404 / :469-470. */
 int qmv_block_sums(int ggml_type, const uint8_t* w, int n_out, int n_in, const int8_t* xq, const int8_t* xq2,
                    int32_t* s, int32_t* s2, void* stream);

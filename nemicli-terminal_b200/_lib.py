@@ -24,6 +24,7 @@ _SIGNATURES = {
     "qmv_last_cuda_error": ([], I),
     "qmv_block_values": ([I], I),
     "qmv_block_bytes": ([I], I),
+    "qmv_unit_values": ([I], I),
     "qmv_supported": ([I, I], I),
     "qmv_quant_q8": ([P, I, P, P, P, P, LL, P], I),
     "qmv_mv": ([I, P, I, I, P, P, P, P, I, P, P], I),
@@ -39,6 +40,8 @@ _SIGNATURES = {
     "qmv_norm_q8": ([P, P, ctypes.c_float, P, P, ctypes.c_float, P, P, P, P, P, I, P], I),
     "qmv_act_q8": ([P, P, I, P, P, P, P, P, I, P], I),
     "qmv_unpack": ([I, P, LL, P, I, P], I),
+    "qmv_moe_workspace_bytes": ([I, I, I, I], LL),
+    "qmv_moe_ffn": ([I, P, P, LL, I, P, LL, LL, P, P, I, I, P, I, LL, I, I, P, P, P], I),
 }
 
 ABI_VERSION = 2

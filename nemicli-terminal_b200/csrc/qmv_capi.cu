@@ -8,6 +8,7 @@
 #include <type_traits>
 
 #include "qmv_host.cuh"
+#include "qmv_moe.cuh"
 #include "../../include/nemicli_qmv.h"
 
 using namespace qmv;
@@ -222,6 +223,8 @@ int qmv_last_cuda_error(void) { return g_last_cuda_error; }
 int qmv_block_values(int ggml_type) { return known_format(ggml_type) ? block_values(ggml_type) : 0; }
 int qmv_block_bytes(int ggml_type) { return known_format(ggml_type) ? block_bytes(ggml_type) : 0; }
 
+int qmv_unit_values(int ggml_type) { return known_format(ggml_type) ? unit_values(ggml_type) : 0; }
+
 int qmv_supported(int ggml_type, int n_in) {
     return known_format(ggml_type) && n_in > 0 && n_in % block_values(ggml_type) == 0;
 }
@@ -405,6 +408,102 @@ int qmv_mv_x(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_ou
                   nullptr, nullptr, static_cast<cudaStream_t>(stream), &st))
         return st;
     return ST_BAD_SHAPE;        // the shape needs the fallback kernel: quantise with qmv_quant_q8, then qmv_mv
+}
+
+// workspace of qmv_moe_ffn: xq, xq2 (L dim bytes each), xd, xs (L dim / 32 floats each), aq, aq2, ad, as
+// (the same for L k rows of ff), gs, us (L k rows of ff floats each), y (L k rows of dim floats), then
+// the counters: one per (touched expert, 32-row group of ff), one per 4 rows of dim
+namespace {
+struct MoeWs {
+    long long xq, xq2, xd, xs, aq, aq2, ad, as, gs, us, y, counters, n_gu, n_counters, total;
+};
+MoeWs moe_ws(int n_tok, int k, int dim, int ff, long long n_exp) {
+    auto part = [](long long b) { return (b + 255) / 256 * 256; };
+    const long long nx = (long long)n_tok * dim, na = (long long)n_tok * k * ff;
+    MoeWs w{};
+    long long o = 0;
+    w.xq = o; o += part(nx);
+    w.xq2 = o; o += part(nx);
+    w.xd = o; o += part(nx / 8);
+    w.xs = o; o += part(nx / 8);
+    w.aq = o; o += part(na);
+    w.aq2 = o; o += part(na);
+    w.ad = o; o += part(na / 8);
+    w.as = o; o += part(na / 8);
+    w.gs = o; o += part(na * 4);
+    w.us = o; o += part(na * 4);
+    w.y = o; o += part((long long)n_tok * k * dim * 4);
+    w.n_gu = std::min<long long>((long long)n_tok * k, n_exp) * (ff / 32);
+    w.n_counters = w.n_gu + dim / kMoeRW;
+    w.counters = o; o += part(w.n_counters * 4);
+    w.total = o;
+    return w;
+}
+}  // namespace
+
+int64_t qmv_moe_workspace_bytes(int n_tok, int k, int dim, int ff) {
+    if (n_tok <= 0 || k <= 0 || dim <= 0 || ff <= 0 || dim % 32 || ff % 32) return 0;
+    return moe_ws(n_tok, k, dim, ff, kMoeMaxExperts).total;
+}
+
+int qmv_moe_ffn(int gate_up_type, const void* gate, const void* up, long long gate_up_per_expert, int down_type,
+                const void* down, long long down_per_expert, long long n_exp, const long long* ids, const float* wts,
+                int n_tok, int k, const void* x, int x_is_f32, long long x_stride, int dim, int ff, void* workspace,
+                float* out, void* stream) {
+    if (!known_format(gate_up_type) || !known_format(down_type)) return ST_BAD_FORMAT;
+    if (!gate || !up || !down || !ids || !wts || !x || !workspace || !out) return ST_NULL;
+    if (n_tok <= 0 || k <= 0 || (long long)n_tok * k > kMoeMaxPairs) return ST_BAD_TOKENS;
+    if (n_exp <= 0 || n_exp > kMoeMaxExperts || dim <= 0 || ff <= 0 || x_stride < dim ||
+        dim % block_values(gate_up_type) || ff % block_values(down_type) || dim % 32 || ff % 32)
+        return ST_BAD_SHAPE;
+    const long long gu_bytes = (long long)ff * (dim / block_values(gate_up_type)) * block_bytes(gate_up_type);
+    const long long d_bytes = (long long)dim * (ff / block_values(down_type)) * block_bytes(down_type);
+    if (gate_up_per_expert < gu_bytes || down_per_expert < d_bytes) return ST_BAD_SHAPE;
+    if (!aligned(gate, weight_align(gate_up_type)) || !aligned(up, weight_align(gate_up_type)) ||
+        !aligned(down, weight_align(down_type)) || gate_up_per_expert % weight_align(gate_up_type) ||
+        down_per_expert % weight_align(down_type) || !aligned(workspace, 256) || !aligned(out, 4) ||
+        !aligned(x, x_is_f32 ? 4 : 2))
+        return ST_BAD_ALIGN;
+    const long long nx = (long long)n_tok * dim;
+    const MoeWs W = moe_ws(n_tok, k, dim, ff, n_exp);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    MoeParams P{};
+    P.gate = static_cast<const uint8_t*>(gate);
+    P.up = static_cast<const uint8_t*>(up);
+    P.down = static_cast<const uint8_t*>(down);
+    P.gate_per = P.up_per = gate_up_per_expert;
+    P.down_per = down_per_expert;
+    P.n_exp = n_exp;
+    P.ids = ids;
+    P.wts = wts;
+    P.L = n_tok; P.k = k; P.dim = dim; P.ff = ff;
+    int8_t* xq = reinterpret_cast<int8_t*>(ws + W.xq);
+    int8_t* xq2 = reinterpret_cast<int8_t*>(ws + W.xq2);
+    float* xd = reinterpret_cast<float*>(ws + W.xd);
+    float* xs = reinterpret_cast<float*>(ws + W.xs);
+    P.xq = xq; P.xq2 = xq2; P.xd = xd; P.xs = xs;
+    P.aq = reinterpret_cast<int8_t*>(ws + W.aq);
+    P.aq2 = reinterpret_cast<int8_t*>(ws + W.aq2);
+    P.ad = reinterpret_cast<float*>(ws + W.ad);
+    P.as = reinterpret_cast<float*>(ws + W.as);
+    P.gs = reinterpret_cast<float*>(ws + W.gs);
+    P.us = reinterpret_cast<float*>(ws + W.us);
+    P.y = reinterpret_cast<float*>(ws + W.y);
+    P.gu_done = reinterpret_cast<int*>(ws + W.counters);
+    P.d_done = P.gu_done + W.n_gu;
+    P.out = out;
+    P.status = device_status_ptr();
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    moe_quant_kernel<<<unsigned((nx + 255) / 256), 256, 0, st>>>(x, x_is_f32, x_stride, dim, nx, xq, xq2, xd, xs,
+                                                                 P.gu_done, int(W.n_counters));
+    int rc = launched();
+    if (rc) return rc;
+    const long long touched = std::min<long long>((long long)n_tok * k, n_exp);
+    const int grid_gu = int(std::min<long long>(touched * (ff / 32) * 16 / (kMoeThreads / 32) + 1, 1 << 20));
+    rc = by_format(gate_up_type, [&](auto c) { return launch_moe_fmt<decltype(c)::value>(0, P, grid_gu, st); });
+    if (rc) return rc;
+    const int grid_d = int(std::min<long long>(touched * (dim / kMoeRW) / (kMoeThreads / 32) + 1, 1 << 20));
+    return by_format(down_type, [&](auto c) { return launch_moe_fmt<decltype(c)::value>(1, P, grid_d, st); });
 }
 
 int qmv_set_pdl(int enabled) {

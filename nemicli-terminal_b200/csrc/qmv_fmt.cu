@@ -2,6 +2,7 @@
 // -DQMV_FMT_ID=<GGML type id> (the build does so for every format of formats.py), so the formats build in
 // parallel and a change to one kernel family does not rebuild the others.
 #include "qmv_host.cuh"
+#include "qmv_moe.cuh"
 
 #ifndef QMV_FMT_ID
 #error "compile with -DQMV_FMT_ID=<GGML type id>"
@@ -123,6 +124,22 @@ int launch_tma_fmt(int xf, bool sums, const TmaParams& P, const TmaPlan& pl, int
     return ST_BAD_SHAPE;
 }
 
+// grid: the work items (an upper bound); launched as min(items, resident CTAs), each CTA looping
+template <int FMT>
+int launch_moe_fmt(int stage, const MoeParams& P, int grid, cudaStream_t st) {
+    static int occ[2] = {0, 0};
+    auto kern = stage == 0 ? moe_gateup_kernel<FMT> : moe_down_kernel<FMT>;
+    if (occ[stage] == 0) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kMoeThreads, 0) != cudaSuccess || n < 1) n = 1;
+        occ[stage] = n;
+    }
+    grid = std::max(1, std::min(grid, occ[stage] * sm_count()));
+    kern<<<grid, kMoeThreads, 0, st>>>(P);
+    return launched();
+}
+
+template int launch_moe_fmt<QMV_FMT_ID>(int, const MoeParams&, int, cudaStream_t);
 template int launch_mv_fmt<QMV_FMT_ID>(const MvParams&, int, cudaStream_t);
 template int launch_sums_fmt<QMV_FMT_ID>(const MvParams&, cudaStream_t);
 template int launch_tma_fmt<QMV_FMT_ID>(int, bool, const TmaParams&, const TmaPlan&, int, cudaStream_t);

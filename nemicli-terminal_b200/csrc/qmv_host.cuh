@@ -44,6 +44,10 @@ template <int FMT> int launch_sums_fmt(const MvParams& P, cudaStream_t st);
 template <int FMT> int launch_tma_fmt(int xf, bool sums, const TmaParams& P, const TmaPlan& pl, int grid,
                                       cudaStream_t st);
 
+struct MoeParams;
+// grouped MoE kernels (qmv_moe.cuh): stage 0 gate/up (FMT = gate and up format), 1 down (FMT = down format)
+template <int FMT> int launch_moe_fmt(int stage, const MoeParams& P, int grid, cudaStream_t st);
+
 // ---- defined in qmv_mma.cu ----
 // few-token (2..8) tensor-core kernels; false when the shape or alignment does not qualify (then the
 // caller uses the fallback kernel), true with *status set otherwise

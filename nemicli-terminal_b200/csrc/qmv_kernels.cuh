@@ -1167,20 +1167,52 @@ __device__ __forceinline__ const uint8_t* slot_base(const MvParams& P, int slot)
     return base;
 }
 
+// codebook of the formats that keep one in shared memory (2 KB), loaded by the whole block
+template <int FMT>
+__host__ __device__ constexpr bool smem_grid_format() { return FMT == F_IQ2_XXS || FMT == F_IQ3_S || FMT == F_IQ3_XXS; }
+template <int FMT>
+__device__ __forceinline__ void load_grid(uint2* grid) {
+    if constexpr (FMT == F_IQ2_XXS) load_iq2xxs_grid(grid);
+    else if constexpr (FMT == F_IQ3_S) load_iq3s_grid(reinterpret_cast<uint32_t*>(grid));
+    else if constexpr (FMT == F_IQ3_XXS) load_iq3xxs_grid(reinterpret_cast<uint32_t*>(grid));
+}
+
+// One lane's part of 256-value piece sb of RW rows for T tokens (the lane layout above), any format.
+template <int FMT, int T, int RW, bool SUMS>
+__device__ __forceinline__ void lane_any(const uint8_t* const (&rows)[RW], int sb, int q, const MvParams& P,
+                                         const Tok<T>& tk, float (&acc)[RW][T], int row0, const uint2* grid) {
+    if constexpr (FMT == F_Q4_K) lane_q4k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+    else if constexpr (FMT == F_Q5_K) lane_q4k<T, RW, SUMS, true>(rows, sb, q, P, tk, acc, row0);
+    else if constexpr (FMT == F_Q6_K) lane_q6k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+    else if constexpr (FMT == F_Q4_0) lane_q4_0<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+    else if constexpr (FMT == F_Q8_0) lane_q8_0<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+    else if constexpr (FMT == F_TQ2_0) lane_tq2_0<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+    else if constexpr (FMT == F_IQ4_XS) lane_iq4xs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+    else if constexpr (FMT == F_MXFP4) lane_mxfp4<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+    else if constexpr (FMT == F_IQ3_S)
+        lane_iq3s<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, reinterpret_cast<const uint32_t*>(grid));
+    else if constexpr (FMT == F_IQ3_XXS)
+        lane_iq3xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, reinterpret_cast<const uint32_t*>(grid));
+    else if constexpr (FMT == F_Q4_1 || FMT == F_Q5_0 || FMT == F_Q5_1 || FMT == F_IQ4_NL)
+        lane_b32<FMT, T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+    else if constexpr (bits_format(FMT)) lane_bits<T, RW, SUMS, FMT>(rows, sb, q, P, tk, acc, row0);
+    else if constexpr (FMT == F_Q3_K) lane_q3k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+    else if constexpr (iq2x_format(FMT)) lane_iq2x<T, RW, SUMS, FMT>(rows, sb, q, P, tk, acc, row0);
+    else if constexpr (FMT == F_Q2_K) lane_q2k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+    else if constexpr (FMT == F_TQ1_0) lane_tq1<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+    else if constexpr (iq1_format(FMT)) lane_iq1<T, RW, SUMS, FMT>(rows, sb, q, P, tk, acc, row0);
+    else if constexpr (FMT == F_PTQ1_0) lane_ptq1<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
+    else lane_iq2xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, grid);
+}
+
 // y[slot][t][row] = W_slot[row, :] . x(slot, t) for T tokens.  Each warp takes RW consecutive rows
 // of one slot at a time (grid-stride over all slots' row groups); SUMS instead adds the int32 unit
 // sums of one token into P.s / P.s2 (T = RW = 1).
 template <int FMT, int T, int RW, bool SUMS>
 __global__ void __launch_bounds__(256) mv_kernel(const MvParams P) {
-    __shared__ uint2 grid[FMT == F_IQ2_XXS || FMT == F_IQ3_S || FMT == F_IQ3_XXS ? 256 : 1];   // 2 KB: a codebook
-    if constexpr (FMT == F_IQ2_XXS) {
-        load_iq2xxs_grid(grid);
-        __syncthreads();
-    } else if constexpr (FMT == F_IQ3_S) {
-        load_iq3s_grid(reinterpret_cast<uint32_t*>(grid));
-        __syncthreads();
-    } else if constexpr (FMT == F_IQ3_XXS) {
-        load_iq3xxs_grid(reinterpret_cast<uint32_t*>(grid));
+    __shared__ uint2 grid[smem_grid_format<FMT>() ? 256 : 1];   // 2 KB: a codebook
+    if constexpr (smem_grid_format<FMT>()) {
+        load_grid<FMT>(grid);
         __syncthreads();
     }
     const int lane = threadIdx.x & 31, q = lane & 7, sb0 = lane >> 3;
@@ -1210,30 +1242,7 @@ __global__ void __launch_bounds__(256) mv_kernel(const MvParams P) {
         for (int r = 0; r < RW; ++r)
 #pragma unroll
             for (int t = 0; t < T; ++t) acc[r][t] = 0.f;
-        for (int sb = sb0; sb < n_sb; sb += 4) {
-            if constexpr (FMT == F_Q4_K) lane_q4k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
-            else if constexpr (FMT == F_Q5_K) lane_q4k<T, RW, SUMS, true>(rows, sb, q, P, tk, acc, row0);
-            else if constexpr (FMT == F_Q6_K) lane_q6k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
-            else if constexpr (FMT == F_Q4_0) lane_q4_0<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
-            else if constexpr (FMT == F_Q8_0) lane_q8_0<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
-            else if constexpr (FMT == F_TQ2_0) lane_tq2_0<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
-            else if constexpr (FMT == F_IQ4_XS) lane_iq4xs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
-            else if constexpr (FMT == F_MXFP4) lane_mxfp4<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
-            else if constexpr (FMT == F_IQ3_S)
-                lane_iq3s<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, reinterpret_cast<const uint32_t*>(grid));
-            else if constexpr (FMT == F_IQ3_XXS)
-                lane_iq3xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, reinterpret_cast<const uint32_t*>(grid));
-            else if constexpr (FMT == F_Q4_1 || FMT == F_Q5_0 || FMT == F_Q5_1 || FMT == F_IQ4_NL)
-                lane_b32<FMT, T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
-            else if constexpr (bits_format(FMT)) lane_bits<T, RW, SUMS, FMT>(rows, sb, q, P, tk, acc, row0);
-            else if constexpr (FMT == F_Q3_K) lane_q3k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
-            else if constexpr (iq2x_format(FMT)) lane_iq2x<T, RW, SUMS, FMT>(rows, sb, q, P, tk, acc, row0);
-            else if constexpr (FMT == F_Q2_K) lane_q2k<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
-            else if constexpr (FMT == F_TQ1_0) lane_tq1<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
-            else if constexpr (iq1_format(FMT)) lane_iq1<T, RW, SUMS, FMT>(rows, sb, q, P, tk, acc, row0);
-            else if constexpr (FMT == F_PTQ1_0) lane_ptq1<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0);
-            else lane_iq2xxs<T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, grid);
-        }
+        for (int sb = sb0; sb < n_sb; sb += 4) lane_any<FMT, T, RW, SUMS>(rows, sb, q, P, tk, acc, row0, grid);
         if constexpr (!SUMS) {
 #pragma unroll
             for (int r = 0; r < RW; ++r)

@@ -231,7 +231,7 @@ def mm(fmt: str, raw: torch.Tensor, x: torch.Tensor, n_out: int, n_in: int) -> t
 def block_sums(fmt: str, raw: torch.Tensor, e: Eingang, n_out: int, n_in: int):
     """Test hook: the int32 sums (code*xq, code*xq2) per row and unit of one token (include/nemicli_qmv.h)."""
     _check_raw(fmt, raw, n_out, n_in)
-    unit = 16 if fmt in ("Q6_K", "Q3_K", "IQ2_XS", "IQ2_S", "Q2_K") else 32
+    unit = _lib.load().qmv_unit_values(TYPE_ID[fmt])        # the kernel's own unit: the buffers fit its writes
     s = torch.empty(n_out, n_in // unit, dtype=torch.int32, device=raw.device)
     s2 = torch.empty_like(s)
     _lib.check(_lib.load().qmv_block_sums(TYPE_ID[fmt], _lib.ptr(raw), n_out, n_in, _lib.ptr(e.xq), _lib.ptr(e.xq2),

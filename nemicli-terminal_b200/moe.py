@@ -8,6 +8,12 @@ graph-safe paths of moe.Experten.__call__ (ggufengine/models/moe.py:264-288: one
 GRAPH_ZEILEN tokens with every (token, slot) pair on its own).  Each token's input is quantised once
 and read by all of its k slots (x_group = k); the down projection reads one activation row per slot.
 Nothing reads the choice on the host, so a whole call can be captured in a CUDA graph.
+
+With the default SiLU gate, experts resident on the device as contiguous tensors, gate and up in one
+format, at most MOE_MAX_PAIRS (token, slot) pairs and MOE_MAX_EXPERTS experts, the call is one grouped
+launch sequence (grouped_ffn, qmv_moe_ffn): quantise x; gate/up of every touched expert read once with
+silu(g) * u quantised in its epilogue; down of every touched expert read once with the weighted sum
+over slots in its epilogue.  Otherwise it runs expert matvecs per (token, slot) as above.
 """
 from __future__ import annotations
 
@@ -22,6 +28,43 @@ from .layers import PackedExperts
 from .mmvq import Eingang
 
 GRAPH_ZEILEN = 16
+MOE_MAX_PAIRS = 1024         # tokens x slots of one grouped call
+MOE_MAX_EXPERTS = 1024       # experts of one grouped call
+
+
+def grouped_ok(gate: PackedExperts, up: PackedExperts, down: PackedExperts, x: torch.Tensor, n_tok: int,
+               k: int) -> bool:
+    """True when grouped_ffn takes this call (SiLU gate assumed by the caller)."""
+    return (1 <= n_tok and n_tok * k <= MOE_MAX_PAIRS and gate.n_exp <= MOE_MAX_EXPERTS and gate.name == up.name
+            and all(ex.adressen is None and not ex.im_ram and _lib.on_gpu(ex.raw) for ex in (gate, up, down))
+            and gate.raw.shape[1] == up.raw.shape[1] and x.device == down.raw.device and x.dim() == 2
+            and x.stride(1) == 1 and gate.n_in % 32 == 0 and gate.n_out % 32 == 0)
+
+
+def grouped_ffn(gate: PackedExperts, up: PackedExperts, down: PackedExperts, x: torch.Tensor, idx: torch.Tensor,
+                w: torch.Tensor) -> torch.Tensor:
+    """sum_j w[t, j] * down_e(silu(gate_e x_t) * up_e x_t) in three launches (qmv_moe_ffn).  x (L, dim)
+    fp32 or bf16 with unit column stride (rows may be further apart), idx / w (L, k) -> (L, dim) float32.
+    Raises where grouped_ok is false."""
+    L, E = x.shape
+    k = idx.shape[1]
+    if not grouped_ok(gate, up, down, x, L, k):
+        raise ValueError("grouped_ffn: shape, placement or expert count not supported")
+    lib = _lib.load()
+    ids = idx.reshape(-1).to(device=x.device, dtype=torch.int64).contiguous()
+    wts = w.reshape(-1).to(device=x.device, dtype=torch.float32).contiguous()
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        x = x.float().contiguous()
+    n_ff = gate.n_out
+    nbytes = lib.qmv_moe_workspace_bytes(L, k, E, n_ff)
+    ws = torch.empty(nbytes + 256, dtype=torch.uint8, device=x.device)
+    off = (-ws.data_ptr()) % 256
+    out = torch.empty(L, E, dtype=torch.float32, device=x.device)
+    _lib.check(lib.qmv_moe_ffn(TYPE_ID[gate.name], _lib.ptr(gate.raw), _lib.ptr(up.raw), gate.raw.shape[1],
+                               TYPE_ID[down.name], _lib.ptr(down.raw), down.raw.shape[1], gate.n_exp, _lib.ptr(ids),
+                               _lib.ptr(wts), L, k, _lib.ptr(x), int(x.dtype == torch.float32), x.stride(0), E,
+                               n_ff, ws.data_ptr() + off, _lib.ptr(out), _lib.stream_ptr(x.device)), "qmv_moe_ffn")
+    return out
 
 
 def route(logits: torch.Tensor, k: int, normalize: bool = True, weights_scale: float = 1.0):
@@ -59,11 +102,23 @@ class MoeFFN:
         self.gate, self.up, self.down = gate, up, down
         self.act = act or F.silu
         self.n_exp = down.n_exp
+        self.grouped = act is None or act is F.silu
+
+    def _grouped_ok(self, x: torch.Tensor, L: int, k: int) -> bool:
+        return self.grouped and grouped_ok(self.gate, self.up, self.down, x, L, k)
+
+    def grouped_call(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """The grouped launch sequence (grouped_ffn); raises where it does not apply."""
+        if not self.grouped:
+            raise ValueError("MoeFFN.grouped_call: the grouped kernels compute the SiLU gate only")
+        return grouped_ffn(self.gate, self.up, self.down, x, idx, w)
 
     def __call__(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         """x (L, E) -> (L, E) float32; idx (L, k) expert ids, w (L, k) their weights."""
         L, E = x.shape
         k = idx.shape[1]
+        if self._grouped_ok(x, L, k):
+            return self.grouped_call(x, idx, w)
         ids = idx.reshape(-1).to(torch.int64).contiguous()
         ex = Eingang(x.float().contiguous())                        # L rows, one per token
         g = _experts_mv(self.gate, ids, ex, k)                      # (L*k, n_ff)

@@ -27,7 +27,7 @@ import torch
 import torch.distributed as dist
 import torch.nn.functional as F
 
-from . import mmvq
+from . import mmvq, moe
 from .formats import row_bytes
 from .layers import PackedExperts
 
@@ -127,9 +127,11 @@ class ExpertShardedMoE:
     """MoE FFN with the experts split over the ranks of `group`; tokens stay on their home rank.
 
     gate, up, down: this rank's experts (PackedExperts holding shard_range(n_exp, world, rank)).
-    ffn(local_ids, a) -> (P, E) float32: optional replacement of the local expert computation (the
-    default runs gate/up -> act -> down through the CUDA kernels, each pair on its own input); ids of
-    -1 mark unused slots, whose rows are ignored."""
+    ffn(local_ids, a) -> (P, E) float32: optional replacement of the local expert computation.  The
+    default with the SiLU gate is the grouped expert FFN (moe.grouped_ffn: every local expert read once
+    per call, one slot per received row); with another act, or beyond the grouped limits, gate/up ->
+    act -> down run through the expert matvecs, each pair on its own input.  Ids of -1 mark unused
+    slots, whose rows are ignored."""
 
     def __init__(self, gate: Optional[PackedExperts], up: Optional[PackedExperts], down: Optional[PackedExperts],
                  n_exp: int, dim: int, group=None, act: Optional[Callable] = None,
@@ -147,6 +149,8 @@ class ExpertShardedMoE:
                 raise ValueError("ExpertShardedMoE: gate/up/down shapes do not chain")
         self.gate, self.up, self.down = gate, up, down
         self._ffn = ffn or self._ffn_cuda
+        self._grouped = ffn is None and act is None
+        self._ones = {}                         # (device, slots) -> unit weights of the grouped owner call
         self.last_sent: Optional[torch.Tensor] = None
         self._lo_tab = {}                       # device -> first expert of every rank
 
@@ -203,6 +207,14 @@ class ExpertShardedMoE:
         for unused slots."""
         ids = recv[:, self.dim].to(torch.int64)
         a = recv[:, :self.dim]
+        if self._grouped and moe.grouped_ok(self.gate, self.up, self.down, a, a.shape[0], 1):
+            # one slot per received row, unit weight: the grouped kernels read each local expert once and
+            # leave unused and refused slots at zero
+            key = (a.device, a.shape[0])
+            ones = self._ones.get(key)
+            if ones is None:
+                ones = self._ones[key] = torch.ones(a.shape[0], 1, dtype=torch.float32, device=a.device)
+            return moe.grouped_ffn(self.gate, self.up, self.down, a, ids.view(-1, 1), ones)
         y = self._ffn(ids, a.contiguous()).float()
         return torch.where(ids[:, None] >= 0, y, torch.zeros_like(y))
 

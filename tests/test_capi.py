@@ -44,6 +44,9 @@ def test_block_geometry_matches_format_table(fmt):
     assert L.qmv_supported(TYPE_ID[fmt], bv * 3) == 1
     assert L.qmv_supported(TYPE_ID[fmt], bv * 3 + 16) == 0
     assert L.qmv_supported(TYPE_ID[fmt], 0) == 0
+    # the unit of the int32 sums (the buffers qmv_block_sums writes are sized from it)
+    from oracle import oracle as O
+    assert L.qmv_unit_values(TYPE_ID[fmt]) == O.unit_values(fmt)
 
 
 def test_unknown_formats_are_refused():
@@ -51,6 +54,7 @@ def test_unknown_formats_are_refused():
     for t in (0, 1, 9, 15, 24, 30, 144):          # F32, F16, Q8_1, Q8_K, I8, BF16 and an unassigned id
         assert L.qmv_supported(t, 4096) == 0
         assert L.qmv_block_values(t) == 0
+        assert L.qmv_unit_values(t) == 0
     st = L.qmv_mv(15, ctypes.c_void_p(16), 1, 256, ctypes.c_void_p(16), ctypes.c_void_p(16),
                   ctypes.c_void_p(16), ctypes.c_void_p(16), 1, ctypes.c_void_p(16), None)
     assert st == 1
@@ -74,3 +78,31 @@ def test_argument_checks_precede_any_launch():
     assert L.qmv_quant_q8(a, 1, a, a, a, a, 33, None) == 2
     assert L.qmv_quant_q8(None, 1, a, a, a, a, 32, None) == 6
     assert L.qmv_block_sums(Q4K, a, 4, 300, a, a, a, a, None) == 2
+
+
+def test_moe_argument_checks():
+    """qmv_moe_ffn refuses before any launch: null pointers, too many pairs or experts, shapes off the
+    block grid, experts smaller than their matrices, misaligned workspace."""
+    L = _lib.load()
+    a = ctypes.c_void_p(4096)
+    Q4K = TYPE_ID["Q4_K"]
+    per = 256 * 144                     # 256 rows of one Q4_K superblock
+
+    def call(**kw):
+        arg = dict(gt=Q4K, gate=a, up=a, gper=per, dt=Q4K, down=a, dper=per, n_exp=8, ids=a, wts=a, L=4, k=2,
+                   x=a, f32=1, stride=256, dim=256, ff=256, ws=a, out=a)
+        arg.update(kw)
+        return L.qmv_moe_ffn(arg["gt"], arg["gate"], arg["up"], arg["gper"], arg["dt"], arg["down"], arg["dper"],
+                             arg["n_exp"], arg["ids"], arg["wts"], arg["L"], arg["k"], arg["x"], arg["f32"],
+                             arg["stride"], arg["dim"], arg["ff"], arg["ws"], arg["out"], None)
+    assert call(gt=15) == 1
+    assert call(ids=None) == 6
+    assert call(L=513) == 4                                   # 1026 pairs
+    assert call(L=0) == 4
+    assert call(n_exp=1025) == 2
+    assert call(dim=288, stride=288) == 2                     # not a whole Q4_K superblock
+    assert call(stride=128) == 2                              # rows overlap
+    assert call(gper=per - 16) == 2
+    assert call(ws=ctypes.c_void_p(4096 + 128)) == 3
+    assert L.qmv_moe_workspace_bytes(4, 2, 256, 256) > 0
+    assert L.qmv_moe_workspace_bytes(4, 2, 250, 256) == 0
