@@ -83,6 +83,20 @@ int qmv_mv_experts(int ggml_type, const void* raw, long long per_expert, long lo
                    int k, const int8_t* xq, const int8_t* xq2, const float* xd, const float* xs,
                    int x_group, float* y, int n_out, int n_in, void* stream);
 
+/* Bytes of the workspace qmv_mm_tc needs (0 for an unsupported format or shape). */
+int64_t qmv_mm_tc_workspace_bytes(int ggml_type, int n_out, int n_in, int n_tok);
+
+/* Several tokens on the 5th-generation tensor cores (Q4_K and Q6_K, n_in a multiple of 256): y[t][r] =
+ * xs[t] * sum_k fp16(W[r, k]) fp16(x[t, k] / xs[t]) with xs[t] = max|x[t, :]| / 256, fp32 sums, y fp32
+ * [n_tok][n_out] overwritten; the weight values are unpacked to fp16 as the reference does (Q4_K d sc q -
+ * dmin m in one fused multiply-add, Q6_K d sc (q - 32)).  Tokens go in groups of 128; K is split over
+ * the SMs and the parts added in a fixed order (deterministic).  x fp32 if x_is_f32, else bf16;
+ * workspace 256-byte aligned, qmv_mm_tc_workspace_bytes long.  Replaces: ggufengine/mmvq.py:536-724
+ * (MMQ: mmq_eingang and mmq_<FMT>_<NT>) as dispatched by mmvq.mm (:902-918) for MMVQ_BIS < M <=
+ * MMQ_BIS (models/common.py:406-407). */
+int qmv_mm_tc(int ggml_type, const uint8_t* w, int n_out, int n_in, const void* x, int x_is_f32, int n_tok,
+              float* y, void* workspace, void* stream);
+
 /* Bytes of the workspace qmv_moe_ffn needs for n_tok tokens of k slots (0 for an invalid shape). */
 int64_t qmv_moe_workspace_bytes(int n_tok, int k, int dim, int ff);
 

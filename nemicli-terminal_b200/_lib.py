@@ -41,6 +41,8 @@ _SIGNATURES = {
     "qmv_act_q8": ([P, P, I, P, P, P, P, P, I, P], I),
     "qmv_unpack": ([I, P, LL, P, I, P], I),
     "qmv_moe_workspace_bytes": ([I, I, I, I], LL),
+    "qmv_mm_tc_workspace_bytes": ([I, I, I, I], LL),
+    "qmv_mm_tc": ([I, P, I, I, P, I, I, P, P, P], I),
     "qmv_moe_ffn": ([I, P, P, LL, I, P, LL, LL, P, P, I, I, P, I, LL, I, I, P, P, P], I),
 }
 

@@ -216,15 +216,45 @@ def _eingang(x2: torch.Tensor) -> Eingang:
     return e
 
 
+TC_FORMATE = ("Q4_K", "Q6_K")                # formats of the tensor-core tile path (the reference's MMQ)
+
+
 def mm(fmt: str, raw: torch.Tensor, x: torch.Tensor, n_out: int, n_in: int) -> torch.Tensor:
-    """Several tokens: x (M, n_in) -> (M, n_out) float32 (reference mmvq.py:902-918)."""
+    """Several tokens: x (M, n_in) -> (M, n_out) float32 (reference mmvq.py:902-918).  Q4_K / Q6_K go to the
+    tensor-core tile path with the reference MMQ's fp16 arithmetic (qmv_mm_tc); the other formats, and
+    an Eingang input, to the int8 kernels."""
     _check_raw(fmt, raw, n_out, n_in)
+    if fmt in TC_FORMATE and not _ist_eingang(x):
+        return mm_tc(fmt, raw, x, n_out, n_in)
     x2 = x.reshape(-1, n_in)
     e = _eingang(x2)
     M = x2.shape[0]
     y = torch.empty(M, n_out, dtype=torch.float32, device=raw.device)
     _lib.check(_lib.load().qmv_mv(TYPE_ID[fmt], _lib.ptr(raw), n_out, n_in, *e.zeiger(), M, _lib.ptr(y),
                                   _lib.stream_ptr(raw.device)), f"qmv_mv {fmt}")
+    return y
+
+
+def mm_tc(fmt: str, raw: torch.Tensor, x: torch.Tensor, n_out: int, n_in: int) -> torch.Tensor:
+    """x (M, n_in) fp32 / bf16 -> (M, n_out) float32 on the tensor cores (Q4_K, Q6_K)."""
+    _check_raw(fmt, raw, n_out, n_in)
+    _need_cuda(x, "mm_tc input")
+    if fmt not in TC_FORMATE:
+        raise RuntimeError(f"mm_tc: {fmt} has no tensor-core tile path (Q4_K, Q6_K)")
+    x2 = x.reshape(-1, n_in)
+    if x2.dtype not in (torch.float32, torch.bfloat16):
+        x2 = x2.float()
+    x2 = x2.contiguous()
+    M = x2.shape[0]
+    lib = _lib.load()
+    nbytes = lib.qmv_mm_tc_workspace_bytes(TYPE_ID[fmt], n_out, n_in, M)
+    if nbytes <= 0:
+        raise RuntimeError(f"mm_tc {fmt}: shape {n_out}x{n_in} not supported")
+    ws = torch.empty(nbytes + 256, dtype=torch.uint8, device=raw.device)
+    y = torch.empty(M, n_out, dtype=torch.float32, device=raw.device)
+    _lib.check(lib.qmv_mm_tc(TYPE_ID[fmt], _lib.ptr(raw), n_out, n_in, _lib.ptr(x2), int(x2.dtype == torch.float32),
+                             M, _lib.ptr(y), ws.data_ptr() + (-ws.data_ptr()) % 256, _lib.stream_ptr(raw.device)),
+               f"qmv_mm_tc {fmt}")
     return y
 
 

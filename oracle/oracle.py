@@ -9,6 +9,9 @@ product package.  Two oracles live here:
 * oracle B, `quant_q8` + `block_sums` + `mv`: the reference's two-stage int8 integer path
   (ggufengine/mmvq.py:59-83 and :341-482), with exact int32 sums per unit and an fp64 epilogue.
   The GPU kernels must reproduce the int32 sums bit for bit from the same activation input.
+* oracle C, `mmq`: the reference's tensor-core path for several tokens (ggufengine/mmvq.py:536-724):
+  weight values unpacked to fp16 by its fp32 formulas, tokens scaled per row to |x| <= 256 in fp16,
+  products summed exactly (fp64) and scaled back.
 """
 from __future__ import annotations
 
@@ -143,3 +146,66 @@ def max_rel(y, ref) -> float:
     y = np.asarray(y, np.float64)
     ref = np.asarray(ref, np.float64)
     return float(np.abs(y - ref).max() / max(np.abs(ref).max(), 1e-300))
+
+
+def _f32(a) -> np.ndarray:
+    return np.asarray(a, np.float64).astype(np.float32)
+
+
+def mmq_weights(fmt, w: np.ndarray, n_out: int, n_in: int) -> np.ndarray:
+    """Oracle C's fp16 weights (n_out, n_in): Q4_K fp16(fma(d sc, q, -dmin m)) (mmvq.py:578-592), Q6_K
+    fp16(d sc (q - 32)) (mmvq.py:606-616), each product and difference rounded to fp32 as there."""
+    nb = n_in // 256
+    if fmt == "Q4_K":
+        b = np.asarray(w, np.uint8).reshape(n_out * nb, 144)
+        d = b[:, 0:2].copy().view(np.float16).astype(np.float32)[:, 0]
+        dm = b[:, 2:4].copy().view(np.float16).astype(np.float32)[:, 0]
+        s = b[:, 4:16].astype(np.int32)
+        sc = np.empty((len(b), 8), np.int32)
+        mn = np.empty((len(b), 8), np.int32)
+        for j in range(8):
+            if j < 4:
+                sc[:, j], mn[:, j] = s[:, j] & 63, s[:, j + 4] & 63
+            else:
+                sc[:, j] = (s[:, j + 4] & 0xF) | ((s[:, j - 4] >> 6) << 4)
+                mn[:, j] = (s[:, j + 4] >> 4) | ((s[:, j] >> 6) << 4)
+        qs = b[:, 16:144].astype(np.int32).reshape(-1, 4, 32)
+        q = np.empty((len(b), 8, 32), np.int32)
+        q[:, 0::2] = qs & 15
+        q[:, 1::2] = qs >> 4
+        a = _f32(d[:, None].astype(np.float64) * sc)                 # d sc, rounded to fp32
+        c = _f32(dm[:, None].astype(np.float64) * mn)                # dmin m
+        v = _f32(a[:, :, None].astype(np.float64) * q - c[:, :, None])   # one fused multiply-add
+        return v.astype(np.float16).reshape(n_out, n_in)
+    if fmt == "Q6_K":
+        b = np.asarray(w, np.uint8).reshape(n_out * nb, 210)
+        ql = b[:, 0:128].astype(np.int32)
+        qh = b[:, 128:192].astype(np.int32)
+        sc = b[:, 192:208].view(np.int8).astype(np.int32)
+        d = b[:, 208:210].copy().view(np.float16).astype(np.float32)[:, 0]
+        v = np.empty((len(b), 256), np.float32)
+        l = np.arange(32)
+        for n in range(2):
+            for g, (lo, sh, hi_sh) in enumerate(((0, 0, 0), (32, 0, 2), (0, 4, 4), (32, 4, 6))):
+                q = ((ql[:, 64 * n + lo + l] >> sh) & 0xF) | (((qh[:, 32 * n + l] >> hi_sh) & 3) << 4)
+                f = _f32(d[:, None].astype(np.float64) * sc[:, 8 * n + l // 16 + 2 * g])
+                v[:, 128 * n + 32 * g + l] = _f32(f.astype(np.float64) * (q - 32))
+        return v.astype(np.float16).reshape(n_out, n_in)
+    raise ValueError(f"mmq: {fmt} (Q4_K, Q6_K)")
+
+
+def mmq_input(x: np.ndarray):
+    """Tokens (T, n) fp32 -> (fp16 values x / xs, xs): xs = max(max|x|, 1e-30) / 256 (mmvq.py:617-640)."""
+    x = np.asarray(x, np.float32)
+    m = np.abs(x).max(axis=1)
+    xs = _f32(np.maximum(m, np.float32(1e-30)).astype(np.float64) / 256.0)
+    inv = _f32(1.0 / xs.astype(np.float64))
+    xh = _f32(x.astype(np.float64) * inv[:, None]).astype(np.float16)
+    return xh, xs
+
+
+def mmq(fmt, w: np.ndarray, n_out: int, n_in: int, x: np.ndarray) -> np.ndarray:
+    """Oracle C: (T, n_in) fp32 tokens -> (T, n_out) fp64, the reference MMQ's values summed exactly."""
+    W = mmq_weights(fmt, w, n_out, n_in).astype(np.float64)
+    xh, xs = mmq_input(np.asarray(x, np.float32).reshape(-1, n_in))
+    return (xh.astype(np.float64) @ W.T) * xs.astype(np.float64)[:, None]

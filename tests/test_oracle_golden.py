@@ -118,3 +118,17 @@ def test_bf16_input_path():
     yb, _ = H.oracle_b("Q4_K", raw, x, 8, 512)
     ya = H.oracle_a("Q4_K", raw, x, 8, 512)
     assert O.max_rel(yb, ya) < 1e-3
+
+
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q6_K"])
+def test_mmq_weights_follow_the_pinned_dequantiser(fmt):
+    """Oracle C's fp16 weights (the reference MMQ's unpacking) lie within one fp16 step of the
+    golden-pinned dequantiser's values at every position: the byte layout it decodes is the pinned one."""
+    from nemicli_terminal_b200 import synth
+    n_out, n_in = 48, 1024
+    raw = synth.blocks(fmt, n_out, n_in, seed=9).numpy()
+    w16 = O.mmq_weights(fmt, raw, n_out, n_in).astype(np.float64)
+    wa = O.dequant(fmt, raw.reshape(-1), n_out * n_in).reshape(n_out, n_in).astype(np.float64)
+    step = np.maximum(np.abs(wa), 2.0 ** -14) * 2.0 ** -10          # one fp16 ulp (normal range)
+    assert np.all(np.abs(w16 - wa) <= step)
+    assert np.mean(w16 == wa.astype(np.float16).astype(np.float64)) > 0.99
