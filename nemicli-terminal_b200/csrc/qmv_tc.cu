@@ -9,19 +9,38 @@ using namespace qmv;
 
 namespace {
 
-// row tiles x K parts: at most one wave of three CTAs per SM (three fit by shared memory), each part
-// at least four K steps so that its stages overlap, and the parts' sums (n_tok x n_out fp32 each) not
-// more bytes than the weights
+bool tc_format(int f) { return f == F_Q4_K || f == F_Q6_K; }
+
+template <int FMT>
+int tc_occupancy(int n_pad) {                         // resident CTAs per SM at this shared-memory size
+    static int attr = 0;
+    if (!attr) {
+        if (cudaFuncSetAttribute(tc_mm_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem) != cudaSuccess)
+            return 1;
+        attr = 1;
+    }
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, tc_mm_kernel<FMT>, kTcThreads, tc_smem(n_pad)) != cudaSuccess)
+        n = 1;
+    return std::max(1, n);
+}
+
+// row tiles x K parts: at most one wave of resident CTAs, each part at least four K steps so that its
+// stages overlap, and the parts' sums (n_tok x n_out fp32 each) not more bytes than the weights.  Planned
+// for the first group of tokens (the largest) and kept for every group.
 struct TcPlan {
-    int tiles, splits, chunks;
+    int tiles, splits, chunks, n_pad;
 };
 TcPlan tc_plan(int fmt, int n_out, int n_in, int n_tok) {
     TcPlan p{};
+    const int g = std::min(n_tok, kTcMaxN);
+    p.n_pad = (g + 15) / 16 * 16;
     p.tiles = (n_out + kTcRows - 1) / kTcRows;
     p.chunks = n_in / kTcK;
-    const int wave = std::max(1, 3 * sm_count() / p.tiles);
+    const int occ = fmt == F_Q4_K ? tc_occupancy<F_Q4_K>(p.n_pad) : tc_occupancy<F_Q6_K>(p.n_pad);
+    const int wave = std::max(1, occ * sm_count() / p.tiles);
     const long long wbytes = (long long)n_out * (n_in / 256) * block_bytes(fmt);
-    const long long pbytes = (long long)std::min(n_tok, kTcMaxN) * n_out * 4;
+    const long long pbytes = (long long)g * n_out * 4;
     const int traffic = int(std::max<long long>(1, wbytes / std::max<long long>(1, pbytes)));
     p.splits = std::max(1, std::min({wave, p.chunks / 4, traffic, 32}));
     return p;
@@ -44,17 +63,9 @@ TcWs tc_ws(int fmt, int n_out, int n_in, int n_tok) {
     return w;
 }
 
-bool tc_format(int f) { return f == F_Q4_K || f == F_Q6_K; }
-
 template <int FMT>
 int launch_tc(const TcParams& P, int grid, cudaStream_t st) {
-    static bool attr = false;
-    if (!attr) {
-        if (cudaFuncSetAttribute(tc_mm_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem) != cudaSuccess)
-            return launched();
-        attr = true;
-    }
-    tc_mm_kernel<FMT><<<grid, kTcThreads, kTcSmem, st>>>(P);
+    tc_mm_kernel<FMT><<<grid, kTcThreads, tc_smem(P.n_pad), st>>>(P);
     return launched();
 }
 

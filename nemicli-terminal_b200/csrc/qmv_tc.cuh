@@ -9,7 +9,7 @@
 //
 //   CTA tile    128 weight rows (the MMA's M) x N tokens (N = tokens rounded up to 16, at most 128), one
 //               fp32 accumulator of 128 lanes x N columns in tensor memory;
-//   K steps     64 values: each of the 128 threads unpacks its row's 64 values (loaded one step ahead in
+//   K steps     64 values (shared memory 2 x (16 KB + N x 128 B): three or four CTAs an SM): each of the 128 threads unpacks its row's 64 values (loaded one step ahead in
 //               registers) into shared memory in the canonical K-major layout without swizzle (core
 //               matrices of 8 rows x 16 bytes, 128 B apart along K, 1 KB apart per 8 rows), copies the
 //               tokens' 64 fp16 values the same way, and one thread issues four kind::f16 MMAs
@@ -34,7 +34,8 @@ constexpr int kTcMaxN = 128;               // tokens per launch
 constexpr int kTcThreads = 128;
 constexpr int kTcStageA = kTcRows * kTcK * 2;    // 16 KB
 constexpr int kTcStageB = kTcMaxN * kTcK * 2;    // 16 KB
-constexpr int kTcSmem = 2 * (kTcStageA + kTcStageB) + 64;
+constexpr int kTcSmem = 2 * (kTcStageA + kTcStageB) + 64;    // at N = 128; a launch takes 2 (A + N 128 B) + 64
+__host__ __device__ constexpr int tc_smem(int n_pad) { return 2 * (kTcStageA + n_pad * kTcK * 2) + 64; }
 constexpr float kTcScale = 256.0f;         // tokens scaled to |x| <= 256 (the reference's MMQ_SKALA)
 
 struct TcParams {
@@ -248,9 +249,10 @@ __global__ void __launch_bounds__(kTcThreads) tc_mm_kernel(const TcParams P) {
     __shared__ int s_last;
     const uint32_t base = smem_u32(tc_smem);
     const uint32_t sa[2] = {base, base + uint32_t(kTcStageA)};
-    const uint32_t sb[2] = {base + uint32_t(2 * kTcStageA), base + uint32_t(2 * kTcStageA + kTcStageB)};
-    const uint32_t bar0 = base + uint32_t(2 * (kTcStageA + kTcStageB));     // two mbarriers, 8 B each
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(tc_smem + 2 * (kTcStageA + kTcStageB) + 16);
+    const uint32_t bst = uint32_t(P.n_pad * kTcK * 2);                        // B stage: N rows of 128 B
+    const uint32_t sb[2] = {base + uint32_t(2 * kTcStageA), base + uint32_t(2 * kTcStageA) + bst};
+    const uint32_t bar0 = base + uint32_t(2 * kTcStageA) + 2 * bst;           // two mbarriers, 8 B each
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(tc_smem + 2 * kTcStageA + 2 * bst + 16);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tile = blockIdx.x / P.splits, part = blockIdx.x % P.splits;
     const int chunks = P.n_in / kTcK;
