@@ -568,6 +568,56 @@ def run_matrices(args):
         dist.destroy_process_group()
 
 
+TILE_MATRICES = [("Q4_K", 14336, 4096), ("Q4_K", 4096, 4096), ("Q6_K", 4096, 14336)]
+TILE_TOKENS = (17, 32, 64, 112)
+
+
+def run_tiles(args):
+    """The tensor-core tile path (mmvq.mm -> qmv_mm_tc) at config-2 matrix shapes for 17..112 tokens (the
+    reference's MMQ range), beside the int8 kernels (mmvq.mv) on the same inputs; CUDA graphs over
+    distinct copies reading more than twice L2 per replay.  Parity of every case against oracle C is in
+    tests/test_gpu_tc.py.  N > 1: independent replicas."""
+    world, rank, local, device, dist = _init_rank()
+    from nemicli_terminal_b200 import mmvq, synth
+    from nemicli_terminal_b200.formats import row_bytes
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    peak, peak_kind = peaks()
+    out = {}
+    tot_flop, tot_s = 0.0, 0.0
+    for fmt, n_out, n_in in TILE_MATRICES:
+        mb = n_out * row_bytes(fmt, n_in)
+        copies = max(1, -(-2 * l2 // mb))
+        mats = [synth.blocks(fmt, n_out, n_in, seed=950 + c, device=device) for c in range(copies)]
+        for M in TILE_TOKENS:
+            x = synth.activations(M, n_in, seed=951 + M, device=device)
+            row = {}
+            for name, fn in (("tile", mmvq.mm_tc), ("int8", mmvq.mv)):
+                g, _ = capture(lambda: [fn(fmt, m, x, n_out, n_in) for m in mats])
+                t = max_over_ranks(time_graph(g, args.steps, max(3, args.warmup), dist) / (args.steps * copies),
+                                   dist, device)
+                del g
+                row[name + "_us"] = t * 1e6
+                if name == "tile":
+                    row["tile_tflops"] = 2.0 * M * n_out * n_in / t / 1e12
+                    row["tile_weight_gbs"] = mb / t / 1e9
+                    tot_flop += 2.0 * M * n_out * n_in
+                    tot_s += t
+            row["speedup_vs_int8"] = row["int8_us"] / row["tile_us"]
+            out[f"{fmt} {n_out}x{n_in} {M}tok"] = row
+    if rank == 0:
+        line = {"metric": "TFLOP/s of the tensor-core tile path (17..112 tokens, config-2 shapes)",
+                "value": world * tot_flop / tot_s / 1e12, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": tot_s * 1e3, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded, config-2 distributions)",
+                "config": {"workload": "tiles: " + ", ".join(f"{f} {o}x{i}" for f, o, i in TILE_MATRICES),
+                           "tokens": list(TILE_TOKENS), "l2": "distinct copies > 2x L2 per replay"},
+                "cases": out, "peak": peak, "peak_kind": peak_kind}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_moe(args):
     """Config 4: MoE FFN of 128 Q4_K experts (gate/up 768x2048, down 2048x768), top-8 routing, batch
     1 / 4 / 16, captured in a CUDA graph over 16 rotating routings.  One GPU: moe.MoeFFN.  N GPUs:
@@ -687,9 +737,10 @@ def main():
     ap.add_argument("--mode", choices=["chain", "calls"], default="chain",
                     help="chain: the step as one decode-chain launch; calls: one launch per matrix group")
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers in the stack (profiling runs use fewer)")
-    ap.add_argument("--workload", choices=["stack", "vocab", "moe", "cfg1", "cfg5"], default="stack",
+    ap.add_argument("--workload", choices=["stack", "vocab", "moe", "cfg1", "cfg5", "tiles"], default="stack",
                     help="stack: config 2 (the headline); vocab: config 3 row-sharded over the GPUs; "
-                         "moe: config 4; cfg1 / cfg5: the single-matrix configs")
+                         "moe: config 4; cfg1 / cfg5: the single-matrix configs; tiles: the tensor-core tile "
+                         "path for 17..112 tokens")
     ap.add_argument("--vocab-format", choices=["Q8_0", "Q6_K"], default="Q8_0")
     ap.add_argument("--tokens", type=int, default=1, help="vocab workload: tokens per call (config 3: 1 and 8)")
     args = ap.parse_args()
@@ -699,6 +750,8 @@ def main():
         run_vocab(args)
     elif args.workload == "moe":
         run_moe(args)
+    elif args.workload == "tiles":
+        run_tiles(args)
     elif args.workload in MATRIX_WORKLOADS:
         run_matrices(args)
     else:

@@ -91,11 +91,12 @@ int64_t qmv_mm_tc_workspace_bytes(int ggml_type, int n_out, int n_in, int n_tok)
  * [n_tok][n_out] overwritten; the weight values are unpacked to fp16 as the reference does (Q4_K d sc q -
  * dmin m in one fused multiply-add, Q6_K d sc (q - 32)).  Tokens go in groups of 128; K is split over
  * the SMs and the parts added in a fixed order (deterministic).  x fp32 if x_is_f32, else bf16;
- * workspace 256-byte aligned, qmv_mm_tc_workspace_bytes long.  Replaces: ggufengine/mmvq.py:536-724
+ * workspace 256-byte aligned, workspace_bytes long: at least qmv_mm_tc_workspace_bytes (else
+ * QMV_ERR_SHAPE, nothing launched).  Replaces: ggufengine/mmvq.py:536-724
  * (MMQ: mmq_eingang and mmq_<FMT>_<NT>) as dispatched by mmvq.mm (:902-918) for MMVQ_BIS < M <=
  * MMQ_BIS (models/common.py:406-407). */
 int qmv_mm_tc(int ggml_type, const uint8_t* w, int n_out, int n_in, const void* x, int x_is_f32, int n_tok,
-              float* y, void* workspace, void* stream);
+              float* y, void* workspace, long long workspace_bytes, void* stream);
 
 /* Bytes of the workspace qmv_moe_ffn needs for n_tok tokens of k slots (0 for an invalid shape). */
 int64_t qmv_moe_workspace_bytes(int n_tok, int k, int dim, int ff);

@@ -42,7 +42,7 @@ _SIGNATURES = {
     "qmv_unpack": ([I, P, LL, P, I, P], I),
     "qmv_moe_workspace_bytes": ([I, I, I, I], LL),
     "qmv_mm_tc_workspace_bytes": ([I, I, I, I], LL),
-    "qmv_mm_tc": ([I, P, I, I, P, I, I, P, P, P], I),
+    "qmv_mm_tc": ([I, P, I, I, P, I, I, P, P, LL, P], I),
     "qmv_moe_ffn": ([I, P, P, LL, I, P, LL, LL, P, P, I, I, P, I, LL, I, I, P, P, P], I),
 }
 

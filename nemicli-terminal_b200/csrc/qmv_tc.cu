@@ -11,18 +11,20 @@ namespace {
 
 bool tc_format(int f) { return f == F_Q4_K || f == F_Q6_K; }
 
+// resident CTAs per SM at this shared-memory size: by shared memory (233472 B an SM, 1 KB reserved per
+// CTA beside its static 1 KB) and by registers (the kernel's count, read once; 168 if unavailable).  No
+// runtime occupancy query: the plan must come out the same for the workspace size and the launch.
 template <int FMT>
-int tc_occupancy(int n_pad) {                         // resident CTAs per SM at this shared-memory size
-    static int attr = 0;
-    if (!attr) {
-        if (cudaFuncSetAttribute(tc_mm_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem) != cudaSuccess)
-            return 1;
-        attr = 1;
+int tc_occupancy(int n_pad) {
+    static int regs = 0;
+    if (regs == 0) {
+        cudaFuncAttributes fa{};
+        regs = cudaFuncGetAttributes(&fa, tc_mm_kernel<FMT>) == cudaSuccess && fa.numRegs > 0 ? fa.numRegs : 168;
     }
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, tc_mm_kernel<FMT>, kTcThreads, tc_smem(n_pad)) != cudaSuccess)
-        n = 1;
-    return std::max(1, n);
+    const int by_smem = 233472 / (tc_smem(n_pad) + 2048);
+    const int per_warp = (regs * 32 + 255) / 256 * 256;
+    const int by_regs = 65536 / (per_warp * (kTcThreads / 32));
+    return std::max(1, std::min({by_smem, by_regs, 32}));
 }
 
 // row tiles x K parts: at most one wave of resident CTAs, each part at least four K steps so that its
@@ -65,6 +67,12 @@ TcWs tc_ws(int fmt, int n_out, int n_in, int n_tok) {
 
 template <int FMT>
 int launch_tc(const TcParams& P, int grid, cudaStream_t st) {
+    static bool attr = false;                        // more than 48 KB of dynamic shared memory
+    if (!attr) {
+        if (cudaFuncSetAttribute(tc_mm_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem) != cudaSuccess)
+            return launched();
+        attr = true;
+    }
     tc_mm_kernel<FMT><<<grid, kTcThreads, tc_smem(P.n_pad), st>>>(P);
     return launched();
 }
@@ -79,7 +87,7 @@ int64_t qmv_mm_tc_workspace_bytes(int ggml_type, int n_out, int n_in, int n_tok)
 }
 
 int qmv_mm_tc(int ggml_type, const uint8_t* w, int n_out, int n_in, const void* x, int x_is_f32, int n_tok,
-              float* y, void* workspace, void* stream) {
+              float* y, void* workspace, long long workspace_bytes, void* stream) {
     if (!tc_format(ggml_type)) return ST_BAD_FORMAT;
     if (!w || !x || !y || !workspace) return ST_NULL;
     if (n_out <= 0 || n_in <= 0 || n_in % 256) return ST_BAD_SHAPE;
@@ -90,6 +98,7 @@ int qmv_mm_tc(int ggml_type, const uint8_t* w, int n_out, int n_in, const void* 
     const long long row_bytes = (long long)(n_in / 256) * block_bytes(ggml_type);
     const TcPlan pl = tc_plan(ggml_type, n_out, n_in, n_tok);
     const TcWs W = tc_ws(ggml_type, n_out, n_in, n_tok);
+    if (workspace_bytes < W.total) return ST_BAD_SHAPE;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     for (int t0 = 0; t0 < n_tok; t0 += kTcMaxN) {          // groups of at most 128 tokens

@@ -217,14 +217,21 @@ def _eingang(x2: torch.Tensor) -> Eingang:
 
 
 TC_FORMATE = ("Q4_K", "Q6_K")                # formats of the tensor-core tile path (the reference's MMQ)
+TC_FROM = 48                                 # tokens from which the tile path beats the int8 kernels (measured)
+
+
+def tc_used(fmt: str, n_tok: int) -> bool:
+    """Whether mm runs n_tok tokens of fmt on the tensor-core tile path."""
+    return fmt in TC_FORMATE and n_tok >= TC_FROM
 
 
 def mm(fmt: str, raw: torch.Tensor, x: torch.Tensor, n_out: int, n_in: int) -> torch.Tensor:
-    """Several tokens: x (M, n_in) -> (M, n_out) float32 (reference mmvq.py:902-918).  Q4_K / Q6_K go to the
-    tensor-core tile path with the reference MMQ's fp16 arithmetic (qmv_mm_tc); the other formats, and
-    an Eingang input, to the int8 kernels."""
+    """Several tokens: x (M, n_in) -> (M, n_out) float32 (reference mmvq.py:902-918).  Q4_K / Q6_K from
+    TC_FROM tokens go to the tensor-core tile path with the reference MMQ's fp16 arithmetic (qmv_mm_tc);
+    fewer tokens, the other formats and an Eingang input to the int8 kernels (faster there, and within
+    the same tolerance of the exact product)."""
     _check_raw(fmt, raw, n_out, n_in)
-    if fmt in TC_FORMATE and not _ist_eingang(x):
+    if not _ist_eingang(x) and tc_used(fmt, x.reshape(-1, n_in).shape[0]):
         return mm_tc(fmt, raw, x, n_out, n_in)
     x2 = x.reshape(-1, n_in)
     e = _eingang(x2)
@@ -253,7 +260,7 @@ def mm_tc(fmt: str, raw: torch.Tensor, x: torch.Tensor, n_out: int, n_in: int) -
     ws = torch.empty(nbytes + 256, dtype=torch.uint8, device=raw.device)
     y = torch.empty(M, n_out, dtype=torch.float32, device=raw.device)
     _lib.check(lib.qmv_mm_tc(TYPE_ID[fmt], _lib.ptr(raw), n_out, n_in, _lib.ptr(x2), int(x2.dtype == torch.float32),
-                             M, _lib.ptr(y), ws.data_ptr() + (-ws.data_ptr()) % 256, _lib.stream_ptr(raw.device)),
+                             M, _lib.ptr(y), ws.data_ptr() + (-ws.data_ptr()) % 256, nbytes, _lib.stream_ptr(raw.device)),
                f"qmv_mm_tc {fmt}")
     return y
 
