@@ -304,7 +304,8 @@ def sharded_suite(world: int, rank: int, dist, device, steps: int, warmup: int) 
         if world == 1:
             # the unsharded layer: the grouped kernels (3 launches) and the per-(token, slot) expert matvecs
             per_slot = moe.MoeFFN(*full_ex, act=lambda t: torch.nn.functional.silu(t))
-            for name, fn in (("grouped_us", ref_layer), ("per_slot_us", per_slot)):
+            grouped = lambda x, ix, w: moe.grouped_ffn(*full_ex, x, ix, w)          # noqa: E731
+            for name, fn in (("grouped_us", grouped), ("per_slot_us", per_slot)):
                 g1, _ = capture(lambda: [fn(x, ix, w) for x, (ix, w) in zip(xs, routes)])
                 single[name] = time_graph(g1, steps, warmup, dist) / (steps * n_rot) * 1e6
                 del g1

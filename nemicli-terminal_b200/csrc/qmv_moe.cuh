@@ -223,15 +223,19 @@ __device__ __forceinline__ void moe_store(float* dst, int n_cols, int row0, cons
         }
 }
 
-// one warp: this lane's stores are published, then the counter is bumped; true on every lane of the
-// warp whose bump completed the count (it then reads the others' stores with __ldcg)
+// one warp: the lanes' stores are published by lane 0's acquire-release add on the counter (after the
+// warp's sync, as the chain's group counters do); true on every lane of the warp whose add completed
+// the count, which then reads the others' stores with __ldcg after the warp's sync
 __device__ __forceinline__ bool moe_arrive(int* counter, int count) {
-    __threadfence();
     __syncwarp();
     int last = 0;
-    if ((threadIdx.x & 31) == 0) last = atomicAdd(counter, 1) == count - 1;
+    if ((threadIdx.x & 31) == 0) {
+        int old;
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(counter) : "memory");
+        last = old == count - 1;
+    }
     last = __shfl_sync(0xffffffffu, last, 0);
-    if (last) __threadfence();
+    __syncwarp();
     return last != 0;
 }
 
@@ -288,11 +292,18 @@ __global__ void __launch_bounds__(kMoeThreads, kMoeMinBlocks) moe_gateup_kernel(
         }
         // the group's last quad: silu(g) * u for every pair of the expert, quantised (lane = value)
         if (moe_arrive(P.gu_done + (long long)u * groups + g, kMoeQuads)) {
-            for (int c = 0; c < ne; ++c) {
-                const long long o = (long long)R.pair[R.start[u] + c] * P.ff + 32 * g + lane;
-                const float gv = __ldcg(P.gs + o), uv = __ldcg(P.us + o);
-                const float a = gv / (1.0f + expf(-gv)) * uv;
-                quantize_group(a, o, P.aq, P.aq2, P.ad, P.as);
+            for (int c0 = 0; c0 < ne; c0 += 4) {        // four pairs' sums in flight at a time
+                float gv[4], uv[4];
+                long long o[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    o[c] = c0 + c < ne ? (long long)R.pair[R.start[u] + c0 + c] * P.ff + 32 * g + lane : 0;
+                    gv[c] = c0 + c < ne ? __ldcg(P.gs + o[c]) : 0.f;
+                    uv[c] = c0 + c < ne ? __ldcg(P.us + o[c]) : 0.f;
+                }
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    if (c0 + c < ne) quantize_group(gv[c] / (1.0f + expf(-gv[c])) * uv[c], o[c], P.aq, P.aq2, P.ad, P.as);
             }
         }
     }
@@ -354,10 +365,20 @@ __global__ void __launch_bounds__(kMoeThreads, kMoeMinBlocks) moe_down_kernel(co
             for (int i = lane; i < P.L * kMoeRW; i += 32) {
                 const int t = i / kMoeRW, r = row0 + i % kMoeRW;
                 float v = 0.f;
-                for (int j = 0; j < P.k; ++j) {
-                    const int p = t * P.k + j;
-                    if (R.ex[p] >= 0)
-                        v = __fadd_rn(v, __fmul_rn(P.wts[p], __ldcg(P.y + (long long)p * P.dim + r)));   // no contraction
+                for (int j0 = 0; j0 < P.k; j0 += 8) {     // eight slots' loads in flight, added in slot order
+                    float yv[8], wv[8];
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj) {
+                        const int p = t * P.k + j0 + jj;
+                        const bool ok = j0 + jj < P.k && R.ex[p] >= 0;
+                        yv[jj] = ok ? __ldcg(P.y + (long long)p * P.dim + r) : 0.f;
+                        wv[jj] = ok ? P.wts[p] : 0.f;
+                    }
+#pragma unroll
+                    for (int jj = 0; jj < 8; ++jj) {
+                        const int p = t * P.k + j0 + jj;
+                        if (j0 + jj < P.k && R.ex[p] >= 0) v = __fadd_rn(v, __fmul_rn(wv[jj], yv[jj]));   // no contraction
+                    }
                 }
                 P.out[(long long)t * P.dim + r] = v;
             }

@@ -9,11 +9,12 @@ GRAPH_ZEILEN tokens with every (token, slot) pair on its own).  Each token's inp
 and read by all of its k slots (x_group = k); the down projection reads one activation row per slot.
 Nothing reads the choice on the host, so a whole call can be captured in a CUDA graph.
 
-With the default SiLU gate, experts resident on the device as contiguous tensors, gate and up in one
-format, at most MOE_MAX_PAIRS (token, slot) pairs and MOE_MAX_EXPERTS experts, the call is one grouped
-launch sequence (grouped_ffn, qmv_moe_ffn): quantise x; gate/up of every touched expert read once with
+With the default SiLU gate, experts resident on the device as contiguous tensors and gate and up in one
+format, grouped_ffn (qmv_moe_ffn, up to MOE_MAX_PAIRS (token, slot) pairs and MOE_MAX_EXPERTS experts)
+runs the FFN as one grouped launch sequence: quantise x; gate/up of every touched expert read once with
 silu(g) * u quantised in its epilogue; down of every touched expert read once with the weighted sum
-over slots in its epilogue.  Otherwise it runs expert matvecs per (token, slot) as above.
+over slots in its epilogue.  MoeFFN uses it up to GROUPED_UP_TO pairs, where it is the faster of the two
+(measured); above that, and otherwise, it runs expert matvecs per (token, slot) as above.
 """
 from __future__ import annotations
 
@@ -30,6 +31,8 @@ from .mmvq import Eingang
 GRAPH_ZEILEN = 16
 MOE_MAX_PAIRS = 1024         # tokens x slots of one grouped call
 MOE_MAX_EXPERTS = 1024       # experts of one grouped call
+GROUPED_UP_TO = 16           # MoeFFN takes the grouped call up to this many pairs: measured at config 4 it
+                             # beats the per-slot path at 8 pairs (batch 1) and loses from 32 (batch 4)
 
 
 def grouped_ok(gate: PackedExperts, up: PackedExperts, down: PackedExperts, x: torch.Tensor, n_tok: int,
@@ -105,7 +108,7 @@ class MoeFFN:
         self.grouped = act is None or act is F.silu
 
     def _grouped_ok(self, x: torch.Tensor, L: int, k: int) -> bool:
-        return self.grouped and grouped_ok(self.gate, self.up, self.down, x, L, k)
+        return self.grouped and L * k <= GROUPED_UP_TO and grouped_ok(self.gate, self.up, self.down, x, L, k)
 
     def grouped_call(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         """The grouped launch sequence (grouped_ffn); raises where it does not apply."""

@@ -128,9 +128,9 @@ class ExpertShardedMoE:
 
     gate, up, down: this rank's experts (PackedExperts holding shard_range(n_exp, world, rank)).
     ffn(local_ids, a) -> (P, E) float32: optional replacement of the local expert computation.  The
-    default with the SiLU gate is the grouped expert FFN (moe.grouped_ffn: every local expert read once
-    per call, one slot per received row); with another act, or beyond the grouped limits, gate/up ->
-    act -> down run through the expert matvecs, each pair on its own input.  Ids of -1 mark unused
+    default with the SiLU gate and at most moe.GROUPED_UP_TO received rows is the grouped expert FFN
+    (moe.grouped_ffn: every local expert read once per call, one slot per received row); otherwise
+    gate/up -> act -> down run through the expert matvecs, each pair on its own input.  Ids of -1 mark unused
     slots, whose rows are ignored."""
 
     def __init__(self, gate: Optional[PackedExperts], up: Optional[PackedExperts], down: Optional[PackedExperts],
@@ -207,7 +207,8 @@ class ExpertShardedMoE:
         for unused slots."""
         ids = recv[:, self.dim].to(torch.int64)
         a = recv[:, :self.dim]
-        if self._grouped and moe.grouped_ok(self.gate, self.up, self.down, a, a.shape[0], 1):
+        if self._grouped and a.shape[0] <= moe.GROUPED_UP_TO and moe.grouped_ok(self.gate, self.up, self.down, a,
+                                                                               a.shape[0], 1):
             # one slot per received row, unit weight: the grouped kernels read each local expert once and
             # leave unused and refused slots at zero
             key = (a.device, a.shape[0])

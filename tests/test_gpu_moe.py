@@ -87,15 +87,17 @@ def test_mixed_formats_dense(cuda, L):
     ffn = moe.MoeFFN(*ex)
     x = synth.activations(L, E, seed=24, device=cuda).to(torch.bfloat16)
     idx, w = moe.route(synth.router_logits(L, n_exp, seed=25, device=cuda), k)
-    out = ffn(x, idx, w)
-    assert _rel(out, _ref(fmts, ex, x.float(), idx, w)) < 1e-3
-    assert torch.equal(out, ffn(x, idx, w))
+    ref = _ref(fmts, ex, x.float(), idx, w)
+    out = ffn.grouped_call(x, idx, w)
+    assert _rel(out, ref) < 1e-3
+    assert torch.equal(out, ffn.grouped_call(x, idx, w))
+    assert _rel(ffn(x, idx, w), ref) < 1e-3             # whichever path __call__ takes at this size
 
 
 def test_largest_call_and_fallback(cuda):
     """256 tokens x 4 slots (the grouped limit of 1024 pairs) with every token on expert 0 in slot 0
-    (256 pairs of one expert, 64 passes of 4); 257 tokens take the per-slot path through the same
-    __call__."""
+    (256 pairs of one expert, 64 passes of 4); 257 tokens are refused by the grouped call (and __call__
+    takes the per-slot path)."""
     n_exp, E, n_ff, k = 16, 256, 128, 4
     ex = (_experts("Q8_0", n_exp, n_ff, E, 31, cuda), _experts("Q8_0", n_exp, n_ff, E, 32, cuda),
           _experts("Q4_0", n_exp, E, n_ff, 33, cuda))
@@ -104,13 +106,15 @@ def test_largest_call_and_fallback(cuda):
         x = synth.activations(L, E, seed=34 + L, device=cuda)
         idx, w = moe.route(synth.router_logits(L, n_exp, seed=35 + L, device=cuda), k)
         idx[:, 0] = 0
-        out = grouped(x, idx, w)
-        assert _rel(out, per_slot(x, idx, w)) < 1e-4
+        ref = per_slot(x, idx, w)
         if L == 256:
+            out = grouped.grouped_call(x, idx, w)
+            assert _rel(out, ref) < 1e-4
             assert torch.equal(out, grouped.grouped_call(x, idx, w))
         else:
             with pytest.raises(ValueError):
                 grouped.grouped_call(x, idx, w)
+            assert torch.equal(grouped(x, idx, w), ref)
 
 
 def test_strided_rows(cuda):
