@@ -540,6 +540,7 @@ def run_matrices(args):
     from nemicli_terminal_b200.formats import row_bytes
     l2 = torch.cuda.get_device_properties(device).L2_cache_size
     peak, peak_kind = peaks()
+    mmvq.pdl(not args.no_pdl)            # static weights: each call may stream them while the previous ends
     per = {}
     tot_bytes, tot_s = 0, 0.0
     for fmt, n_out, n_in in MATRIX_WORKLOADS[args.workload]:
@@ -561,7 +562,8 @@ def run_matrices(args):
                 "warmup": args.warmup, "ms_per_step": tot_s * 1e3, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "int8", "data": f"synthetic (seeded, {args.workload} distributions)",
                 "config": {"workload": args.workload + ": " + ", ".join(per), "batch": 1,
-                           "l2": "distinct copies of each matrix totalling > 2x L2 per replay"},
+                           "l2": "distinct copies of each matrix totalling > 2x L2 per replay",
+                           "pdl": not args.no_pdl},
                 "matrices": per, "peak": peak, "peak_kind": peak_kind}
         print(json.dumps(line), flush=True)
     if dist is not None:
