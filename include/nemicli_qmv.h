@@ -83,6 +83,23 @@ int qmv_mv_experts(int ggml_type, const void* raw, long long per_expert, long lo
                    int k, const int8_t* xq, const int8_t* xq2, const float* xd, const float* xs,
                    int x_group, float* y, int n_out, int n_in, void* stream);
 
+/* Expert-parallel exchange, send side: pair p = t * k + j of the n_tok x k device ids goes to the rank
+ * holding its expert (experts split over `world` ranks by whole items, the first n_exp % world ranks
+ * one more) at the next free slot of that rank's block of P = n_tok * k slots (pairs in index order).
+ * send: world * P rows of row_floats floats (>= dim + 1): the token's activation (x fp32 if x_is_f32,
+ * else bf16) in [0, dim), the owner-local expert id as a float at dim, zeros after; ids outside
+ * [0, n_exp) go to rank 0 with id -2, slots no pair takes get id -1 (their data is not written).
+ * slot: P int64 (the pair's row in send), sent: world int32 (pairs per rank).  Two launches.
+ * Replaces: nothing in the reference (single-GPU); the dispatch of shard.ExpertShardedMoE. */
+int qmv_expert_dispatch(const long long* ids, int n_tok, int k, long long n_exp, int world, const void* x,
+                        int x_is_f32, int dim, float* send, int row_floats, long long* slot, int* sent, void* stream);
+
+/* Expert-parallel exchange, home side: out[t][c] = sum_j w[t][j] * y[slot[t k + j]][c] over j = 0..k-1
+ * in slot order (each product and sum rounded; y rows y_stride floats apart).  One launch.  Replaces:
+ * nothing in the reference; the weighted sum of shard.ExpertShardedMoE (the order of moe.py:319-321). */
+int qmv_expert_combine(const float* y, int y_stride, const long long* slot, const float* w, int n_tok, int k, int dim,
+                       float* out, void* stream);
+
 /* Bytes of the workspace qmv_mm_tc needs (0 for an unsupported format or shape). */
 int64_t qmv_mm_tc_workspace_bytes(int ggml_type, int n_out, int n_in, int n_tok);
 

@@ -42,6 +42,8 @@ _SIGNATURES = {
     "qmv_unpack": ([I, P, LL, P, I, P], I),
     "qmv_moe_workspace_bytes": ([I, I, I, I], LL),
     "qmv_mm_tc_workspace_bytes": ([I, I, I, I], LL),
+    "qmv_expert_dispatch": ([P, I, I, LL, I, P, I, I, P, I, P, P, P], I),
+    "qmv_expert_combine": ([P, I, P, P, I, I, I, P, P], I),
     "qmv_mm_tc": ([I, P, I, I, P, I, I, P, P, LL, P], I),
     "qmv_moe_ffn": ([I, P, P, LL, I, P, LL, LL, P, P, I, I, P, I, LL, I, I, P, P, P], I),
 }

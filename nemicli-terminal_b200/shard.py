@@ -27,7 +27,7 @@ import torch
 import torch.distributed as dist
 import torch.nn.functional as F
 
-from . import mmvq, moe
+from . import _lib, mmvq, moe
 from .formats import row_bytes
 from .layers import PackedExperts
 
@@ -180,6 +180,19 @@ class ExpertShardedMoE:
         dev = x.device
         P = L * k
         pair_e = idx.reshape(-1).to(torch.int64)
+        if _lib.on_gpu(x):                       # two kernels (qmv_expert_dispatch), same layout as below
+            xin = x if x.dtype in (torch.float32, torch.bfloat16) else x.float()
+            xin = xin.contiguous()
+            ids = pair_e.to(dev).contiguous()
+            send = torch.empty(self.world * P, self.dim + self._ID, dtype=torch.float32, device=dev)
+            slot = torch.empty(P, dtype=torch.int64, device=dev)
+            sent = torch.empty(self.world, dtype=torch.int32, device=dev)
+            _lib.check(_lib.load().qmv_expert_dispatch(_lib.ptr(ids), L, k, self.n_exp, self.world, _lib.ptr(xin),
+                                                       int(xin.dtype == torch.float32), self.dim, _lib.ptr(send),
+                                                       self.dim + self._ID, _lib.ptr(slot), _lib.ptr(sent),
+                                                       _lib.stream_ptr(dev)), "qmv_expert_dispatch")
+            self.last_sent = sent
+            return self._a2a(send), slot
         # an id outside [0, n_exp) goes to rank 0 as local id -2: the owner's kernels refuse it (zero rows and
         # the device status bit, as the single-GPU path does) and its weight adds nothing
         valid = (pair_e >= 0) & (pair_e < self.n_exp)
@@ -226,6 +239,13 @@ class ExpertShardedMoE:
         L, k = idx.shape
         recv, slot = self.dispatch(x, idx)
         y_back = self._a2a(self.compute(recv).contiguous())
+        if _lib.on_gpu(y_back):                  # one kernel (qmv_expert_combine), the order of combine()
+            wf = w.reshape(-1).to(device=y_back.device, dtype=torch.float32).contiguous()
+            out = torch.empty(L, self.dim, dtype=torch.float32, device=y_back.device)
+            _lib.check(_lib.load().qmv_expert_combine(_lib.ptr(y_back), self.dim, _lib.ptr(slot), _lib.ptr(wf), L, k,
+                                                      self.dim, _lib.ptr(out), _lib.stream_ptr(y_back.device)),
+                       "qmv_expert_combine")
+            return out
         return combine(y_back[slot].view(L, k, self.dim), w)
 
 

@@ -54,3 +54,45 @@ def test_two_nccl_ranks(tmp_path):
     for r in range(world):
         status = (tmp_path / f"rank{r}.txt").read_text()
         assert status == "ok", f"rank {r}:\n{status}"
+
+
+def test_exchange_kernels_match_the_tensor_path(cuda):
+    """qmv_expert_dispatch / qmv_expert_combine give the layout and the sums of the tensor-operation path
+    of ExpertShardedMoE (4 owners, ids out of range, bf16 input), bit for bit."""
+    from nemicli_terminal_b200 import _lib, shard
+    n_tok, k, n_exp, world, dim = 5, 3, 10, 4, 64
+    g = torch.Generator().manual_seed(3)
+    ids = torch.randint(0, n_exp, (n_tok, k), generator=g)
+    ids[1, 2], ids[3, 0] = -1, n_exp + 3
+    x = torch.randn(n_tok, dim, generator=g).to(torch.bfloat16)
+    P = n_tok * k
+    # the tensor path (shard.ExpertShardedMoE.dispatch on a CPU tensor)
+    pe = ids.reshape(-1)
+    valid = (pe >= 0) & (pe < n_exp)
+    dest = torch.where(valid, shard.owner_of(pe.clamp(0, n_exp - 1), n_exp, world), torch.zeros_like(pe))
+    onehot = (dest[:, None] == torch.arange(world)[None, :]).to(torch.int64)
+    pos = (onehot.cumsum(0) - 1).gather(1, dest[:, None]).squeeze(1)
+    slot_ref = dest * P + pos
+    lo = torch.tensor([shard.shard_range(n_exp, world, r)[0] for r in range(world)])
+    id_ref = torch.full((world * P,), -1.0)
+    id_ref[slot_ref] = torch.where(valid, pe - lo[dest], torch.full_like(pe, -2)).float()
+    lib = _lib.load()
+    send = torch.full((world * P, dim + 4), 7.0, device=cuda)
+    slot = torch.empty(P, dtype=torch.int64, device=cuda)
+    sent = torch.empty(world, dtype=torch.int32, device=cuda)
+    idc, xc = ids.reshape(-1).to(cuda), x.to(cuda)
+    _lib.check(lib.qmv_expert_dispatch(_lib.ptr(idc), n_tok, k, n_exp, world, _lib.ptr(xc), 0, dim, _lib.ptr(send),
+                                       dim + 4, _lib.ptr(slot), _lib.ptr(sent), _lib.stream_ptr(cuda)), "dispatch")
+    send = send.cpu()
+    assert torch.equal(slot.cpu(), slot_ref)
+    assert torch.equal(send[:, dim], id_ref)
+    assert torch.equal(sent.cpu().long(), onehot.sum(0))
+    assert torch.equal(send[slot_ref, :dim], x.float()[torch.arange(P) // k])
+    assert torch.count_nonzero(send[slot_ref, dim + 1:]) == 0
+    y = torch.randn(world * P, dim, generator=g)
+    w = torch.rand(n_tok, k, generator=g)
+    out = torch.empty(n_tok, dim, device=cuda)
+    yc, wc, sc = y.to(cuda), w.to(cuda), slot_ref.to(cuda)
+    _lib.check(lib.qmv_expert_combine(_lib.ptr(yc), dim, _lib.ptr(sc), _lib.ptr(wc), n_tok, k, dim, _lib.ptr(out),
+                                      _lib.stream_ptr(cuda)), "combine")
+    assert torch.equal(out.cpu(), shard.combine(y[slot_ref].view(n_tok, k, dim), w))
