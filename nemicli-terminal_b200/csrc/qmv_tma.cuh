@@ -311,18 +311,21 @@ struct UnitSums<F_Q4_K> {
 template <>
 struct UnitSums<F_Q5_K> : UnitSums<F_Q4_K> {};
 
-// 6-bit scales / mins of sub-blocks 2p, 2p + 1 from a K-quant header word hd (quant.py:99-108), four per
-// word; no branch on p
+// 6-bit scales / mins of sub-blocks 2p, 2p + 1 from a K-quant header word hd (quant.py:99-108): the two
+// scale bytes and the two min bytes of the pair gathered by byte permutes (sub-blocks 0..3: low 6 bits of
+// bytes j and j + 4 of the 12; 4..7: the nibbles of byte j + 4 with the top two bits of bytes j - 4 and
+// j), no branch on p
 __device__ __forceinline__ void kquant_scales(const uint4& hd, int p, int (&isc)[2], uint32_t (&imn)[2]) {
-    const uint32_t sc_lo = hd.y & 0x3F3F3F3Fu, m_lo = hd.z & 0x3F3F3F3Fu;
-    const uint32_t sc_hi = (hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u);
-    const uint32_t m_hi = ((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u);
-    const uint32_t scw = p < 2 ? sc_lo : sc_hi, mw = p < 2 ? m_lo : m_hi;
-    const int sh = 16 * (p & 1);
-    isc[0] = int((scw >> sh) & 0xFFu);
-    isc[1] = int((scw >> (sh + 8)) & 0xFFu);
-    imn[0] = (mw >> sh) & 0xFFu;
-    imn[1] = (mw >> (sh + 8)) & 0xFFu;
+    const uint32_t b = 2u * uint32_t(p & 1);                            // first byte of the pair in its word
+    const uint32_t yz = __byte_perm(hd.y, hd.z, b | ((b + 1) << 4) | ((b + 4) << 8) | ((b + 5) << 12));
+    const uint32_t ww = __byte_perm(hd.w, 0u, b | ((b + 1) << 4) | (b << 8) | ((b + 1) << 12));
+    const uint32_t lo = yz & 0x3F3F3F3Fu;
+    const uint32_t hi = (ww & 0x00000F0Fu) | ((ww >> 4) & 0x0F0F0000u) | ((yz >> 2) & 0x30303030u);
+    const uint32_t pk = p < 2 ? lo : hi;                                // [sc0, sc1, m0, m1]
+    isc[0] = int(pk & 0xFFu);
+    isc[1] = int((pk >> 8) & 0xFFu);
+    imn[0] = (pk >> 16) & 0xFFu;
+    imn[1] = pk >> 24;
 }
 
 // unsigned 6-bit codes of a Q6_K unit (w[g][i]: 4 codes of group g, positions 16h + 4i..): group g's low
