@@ -31,7 +31,7 @@ namespace qmv {
 constexpr int kTcRows = 128;               // weight rows per CTA tile (MMA M)
 constexpr int kTcK = 64;                   // K values per step
 constexpr int kTcMaxN = 128;               // tokens per launch
-constexpr int kTcThreads = 128;
+constexpr int kTcThreads = 256;            // two threads per weight row
 constexpr int kTcStageA = kTcRows * kTcK * 2;    // 16 KB
 constexpr int kTcStageB = kTcMaxN * kTcK * 2;    // 16 KB
 constexpr int kTcSmem = 2 * (kTcStageA + kTcStageB) + 64;    // at N = 128; a launch takes 2 (A + N 128 B) + 64
@@ -127,30 +127,30 @@ __global__ void __launch_bounds__(256) tc_input_kernel(const void* __restrict__ 
 // ---- one thread's row of a K step: raw bytes (loaded a step ahead), then 64 fp16 values --------
 
 template <int FMT> struct TcRaw;
-// Q4_K: the 16-byte header and the 32 qs bytes of sub-blocks 2p (low nibbles) and 2p + 1 (high nibbles)
+// Thread half hf of a row takes k-cores 2 hf, 2 hf + 1 of each 32-value half of the step (values
+// 16 hf .. 16 hf + 15 of each).
+// Q4_K: the 16-byte header and qs bytes 32 p + 16 hf .. + 15 (their low nibbles: sub-block 2p, high: 2p + 1)
 template <> struct TcRaw<F_Q4_K> {
-    uint4 hd, q0, q1;
-    __device__ __forceinline__ void load(const uint8_t* row, int c) {
+    uint4 hd, q;
+    __device__ __forceinline__ void load(const uint8_t* row, int c, int hf) {
         const uint8_t* sb = row + (c >> 2) * 144;
-        const int p = c & 3;
         hd = ldw16(sb);
-        q0 = ldw16(sb + 16 + 32 * p);
-        q1 = ldw16(sb + 32 + 32 * p);
+        q = ldw16(sb + 16 + 32 * (c & 3) + 16 * hf);
     }
 };
-// Q6_K: for half n = (c >> 1) & 1 of superblock c >> 2, groups 2h, 2h + 1 (h = c & 1): the 64 ql bytes of
-// the half, its 32 qh bytes, its 8 int8 scales and d (2-byte aligned superblocks)
+// Q6_K: for half n = (c >> 1) & 1 of superblock c >> 2 (groups 2 (c & 1), 2 (c & 1) + 1): ql bytes
+// 64 n + 16 hf .. and 64 n + 32 + 16 hf .. (16 each), qh bytes 32 n + 16 hf .., the half's 8 int8 scales
+// and d (2-byte aligned superblocks); the same bytes serve steps c and c ^ 1
 template <> struct TcRaw<F_Q6_K> {
-    uint4 l[4], h[2];
+    uint4 la, lb, hq;
     uint2 sc;
     uint32_t d;
-    __device__ __forceinline__ void load(const uint8_t* row, int c) {
+    __device__ __forceinline__ void load(const uint8_t* row, int c, int hf) {
         const uint8_t* sb = row + (c >> 2) * 210;
         const int n = (c >> 1) & 1;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) l[i] = ldw16_a2(sb + 64 * n + 16 * i);
-        h[0] = ldw16_a2(sb + 128 + 32 * n);
-        h[1] = ldw16_a2(sb + 144 + 32 * n);
+        la = ldw16_a2(sb + 64 * n + 16 * hf);
+        lb = ldw16_a2(sb + 64 * n + 32 + 16 * hf);
+        hq = ldw16_a2(sb + 128 + 32 * n + 16 * hf);
         sc = ldw8_a2(sb + 192 + 8 * n);
         d = ldw2(sb + 208);
     }
@@ -174,8 +174,8 @@ template <>
 __device__ __forceinline__ uint4 tc_unpack<F_Q4_K>(const TcRaw<F_Q4_K>& r, int, int kc, const float (&a)[2],
                                                    const float (&b)[2]) {
     const int g = kc >> 2;                              // 0: sub-block 2p (low nibbles), 1: 2p + 1 (high)
-    const int w = 2 * (kc & 3);                         // qs words w, w + 1 (bytes 8 (kc & 3) ..)
-    const uint32_t W[8] = {r.q0.x, r.q0.y, r.q0.z, r.q0.w, r.q1.x, r.q1.y, r.q1.z, r.q1.w};
+    const int w = 2 * (kc & 1);                         // the thread's qs words w, w + 1 (bytes 8 (kc & 3) ..)
+    const uint32_t W[4] = {r.q.x, r.q.y, r.q.z, r.q.w};
     const uint32_t sh = 4u * uint32_t(g);
     uint32_t o[4];
 #pragma unroll
@@ -199,16 +199,17 @@ template <>
 __device__ __forceinline__ uint4 tc_unpack<F_Q6_K>(const TcRaw<F_Q6_K>& r, int c, int kc, const float (&)[2],
                                                    const float (&)[2]) {
     const int hsel = c & 1, j = kc >> 2, G = 2 * hsel + j;
-    const int l0 = 8 * (kc & 3);                         // first l of the k-core
-    const uint32_t L[16] = {r.l[0].x, r.l[0].y, r.l[0].z, r.l[0].w, r.l[1].x, r.l[1].y, r.l[1].z, r.l[1].w,
-                            r.l[2].x, r.l[2].y, r.l[2].z, r.l[2].w, r.l[3].x, r.l[3].y, r.l[3].z, r.l[3].w};
-    const uint32_t H[8] = {r.h[0].x, r.h[0].y, r.h[0].z, r.h[0].w, r.h[1].x, r.h[1].y, r.h[1].z, r.h[1].w};
+    const int l0 = 8 * (kc & 3);                         // first l of the k-core (16 hf or 16 hf + 8)
+    const int lw0 = 2 * (kc & 1);                        // its words in the thread's 16-byte runs
+    const uint4 lsel = j ? r.lb : r.la;
+    const uint32_t L[4] = {lsel.x, lsel.y, lsel.z, lsel.w};
+    const uint32_t H[4] = {r.hq.x, r.hq.y, r.hq.z, r.hq.w};
     const float f = tc_scale_q6k(r, G, l0 >> 4);         // d * sc[l / 16 + 2 G]
     uint32_t o[4];
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-        const uint32_t lw = L[(32 * (G & 1) + l0) / 4 + i] >> (G >= 2 ? 4 : 0);
-        const uint32_t hw = H[l0 / 4 + i] >> (2 * G);
+        const uint32_t lw = L[lw0 + i] >> (G >= 2 ? 4 : 0);
+        const uint32_t hw = H[lw0 + i] >> (2 * G);
         const uint32_t q = (lw & 0x0F0F0F0Fu) | ((hw & 0x03030303u) << 4);
         float v[4];
 #pragma unroll
@@ -257,7 +258,8 @@ __global__ void __launch_bounds__(kTcThreads) tc_mm_kernel(const TcParams P) {
     const int tile = blockIdx.x / P.splits, part = blockIdx.x % P.splits;
     const int chunks = P.n_in / kTcK;
     const int c0 = int((long long)part * chunks / P.splits), c1 = int((long long)(part + 1) * chunks / P.splits);
-    const int row = tile * kTcRows + tid;
+    const int rr = tid >> 1, hf = tid & 1;                 // this thread's row of the tile and its half
+    const int row = tile * kTcRows + rr;
     const uint8_t* wrow = P.w + (long long)min(row, P.n_out - 1) * P.row_bytes;   // rows past the end: discarded
     const uint32_t cols = P.n_pad <= 32 ? 32u : P.n_pad <= 64 ? 64u : 128u;
     if (warp == 0) {
@@ -290,13 +292,13 @@ __global__ void __launch_bounds__(kTcThreads) tc_mm_kernel(const TcParams P) {
     bool dead = false;
     int issued = c0;                                     // steps whose MMAs were issued: [c0, issued)
     if (c0 < c1) {
-        raw.load(wrow, c0);
+        raw.load(wrow, c0, hf);
         load_x(c0);
     }
     // a Q6_K half serves two steps (c even, c + 1): the odd step reuses the even one's bytes
     auto next_of = [&](int c) {
         if (FMT == F_Q6_K && (c & 1)) raw_next = raw;
-        else raw_next.load(wrow, c);
+        else raw_next.load(wrow, c, hf);
     };
     if (c0 + 1 < c1) next_of(c0 + 1);
     for (int c = c0; c < c1; ++c) {
@@ -305,9 +307,12 @@ __global__ void __launch_bounds__(kTcThreads) tc_mm_kernel(const TcParams P) {
         const bool ok = c - c0 < 2 || mbar_wait(bar0 + 8 * s, uint32_t(use - 1) & 1u);
         float a[2], b[2];
         tc_scales(raw, c, a, b);
-        const uint32_t arow = sa[s] + uint32_t((tid >> 3) * 1024 + (tid & 7) * 16);
+        const uint32_t arow = sa[s] + uint32_t((rr >> 3) * 1024 + (rr & 7) * 16);
 #pragma unroll
-        for (int kc = 0; kc < 8; ++kc) sts128(arow + kc * 128, tc_unpack<FMT>(raw, c, kc, a, b));
+        for (int i = 0; i < 4; ++i) {                       // k-cores 2 hf, 2 hf + 1, 4 + 2 hf, 5 + 2 hf
+            const int kc = (i >> 1) * 4 + 2 * hf + (i & 1);
+            sts128(arow + kc * 128, tc_unpack<FMT>(raw, c, kc, a, b));
+        }
 #pragma unroll
         for (int i = 0; i < kBPer; ++i) {
             const int j = tid + kTcThreads * i, n = j >> 3, kc = j & 7;
@@ -345,11 +350,13 @@ __global__ void __launch_bounds__(kTcThreads) tc_mm_kernel(const TcParams P) {
     if (dead || fail || issued == c0) {
         if (tid == 0 && P.status) atomicOr(P.status, DEV_TIMEOUT);
     } else {
-        const int r = tile * kTcRows + 32 * warp + lane;
+        // warp w reads lanes 32 (w & 3) .. (its quadrant) and the columns of half w >> 2
+        const int quad = warp & 3, half_cols = P.n_pad / 2;
+        const int r = tile * kTcRows + 32 * quad + lane;
         float* dst = P.splits > 1 ? P.part + (long long)part * P.n_tok * P.n_out : P.y;
-        for (int col = 0; col < P.n_pad; col += 8) {
+        for (int col = (warp >> 2) * half_cols; col < (warp >> 2) * half_cols + half_cols; col += 8) {
             float v[8];
-            tc_ld8(tmem + (uint32_t(32 * warp) << 16) + uint32_t(col), v);
+            tc_ld8(tmem + (uint32_t(32 * quad) << 16) + uint32_t(col), v);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const int t = col + j;
@@ -369,10 +376,11 @@ __global__ void __launch_bounds__(kTcThreads) tc_mm_kernel(const TcParams P) {
         __syncthreads();
         if (s_last) {
             __threadfence();
-            // row per thread, 8 tokens at a time: 8 independent loads per part in flight
-            const int r = tile * kTcRows + tid;
+            // row per thread (two threads a row: alternate blocks of 8 tokens), 8 independent loads per
+            // part in flight
+            const int r = tile * kTcRows + (tid & (kTcRows - 1));
             if (r < P.n_out) {
-                for (int t0 = 0; t0 < P.n_tok; t0 += 8) {
+                for (int t0 = 8 * (tid / kTcRows); t0 < P.n_tok; t0 += 8 * (kTcThreads / kTcRows)) {
                     float v[8];
 #pragma unroll
                     for (int j = 0; j < 8; ++j) v[j] = 0.f;

@@ -217,12 +217,16 @@ def _eingang(x2: torch.Tensor) -> Eingang:
 
 
 TC_FORMATE = ("Q4_K", "Q6_K")                # formats of the tensor-core tile path (the reference's MMQ)
-TC_FROM = 48                                 # tokens from which the tile path beats the int8 kernels (measured)
+TC_FROM = 48                                 # tokens from which the tile path beats the int8 kernels (measured),
+TC_FROM_LARGE = 32                           # ... and for matrices of at least TC_LARGE weights
+TC_LARGE = 32 * 2 ** 20
 
 
-def tc_used(fmt: str, n_tok: int) -> bool:
-    """Whether mm runs n_tok tokens of fmt on the tensor-core tile path."""
-    return fmt in TC_FORMATE and n_tok >= TC_FROM
+def tc_used(fmt: str, n_tok: int, n_out: int = 0, n_in: int = 0) -> bool:
+    """Whether mm runs n_tok tokens of fmt (an n_out x n_in matrix) on the tensor-core tile path."""
+    if fmt not in TC_FORMATE:
+        return False
+    return n_tok >= (TC_FROM_LARGE if n_out * n_in >= TC_LARGE else TC_FROM)
 
 
 def mm(fmt: str, raw: torch.Tensor, x: torch.Tensor, n_out: int, n_in: int) -> torch.Tensor:
@@ -231,7 +235,7 @@ def mm(fmt: str, raw: torch.Tensor, x: torch.Tensor, n_out: int, n_in: int) -> t
     fewer tokens, the other formats and an Eingang input to the int8 kernels (faster there, and within
     the same tolerance of the exact product)."""
     _check_raw(fmt, raw, n_out, n_in)
-    if not _ist_eingang(x) and tc_used(fmt, x.reshape(-1, n_in).shape[0]):
+    if not _ist_eingang(x) and tc_used(fmt, x.reshape(-1, n_in).shape[0], n_out, n_in):
         return mm_tc(fmt, raw, x, n_out, n_in)
     x2 = x.reshape(-1, n_in)
     e = _eingang(x2)

@@ -161,7 +161,7 @@ def test_mm_long_inputs(cuda, fmt, n_out, n_in, M):
     y = mmvq.mm(fmt, raw, x, n_out, n_in)
     assert y.shape == (M, n_out)
     xc = x.cpu()
-    if mmvq.tc_used(fmt, M):             # the tensor-core tile path: the reference MMQ's fp16 arithmetic
+    if mmvq.tc_used(fmt, M, n_out, n_in):  # the tensor-core tile path: the reference MMQ's fp16 arithmetic
         yc = O.mmq(fmt, raw.cpu().numpy(), n_out, n_in, xc.numpy())
         assert O.max_rel(y.cpu().numpy(), yc) < 2e-5
     else:
