@@ -38,6 +38,43 @@ __device__ __forceinline__ void quantize_group(float v, long long i, int8_t* __r
     }
 }
 
+// One group of 32 values on 8 lanes (an aligned eighth of a warp): lane m holds values m, m+8, m+16
+// and m+24 of the group starting at value i0 in v[0..3].  The arithmetic of quantize_group: the group
+// maximum in any order (exact), and the fp32 sum in the butterfly order of warp_sum as lane 0 forms it,
+// (v_m + v_m+16) + (v_m+8 + v_m+24) in the lane, then xor 4, 2, 1 across the eight lanes.  Stores only
+// if `store` (the shuffles run in every lane).
+__device__ __forceinline__ void quantize_group8(const float (&v)[4], long long i0, bool store,
+                                                int8_t* __restrict__ xq, int8_t* __restrict__ xq2,
+                                                float* __restrict__ xd, float* __restrict__ xs) {
+    float a = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    float s = (v[0] + v[2]) + (v[1] + v[3]);
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+        a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+        s += __shfl_xor_sync(0xffffffffu, s, o);
+    }
+    const float d = __fdiv_rn(a, 127.0f);
+    const float d2 = __fdiv_rn(d, 254.0f);
+    const int m = threadIdx.x & 7;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        int q = 0, q2 = 0;
+        if (d > 0.f) {
+            q = __float2int_rn(__fdiv_rn(v[k], d));
+            const float r = __fmaf_rn(-float(q), d, v[k]);
+            q2 = max(-127, min(127, __float2int_rn(__fdiv_rn(r, d2))));
+        }
+        if (store) {
+            xq[i0 + m + 8 * k] = int8_t(q);
+            xq2[i0 + m + 8 * k] = int8_t(q2);
+        }
+    }
+    if (store && m == 0) {
+        xd[i0 >> 5] = d;
+        xs[i0 >> 5] = s;
+    }
+}
+
 static __global__ void __launch_bounds__(256) quant_q8_kernel(const void* __restrict__ x, int x_f32,
                                                        int8_t* __restrict__ xq, int8_t* __restrict__ xq2,
                                                        float* __restrict__ xd, float* __restrict__ xs,

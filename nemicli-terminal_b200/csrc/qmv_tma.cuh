@@ -286,11 +286,13 @@ __device__ __forceinline__ void load_act(Act<FMT>& a, int u, const int8_t* xq, c
                    h3 = ldq8<GLOBAL>(xq2 + o + 96);
         a.q[0] = make_int4(g0.x, g0.y, g1.x, g1.y); a.q[1] = make_int4(g2.x, g2.y, g3.x, g3.y);
         a.r[0] = make_int4(h0.x, h0.y, h1.x, h1.y); a.r[1] = make_int4(h2.x, h2.y, h3.x, h3.y);
+        // a.d[g] carries 4^-g (exact): unit_dot takes group g's codes in place, 4^g times their value;
+        // a.s[0] the four groups' xs (applied by one lane of the four that share the groups)
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-            a.d[g] = ldf<GLOBAL, SCALES>(xd, b * 8 + 4 * n + g) * kInv254;
-            if (j == 0) a.s[g] = ldf<GLOBAL, SCALES>(xs, b * 8 + 4 * n + g);
-        }
+        for (int g = 0; g < 4; ++g) a.d[g] = ldf<GLOBAL, SCALES>(xd, b * 8 + 4 * n + g) * (kInv254 / float(1 << (2 * g)));
+        if (j == 0)
+            a.s[0] = (ldf<GLOBAL, SCALES>(xs, b * 8 + 4 * n) + ldf<GLOBAL, SCALES>(xs, b * 8 + 4 * n + 1)) +
+                     (ldf<GLOBAL, SCALES>(xs, b * 8 + 4 * n + 2) + ldf<GLOBAL, SCALES>(xs, b * 8 + 4 * n + 3));
     }
 }
 
@@ -709,6 +711,25 @@ __device__ __forceinline__ float unit_dot(uint32_t rs, int u, const Act<FMT>& a,
             acc = fmaf(wsc * a.d[g], float(254 * s_ + t_ - a.kk[g]), acc);
         }
         return acc;
+    } else if constexpr (FMT == F_TQ2_0) {
+        // d * (sum_g (xd_g / 254) (254 S_g + S2_g) - sum_g xs_g), codes c - 1 (quant.py:417-421): group g's
+        // codes are bits 2g, 2g + 1 of each byte, masked in place (4^g times the code, exact in the int32
+        // sums; a.d[g] carries the 4^-g)
+        const int b = u >> 3, q = u & 7, n = q >> 2, j = q & 3;
+        const uint32_t sb = rs + b * 66;
+        const uint2 c = lds8_a2(sb + 32 * n + 8 * j);
+        const float d = h2f(lds16u(sb + 64));
+        const int xq[8] = {a.q[0].x, a.q[0].y, a.q[0].z, a.q[0].w, a.q[1].x, a.q[1].y, a.q[1].z, a.q[1].w};
+        const int xr[8] = {a.r[0].x, a.r[0].y, a.r[0].z, a.r[0].w, a.r[1].x, a.r[1].y, a.r[1].z, a.r[1].w};
+        float t = -a.s[0];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            const uint32_t m = 0x03030303u << (2 * g), c0 = c.x & m, c1 = c.y & m;
+            const int s_ = dp4us(c1, xq[2 * g + 1], dp4us(c0, xq[2 * g], 0));
+            const int u_ = dp4us(c1, xr[2 * g + 1], dp4us(c0, xr[2 * g], 0));
+            t = fmaf(a.d[g], float(254 * s_ + u_), t);
+        }
+        return d * t;
     } else if constexpr (FMT == F_Q4_K || FMT == F_Q5_K) {
         // d * sum_k sc_k * (254 S_k + S2_k) * xd_k / 254  -  dmin * sum_k m_k * xs_k
         const float w = float(o.isc[0] * (254 * o.s[0] + o.u[0])) * a.d[0]
@@ -865,10 +886,26 @@ __global__ void __launch_bounds__(32 * (NCW + 1), NCW <= 8 ? 2 : 1) mv_tma_kerne
         int8_t* wq2 = wq + P.n_in;
         float* wd = reinterpret_cast<float*>(wq2 + P.n_in);
         float* ws = wd + P.n_in / 32;
-        for (int grp = warp; grp < P.n_in / 32; grp += NCW) {
-            const int i = 32 * grp + lane;
-            const float v = XF == 1 ? static_cast<const float*>(P.x)[i] : bf2f(static_cast<const uint16_t*>(P.x)[i]);
-            quantize_group(v, i, wq, wq2, wd, ws);
+        // a group on each eighth of a warp, QB rounds of a warp's loads in flight before their groups
+        constexpr int QB = 4;
+        const int n_grp = P.n_in / 32;
+        const int eighth = lane >> 3, m = lane & 7;
+        for (int g0 = warp * 4 * QB; g0 < n_grp; g0 += NCW * 4 * QB) {
+            float v[QB][4];
+#pragma unroll
+            for (int b = 0; b < QB; ++b) {
+                const int grp = min(g0 + 4 * b + eighth, n_grp - 1);      // past the end: a copy, not stored
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int i = 32 * grp + m + 8 * k;
+                    v[b][k] = XF == 1 ? static_cast<const float*>(P.x)[i] : bf2f(static_cast<const uint16_t*>(P.x)[i]);
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < QB; ++b) {
+                const int grp = g0 + 4 * b + eighth;
+                quantize_group8(v[b], 32LL * grp, grp < n_grp, wq, wq2, wd, ws);
+            }
         }
         named_sync(kConsumerBarrier, 32 * NCW);
         sxq = wq; sxq2 = wq2; sxd = wd; sxs = ws;

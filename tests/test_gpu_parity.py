@@ -89,6 +89,48 @@ def test_input_forms_agree(cuda, fmt):
     assert O.max_rel(yb16, yb[0]) < TOL_B
 
 
+@pytest.mark.parametrize("fmt,n_in", [("Q8_0", 256), ("Q8_0", 4352), ("Q4_0", 14336 + 256), ("Q4_K", 14336),
+                                       ("IQ2_XXS", 14336), ("TQ2_0", 10240)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_fused_quantisation_equals_eingang(cuda, fmt, n_in, dtype):
+    """The one-token kernel quantises the row itself, a group on each eighth of a warp (the last round
+    of a warp partly past the row's end): bit-identical to the separate quantiser's input.  Rows past
+    FUSED_MAX_IN are forced onto the fused kernel (mv takes the separate quantiser there)."""
+    n_out = 512
+    raw = synth.blocks(fmt, n_out, n_in, seed=n_in, device=cuda)
+    x = synth.activations(1, n_in, seed=5, device=cuda)[0].to(dtype)
+    fused = mmvq._fused(fmt, [(raw, n_out)], x, n_in, force=True)
+    assert fused is not None                      # rows of a multiple of 16 bytes: the staged kernel
+    fused = fused[0]
+    assert torch.equal(fused, mmvq.mv(fmt, raw, mmvq.Eingang(x), n_out, n_in))
+    assert torch.equal(mmvq.mv(fmt, raw, x, n_out, n_in), fused)
+
+
+def test_fused_quantisation_ties(cuda):
+    """Values exactly on the half-way points of the 8-bit steps (group maximum 15.875, so the step d
+    is 1/8 and v = (k + 1/2) / 8 divides to a tie), their fp32 neighbours, the steps themselves, all-zero
+    groups and groups with one nonzero value: the fused kernel's input equals the separate quantiser's."""
+    n_in, n_out = 4096, 256
+    k = torch.arange(-127, 127, dtype=torch.float32)
+    half = (k + 0.5) / 8
+    vals = torch.cat([half, torch.nextafter(half, torch.tensor(16.0)), torch.nextafter(half, torch.tensor(-16.0)),
+                      k / 8])
+    x = torch.zeros(n_in)
+    n_full = (vals.numel() + 30) // 31
+    for g in range(n_full):
+        part = vals[31 * g: 31 * g + 31]
+        x[32 * g: 32 * g + part.numel()] = part
+        x[32 * g + 31] = 15.875 if g % 2 else -15.875
+    for g in range(n_full + 8, n_in // 32, 2):               # one nonzero value; the others stay zero groups
+        x[32 * g + g % 32] = 1e-3 * (g - 60)
+    xc = x.to(cuda)
+    raw = synth.blocks("Q8_0", n_out, n_in, seed=9, device=cuda)
+    e = mmvq.Eingang(xc)
+    assert int((e.xd[:n_full].cpu() == 0.125).sum()) == n_full
+    fused = mmvq._fused("Q8_0", [(raw, n_out)], xc, n_in, force=True)[0]
+    assert torch.equal(fused, mmvq.mv("Q8_0", raw, e, n_out, n_in))
+
+
 @pytest.mark.parametrize("key", GKEYS)
 def test_golden_fixtures_on_gpu(cuda, key):
     t, rows, cols = (int(v) for v in GOLDEN[key + "__shape"])
