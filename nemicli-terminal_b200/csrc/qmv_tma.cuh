@@ -656,13 +656,15 @@ __device__ __forceinline__ void unit_sums(uint32_t rs, int u, const Act<FMT>& a,
         uint32_t w[8];
 #pragma unroll
         for (int l = 0; l < 4; ++l) {
-            const uint2 g = grid[(ax.x >> (8 * l)) & 0xFFu];
+            const uint2 g = grid[__byte_perm(ax.x, 0u, 0x4440u + l)];      // byte l of the index word
             const uint32_t s7 = (ax.y >> (7 * l)) & 127u;
-            const uint32_t s8 = s7 | (uint32_t(__popc(s7) & 1) << 7);
-            const uint32_t mlo = (((s8 & 15u) * 0x00204081u) & 0x01010101u) * 0xFFu;
-            const uint32_t mhi = (((s8 >> 4) * 0x00204081u) & 0x01010101u) * 0xFFu;
-            w[2 * l] = __vsub4(g.x ^ mlo, mlo);
-            w[2 * l + 1] = __vsub4(g.y ^ mhi, mhi);
+            const uint32_t s8 = s7 | ((uint32_t(__popc(s7)) << 7) & 0x80u);   // eighth sign: even parity
+            // one bit per byte, then a negated byte as (g ^ 0xFF) + 1: the magnitudes are 8, 25 or 43,
+            // so the +1 never carries into the next byte
+            const uint32_t nlo = ((s8 & 15u) * 0x00204081u) & 0x01010101u;
+            const uint32_t nhi = ((s8 >> 4) * 0x00204081u) & 0x01010101u;
+            w[2 * l] = (g.x ^ (nlo * 0xFFu)) + nlo;
+            w[2 * l + 1] = (g.y ^ (nhi * 0xFFu)) + nhi;
         }
         const uint32_t w0[4] = {w[0], w[1], w[2], w[3]}, w1[4] = {w[4], w[5], w[6], w[7]};
         o.s[0] = dot4(w1, a.q[1]) + dot4(w0, a.q[0]);
