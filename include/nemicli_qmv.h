@@ -151,6 +151,16 @@ int qmv_mv_multi(int ggml_type, int n_jobs, const uint8_t* const* w, const int* 
 int qmv_mv_x(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
              const void* x, int x_is_f32, void* stream);
 
+/* Single token, RMS norm fused in front: qmv_norm_q8 (h, r, rs, h_out, norm_w, eps; n = n_in) followed by
+ * qmv_mv_multi on its activation input, in one launch.  The quantised input is bit-identical to
+ * qmv_norm_q8's (the same order of the sum of squares and the same roundings), so are the outputs; xn is
+ * not written.  h_out (given with r) is written once.  Returns QMV_ERR_SHAPE for a row length the staged
+ * kernel does not take (then call qmv_norm_q8 and qmv_mv_multi).  Replaces: norm_q8 + the mv calls on
+ * its Eingang in the reference's one-token step (ggufengine/models/baukasten.py:205-240,
+ * ggufengine/mmvq.py:946-956). */
+int qmv_mv_norm(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
+                const float* h, const float* r, float rs, float* h_out, const float* norm_w, float eps, void* stream);
+
 /* ---- fused producers of the activation input (one token) and unpacking --------------------------- */
 
 /* RMS norm of one row and its activation input: v = h (+ rs * r, written to h_out when r is given),
@@ -177,10 +187,12 @@ int qmv_act_q8(const float* g, const float* u, int gelu, float* a, int8_t* xq, i
  * models/common.py:456-460, and QuantLinear.bf16_weight, qlinear.py:217). */
 int qmv_unpack(int ggml_type, const uint8_t* w, long long n_values, void* out, int out_dtype, void* stream);
 
-/* Programmatic dependent launch for the staged single-token kernels (default off): when on, each such
- * kernel lets the next kernel of the stream start early and streams its weights before the previous
- * kernel has finished; its inputs are read only after the previous kernel completed.  Turn it on only
- * when no kernel launched right before a matvec writes that matvec's weights.  Returns the old value.
+/* Programmatic dependent launch for the staged single-token kernels and the activation producers
+ * (qmv_quant_q8, qmv_norm_q8, qmv_act_q8) (default off): when on, each such kernel lets the next kernel
+ * of the stream start early; a matvec streams its weights before the previous kernel has finished, and
+ * every kernel reads its inputs and writes anything only after the previous kernel completed.  Turn it
+ * on only when no kernel launched right before a matvec writes that matvec's weights.  Returns the old
+ * value.
  * Replaces: nothing in the reference (its decoder relies on plain stream order, models/common.py:1185). */
 int qmv_set_pdl(int enabled);
 

@@ -11,39 +11,56 @@ using namespace qmv;
 
 namespace {
 
-constexpr int kNormThreads = 1024;
+constexpr int kNormThreads = 1024;       // threads of the sum's order (see norm_q8_kernel)
+constexpr int kNormBlock = 256;          // threads of a CTA
 
-// RMS norm of one row in one CTA (ggufengine/mmvq.py:100-118): v = h (+ rs r, written to hout),
-// xn = v * rsqrt(mean(v^2) + eps) * w, quantised per 32 values into the activation input.
-__global__ void __launch_bounds__(kNormThreads) norm_q8_kernel(const float* __restrict__ h, const float* __restrict__ r,
-                                                               float rs, float* __restrict__ hout,
-                                                               const float* __restrict__ w, float eps,
-                                                               float* __restrict__ xn, int8_t* __restrict__ xq,
-                                                               int8_t* __restrict__ xq2, float* __restrict__ xd,
-                                                               float* __restrict__ xs, int n) {
+// RMS norm of one row (ggufengine/mmvq.py:100-118): v = h (+ rs r, written to hout),
+// xn = v * rsqrt(mean(v^2) + eps) * w, quantised per 32 values into the activation input.  The sum of
+// v^2 has one fixed order, that of 1024 threads where thread t adds v[t], v[t + 1024], ... with fmaf,
+// then a warp sum per 32 of them and a warp sum of the 32 results (the order the fused form in the
+// staged matvec follows too).  Every CTA forms that sum over the whole row (the row is a few KB, read
+// from L2) and then normalises and quantises its own 256 values, one group per warp: no single CTA
+// walks the row alone.
+__global__ void __launch_bounds__(kNormBlock) norm_q8_kernel(const float* __restrict__ h, const float* __restrict__ r,
+                                                             float rs, float* __restrict__ hout,
+                                                             const float* __restrict__ w, float eps,
+                                                             float* __restrict__ xn, int8_t* __restrict__ xq,
+                                                             int8_t* __restrict__ xq2, float* __restrict__ xd,
+                                                             float* __restrict__ xs, int n) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // the next matvec may stream weights
+    asm volatile("griddepcontrol.wait;" ::: "memory");                // inputs and outputs after the previous kernel
     __shared__ float red[32];
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        float v = h[i];
-        if (r) {
-            v = __fadd_rn(v, __fmul_rn(rs, r[i]));
-            hout[i] = v;
-        }
-        ss = __fmaf_rn(v, v, ss);
+    constexpr int K = kNormThreads / kNormBlock;       // order threads per thread: t = p + kNormBlock k
+    const int p = threadIdx.x, warp = p >> 5, lane = p & 31;
+    float ss[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) ss[k] = 0.f;
+    for (int i0 = 0; i0 < n; i0 += 4 * kNormThreads) {             // four of each thread's terms in flight
+        float v[4][K];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                const int i = i0 + kNormThreads * q + p + kNormBlock * k;
+                v[q][k] = i < n ? (r ? __fadd_rn(h[i], __fmul_rn(rs, r[i])) : h[i]) : 0.f;
+            }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int k = 0; k < K; ++k)
+                if (i0 + kNormThreads * q + p + kNormBlock * k < n) ss[k] = __fmaf_rn(v[q][k], v[q][k], ss[k]);
     }
-    ss = warp_sum(ss);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    if (lane == 0) red[warp] = ss;
-    __syncthreads();
-    if (warp == 0) {
-        ss = warp_sum(lane < nw ? red[lane] : 0.f);
-        if (lane == 0) red[0] = ss;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {                      // order warp (p + kNormBlock k) / 32 = warp + 8 k
+        const float t = warp_sum(ss[k]);
+        if (lane == 0) red[warp + (kNormBlock / 32) * k] = t;
     }
     __syncthreads();
-    const float inv = rsqrtf(red[0] / float(n) + eps);
-    for (int g = warp; g < n / 32; g += nw) {
-        const int i = 32 * g + lane;
+    const float inv = rsqrtf(warp_sum(red[lane]) / float(n) + eps);
+    const int i = blockIdx.x * kNormBlock + p;
+    if (i - lane < n) {                                // the whole warp (n % 32 == 0)
         const float v = r ? __fadd_rn(h[i], __fmul_rn(rs, r[i])) : h[i];
+        if (r) hout[i] = v;
         const float x = __fmul_rn(__fmul_rn(v, inv), w[i]);
         xn[i] = x;
         quantize_group(x, i, xq, xq2, xd, xs);
@@ -56,6 +73,8 @@ __global__ void __launch_bounds__(256) act_q8_kernel(const float* __restrict__ g
                                                      float* __restrict__ a, int8_t* __restrict__ xq,
                                                      int8_t* __restrict__ xq2, float* __restrict__ xd,
                                                      float* __restrict__ xs, int n) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if ((i & ~31) >= n) return;                       // whole warps: n % 32 == 0
     const float x = g[i];
@@ -102,9 +121,8 @@ int qmv_norm_q8(const float* h, const float* r, float rs, float* h_out, const fl
     if (!h || !w || !xn || !xq || !xq2 || !xd || !xs || (r && !h_out)) return ST_NULL;
     if (n <= 0 || n % 32) return ST_BAD_SHAPE;
     if (!aligned(xq, 16) || !aligned(xq2, 16) || !aligned(xd, 4) || !aligned(xs, 4)) return ST_BAD_ALIGN;
-    norm_q8_kernel<<<1, kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(h, r, rs, h_out, w, eps, xn, xq, xq2,
-                                                                              xd, xs, n);
-    return launched();
+    return launch_pdl(norm_q8_kernel, dim3((n + kNormBlock - 1) / kNormBlock), dim3(kNormBlock),
+                      static_cast<cudaStream_t>(stream), h, r, rs, h_out, w, eps, xn, xq, xq2, xd, xs, n);
 }
 
 int qmv_act_q8(const float* g, const float* u, int gelu, float* a, int8_t* xq, int8_t* xq2, float* xd, float* xs,
@@ -112,8 +130,8 @@ int qmv_act_q8(const float* g, const float* u, int gelu, float* a, int8_t* xq, i
     if (!g || !a || !xq || !xq2 || !xd || !xs) return ST_NULL;
     if (n <= 0 || n % 32) return ST_BAD_SHAPE;
     if (!aligned(xq, 16) || !aligned(xq2, 16) || !aligned(xd, 4) || !aligned(xs, 4)) return ST_BAD_ALIGN;
-    act_q8_kernel<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(g, u, gelu, a, xq, xq2, xd, xs, n);
-    return launched();
+    return launch_pdl(act_q8_kernel, dim3((n + 255) / 256), dim3(256), static_cast<cudaStream_t>(stream), g, u, gelu,
+                      a, xq, xq2, xd, xs, n);
 }
 
 int qmv_unpack(int ggml_type, const uint8_t* w, long long n_values, void* out, int out_dtype, void* stream) {

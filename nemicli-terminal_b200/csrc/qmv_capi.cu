@@ -164,9 +164,17 @@ int launch_tma(int fmt, TmaParams& P, const TmaPlan& pl, cudaStream_t st) {
 
 // dense jobs sharing one activation row (n_jobs <= kMaxJobs): pre-quantised (x == nullptr) or raw x
 // (x_kind 1 = fp32, 2 = bf16) quantised in the kernel.  false -> the caller uses the fallback kernel.
+struct NormIn {                  // fused RMS norm of an fp32 x (TmaParams nr .. neps)
+    const float* r;
+    float rs;
+    float* h_out;
+    const float* w;
+    float eps;
+};
+
 bool tma_dense(int fmt, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
                const int8_t* xq, const int8_t* xq2, const float* xd, const float* xs, const void* x, int x_kind,
-               int32_t* s, int32_t* s2, cudaStream_t st, int* status) {
+               int32_t* s, int32_t* s2, cudaStream_t st, int* status, const NormIn* norm = nullptr) {
     const long long row_bytes = (long long)(n_in / block_values(fmt)) * block_bytes(fmt);
     TmaPlan pl;
     if (!tma_plan(fmt, n_in, row_bytes, x != nullptr, pl)) return false;
@@ -190,6 +198,9 @@ bool tma_dense(int fmt, int n_jobs, const uint8_t* const* w, const int* n_out, f
     P.n_in = n_in;
     P.total_rows = rows;
     P.s = s; P.s2 = s2;
+    if (norm) {
+        P.nr = norm->r; P.nrs = norm->rs; P.nh = norm->h_out; P.nw = norm->w; P.neps = norm->eps;
+    }
     if (s) *status = launch_tma<0, true>(fmt, P, pl, st);
     else if (!x) *status = launch_tma<0, false>(fmt, P, pl, st);
     else if (x_kind == 1) *status = launch_tma<1, false>(fmt, P, pl, st);
@@ -235,8 +246,8 @@ int qmv_quant_q8(const void* x, int x_is_f32, int8_t* xq, int8_t* xq2, float* xd
     if (n <= 0 || n % 32) return ST_BAD_SHAPE;
     if (!aligned(x, x_is_f32 ? 4 : 2)) return ST_BAD_ALIGN;
     const long long blocks = (n + 255) / 256;
-    quant_q8_kernel<<<unsigned(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, x_is_f32, xq, xq2, xd, xs, n);
-    return launched();
+    return launch_pdl(quant_q8_kernel, dim3(unsigned(blocks)), dim3(256), static_cast<cudaStream_t>(stream), x,
+                      x_is_f32, xq, xq2, xd, xs, n);
 }
 
 int qmv_mv(int ggml_type, const uint8_t* w, int n_out, int n_in, const int8_t* xq, const int8_t* xq2,
@@ -408,6 +419,26 @@ int qmv_mv_x(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_ou
                   nullptr, nullptr, static_cast<cudaStream_t>(stream), &st))
         return st;
     return ST_BAD_SHAPE;        // the shape needs the fallback kernel: quantise with qmv_quant_q8, then qmv_mv
+}
+
+int qmv_mv_norm(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
+                const float* h, const float* r, float rs, float* h_out, const float* norm_w, float eps, void* stream) {
+    if (!w || !n_out || !y || !h || !norm_w || (r && !h_out)) return ST_NULL;
+    if (!known_format(ggml_type)) return ST_BAD_FORMAT;
+    if (n_jobs < 1 || n_jobs > kMaxJobs) return ST_BAD_TOKENS;
+    if (n_in <= 0 || n_in % block_values(ggml_type)) return ST_BAD_SHAPE;
+    if (!aligned(h, 4) || !aligned(norm_w, 4) || (r && (!aligned(r, 4) || !aligned(h_out, 4)))) return ST_BAD_ALIGN;
+    for (int j = 0; j < n_jobs; ++j) {
+        if (!w[j] || !y[j]) return ST_NULL;
+        if (n_out[j] <= 0) return ST_BAD_SHAPE;
+        if (!aligned(w[j], weight_align(ggml_type)) || !aligned(y[j], 4)) return ST_BAD_ALIGN;
+    }
+    const NormIn norm{r, rs, h_out, norm_w, eps};
+    int st = ST_OK;
+    if (tma_dense(ggml_type, n_jobs, w, n_out, y, n_in, nullptr, nullptr, nullptr, nullptr, h, 1, nullptr, nullptr,
+                  static_cast<cudaStream_t>(stream), &st, &norm))
+        return st;
+    return ST_BAD_SHAPE;        // the shape needs the fallback: qmv_norm_q8, then qmv_mv_multi
 }
 
 // workspace of qmv_moe_ffn: xq, xq2 (L dim bytes each), xd, xs (L dim / 32 floats each), aq, aq2, ad, as

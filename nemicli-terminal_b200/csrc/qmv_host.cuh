@@ -34,6 +34,23 @@ int* device_status_ptr();       // the device status word of the current device 
 bool pdl_enabled();             // qmv_set_pdl
 bool tma_enabled();             // the staged / tensor-core kernels may be used (sweep builds can turn them off)
 
+// a kernel launch with programmatic dependent launch when qmv_set_pdl is on (the kernel must take
+// griddepcontrol.wait before it touches memory); plain stream order otherwise
+template <class... KArgs, class... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+    return launched();
+}
+
 // ---- defined per format in qmv_fmt.cu (one object file per format) ----
 // fallback kernel, T = 1..8 tokens
 template <int FMT> int launch_mv_fmt(const MvParams& P, int T, cudaStream_t st);

@@ -79,6 +79,10 @@ static __global__ void __launch_bounds__(256) quant_q8_kernel(const void* __rest
                                                        int8_t* __restrict__ xq, int8_t* __restrict__ xq2,
                                                        float* __restrict__ xd, float* __restrict__ xs,
                                                        long long n) {
+    // with programmatic dependent launch: the next kernel may launch now; nothing is read or written
+    // before the previous kernel has completed
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if ((i & ~31LL) >= n) return;          // n % 32 == 0: whole warps leave together
     const float v = x_f32 ? static_cast<const float*>(x)[i] : bf2f(static_cast<const uint16_t*>(x)[i]);

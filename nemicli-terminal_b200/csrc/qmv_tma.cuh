@@ -46,6 +46,12 @@ struct TmaParams {
     int32_t* s;                       // sums mode (test hook): int32 sums per (row, sum unit)
     int32_t* s2;
     const void* x;                    // fused quantisation (XF != 0): the raw activation row, fp32 or bf16
+    // fused RMS norm (XF == 1 and nw set; the arithmetic and sum order of the norm kernel, qmv_aux.cu):
+    // v = x (+ nrs * nr, written to nh, a slice per CTA), quantised input v * rsqrt(mean(v^2) + neps) * nw
+    const float* nr;
+    const float* nw;
+    float* nh;
+    float nrs, neps;
 };
 
 // ---- shared-memory access -----------------------------------------------------------------------
@@ -840,12 +846,12 @@ __global__ void __launch_bounds__(32 * (NCW + 1), NCW <= 8 ? 2 : 1) mv_tma_kerne
     if (warp == NCW) {
         // ---------------- producer: weights only, no dependence on the previous kernel ----------------
         if (lane != 0) return;
-        int it = 0;
+        int it = 0, s = 0;                        // s = it % S, ph = (it / S) & 1, kept by increments
+        uint32_t ph = 0;
         bool ok = true;
         const long long hi = cta_row_begin(P, blockIdx.x + 1);
         for (long long g = cta_row_begin(P, blockIdx.x); g < hi; ++it) {
-            const int s = it % S;
-            if (it >= S && !mbar_wait(empty0 + 8 * s, ((it / S) & 1) ^ 1)) {
+            if (it >= S && !mbar_wait(empty0 + 8 * s, ph ^ 1)) {
                 ok = false;
                 break;
             }
@@ -861,6 +867,10 @@ __global__ void __launch_bounds__(32 * (NCW + 1), NCW <= 8 ? 2 : 1) mv_tma_kerne
                 mbar_arrive_tx(full0 + 8 * s, bytes);
                 bulk_g2s(stage0 + uint32_t(s * stage_bytes), base + (long long)ti.row0 * P.row_bytes, bytes,
                          full0 + 8 * s);
+            }
+            if (++s == S) {
+                s = 0;
+                ph ^= 1;
             }
         }
         if (!ok) {
@@ -888,6 +898,41 @@ __global__ void __launch_bounds__(32 * (NCW + 1), NCW <= 8 ? 2 : 1) mv_tma_kerne
         int8_t* wq2 = wq + P.n_in;
         float* wd = reinterpret_cast<float*>(wq2 + P.n_in);
         float* ws = wd + P.n_in / 32;
+        const float* xf = static_cast<const float*>(P.x);
+        const bool norm = XF == 1 && P.nw != nullptr;
+        float inv = 1.f;
+        if (norm) {
+            // sum of v^2 in the norm kernel's order: 1024 threads, thread t over values t, t + 1024, ...,
+            // a warp sum per warp of them, then one warp sum over the 32 warp sums (here every consumer
+            // warp forms that last sum itself from shared memory; `red` is free until the first tile).
+            // Warp w stands for norm-kernel warps w, w + NCW, ...; four rounds of loads in flight.
+            constexpr int VPW = 32 / NCW;
+            float ss[VPW];
+#pragma unroll
+            for (int j = 0; j < VPW; ++j) ss[j] = 0.f;
+            for (int i0 = 0; i0 < P.n_in; i0 += 4 * 1024) {
+                float v[VPW][4];
+#pragma unroll
+                for (int j = 0; j < VPW; ++j)
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const int i = i0 + 1024 * k + 32 * (warp + NCW * j) + lane;
+                        v[j][k] = i < P.n_in ? (P.nr ? __fadd_rn(xf[i], __fmul_rn(P.nrs, P.nr[i])) : xf[i]) : 0.f;
+                    }
+#pragma unroll
+                for (int j = 0; j < VPW; ++j)
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        if (i0 + 1024 * k + 32 * (warp + NCW * j) + lane < P.n_in) ss[j] = __fmaf_rn(v[j][k], v[j][k], ss[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < VPW; ++j) {
+                const float t = warp_sum(ss[j]);
+                if (lane == 0) red[warp + NCW * j] = t;
+            }
+            named_sync(kConsumerBarrier, 32 * NCW);
+            inv = rsqrtf(warp_sum(red[lane]) / float(P.n_in) + P.neps);
+        }
         // a group on each eighth of a warp, QB rounds of a warp's loads in flight before their groups
         constexpr int QB = 4;
         const int n_grp = P.n_in / 32;
@@ -900,7 +945,12 @@ __global__ void __launch_bounds__(32 * (NCW + 1), NCW <= 8 ? 2 : 1) mv_tma_kerne
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     const int i = 32 * grp + m + 8 * k;
-                    v[b][k] = XF == 1 ? static_cast<const float*>(P.x)[i] : bf2f(static_cast<const uint16_t*>(P.x)[i]);
+                    if (XF == 1 && norm) {
+                        const float h = P.nr ? __fadd_rn(xf[i], __fmul_rn(P.nrs, P.nr[i])) : xf[i];
+                        v[b][k] = __fmul_rn(__fmul_rn(h, inv), P.nw[i]);
+                    } else {
+                        v[b][k] = XF == 1 ? xf[i] : bf2f(static_cast<const uint16_t*>(P.x)[i]);
+                    }
                 }
             }
 #pragma unroll
@@ -909,13 +959,22 @@ __global__ void __launch_bounds__(32 * (NCW + 1), NCW <= 8 ? 2 : 1) mv_tma_kerne
                 quantize_group8(v[b], 32LL * grp, grp < n_grp, wq, wq2, wd, ws);
             }
         }
+        if (norm && P.nr && P.nh) {
+            // v = h + rs r back to memory, a slice per CTA (no store among the loads above: a store there
+            // would keep the compiler from batching them)
+            const int lo = int((long long)blockIdx.x * P.n_in / gridDim.x);
+            const int hi = int((long long)(blockIdx.x + 1) * P.n_in / gridDim.x);
+            for (int i = lo + int(threadIdx.x); i < hi; i += 32 * NCW)
+                P.nh[i] = __fadd_rn(xf[i], __fmul_rn(P.nrs, P.nr[i]));
+        }
         named_sync(kConsumerBarrier, 32 * NCW);
         sxq = wq; sxq2 = wq2; sxd = wd; sxs = ws;
     }
     Act<FMT> act[UPL];
     long long cur_row = -1;
     bool dead = false;
-    int it = 0;
+    int it = 0, s = 0;                          // s = it % S, ph = (it / S) & 1
+    uint32_t ph = 0;
     // window of rows whose cross-warp partial sums wait in shared memory (teams wider than a warp)
     constexpr int PR = kPartFloats / WPT;
     float* part = red;
@@ -951,8 +1010,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), NCW <= 8 ? 2 : 1) mv_tma_kerne
             }
             cur_row = arow;
         }
-        const int s = it % S;
-        const bool got = !dead && mbar_wait(full0 + 8 * s, (it / S) & 1);
+        const bool got = !dead && mbar_wait(full0 + 8 * s, ph);
         if (!got && !dead) {
             dead = true;
             if (lane == 0 && P.status) atomicOr(P.status, DEV_TIMEOUT);
@@ -1003,6 +1061,10 @@ __global__ void __launch_bounds__(32 * (NCW + 1), NCW <= 8 ? 2 : 1) mv_tma_kerne
         }
         __syncwarp();
         if (got && lane == 0) mbar_arrive(empty0 + 8 * s);   // this warp is done with the stage
+        if (++s == S) {
+            s = 0;
+            ph ^= 1;
+        }
         if constexpr (!SUMS) {
             if constexpr (G <= 32) {
                 float* y = P.ids == nullptr ? P.y[ti.job] : P.y[0] + (long long)ti.slot * P.n_out[0];

@@ -10,6 +10,8 @@ meaning and return shapes, computed by this package's sm_100a kernels through th
 * `entpacken` — a block-format matrix unpacked to bf16 for long inputs (mmvq.py:931-940), every format.
 * `norm_q8`, `akt_q8` — the fused one-token producers of an Eingang (mmvq.py:946-966): RMS norm with the
   residual add, and the gated activation, each one launch that also quantises its output.
+* `mv_geteilt`, `mv_norm` (new) — up to four matrices on one single-token input in one launch;
+  `mv_norm` forms norm_q8's RMS norm inside that launch (bit-identical to the two calls).
 * `rope_kv`, `attention1`, `schritt_moeglich` — the attention steps of the reference's fused one-token
   layer (mmvq.py:969-1014) are not part of this package (the matvec path ends where attention begins).
   They are forwarded to an attention provider registered with `set_attention` (the reference's own
@@ -101,10 +103,15 @@ def _check_raw(fmt: str, raw: torch.Tensor, n_out: int, n_in: int) -> None:
         raise RuntimeError(f"{fmt}: raw must be contiguous uint8 with {n_out * (n_in // bv) * bb} bytes")
 
 
+_PDL = [False]
+
+
 def pdl(enabled: bool) -> bool:
-    """Programmatic dependent launch for the single-token kernels (off by default; see
-    include/nemicli_qmv.h, qmv_set_pdl): the next matvec streams its weights while the previous kernel
-    finishes.  Only for weights that no kernel launched right before the matvec writes."""
+    """Programmatic dependent launch for the single-token kernels and the activation producers (off by
+    default; see include/nemicli_qmv.h, qmv_set_pdl): the next matvec streams its weights while the
+    previous kernel finishes, a producer (quant_q8, norm_q8, akt_q8) launches while its input is still
+    being written.  Only for weights that no kernel launched right before the matvec writes."""
+    _PDL[0] = bool(enabled)
     return bool(_lib.load().qmv_set_pdl(int(bool(enabled))))
 
 
@@ -118,15 +125,20 @@ def _raw_x(x: torch.Tensor, n_in: int):
     return x.contiguous()
 
 
-FUSED_MAX_IN = 8192     # row length up to which quantising the input inside every CTA of the matvec
-                        # beats a separate quantisation launch (measured: 4096 fused ahead by about
-                        # 1 us, 14336 behind by 1.5-2.5 us)
+FUSED_MAX_IN = 8192     # without PDL: row length up to which quantising the input inside every CTA of
+                        # the matvec beats a separate quantisation launch (measured: 4096 fused ahead
+                        # by about 1 us, 14336 behind by 1.5-2.5 us).  With PDL the separate launch
+                        # overlaps the previous kernel and is ahead at every length (2-2.5 us at 4096)
+
+
+def _fused_ok(n_in: int) -> bool:
+    return not _PDL[0] and n_in <= FUSED_MAX_IN
 
 
 def _fused(fmt: str, mats, x: torch.Tensor, n_in: int, outs=None, force: bool = False):
     """One launch that quantises x itself; None where the staged kernel does not take the shape or
-    the row is longer than FUSED_MAX_IN (unless force)."""
-    if n_in > FUSED_MAX_IN and not force:
+    the separate quantisation is faster (_fused_ok; unless force)."""
+    if not (force or _fused_ok(n_in)):
         return None
     xr = _raw_x(x, n_in)
     if xr is None:
@@ -149,8 +161,9 @@ def _fused(fmt: str, mats, x: torch.Tensor, n_in: int, outs=None, force: bool = 
 def mv(fmt: str, raw: torch.Tensor, x, n_out: int, n_in: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """raw: (n_out, n_in) in block format on the GPU; x: (M, n_in) or (n_in,) bf16/float32, or an
     Eingang with M rows -> (M, n_out) float32, or (n_out,) for a vector.  One token given as a tensor
-    is quantised inside the matvec kernel (no separate Eingang) for rows up to FUSED_MAX_IN values.  out: a contiguous float32 tensor of
-    M * n_out values to write into (this package's sharded layers gather from it in place)."""
+    is quantised inside the matvec kernel (no separate Eingang) for rows up to FUSED_MAX_IN values when
+    PDL is off.  out: a contiguous float32 tensor of M * n_out values to write into (this package's
+    sharded layers gather from it in place)."""
     _check_raw(fmt, raw, n_out, n_in)
     ist_eingang = _ist_eingang(x)
     M = (x.n if ist_eingang else x.numel()) // n_in
@@ -196,6 +209,44 @@ def mv_geteilt(fmt: str, mats, x, n_in: int) -> list:
     _lib.check(_lib.load().qmv_mv_multi(TYPE_ID[fmt], n, w_arr, n_arr, y_arr, n_in, *e.zeiger(),
                                         _lib.stream_ptr(dev)), f"qmv_mv_multi {fmt}")
     return ys
+
+
+def mv_norm(fmt: str, mats, h: torch.Tensor, w: torch.Tensor, eps: float, rest: Optional[torch.Tensor] = None,
+            rs: float = 1.0, force: bool = False):
+    """norm_q8(h, w, eps, rest, rs) followed by mv_geteilt on its input, in one launch: every CTA of the
+    matvec forms the RMS norm (the norm kernel's sum order, so the quantised input and the outputs are
+    bit-identical to the two calls).  mats = [(raw, n_out), ...] (1 to 4, one token) -> ([y (n_out,)
+    float32, ...], new h) where new h = h + rs * rest (h itself without rest).  With PDL on (the two
+    launches are faster then), for rows longer than FUSED_MAX_IN and for shapes the staged kernel does
+    not take it is the two calls; force takes the one launch wherever the kernel takes the shape.
+    New entry point (the reference's one-token step calls norm_q8 and then mv per matrix,
+    models/baukasten.py:205-240)."""
+    if not 1 <= len(mats) <= 4:
+        raise RuntimeError("mv_norm: 1 to 4 matrices")
+    hv, wv = _vektor(h, "mv_norm"), _vektor(w, "mv_norm")
+    n_in = hv.numel()
+    if rest is not None:
+        rest = _vektor(rest, "mv_norm")
+    if wv.numel() != n_in or (rest is not None and rest.numel() != n_in):
+        raise RuntimeError(f"mv_norm: h, w and rest must have the same length ({n_in})")
+    for raw, n_out in mats:
+        _check_raw(fmt, raw, n_out, n_in)
+    if force or _fused_ok(n_in):
+        dev = mats[0][0].device
+        ys = [torch.empty(n_out, dtype=torch.float32, device=dev) for _, n_out in mats]
+        hn = None if rest is None else torch.empty(n_in, dtype=torch.float32, device=dev)
+        n = len(mats)
+        w_arr = (ctypes.c_void_p * n)(*[raw.data_ptr() for raw, _ in mats])
+        n_arr = (ctypes.c_int * n)(*[n_out for _, n_out in mats])
+        y_arr = (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys])
+        st = _lib.load().qmv_mv_norm(TYPE_ID[fmt], n, w_arr, n_arr, y_arr, n_in, _lib.ptr(hv), _lib.ptr(rest),
+                                     ctypes.c_float(rs), _lib.ptr(hn), _lib.ptr(wv), ctypes.c_float(eps),
+                                     _lib.stream_ptr(dev))
+        if st != 2:
+            _lib.check(st, f"qmv_mv_norm {fmt}")
+            return ys, (h if hn is None else hn)
+    _, e, h_new = norm_q8(h, w, eps, rest, rs)
+    return mv_geteilt(fmt, mats, e, n_in), h_new
 
 
 _TEILEN = threading.local()

@@ -1,11 +1,13 @@
 """The kernels around the matvecs on the GPU: unpacking (qmv_unpack: mmvq.entpacken, PackedExperts.weights,
 QuantLinear.bf16_weight, PackedLinear's long-input path) and the fused one-token producers (qmv_norm_q8,
-qmv_act_q8: mmvq.norm_q8, mmvq.akt_q8).
+qmv_act_q8: mmvq.norm_q8, mmvq.akt_q8), and the norm fused into the matvec (qmv_mv_norm: mmvq.mv_norm,
+bit-identical to norm_q8 followed by the matvecs).
 
 Unpacking is bit-exact: its fp32 values against the reference's own dequantised golden vectors
 (tests/golden, every format and every codebook entry), bf16 / fp16 against torch's round-to-nearest-even
 of those.  The producers against torch fp32 (1e-6), and their activation input bit-exact against the
 oracle's quantisation of the kernel's own normalised / activated output."""
+import ctypes
 import os
 
 import numpy as np
@@ -13,7 +15,7 @@ import pytest
 import torch
 import torch.nn.functional as F
 
-from nemicli_terminal_b200 import layers, mmvq, qlinear, synth
+from nemicli_terminal_b200 import _lib, layers, mmvq, qlinear, synth
 from nemicli_terminal_b200.formats import FORMATS, TYPE_ID
 from oracle import oracle as O
 
@@ -135,3 +137,50 @@ def test_akt_q8(cuda, gelu, with_u):
         ref = ref * u
     assert float((a - ref).abs().max() / ref.abs().max()) < 1e-6
     _eingang_matches_oracle(e, a)
+
+
+@pytest.mark.parametrize("fmt,n,force", [("Q4_K", 4096, False), ("Q8_0", 4096, False), ("IQ2_XXS", 2048, False),
+                                         ("Q6_K", 14336, True), ("Q6_K", 14336, False), ("Q4_0", 14336 + 256, True),
+                                         ("Q4_K", 4096, True)])
+@pytest.mark.parametrize("rest", [False, True])
+@pytest.mark.parametrize("pdl", [False, True])
+def test_mv_norm_equals_two_calls(cuda, fmt, n, force, rest, pdl):
+    """mv_norm (the RMS norm formed by every CTA of the matvec) gives the quantised input of norm_q8 and
+    so the same outputs, bit for bit, with one and several matrices, with and without the residual add
+    (scaled); the new h equals norm_q8's.  Without force and with PDL on, or past FUSED_MAX_IN, it is
+    the two calls (launched with PDL when it is on)."""
+    old = mmvq.pdl(pdl)
+    try:
+        h = synth.activations(1, n, seed=n, device=cuda)[0]
+        w = torch.rand(n, device=cuda) + 0.5
+        r = synth.activations(1, n, seed=n + 1, device=cuda)[0] if rest else None
+        rs = 0.75 if rest else 1.0
+        mats = [(synth.blocks(fmt, n_out, n, seed=5 + n_out, device=cuda), n_out) for n_out in (512, 128, 256)]
+        ys, h_new = mmvq.mv_norm(fmt, mats, h, w, 1e-5, rest=r, rs=rs, force=force)
+        _, e, h_ref = mmvq.norm_q8(h, w, 1e-5, rest=r, rs=rs)
+        ref = mmvq.mv_geteilt(fmt, mats, e, n)
+        assert all(torch.equal(a, b) for a, b in zip(ys, ref))
+        assert torch.equal(h_new, h_ref) if rest else h_new is h
+        y1, _ = mmvq.mv_norm(fmt, mats[:1], h, w, 1e-5, rest=r, rs=rs, force=force)
+        assert torch.equal(y1[0], ref[0])
+    finally:
+        mmvq.pdl(old)
+
+
+def test_mv_norm_refusals(cuda):
+    lib = _lib.load()
+    h = torch.zeros(4096, device=cuda)
+    w = torch.ones(4096, device=cuda)
+    raw = synth.blocks("Q4_K", 64, 4096, seed=1, device=cuda)
+    y = torch.empty(64, device=cuda)
+    wa = (ctypes.c_void_p * 1)(raw.data_ptr())
+    na = (ctypes.c_int * 1)(64)
+    ya = (ctypes.c_void_p * 1)(y.data_ptr())
+
+    def st(*a):
+        return lib.qmv_mv_norm(TYPE_ID["Q4_K"], *a)
+    one, eps = ctypes.c_float(1.0), ctypes.c_float(1e-5)
+    assert st(1, wa, na, ya, 4096, _lib.ptr(h), None, one, None, None, eps, None) == 6          # no norm weights
+    assert st(1, wa, na, ya, 4096, _lib.ptr(h), _lib.ptr(h), one, None, _lib.ptr(w), eps, None) == 6   # r, no h_out
+    assert st(5, wa, na, ya, 4096, _lib.ptr(h), None, one, None, _lib.ptr(w), eps, None) == 4    # > 4 matrices
+    assert st(1, wa, na, ya, 4000, _lib.ptr(h), None, one, None, _lib.ptr(w), eps, None) == 2    # row length
