@@ -3,14 +3,18 @@
 Workload (the headline metric): one decode step of a 32-layer stack of
 Llama-3-8B-shaped projections at batch 1 — per layer q_proj/o_proj 4096x4096, k_proj/v_proj
 1024x4096, gate/up 14336x4096 (Q4_K) and down 4096x14336 (Q6_K), 137,822,208 weight bytes per layer,
-4.41 GB per step.  Per layer the step quantises four inputs (attention input shared by q/k/v, o input,
-FFN input shared by gate/up, down input) and runs the seven matvecs, exactly the calls of a decode step
-through mmvq.Eingang / mmvq.mv, captured once in a CUDA graph as the reference's decoder does.  Weights
-and activations are seeded synthetic data with the config's distributions; every step reads 4.41 GB of
-distinct weights, far more than L2 (126 MB), so no L2 flush is needed.
+4.41 GB per step.  Per layer the step forms four inputs from the residual stream and the previous
+outputs (RMS norm of h -> q/k/v, q's output -> o, RMS norm of h + o -> gate/up, SiLU(gate) * up -> down;
+o_proj reads q_proj's output where attention would be) and runs the seven matvecs.  Default `--mode
+calls`: the reference's call pattern (norm_q8 / Eingang / akt_q8 producers, then mmvq.mv_geteilt / mv)
+with programmatic dependent launch, captured once in a CUDA graph as the reference's decoder does;
+`--mode chain`: the same step as one persistent decode-chain launch.  Weights and activations are
+seeded synthetic data with the config's distributions; every step reads 4.41 GB of distinct weights,
+far more than L2 (126 MB), so no L2 flush is needed.  The batch-4 / batch-8 lines run the seven matvecs
+per layer on fixed inputs (one Eingang per input).
 
 value: weight GB/s of the whole job (all ranks; weak scaling: every GPU runs its own stack replica).
-e2e: the same step with its activation inputs copied from pinned host memory and all outputs read back.
+e2e: the same step with its first input copied from pinned host memory and its last output read back.
 --impl reference: the reference's CPU path for the same workload on the host cores (a restatement in
 oracle/: GGUF weights dequantised once to bf16, then torch F.linear, as the reference engine does on a
 CPU device, ggufengine/models/common.py:516-527), one layer per step.
@@ -154,6 +158,49 @@ def build_chain(stack, device, seed: int = 0):
         outs += [y for s_ in st for y in s_.ys]
         h, r = h_mid, y_down
     return chain.Chain(stages), h0, r, outs
+
+
+def build_calls(stack, device, seed: int = 0):
+    """The chain's step (same weights, norms and residual stream as build_chain with the same seed) as
+    per-call launches with their true dependencies, the reference's one-token step pattern: per layer
+    RMS norm -> q,k,v (mmvq.mv_norm) | o on q's output | RMS norm of h + o -> gate,up | SiLU(gate) * up
+    (mmvq.akt_q8) -> down.  With PDL on every producer (norm_q8, quant_q8, akt_q8) is its own launch that
+    starts while the previous matvec finishes, and each matvec streams its weights early; with PDL off
+    the norms and quantisations run inside the matvec launches.
+    Returns (step function -> outputs, h0, the list the last down output is written to)."""
+    from nemicli_terminal_b200 import mmvq, synth
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    h0 = synth.activations(1, 4096, seed=seed + 11, device=device)[0].contiguous()
+    norms = []
+    for _ in stack:
+        wa = (torch.rand(4096, generator=g, device=device) + 0.5).contiguous()
+        wf = (torch.rand(4096, generator=g, device=device) + 0.5).contiguous()
+        norms.append((wa, wf))
+    last = [None]
+
+    def step():
+        h, r, outs = h0, None, []
+        for mats, (wa, wf) in zip(stack, norms):
+            m = {name: (fmt, raw, n_out, n_in) for name, fmt, n_out, n_in, slot, raw in mats}
+            (q, k, v), h = mmvq.mv_norm("Q4_K", [(m[x][1], m[x][2]) for x in ("q", "k", "v")], h, wa, 1e-5, rest=r)
+            o = mmvq.mv("Q4_K", m["o"][1], q, 4096, 4096)
+            (gt, up), h = mmvq.mv_norm("Q4_K", [(m[x][1], m[x][2]) for x in ("gate", "up")], h, wf, 1e-5, rest=o)
+            _, e = mmvq.akt_q8(gt, up, False)
+            d = mmvq.mv("Q6_K", m["down"][1], e, 4096, 14336)
+            outs += [q, k, v, o, gt, up, d]
+            r = d
+        last[0] = r
+        return outs
+
+    step.norms = norms
+    return step, h0, last
+
+
+def calls_launches_per_layer(pdl: bool) -> int:
+    """Kernels per layer of build_calls' step: with PDL norm, q,k,v | quantise, o | norm, gate,up |
+    SiLU gate, down; without it q,k,v (norm inside) | o | gate,up (norm inside) | SiLU gate, down."""
+    return 8 if pdl else 5
 
 
 def capture(fn):
@@ -386,24 +433,26 @@ def run_ours(args):
         clocks = clk.summary()
         t = max_over_ranks(t, dist, device)
         results[1] = {"s_per_step": t / args.steps, "steps": args.steps}
+    if args.mode == "calls":
+        calls_step, h0_dev, calls_last = build_calls(stack, device, seed=100000 * rank)
+        g1, _ = capture(calls_step)
+        last_out = calls_last[0]
+        with Clocks(local) as clk:
+            t = time_graph(g1, args.steps, max(3, args.warmup), dist)
+        clocks = clk.summary()
+        t = max_over_ranks(t, dist, device)
+        results[1] = {"s_per_step": t / args.steps, "steps": args.steps}
     for batch in ([1] + [b for b in args.batches if b != 1]):
-        if batch == 1 and args.mode == "chain":
+        if batch == 1:
             continue
         xs = [[synth.activations(batch, n, seed=7919 * l + s + batch, device=device) for s, n in enumerate(INPUTS)]
               for l in range(args.layers)]
         g, outs = capture(lambda: step_fn(stack, xs, batch))
-        steps = args.steps if batch == 1 else max(5, args.steps // 2)
-        if batch == 1:
-            with Clocks(local) as clk:
-                t = time_graph(g, steps, max(3, args.warmup), dist)
-            clocks = clk.summary()
-            g1, xs1, outs1 = g, xs, outs
-        else:
-            t = time_graph(g, steps, max(3, args.warmup), dist)
+        steps = max(5, args.steps // 2)
+        t = time_graph(g, steps, max(3, args.warmup), dist)
         t = max_over_ranks(t, dist, device)
         results[batch] = {"s_per_step": t / steps, "steps": steps}
-        if batch != 1:
-            del g
+        del g
     t1 = results[1]["s_per_step"]
     value = world * step_bytes / t1 / 1e9
 
@@ -414,12 +463,13 @@ def run_ours(args):
     else:
         # dominant kernel alone: the gate_proj launches (Q4_K 14336x4096, 33.0 MB each) of the stack
         gate_raw = [mats[4][5] for mats in stack]
-        x_gate = xs1[0][2]
-        gk, _ = capture(lambda: [mmvq.mv("Q4_K", r, x_gate, 14336, 4096) for r in gate_raw])
+        e_gate = mmvq.Eingang(synth.activations(1, 4096, seed=17, device=device)[0].contiguous())
+        gk, _ = capture(lambda: [mmvq.mv("Q4_K", r, e_gate, 14336, 4096) for r in gate_raw])
         reps = 20
         tk = time_graph(gk, reps, 3) / (reps * len(gate_raw))
         kbytes = 14336 * (4096 // 256) * 144
-        kernel_name = "mv_tma_kernel<Q4_K> gate_proj 14336x4096 (fused quantisation)"
+        kernel_name = ("mv_tma_kernel<Q4_K> gate_proj 14336x4096, quantised input, back to back over the "
+                       f"{len(gate_raw)} layers' matrices" + (" with PDL" if not args.no_pdl else ""))
     achieved = kbytes / tk / 1e9
     traffic = None
     tf = os.path.join(ROOT, "profiles", "traffic.txt")
@@ -429,14 +479,9 @@ def run_ours(args):
                 traffic = int(line.split("=")[1])
 
     # e2e: the step's inputs from pinned host memory to the device, the step, its results back
-    if args.mode == "chain":
-        h_in = [[h0_dev.cpu().pin_memory()]]
-        dev_in = [[h0_dev]]
-        res_dev = [last_out]
-    else:
-        h_in = [[x.cpu().pin_memory() for x in row] for row in xs1]
-        dev_in = xs1
-        res_dev = outs1
+    h_in = [[h0_dev.cpu().pin_memory()]]
+    dev_in = [[h0_dev]]
+    res_dev = [last_out]
     h_out = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in res_dev]
     h2d = sum(x.numel() * x.element_size() for row in h_in for x in row)
     d2h = sum(o.numel() * o.element_size() for o in res_dev)
@@ -466,16 +511,18 @@ def run_ours(args):
     sharded = None if args.no_sharded else sharded_suite(world, rank, dist, device, max(5, args.steps // 10),
                                                           max(3, args.warmup))
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
-    launches_per_step = 1 if args.mode == "chain" else args.layers * 4   # chain: one launch per step
+    launches_per_step = 1 if args.mode == "chain" else args.layers * calls_launches_per_layer(not args.no_pdl)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t1 * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded, config-2 distributions)",
             "config": {"workload": "config2: decode step of a 32-layer Llama-3-8B projection stack "
-                                   "(q,k,v,o,gate,up Q4_K; down Q6_K), batch 1" + (
-                                       "; chain: RMS norm + residual and SiLU gate fused as stage inputs, "
-                                       "o_proj reads q_proj's output in place of attention" if args.mode == "chain" else ""),
+                                   "(q,k,v,o,gate,up Q4_K; down Q6_K), batch 1; RMS norms with the residual "
+                                   "adds and the SiLU gate between the matvecs, o_proj reads q_proj's output in "
+                                   "place of attention" + ("; one decode-chain launch per step" if args.mode == "chain"
+                                                           else "; per-call launches (norm_q8 / quant_q8 / akt_q8, "
+                                                                "then the matvecs on the input), PDL"),
                        "layers": args.layers, "batch": 1, "weight_bytes_per_step": step_bytes,
                        "l2": "inputs larger than L2 (4.41 GB distinct weights per step), no flush",
                        "parallelism": (f"value: replicas x{world} of the config-2 stack (one per GPU, no "
@@ -737,8 +784,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-pdl", action="store_true", help="plain stream order between the matvec launches")
     ap.add_argument("--no-sharded", action="store_true", help="skip configs 3 and 4 (row / expert sharded)")
-    ap.add_argument("--mode", choices=["chain", "calls"], default="chain",
-                    help="chain: the step as one decode-chain launch; calls: one launch per matrix group")
+    ap.add_argument("--mode", choices=["chain", "calls"], default="calls",
+                    help="calls: the step as per-call launches with PDL (the reference's call pattern, faster "
+                         "here); chain: the step as one decode-chain launch")
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers in the stack (profiling runs use fewer)")
     ap.add_argument("--workload", choices=["stack", "vocab", "moe", "cfg1", "cfg5", "tiles"], default="stack",
                     help="stack: config 2 (the headline); vocab: config 3 row-sharded over the GPUs; "

@@ -1,10 +1,13 @@
 """Parity of exactly what bench.py measures, at the benchmark's full sizes.
 
-* the headline decode chain: the 32-layer, 128-stage Llama-3-8B projection stack that bench.py builds
+* the decode chain (`--mode chain`): the 32-layer, 128-stage Llama-3-8B projection stack that bench.py builds
   (bench.build_chain), captured in a CUDA graph and replayed several times; every stage's outputs are
   checked against the per-call API (mmvq.mv on the stage input recomputed in torch from the chain's own
   earlier outputs, 1e-5), and the stages of three layers against the dequantise-and-matmul oracle (oracle
   A, 1e-3);
+* the per-call step (bench.build_calls, `--mode calls`, the BENCH value): replays identical, every output
+  bit-identical to the unfused calls (norm_q8 / akt_q8 then the matvecs) on its own inputs, oracle A at
+  three layers, with and without PDL;
 * the batch-4 and batch-8 stack lines (bench.step_fn: the few-token tensor-core kernels) against the
   integer-path oracle (1e-5) and oracle A (1e-3);
 * the config-4 MoE FFN (128 Q4_K experts, gate/up 768x2048, down 2048x768, top-8) at batch 1, 4 and 16
@@ -90,6 +93,63 @@ def test_headline_chain_128_stages(cuda, stack):
                 assert _rel(y, ya) < 1e-3, (l, name)
         h, r = hm, s4.ys[0]
     assert last.data_ptr() == ch.stages[-1].ys[0].data_ptr()
+
+
+@pytest.mark.parametrize("pdl", [False, True])
+def test_headline_calls_128_stages(cuda, stack, pdl):
+    """bench.py's per-call step (--mode calls), with PDL (the bench: separate producer launches that
+    overlap) and without (norms and quantisation inside the matvecs): graph replays are identical; every
+    output equals, bit for bit, the unfused calls (norm_q8, then the matvecs on its Eingang; akt_q8, then
+    down) fed with the step's own earlier outputs; layers 0, 15 and 31 match oracle A; layer 0 matches
+    the chain."""
+    old = mmvq.pdl(pdl)
+    try:
+        _calls_step_parity(cuda, stack)
+    finally:
+        mmvq.pdl(old)
+
+
+def _calls_step_parity(cuda, stack):
+    step, h0, last = bench.build_calls(stack, cuda, seed=0)
+    g, outs = bench.capture(step)
+    assert len(outs) == 7 * bench.LAYERS
+    snaps = []
+    for _ in range(3):
+        for y in outs:
+            y.fill_(float("nan"))
+        g.replay()
+        torch.cuda.synchronize()
+        snaps.append([y.clone() for y in outs])
+    for s in snaps[1:]:
+        assert all(torch.equal(a, b) for a, b in zip(snaps[0], s))
+    eps = 1e-5
+    h, r = h0, None
+    for l in range(bench.LAYERS):
+        q, k, v, o, gt, up, d = outs[7 * l:7 * l + 7]
+        wa, wf = step.norms[l]
+        m = {name: (fmt, raw, n_out, n_in) for name, fmt, n_out, n_in, slot, raw in stack[l]}
+        x1, e1, h = mmvq.norm_q8(h, wa, eps, r)
+        ref = mmvq.mv_geteilt("Q4_K", [(m[x][1], m[x][2]) for x in ("q", "k", "v")], e1, 4096)
+        assert all(torch.equal(a, b) for a, b in zip((q, k, v), ref)), l
+        assert torch.equal(o, mmvq.mv("Q4_K", m["o"][1], mmvq.Eingang(q), 4096, 4096)), l
+        x3, e3, h = mmvq.norm_q8(h, wf, eps, o)
+        ref = mmvq.mv_geteilt("Q4_K", [(m[x][1], m[x][2]) for x in ("gate", "up")], e3, 4096)
+        assert all(torch.equal(a, b) for a, b in zip((gt, up), ref)), l
+        x4, e4 = mmvq.akt_q8(gt, up, False)
+        assert torch.equal(d, mmvq.mv("Q6_K", m["down"][1], e4, 4096, 14336)), l
+        if l in (0, 15, 31):
+            for name, x, y in (("q", x1, q), ("k", x1, k), ("v", x1, v), ("o", q, o), ("gate", x3, gt),
+                               ("up", x3, up), ("down", x4, d)):
+                f, raw, n_out, n_in = m[name]
+                ya = _dense(f, raw, n_out, n_in) @ x.double().cpu()
+                assert _rel(y, ya) < 1e-3, (l, name)
+        r = d
+    assert last[0].data_ptr() == outs[-1].data_ptr()
+    ch, _, _, chain_outs = bench.build_chain(stack[:1], cuda, seed=0)
+    ch.run()
+    torch.cuda.synchronize()
+    for a, b in zip(chain_outs, snaps[0][:7]):
+        assert _rel(a, b) < 1e-4
 
 
 @pytest.mark.parametrize("batch", [4, 8])
