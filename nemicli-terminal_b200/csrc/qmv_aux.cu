@@ -32,6 +32,10 @@ __global__ void __launch_bounds__(kNormBlock) norm_q8_kernel(const float* __rest
     __shared__ float red[32];
     constexpr int K = kNormThreads / kNormBlock;       // order threads per thread: t = p + kNormBlock k
     const int p = threadIdx.x, warp = p >> 5, lane = p & 31;
+    const int i = blockIdx.x * kNormBlock + p;         // this thread's own value (second pass)
+    const bool own = i - lane < n;                     // the whole warp (n % 32 == 0)
+    // loaded together with the first pass's terms: no second round trip to memory after the barrier
+    const float hi = own ? h[i] : 0.f, ri = own && r ? r[i] : 0.f, wi = own ? w[i] : 0.f;
     float ss[K];
 #pragma unroll
     for (int k = 0; k < K; ++k) ss[k] = 0.f;
@@ -57,11 +61,10 @@ __global__ void __launch_bounds__(kNormBlock) norm_q8_kernel(const float* __rest
     }
     __syncthreads();
     const float inv = rsqrtf(warp_sum(red[lane]) / float(n) + eps);
-    const int i = blockIdx.x * kNormBlock + p;
-    if (i - lane < n) {                                // the whole warp (n % 32 == 0)
-        const float v = r ? __fadd_rn(h[i], __fmul_rn(rs, r[i])) : h[i];
+    if (own) {
+        const float v = r ? __fadd_rn(hi, __fmul_rn(rs, ri)) : hi;
         if (r) hout[i] = v;
-        const float x = __fmul_rn(__fmul_rn(v, inv), w[i]);
+        const float x = __fmul_rn(__fmul_rn(v, inv), wi);
         xn[i] = x;
         quantize_group(x, i, xq, xq2, xd, xs);
     }

@@ -23,9 +23,10 @@ int g_pdl = 0;                            // programmatic dependent launch (qmv_
 // sweeps only, never the shipped library) reads them once from the environment: NEMICLI_QMV_TMA=0 sends
 // every call to the fallback kernel, NEMICLI_QMV_TMA_G forces the team width (16..512) where it fits.
 struct TmaKnobs {
-    int enabled = 1, force_g = 0, ncw = 16;
+    int enabled = 1, force_g = 0, ncw = 16, rows_per_team = kTmaRowsPerTeam;
     TmaKnobs() {
 #ifdef QMV_SWEEP
+        if (const char* e = std::getenv("NEMICLI_QMV_ROWS")) rows_per_team = std::max(1, std::min(4, std::atoi(e)));
         if (const char* e = std::getenv("NEMICLI_QMV_TMA")) enabled = std::atoi(e) != 0;
         if (const char* g = std::getenv("NEMICLI_QMV_TMA_G")) force_g = std::atoi(g);
         if (const char* n = std::getenv("NEMICLI_QMV_NCW")) ncw = std::atoi(n) == 8 ? 8 : 16;
@@ -136,7 +137,7 @@ bool tma_plan(int fmt, int n_in, long long row_bytes, bool fused, TmaPlan& pl) {
     if (UPL > 2) return false;
     const int teams = 32 * ncw / G;
     const long long other = tma_red_bytes(ncw) + 2048 + (fused ? tma_act_bytes(n_in) : 0) + 2 * 8 * 32;
-    long long R = (long long)kTmaRowsPerTeam * teams;
+    long long R = (long long)knobs().rows_per_team * teams;
     while (R > 1 && 2 * R * row_bytes > cap - other) R = R > teams ? R - teams : R / 2;
     const long long stage = R * row_bytes;
     long long S = (cap - other) / stage;
