@@ -37,10 +37,11 @@ bool tma_enabled();             // the staged / tensor-core kernels may be used 
 // a kernel launch with programmatic dependent launch when qmv_set_pdl is on (the kernel must take
 // griddepcontrol.wait before it touches memory); plain stream order otherwise
 template <class... KArgs, class... Args>
-int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+int launch_pdl_smem(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -49,6 +50,10 @@ int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, A
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
     cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
     return launched();
+}
+template <class... KArgs, class... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+    return launch_pdl_smem(kern, grid, block, 0, st, args...);
 }
 
 // ---- defined per format in qmv_fmt.cu (one object file per format) ----

@@ -35,8 +35,7 @@ bool mma_dense_k(const uint8_t* w, int n_out, int n_in, long long row_bytes, con
     }
     const int tiles = (n_out + kMmaRows - 1) / kMmaRows;
     const int grid = std::min(tiles, sm_count());
-    mv_mma_kernel<FMT, NCW><<<grid, 32 * (NCW + 1), int(S * slot + other), st>>>(P);
-    *status = launched();
+    *status = launch_pdl_smem(mv_mma_kernel<FMT, NCW>, dim3(grid), dim3(32 * (NCW + 1)), size_t(S * slot + other), st, P);
     return true;
 }
 }  // namespace
@@ -77,8 +76,8 @@ bool mma_q6k(const uint8_t* w, int n_out, int n_in, long long row_bytes, const i
         }
         configured[dev] = 1;
     }
-    mv_mma_q6k_kernel<NCW><<<grid, 32 * (NCW + 1), int(S * slot + other), st>>>(P);
-    *status = launched();
+    *status = launch_pdl_smem(mv_mma_q6k_kernel<NCW>, dim3(grid), dim3(32 * (NCW + 1)), size_t(S * slot + other), st,
+                              P);
     return true;
 }
 }  // namespace qmv

@@ -93,6 +93,9 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) mv_mma_kernel(const MmaPara
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S), stage0 = smem_u32(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tiles = (P.n_out + kMmaRows - 1) / kMmaRows;
+    // programmatic dependent launch: the next kernel may launch now (its weight copies do not read our
+    // outputs); the consumers read the activation only after the previous kernel has completed
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -129,6 +132,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) mv_mma_kernel(const MmaPara
 
     // ---------------- consumers ----------------
     // the tokens' activations (tokens >= n_tok: zeros) into shared memory
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int cl = threadIdx.x, nthr = 32 * NCW;
     for (int i = cl; i < kMmaMaxTok * (P.n_in / 16); i += nthr) {
         const int t = i / (P.n_in / 16), c = i % (P.n_in / 16);
@@ -293,6 +297,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) mv_mma_q6k_kernel(const Mma
     const uint32_t afull0 = smem_u32(bars + 2 * S), aempty0 = smem_u32(bars + 2 * S + 2);
     const int ng = P.n_in / 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // as in mv_mma_kernel
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -319,15 +324,26 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) mv_mma_q6k_kernel(const Mma
                 break;
             }
             const uint32_t abuf = smem_u32(actb + ab * kQ6ActBytes);
-            mbar_arrive_tx(afull0 + 8 * ab, uint32_t(P.n_tok * (2 * kQ6Chunk + 4 * (kQ6Chunk / 32))));
-            for (int t = 0; t < P.n_tok; ++t) {
-                const long long o = (long long)t * P.n_in + (long long)kc * kQ6Chunk;
-                bulk_g2s(abuf + t * kQ6ActStride, P.xq + o, kQ6Chunk, afull0 + 8 * ab);
-                bulk_g2s(abuf + (kMmaMaxTok + t) * kQ6ActStride, P.xq2 + o, kQ6Chunk, afull0 + 8 * ab);
-                bulk_g2s(abuf + 2 * kMmaMaxTok * kQ6ActStride + t * (kQ6Chunk / 32 + 4) * 4,
-                         P.xd + (long long)t * ng + kc * (kQ6Chunk / 32), 4 * (kQ6Chunk / 32), afull0 + 8 * ab);
-            }
+            auto copy_act = [&]() {
+                mbar_arrive_tx(afull0 + 8 * ab, uint32_t(P.n_tok * (2 * kQ6Chunk + 4 * (kQ6Chunk / 32))));
+                for (int t = 0; t < P.n_tok; ++t) {
+                    const long long o = (long long)t * P.n_in + (long long)kc * kQ6Chunk;
+                    bulk_g2s(abuf + t * kQ6ActStride, P.xq + o, kQ6Chunk, afull0 + 8 * ab);
+                    bulk_g2s(abuf + (kMmaMaxTok + t) * kQ6ActStride, P.xq2 + o, kQ6Chunk, afull0 + 8 * ab);
+                    bulk_g2s(abuf + 2 * kMmaMaxTok * kQ6ActStride + t * (kQ6Chunk / 32 + 4) * 4,
+                             P.xd + (long long)t * ng + kc * (kQ6Chunk / 32), 4 * (kQ6Chunk / 32), afull0 + 8 * ab);
+                }
+            };
+            // chunk 0: the first S tiles (no slot to wait for) go out before its activation, which is
+            // read only after the previous kernel has completed; later chunks: activation first
+            const int pre = kc == 0 ? min(S, my_rb) : 0;
+            bool act_sent = false;
             for (int i = 0; i < my_rb; ++i, ++it) {
+                if (!act_sent && i >= pre) {
+                    if (kc == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
+                    copy_act();
+                    act_sent = true;
+                }
                 const int s = it % S;
                 if (it >= S && !mbar_wait(empty0 + 8 * s, ((it / S) & 1) ^ 1)) {
                     ok = false;
@@ -339,6 +355,10 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) mv_mma_q6k_kernel(const Mma
                     bulk_g2s(stage0 + uint32_t(s) * slot_bytes + uint32_t(r * kQ6ChunkBytes),
                              P.w + (long long)(r0 + r) * P.row_bytes + (long long)kc * kQ6ChunkBytes, kQ6ChunkBytes,
                              full0 + 8 * s);
+            }
+            if (!act_sent && ok) {
+                if (kc == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
+                copy_act();
             }
         }
         if (!ok) {
