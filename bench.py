@@ -123,20 +123,18 @@ def layer_bytes() -> int:
 
 
 def step_fn(stack, xs, batch):
-    """One decode step through the public API: returns the outputs (list).  At batch 1 each group of
-    matrices that shares an input (q/k/v, o, gate/up, down) is one launch that quantises the raw
-    activation itself (mmvq.mv_geteilt / mmvq.mv); larger batches quantise once per input (Eingang)."""
+    """The seven matvecs of each layer on fixed inputs through the public API (mmvq.mv_geteilt: one
+    launch per group of matrices that shares an input, q/k/v, o, gate/up, down): returns the outputs
+    (list).  Batches above 1 quantise once per input (Eingang)."""
     from nemicli_terminal_b200 import mmvq
     outs = []
     for l, mats in enumerate(stack):
         for slot in range(4):
             group = [m for m in mats if m[4] == slot]
             fmt, n_in = group[0][1], group[0][3]
-            if batch == 1:
-                outs += mmvq.mv_geteilt(fmt, [(m[5], m[2]) for m in group], xs[l][slot], n_in)
-            else:
-                e = mmvq.Eingang(xs[l][slot])
-                outs += [mmvq.mv(fmt, m[5], e, m[2], n_in) for m in group]
+            # one launch per group (q/k/v, gate/up share it); more tokens: one Eingang per input
+            x = xs[l][slot] if batch == 1 else mmvq.Eingang(xs[l][slot])
+            outs += mmvq.mv_geteilt(fmt, [(m[5], m[2]) for m in group], x, n_in)
     return outs
 
 

@@ -143,6 +143,14 @@ int qmv_moe_ffn(int gate_up_type, const void* gate, const void* up, long long ga
 int qmv_mv_multi(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
                  const int8_t* xq, const int8_t* xq2, const float* xd, const float* xs, void* stream);
 
+/* qmv_mv_multi for n_tok tokens (Eingang rows of n_in values; y[j] holds n_tok rows of n_out[j] floats):
+ * per group of up to 8 tokens, Q4_K and Q8_0 matrices (rows up to 4096 values) in one tensor-core launch
+ * for all n_jobs matrices, other formats one qmv_mv call per matrix.  Replaces: the reference's separate
+ * mmvq.mv calls on a shared Eingang for q/k/v and gate/up at 2..16 tokens
+ * (ggufengine/models/common.py:404-407, ggufengine/mmvq.py:852-865). */
+int qmv_mv_multi_tok(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
+                     const int8_t* xq, const int8_t* xq2, const float* xd, const float* xs, int n_tok, void* stream);
+
 /* Single token, raw activation: like qmv_mv_multi, but x (n_in values, fp32 if x_is_f32 else bf16) is
  * quantised inside the kernel (the same arithmetic as qmv_quant_q8), so no activation buffers and no
  * separate launch are needed.  Returns QMV_ERR_SHAPE for a row length the staged kernel does not take

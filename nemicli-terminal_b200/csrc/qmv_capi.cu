@@ -403,6 +403,38 @@ int qmv_mv_multi(int ggml_type, int n_jobs, const uint8_t* const* w, const int* 
     return ST_OK;
 }
 
+int qmv_mv_multi_tok(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
+                     const int8_t* xq, const int8_t* xq2, const float* xd, const float* xs, int n_tok, void* stream) {
+    if (!w || !n_out || !y) return ST_NULL;
+    if (n_jobs < 1 || n_jobs > kMaxJobs || n_tok <= 0) return ST_BAD_TOKENS;
+    if (n_tok == 1) return qmv_mv_multi(ggml_type, n_jobs, w, n_out, y, n_in, xq, xq2, xd, xs, stream);
+    for (int j = 0; j < n_jobs; ++j) {
+        const int st = check_mv(ggml_type, w[j], n_out[j], n_in, xq, xq2, xd, xs, y[j]);
+        if (st) return st;
+        if (!aligned(w[j], weight_align(ggml_type))) return ST_BAD_ALIGN;
+    }
+    const long long row_bytes = (long long)(n_in / block_values(ggml_type)) * block_bytes(ggml_type);
+    cudaStream_t cs = static_cast<cudaStream_t>(stream);
+    for (int c0 = 0; c0 < n_tok; c0 += kMaxTokens) {         // groups of up to 8 tokens
+        const int T = n_tok - c0 < kMaxTokens ? n_tok - c0 : kMaxTokens;
+        const long long off = (long long)c0 * n_in;
+        float* yc[kMaxJobs];
+        for (int j = 0; j < n_jobs; ++j) yc[j] = y[j] + (long long)c0 * n_out[j];
+        int st = ST_OK;
+        if (T >= 2 &&
+            mma_q4k_multi(n_jobs, w, n_out, yc, n_in, row_bytes, xq + off, xq2 + off, xd + off / 32, xs + off / 32, T,
+                          ggml_type, cs, &st)) {
+            if (st) return st;
+            continue;
+        }
+        for (int j = 0; j < n_jobs; ++j)
+            if ((st = qmv_mv(ggml_type, w[j], n_out[j], n_in, xq + off, xq2 + off, xd + off / 32, xs + off / 32, T,
+                             yc[j], stream)))
+                return st;
+    }
+    return ST_OK;
+}
+
 int qmv_mv_x(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
              const void* x, int x_is_f32, void* stream) {
     if (!w || !n_out || !y || !x) return ST_NULL;

@@ -75,6 +75,10 @@ template <int FMT> int launch_moe_fmt(int stage, const MoeParams& P, int grid, c
 // caller uses the fallback kernel), true with *status set otherwise
 bool mma_q4k(const uint8_t* w, int n_out, int n_in, long long row_bytes, const int8_t* xq, const int8_t* xq2,
              const float* xd, const float* xs, int T, float* y, int fmt, cudaStream_t st, int* status);
+// the same for 1..4 matrices of one row length that read the same tokens, in one launch
+bool mma_q4k_multi(int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
+                   long long row_bytes, const int8_t* xq, const int8_t* xq2, const float* xd, const float* xs, int T,
+                   int fmt, cudaStream_t st, int* status);
 bool mma_q6k(const uint8_t* w, int n_out, int n_in, long long row_bytes, const int8_t* xq, const int8_t* xq2,
              const float* xd, int T, float* y, int fmt, cudaStream_t st, int* status);
 

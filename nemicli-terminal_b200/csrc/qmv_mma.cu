@@ -7,12 +7,16 @@
 namespace qmv {
 namespace {
 
-// Few-token Q4_K / Q8_0 matvec on the tensor cores; false when the shape or alignment does not qualify.
+// Few-token Q4_K / Q8_0 matvec on the tensor cores, 1..kMmaJobs matrices of the same row length reading
+// the same tokens in one launch; false when the shape or alignment does not qualify.
 template <int FMT>
-bool mma_dense_k(const uint8_t* w, int n_out, int n_in, long long row_bytes, const int8_t* xq, const int8_t* xq2,
-                 const float* xd, const float* xs, int T, float* y, cudaStream_t st, int* status) {
+bool mma_dense_k(int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
+                 long long row_bytes, const int8_t* xq, const int8_t* xq2, const float* xd, const float* xs, int T,
+                 cudaStream_t st, int* status) {
     if (T < 2 || T > kMmaMaxTok || n_in % block_values(FMT) || n_in > kMmaMaxIn || !tma_enabled()) return false;
-    if (!aligned(w, 16) || !aligned(xq, 16) || !aligned(xq2, 16) || row_bytes % 16) return false;
+    if (n_jobs < 1 || n_jobs > kMmaJobs || !aligned(xq, 16) || !aligned(xq2, 16) || row_bytes % 16) return false;
+    for (int j = 0; j < n_jobs; ++j)
+        if (!aligned(w[j], 16) || n_out[j] <= 0) return false;
     constexpr int NCW = 16;
     const long long other = mma_act_bytes(n_in) + mma_red_bytes(NCW) + 2 * 8 * 32;
     const long long slot = kMmaRows * mma_row_stride(row_bytes);
@@ -20,9 +24,19 @@ bool mma_dense_k(const uint8_t* w, int n_out, int n_in, long long row_bytes, con
     if (S > 4) S = 4;
     if (S < 2) return false;
     MmaParams P{};
-    P.w = w; P.y = y; P.xq = xq; P.xq2 = xq2; P.xd = xd; P.xs = xs;
-    P.row_bytes = row_bytes; P.n_out = n_out; P.n_in = n_in; P.n_tok = T; P.stages = int(S);
+    P.w = w[0]; P.y = y[0]; P.xq = xq; P.xq2 = xq2; P.xd = xd; P.xs = xs;
+    P.row_bytes = row_bytes; P.n_out = n_out[0]; P.n_in = n_in; P.n_tok = T; P.stages = int(S);
     P.status = device_status_ptr();
+    P.n_jobs = n_jobs;
+    int tiles = 0;
+    for (int j = 0; j < n_jobs; ++j) {
+        P.jw[j] = w[j];
+        P.jy[j] = y[j];
+        P.jn[j] = n_out[j];
+        P.jt[j] = tiles;
+        tiles += (n_out[j] + kMmaRows - 1) / kMmaRows;
+    }
+    P.jt[n_jobs] = tiles;
     static int configured[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -33,7 +47,6 @@ bool mma_dense_k(const uint8_t* w, int n_out, int n_in, long long row_bytes, con
         }
         configured[dev] = 1;
     }
-    const int tiles = (n_out + kMmaRows - 1) / kMmaRows;
     const int grid = std::min(tiles, sm_count());
     *status = launch_pdl_smem(mv_mma_kernel<FMT, NCW>, dim3(grid), dim3(32 * (NCW + 1)), size_t(S * slot + other), st, P);
     return true;
@@ -42,8 +55,16 @@ bool mma_dense_k(const uint8_t* w, int n_out, int n_in, long long row_bytes, con
 
 bool mma_q4k(const uint8_t* w, int n_out, int n_in, long long row_bytes, const int8_t* xq, const int8_t* xq2,
              const float* xd, const float* xs, int T, float* y, int fmt, cudaStream_t st, int* status) {
-    if (fmt == F_Q4_K) return mma_dense_k<F_Q4_K>(w, n_out, n_in, row_bytes, xq, xq2, xd, xs, T, y, st, status);
-    if (fmt == F_Q8_0) return mma_dense_k<F_Q8_0>(w, n_out, n_in, row_bytes, xq, xq2, xd, xs, T, y, st, status);
+    return mma_q4k_multi(1, &w, &n_out, &y, n_in, row_bytes, xq, xq2, xd, xs, T, fmt, st, status);
+}
+
+bool mma_q4k_multi(int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
+                   long long row_bytes, const int8_t* xq, const int8_t* xq2, const float* xd, const float* xs, int T,
+                   int fmt, cudaStream_t st, int* status) {
+    if (fmt == F_Q4_K)
+        return mma_dense_k<F_Q4_K>(n_jobs, w, n_out, y, n_in, row_bytes, xq, xq2, xd, xs, T, st, status);
+    if (fmt == F_Q8_0)
+        return mma_dense_k<F_Q8_0>(n_jobs, w, n_out, y, n_in, row_bytes, xq, xq2, xd, xs, T, st, status);
     return false;
 }
 

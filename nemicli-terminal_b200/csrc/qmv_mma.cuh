@@ -24,6 +24,8 @@ constexpr int kMmaRows = 16;                     // rows per tile (the MMA's M)
 constexpr int kMmaMaxTok = 8;                    // the MMA's N
 constexpr int kMmaMaxIn = 4096;                  // activation rows staged in shared memory
 
+constexpr int kMmaJobs = 4;                       // matrices of one mv_mma_kernel launch (same input)
+
 struct MmaParams {
     const uint8_t* w;
     float* y;                                    // [token][n_out]
@@ -34,7 +36,32 @@ struct MmaParams {
     long long row_bytes;
     int n_out, n_in, n_tok, stages;
     int* status;
+    // mv_mma_kernel: jobs j < n_jobs (matrices reading the same tokens), weights jw[j], outputs jy[j]
+    // ([token][jn[j]]), 16-row tiles jt[j] .. jt[j + 1] - 1 of the launch's tile list
+    int n_jobs;
+    const uint8_t* jw[kMmaJobs];
+    float* jy[kMmaJobs];
+    int jn[kMmaJobs];
+    int jt[kMmaJobs + 1];
 };
+
+struct MmaTile {
+    const uint8_t* w;
+    float* y;
+    int r0, nr, n_out;
+};
+// tile t of the launch: its job's weights and outputs, first row and rows
+__device__ __forceinline__ MmaTile mma_tile(const MmaParams& P, int t) {
+    int j = 0;
+    while (j + 1 < P.n_jobs && t >= P.jt[j + 1]) ++j;
+    MmaTile m;
+    m.w = P.jw[j];
+    m.y = P.jy[j];
+    m.n_out = P.jn[j];
+    m.r0 = (t - P.jt[j]) * kMmaRows;
+    m.nr = min(kMmaRows, m.n_out - m.r0);
+    return m;
+}
 
 __host__ __device__ constexpr int mma_act_stride(int n_in) { return n_in + 16; }
 __host__ __device__ constexpr int mma_scale_stride(int n_in) { return n_in / 32 + 4; }   // floats per token
@@ -92,7 +119,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) mv_mma_kernel(const MmaPara
     uint64_t* bars = reinterpret_cast<uint64_t*>(red + NCW * kMmaRows * kMmaMaxTok);
     const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + S), stage0 = smem_u32(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_tiles = (P.n_out + kMmaRows - 1) / kMmaRows;
+    const int n_tiles = P.jt[P.n_jobs];
     // programmatic dependent launch: the next kernel may launch now (its weight copies do not read our
     // outputs); the consumers read the activation only after the previous kernel has completed
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -117,10 +144,10 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) mv_mma_kernel(const MmaPara
                 ok = false;
                 break;
             }
-            const int r0 = t * kMmaRows, nr = min(kMmaRows, P.n_out - r0);
-            mbar_arrive_tx(full0 + 8 * s, uint32_t(nr * P.row_bytes));
-            for (int r = 0; r < nr; ++r)
-                bulk_g2s(stage0 + uint32_t(s) * slot_bytes + uint32_t(r) * rstride, P.w + (long long)(r0 + r) * P.row_bytes,
+            const MmaTile m = mma_tile(P, t);
+            mbar_arrive_tx(full0 + 8 * s, uint32_t(m.nr * P.row_bytes));
+            for (int r = 0; r < m.nr; ++r)
+                bulk_g2s(stage0 + uint32_t(s) * slot_bytes + uint32_t(r) * rstride, m.w + (long long)(m.r0 + r) * P.row_bytes,
                          uint32_t(P.row_bytes), full0 + 8 * s);
         }
         if (!ok) {
@@ -242,10 +269,11 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) mv_mma_kernel(const MmaPara
         rw[(gid + 8) * kMmaMaxTok + 2 * tig + 1] = acc[3];
         named_sync(kConsumerBarrier, nthr);
         if (cl < kMmaRows * kMmaMaxTok && !dead) {
-            const int r = cl / kMmaMaxTok, tk = cl % kMmaMaxTok, row = t * kMmaRows + r;
+            const MmaTile m = mma_tile(P, t);
+            const int r = cl / kMmaMaxTok, tk = cl % kMmaMaxTok, row = m.r0 + r;
             float v = 0.f;
             for (int w = 0; w < NCW; ++w) v += red[w * kMmaRows * kMmaMaxTok + cl];   // fixed order
-            if (tk < P.n_tok && row < P.n_out) P.y[(long long)tk * P.n_out + row] = v;
+            if (tk < P.n_tok && r < m.nr) m.y[(long long)tk * m.n_out + row] = v;
         }
         named_sync(kConsumerBarrier, nthr);
     }

@@ -186,28 +186,31 @@ def mv(fmt: str, raw: torch.Tensor, x, n_out: int, n_in: int, out: Optional[torc
 
 
 def mv_geteilt(fmt: str, mats, x, n_in: int) -> list:
-    """Several matrices that read the same single-token input (q/k/v, gate/up) in one launch:
-    mats = [(raw, n_out), ...] (at most 4) -> [y (n_out,) float32, ...].  Each weight byte is read once;
-    the input is quantised once.  New entry point (the reference launches each matrix on its own)."""
+    """Several matrices that read the same input (q/k/v, gate/up) in one launch: mats = [(raw, n_out),
+    ...] (at most 4); x one token ((n_in,) tensor or Eingang) -> [y (n_out,) float32, ...], or M tokens
+    ((M, n_in) tensor or Eingang of M rows) -> [y (M, n_out), ...].  Each weight byte is read once per
+    group of up to 8 tokens (Q4_K / Q8_0 several tokens: one tensor-core launch for all matrices); the
+    input is quantised once.  New entry point (the reference launches each matrix on its own)."""
     if not 1 <= len(mats) <= 4:
         raise RuntimeError("mv_geteilt: 1 to 4 matrices")
     for raw, n_out in mats:
         _check_raw(fmt, raw, n_out, n_in)
-    if not _ist_eingang(x):
+    if not _ist_eingang(x) and x.numel() == n_in:
         ys = _fused(fmt, mats, x, n_in)
         if ys is not None:
             return ys
     e = x if _ist_eingang(x) else Eingang(x)
-    if e.n != n_in:
-        raise RuntimeError(f"mv_geteilt: one token of {n_in} values expected, got {e.n}")
+    if e.n % n_in or e.n == 0:
+        raise RuntimeError(f"mv_geteilt: rows of {n_in} values expected, got {e.n} values")
+    M = e.n // n_in
     dev = mats[0][0].device
-    ys = [torch.empty(n_out, dtype=torch.float32, device=dev) for _, n_out in mats]
+    ys = [torch.empty((n_out,) if M == 1 else (M, n_out), dtype=torch.float32, device=dev) for _, n_out in mats]
     n = len(mats)
     w_arr = (ctypes.c_void_p * n)(*[raw.data_ptr() for raw, _ in mats])
     n_arr = (ctypes.c_int * n)(*[n_out for _, n_out in mats])
     y_arr = (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys])
-    _lib.check(_lib.load().qmv_mv_multi(TYPE_ID[fmt], n, w_arr, n_arr, y_arr, n_in, *e.zeiger(),
-                                        _lib.stream_ptr(dev)), f"qmv_mv_multi {fmt}")
+    _lib.check(_lib.load().qmv_mv_multi_tok(TYPE_ID[fmt], n, w_arr, n_arr, y_arr, n_in, *e.zeiger(), M,
+                                            _lib.stream_ptr(dev)), f"qmv_mv_multi_tok {fmt}")
     return ys
 
 

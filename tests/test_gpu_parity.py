@@ -131,6 +131,22 @@ def test_fused_quantisation_ties(cuda):
     assert torch.equal(fused, mmvq.mv("Q8_0", raw, e, n_out, n_in))
 
 
+@pytest.mark.parametrize("fmt", ["Q4_K", "Q8_0", "Q6_K", "IQ2_XXS"])
+@pytest.mark.parametrize("n_tok", [1, 2, 5, 8, 11])
+def test_several_matrices_equal_single_calls(cuda, fmt, n_tok):
+    """mv_geteilt on several matrices (three, of 512, 136 and 256 rows, sharing one input) gives, bit for
+    bit, what one mv per matrix gives: at several tokens Q4_K and Q8_0 run all matrices in one
+    tensor-core launch (one tile list over the matrices; the 136-row matrix ends in a half tile)."""
+    n_in = 4096
+    mats = [(synth.blocks(fmt, n_out, n_in, seed=n_out + n_tok, device=cuda), n_out) for n_out in (512, 136, 256)]
+    e = mmvq.Eingang(synth.activations(n_tok, n_in, seed=n_tok, device=cuda))
+    ys = mmvq.mv_geteilt(fmt, mats, e, n_in)
+    for (raw, n_out), y in zip(mats, ys):
+        ref = mmvq.mv(fmt, raw, e, n_out, n_in)
+        assert y.shape == ref.shape
+        assert torch.equal(y, ref)
+
+
 @pytest.mark.parametrize("key", GKEYS)
 def test_golden_fixtures_on_gpu(cuda, key):
     t, rows, cols = (int(v) for v in GOLDEN[key + "__shape"])
