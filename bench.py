@@ -672,8 +672,9 @@ def run_moe(args):
     shard.ExpertShardedMoE (experts split, fixed-capacity all-to-all exchanges; each rank has its own
     tokens).  Bytes per call = distinct experts touched x 2,654,208 (per rank)."""
     world, rank, local, device, dist = _init_rank()
-    from nemicli_terminal_b200 import moe, shard, synth
+    from nemicli_terminal_b200 import mmvq, moe, shard, synth
     from nemicli_terminal_b200.formats import TYPE_ID, row_bytes
+    mmvq.pdl(not args.no_pdl)            # static experts; each kernel reads the routing after the previous ends
     from nemicli_terminal_b200.layers import PackedExperts
     lo, hi = shard.shard_range(MOE_EXPERTS, world, rank)
     ne = hi - lo
@@ -702,7 +703,7 @@ def run_moe(args):
                 "config": {"workload": "config4: 128 experts x {gate, up 768x2048, down 2048x768} Q4_K, top-8, "
                                        + ("one GPU, graph-captured" if world == 1 else f"expert-sharded over {world} GPUs, "
                                           "own tokens per rank, fixed-capacity all-to-all exchanges, graph-captured"),
-                           "bytes_per_expert": per_expert, "rotating_routings": 16},
+                           "bytes_per_expert": per_expert, "rotating_routings": 16, "pdl": not args.no_pdl},
                 "batches": results}
         print(json.dumps(line), flush=True)
     if dist is not None:

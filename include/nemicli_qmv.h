@@ -195,8 +195,9 @@ int qmv_act_q8(const float* g, const float* u, int gelu, float* a, int8_t* xq, i
  * models/common.py:456-460, and QuantLinear.bf16_weight, qlinear.py:217). */
 int qmv_unpack(int ggml_type, const uint8_t* w, long long n_values, void* out, int out_dtype, void* stream);
 
-/* Programmatic dependent launch for the staged single-token kernels and the activation producers
- * (qmv_quant_q8, qmv_norm_q8, qmv_act_q8) (default off): when on, each such kernel lets the next kernel
+/* Programmatic dependent launch for the staged single-token kernels, the few-token tensor-core kernels,
+ * the grouped MoE kernels and the activation producers (qmv_quant_q8, qmv_norm_q8, qmv_act_q8) (default
+ * off): when on, each such kernel lets the next kernel
  * of the stream start early; a matvec streams its weights before the previous kernel has finished, and
  * every kernel reads its inputs and writes anything only after the previous kernel completed.  Turn it
  * on only when no kernel launched right before a matvec writes that matvec's weights.  Returns the old

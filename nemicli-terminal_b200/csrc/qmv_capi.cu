@@ -558,9 +558,8 @@ int qmv_moe_ffn(int gate_up_type, const void* gate, const void* up, long long ga
     P.out = out;
     P.status = device_status_ptr();
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    moe_quant_kernel<<<unsigned((nx + 255) / 256), 256, 0, st>>>(x, x_is_f32, x_stride, dim, nx, xq, xq2, xd, xs,
-                                                                 P.gu_done, int(W.n_counters));
-    int rc = launched();
+    int rc = launch_pdl(moe_quant_kernel, dim3(unsigned((nx + 255) / 256)), dim3(256), st, x, x_is_f32, x_stride, dim,
+                        nx, xq, xq2, xd, xs, P.gu_done, int(W.n_counters));
     if (rc) return rc;
     const long long touched = std::min<long long>((long long)n_tok * k, n_exp);
     const int grid_gu = int(std::min<long long>(touched * (ff / 32) * 16 / (kMoeThreads / 32) + 1, 1 << 20));

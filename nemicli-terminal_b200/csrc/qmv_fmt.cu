@@ -135,8 +135,7 @@ int launch_moe_fmt(int stage, const MoeParams& P, int grid, cudaStream_t st) {
         occ[stage] = n;
     }
     grid = std::max(1, std::min(grid, occ[stage] * sm_count()));
-    kern<<<grid, kMoeThreads, 0, st>>>(P);
-    return launched();
+    return launch_pdl(kern, dim3(grid), dim3(kMoeThreads), st, P);
 }
 
 template int launch_moe_fmt<QMV_FMT_ID>(int, const MoeParams&, int, cudaStream_t);

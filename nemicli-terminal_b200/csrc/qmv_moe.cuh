@@ -158,6 +158,8 @@ static __global__ void __launch_bounds__(256) moe_quant_kernel(const void* __res
                                                         int8_t* __restrict__ xq2, float* __restrict__ xd,
                                                         float* __restrict__ xs, int* __restrict__ counters,
                                                         int n_counters) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");           // nothing touched before the previous kernel ends
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     for (long long c = i; c < n_counters; c += (long long)gridDim.x * blockDim.x) counters[c] = 0;
     if ((i & ~31LL) >= n) return;          // dim % 32 == 0: whole warps leave together
@@ -243,7 +245,11 @@ template <int FMT>
 __global__ void __launch_bounds__(kMoeThreads, kMoeMinBlocks) moe_gateup_kernel(const MoeParams P) {
     __shared__ MoeRoute R;
     __shared__ uint2 grid[smem_grid_format<FMT>() ? 256 : 1];
+    // programmatic dependent launch: the next kernel may launch now; the routing ids, the activation
+    // and the counters are read only after the previous kernel has completed (the codebook is a constant)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if constexpr (smem_grid_format<FMT>()) load_grid<FMT>(grid);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     moe_route(P, R);
     MvParams A{};
     A.xq = P.xq; A.xq2 = P.xq2; A.xd = P.xd; A.xs = P.xs; A.n_in = P.dim;
@@ -313,7 +319,11 @@ template <int FMT>
 __global__ void __launch_bounds__(kMoeThreads, kMoeMinBlocks) moe_down_kernel(const MoeParams P) {
     __shared__ MoeRoute R;
     __shared__ uint2 grid[smem_grid_format<FMT>() ? 256 : 1];
+    // programmatic dependent launch: the next kernel may launch now; the routing ids, the activation
+    // and the counters are read only after the previous kernel has completed (the codebook is a constant)
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if constexpr (smem_grid_format<FMT>()) load_grid<FMT>(grid);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     moe_route(P, R);
     MvParams A{};
     A.xq = P.aq; A.xq2 = P.aq2; A.xd = P.ad; A.xs = P.as; A.n_in = P.ff;
