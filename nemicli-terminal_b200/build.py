@@ -10,6 +10,7 @@ without depending on where torch keeps its own runtime.
 from __future__ import annotations
 
 import concurrent.futures as cf
+import fcntl
 import glob
 import os
 import shutil
@@ -98,10 +99,20 @@ def up_to_date(out: str = LIB_PATH, obj_dir: str = OBJ_DIR) -> bool:
 
 def build(force: bool = False, verbose: bool = False, extra: tuple = (), out: str = LIB_PATH,
           obj_dir: str = OBJ_DIR, jobs: int = 0) -> str:
-    """Compile the stale objects in parallel and link `out`.  extra: more nvcc flags (e.g. -D...)."""
+    """Compile the stale objects in parallel and link `out`.  extra: more nvcc flags (e.g. -D...).
+    Processes that build at the same time (one per rank under torchrun) take turns on a lock file in
+    obj_dir; the later ones find the library up to date."""
     if not force and up_to_date(out, obj_dir):
         return out
     os.makedirs(obj_dir, exist_ok=True)
+    with open(os.path.join(obj_dir, ".lock"), "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        if not force and up_to_date(out, obj_dir):
+            return out
+        return _build_locked(force, verbose, extra, out, obj_dir, jobs)
+
+
+def _build_locked(force: bool, verbose: bool, extra: tuple, out: str, obj_dir: str, jobs: int) -> str:
     stamp = os.path.join(obj_dir, "flags.txt")
     flags = " ".join(extra)
     if not os.path.exists(stamp) or open(stamp).read() != flags:
