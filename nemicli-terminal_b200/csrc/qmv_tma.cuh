@@ -801,7 +801,10 @@ __device__ __forceinline__ const uint8_t* tma_slot_base(const TmaParams& P, int 
 
 // shared-memory layout: [stages x stage bytes][reduction 2 x NCW x R floats][codebook 2 KB]
 //                      [fused activation: xq K, xq2 K, xd K/32, xs K/32 (XF only)][mbarriers]
-constexpr int kTmaRowsPerTeam = 4;          // rows of a full tile per team (compile-time fast path)
+#ifndef QMV_TMA_NPER                        // sweep builds may set another value
+#define QMV_TMA_NPER 4
+#endif
+constexpr int kTmaRowsPerTeam = QMV_TMA_NPER;   // rows of a full tile per team (compile-time fast path)
 // partial sums of rows spread over several warps: [row in window][warp in team], reduced once per window
 constexpr int kPartFloats = 2048;
 __host__ __device__ constexpr int tma_red_bytes(int ncw) { return kPartFloats * 4 + 0 * ncw; }
