@@ -296,6 +296,7 @@ namespace qmv {
 constexpr int kQ6Chunk = 2048;                     // values per K-chunk
 constexpr int kQ6ChunkBytes = kQ6Chunk / 256 * 210;  // 1680
 constexpr int kQ6MaxBlocks = 64;                   // row blocks per CTA whose sums fit in shared memory
+constexpr int kQ6RegBlocks = 4;                    // row blocks per CTA whose sums stay in registers
 constexpr int kQ6ActStride = kQ6Chunk + 16;        // bytes per token row of a staged activation chunk
 // one staged chunk: xq [8][stride], xq2 [8][stride], xd [8][64 + 4] floats
 constexpr int kQ6ActBytes = 2 * kMmaMaxTok * kQ6ActStride + kMmaMaxTok * (kQ6Chunk / 32 + 4) * 4;
@@ -403,6 +404,14 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) mv_mma_q6k_kernel(const Mma
     const int sbw = warp >> 1, nw = warp & 1;           // this warp: superblock sbw of the chunk, half nw
     const bool tok_ok = gid < P.n_tok;                  // B fragment: token gid (zero beyond n_tok)
     const int t0 = 2 * tig, t1 = 2 * tig + 1;           // tokens of this thread's C values
+    // up to kQ6RegBlocks row blocks a CTA: each warp keeps its running sums in registers across the
+    // chunks and the warps' sums are added once at the end (no barrier per tile); more: per tile
+    // through shared memory into `run`
+    const bool in_regs = my_rb <= kQ6RegBlocks;
+    float racc[kQ6RegBlocks][4];
+#pragma unroll
+    for (int b = 0; b < kQ6RegBlocks; ++b) racc[b][0] = racc[b][1] = racc[b][2] = racc[b][3] = 0.f;
+    float* rw = red + warp * kMmaRows * kMmaMaxTok;
     bool dead = false;
     int it = 0;
     for (int kc = 0; kc < n_kc; ++kc) {
@@ -462,7 +471,17 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) mv_mma_q6k_kernel(const Mma
             }
             __syncwarp();
             if (got && lane == 0) mbar_arrive(empty0 + 8 * s);
-            float* rw = red + warp * kMmaRows * kMmaMaxTok;
+            if (in_regs) {
+#pragma unroll
+                for (int b = 0; b < kQ6RegBlocks; ++b)
+                    if (b == i) {
+                        racc[b][0] += acc[0];
+                        racc[b][1] += acc[1];
+                        racc[b][2] += acc[2];
+                        racc[b][3] += acc[3];
+                    }
+                continue;
+            }
             rw[gid * kMmaMaxTok + t0] = acc[0];
             rw[gid * kMmaMaxTok + t1] = acc[1];
             rw[(gid + 8) * kMmaMaxTok + t0] = acc[2];
@@ -479,6 +498,30 @@ __global__ void __launch_bounds__(32 * (NCW + 1), 1) mv_mma_q6k_kernel(const Mma
     }
     for (int i = 0; i < my_rb; ++i) {
         const int r0 = (int(blockIdx.x) + int(gridDim.x) * i) * kMmaRows;
+        if (in_regs) {                                  // the warps' register sums, added in warp order
+            float v4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int b = 0; b < kQ6RegBlocks; ++b)
+                if (b == i) {
+                    v4[0] = racc[b][0];
+                    v4[1] = racc[b][1];
+                    v4[2] = racc[b][2];
+                    v4[3] = racc[b][3];
+                }
+            rw[gid * kMmaMaxTok + t0] = v4[0];
+            rw[gid * kMmaMaxTok + t1] = v4[1];
+            rw[(gid + 8) * kMmaMaxTok + t0] = v4[2];
+            rw[(gid + 8) * kMmaMaxTok + t1] = v4[3];
+            named_sync(kConsumerBarrier, nthr);
+            if (cl < kMmaRows * kMmaMaxTok && !dead) {
+                const int r = cl / kMmaMaxTok, tk = cl % kMmaMaxTok;
+                float v = 0.f;
+                for (int w = 0; w < NCW; ++w) v += red[w * kMmaRows * kMmaMaxTok + cl];   // fixed order
+                if (tk < P.n_tok && r0 + r < P.n_out) P.y[(long long)tk * P.n_out + r0 + r] = v;
+            }
+            named_sync(kConsumerBarrier, nthr);
+            continue;
+        }
         if (cl < kMmaRows * kMmaMaxTok && !dead) {
             const int r = cl / kMmaMaxTok, tk = cl % kMmaMaxTok;
             if (tk < P.n_tok && r0 + r < P.n_out) P.y[(long long)tk * P.n_out + r0 + r] = run[i * kMmaRows * kMmaMaxTok + cl];
