@@ -162,30 +162,34 @@ def build_calls(stack, device, seed: int = 0):
     """The chain's step (same weights, norms and residual stream as build_chain with the same seed) as
     per-call launches with their true dependencies, the reference's one-token step pattern: per layer
     RMS norm -> q,k,v (mmvq.mv_norm) | o on q's output | RMS norm of h + o -> gate,up | SiLU(gate) * up
-    (mmvq.akt_q8) -> down.  With PDL on every producer (norm_q8, quant_q8, akt_q8) is its own launch that
-    starts while the previous matvec finishes, and each matvec streams its weights early; with PDL off
-    the norms and quantisations run inside the matvec launches.
+    -> down.  The RMS norms are norm_q8 launches; q's quantised output (o's input) and SiLU(gate) * up
+    quantised (down's input) are formed by the q/k/v and gate/up launches themselves (mmvq.NextInput),
+    so a layer is six launches.  With PDL every launch starts while the previous one finishes and each
+    matvec streams its weights early.
     Returns (step function -> outputs, h0, the list the last down output is written to)."""
     from nemicli_terminal_b200 import mmvq, synth
     g = torch.Generator(device=device)
     g.manual_seed(seed)
     h0 = synth.activations(1, 4096, seed=seed + 11, device=device)[0].contiguous()
-    norms = []
+    norms, nexts = [], []
     for _ in stack:
         wa = (torch.rand(4096, generator=g, device=device) + 0.5).contiguous()
         wf = (torch.rand(4096, generator=g, device=device) + 0.5).contiguous()
         norms.append((wa, wf))
+        # o's input (q's outputs quantised) and down's (SiLU(gate) * up) formed by the launches before them
+        nexts.append((mmvq.NextInput(4096, "quant", device), mmvq.NextInput(14336, "silu_mul", device)))
     last = [None]
 
     def step():
         h, r, outs = h0, None, []
-        for mats, (wa, wf) in zip(stack, norms):
+        for mats, (wa, wf), (n_o, n_d) in zip(stack, norms, nexts):
             m = {name: (fmt, raw, n_out, n_in) for name, fmt, n_out, n_in, slot, raw in mats}
-            (q, k, v), h = mmvq.mv_norm("Q4_K", [(m[x][1], m[x][2]) for x in ("q", "k", "v")], h, wa, 1e-5, rest=r)
-            o = mmvq.mv("Q4_K", m["o"][1], q, 4096, 4096)
-            (gt, up), h = mmvq.mv_norm("Q4_K", [(m[x][1], m[x][2]) for x in ("gate", "up")], h, wf, 1e-5, rest=o)
-            _, e = mmvq.akt_q8(gt, up, False)
-            d = mmvq.mv("Q6_K", m["down"][1], e, 4096, 14336)
+            (q, k, v), h = mmvq.mv_norm("Q4_K", [(m[x][1], m[x][2]) for x in ("q", "k", "v")], h, wa, 1e-5, rest=r,
+                                        next_input=n_o, src=(0,))
+            o = mmvq.mv("Q4_K", m["o"][1], n_o.eingang, 4096, 4096)
+            (gt, up), h = mmvq.mv_norm("Q4_K", [(m[x][1], m[x][2]) for x in ("gate", "up")], h, wf, 1e-5, rest=o,
+                                        next_input=n_d, src=(0, 1))
+            d = mmvq.mv("Q6_K", m["down"][1], n_d.eingang, 4096, 14336)
             outs += [q, k, v, o, gt, up, d]
             r = d
         last[0] = r
@@ -196,9 +200,9 @@ def build_calls(stack, device, seed: int = 0):
 
 
 def calls_launches_per_layer(pdl: bool) -> int:
-    """Kernels per layer of build_calls' step: with PDL norm, q,k,v | quantise, o | norm, gate,up |
-    SiLU gate, down; without it q,k,v (norm inside) | o | gate,up (norm inside) | SiLU gate, down."""
-    return 8 if pdl else 5
+    """Kernels per layer of build_calls' step: norm, q,k,v (forming o's input) | o | norm, gate,up
+    (forming down's input) | down, with or without PDL."""
+    return 6
 
 
 def capture(fn):
@@ -519,8 +523,8 @@ def run_ours(args):
                                    "(q,k,v,o,gate,up Q4_K; down Q6_K), batch 1; RMS norms with the residual "
                                    "adds and the SiLU gate between the matvecs, o_proj reads q_proj's output in "
                                    "place of attention" + ("; one decode-chain launch per step" if args.mode == "chain"
-                                                           else "; per-call launches (norm_q8 / quant_q8 / akt_q8, "
-                                                                "then the matvecs on the input), PDL"),
+                                                           else "; per-call launches (norm_q8, then the matvecs; o's and "
+                                                                "down's inputs formed by the launches before them), PDL"),
                        "layers": args.layers, "batch": 1, "weight_bytes_per_step": step_bytes,
                        "l2": "inputs larger than L2 (4.41 GB distinct weights per step), no flush",
                        "parallelism": (f"value: replicas x{world} of the config-2 stack (one per GPU, no "

@@ -159,6 +159,20 @@ int qmv_mv_multi_tok(int ggml_type, int n_jobs, const uint8_t* const* w, const i
 int qmv_mv_x(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
              const void* x, int x_is_f32, void* stream);
 
+/* qmv_mv_multi (one token, pre-quantised input) that also forms the NEXT matvec's activation input from
+ * its own outputs: ep_kind 1 quantises y[ep_j0] (as qmv_quant_q8 would, bit for bit); ep_kind 2 forms
+ * a = SiLU(y[ep_j0]) * y[ep_j1] into ep_a and quantises it (as qmv_act_q8 with gelu = 0 would).  The CTA
+ * that writes the last rows of a 32-row group does that group, so no producer launch follows the
+ * matvec.  ep_counters: n_out[ep_j0] / 32 ints, zero before the first call; each call leaves them zero
+ * again (calls sharing them must not overlap).  n_out[ep_j0] % 32 == 0 (ep_kind 2: the same n_out for
+ * both jobs).  Returns QMV_ERR_SHAPE where the staged kernel cannot do it (then qmv_mv_multi and the
+ * producer).  Replaces: mv + Eingang / akt_q8 on its outputs in the reference's one-token step
+ * (ggufengine/models/baukasten.py:222-240, ggufengine/mmvq.py:959-966). */
+int qmv_mv_multi_ep(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
+                    const int8_t* xq, const int8_t* xq2, const float* xd, const float* xs, int ep_kind, int ep_j0,
+                    int ep_j1, int* ep_counters, int8_t* ep_xq, int8_t* ep_xq2, float* ep_xd, float* ep_xs,
+                    float* ep_a, void* stream);
+
 /* Single token, RMS norm fused in front: qmv_norm_q8 (h, r, rs, h_out, norm_w, eps; n = n_in) followed by
  * qmv_mv_multi on its activation input, in one launch.  The quantised input is bit-identical to
  * qmv_norm_q8's (the same order of the sum of squares and the same roundings), so are the outputs; xn is

@@ -33,6 +33,7 @@ _SIGNATURES = {
     "qmv_mv_multi": ([I, I, P, P, P, I, P, P, P, P, P], I),
     "qmv_mv_x": ([I, I, P, P, P, I, P, I, P], I),
     "qmv_mv_multi_tok": ([I, I, P, P, P, I, P, P, P, P, I, P], I),
+    "qmv_mv_multi_ep": ([I, I, P, P, P, I, P, P, P, P, I, I, I, P, P, P, P, P, P, P], I),
     "qmv_mv_norm": ([I, I, P, P, P, I, P, P, ctypes.c_float, P, P, ctypes.c_float, P], I),
     "qmv_set_pdl": ([I], I),
     "qmv_chain": ([P, I, P, P], I),

@@ -80,9 +80,7 @@ __global__ void __launch_bounds__(256) act_q8_kernel(const float* __restrict__ g
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if ((i & ~31) >= n) return;                       // whole warps: n % 32 == 0
-    const float x = g[i];
-    float v = gelu ? 0.5f * x * (1.f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x))) : x / (1.f + expf(-x));
-    if (u) v *= u[i];
+    const float v = act_value(g[i], u ? u[i] : 0.f, u != nullptr, gelu);
     a[i] = v;
     quantize_group(v, i, xq, xq2, xd, xs);
 }

@@ -165,6 +165,16 @@ int launch_tma(int fmt, TmaParams& P, const TmaPlan& pl, cudaStream_t st) {
 
 // dense jobs sharing one activation row (n_jobs <= kMaxJobs): pre-quantised (x == nullptr) or raw x
 // (x_kind 1 = fp32, 2 = bf16) quantised in the kernel.  false -> the caller uses the fallback kernel.
+struct EpOut {                   // epilogue producer (TmaParams ep_*)
+    int kind, j0, j1;
+    int* cnt;
+    int8_t* xq;
+    int8_t* xq2;
+    float* xd;
+    float* xs;
+    float* a;
+};
+
 struct NormIn {                  // fused RMS norm of an fp32 x (TmaParams nr .. neps)
     const float* r;
     float rs;
@@ -175,10 +185,12 @@ struct NormIn {                  // fused RMS norm of an fp32 x (TmaParams nr ..
 
 bool tma_dense(int fmt, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
                const int8_t* xq, const int8_t* xq2, const float* xd, const float* xs, const void* x, int x_kind,
-               int32_t* s, int32_t* s2, cudaStream_t st, int* status, const NormIn* norm = nullptr) {
+               int32_t* s, int32_t* s2, cudaStream_t st, int* status, const NormIn* norm = nullptr,
+               const EpOut* ep = nullptr) {
     const long long row_bytes = (long long)(n_in / block_values(fmt)) * block_bytes(fmt);
     TmaPlan pl;
     if (!tma_plan(fmt, n_in, row_bytes, x != nullptr, pl)) return false;
+    if (ep && pl.G <= 32) return false;          // the epilogue runs in the wide teams' window flush
     for (int j = 0; j < n_jobs; ++j)
         if (!aligned(w[j], 16)) return false;
     TmaParams P{};
@@ -201,6 +213,10 @@ bool tma_dense(int fmt, int n_jobs, const uint8_t* const* w, const int* n_out, f
     P.s = s; P.s2 = s2;
     if (norm) {
         P.nr = norm->r; P.nrs = norm->rs; P.nh = norm->h_out; P.nw = norm->w; P.neps = norm->eps;
+    }
+    if (ep) {
+        P.ep_kind = ep->kind; P.ep_j0 = ep->j0; P.ep_j1 = ep->j1; P.ep_cnt = ep->cnt;
+        P.ep_xq = ep->xq; P.ep_xq2 = ep->xq2; P.ep_xd = ep->xd; P.ep_xs = ep->xs; P.ep_a = ep->a;
     }
     if (s) *status = launch_tma<0, true>(fmt, P, pl, st);
     else if (!x) *status = launch_tma<0, false>(fmt, P, pl, st);
@@ -452,6 +468,32 @@ int qmv_mv_x(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_ou
                   nullptr, nullptr, static_cast<cudaStream_t>(stream), &st))
         return st;
     return ST_BAD_SHAPE;        // the shape needs the fallback kernel: quantise with qmv_quant_q8, then qmv_mv
+}
+
+int qmv_mv_multi_ep(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,
+                    const int8_t* xq, const int8_t* xq2, const float* xd, const float* xs, int ep_kind, int ep_j0,
+                    int ep_j1, int* ep_counters, int8_t* ep_xq, int8_t* ep_xq2, float* ep_xd, float* ep_xs,
+                    float* ep_a, void* stream) {
+    if (!w || !n_out || !y || !ep_counters || !ep_xq || !ep_xq2 || !ep_xd || !ep_xs) return ST_NULL;
+    if (n_jobs < 1 || n_jobs > kMaxJobs) return ST_BAD_TOKENS;
+    if (ep_kind != 1 && ep_kind != 2) return ST_BAD_SHAPE;
+    if (ep_j0 < 0 || ep_j0 >= n_jobs || (ep_kind == 2 && (ep_j1 < 0 || ep_j1 >= n_jobs || ep_j1 == ep_j0 || !ep_a)))
+        return ep_kind == 2 && !ep_a ? ST_NULL : ST_BAD_SHAPE;
+    if (n_out[ep_j0] % 32 || (ep_kind == 2 && n_out[ep_j1] != n_out[ep_j0])) return ST_BAD_SHAPE;
+    if (!aligned(ep_counters, 4) || !aligned(ep_xq, 16) || !aligned(ep_xq2, 16) || !aligned(ep_xd, 4) ||
+        !aligned(ep_xs, 4) || (ep_a && !aligned(ep_a, 4)))
+        return ST_BAD_ALIGN;
+    for (int j = 0; j < n_jobs; ++j) {
+        const int st = check_mv(ggml_type, w[j], n_out[j], n_in, xq, xq2, xd, xs, y[j]);
+        if (st) return st;
+        if (!aligned(w[j], weight_align(ggml_type))) return ST_BAD_ALIGN;
+    }
+    const EpOut ep{ep_kind, ep_j0, ep_kind == 2 ? ep_j1 : -1, ep_counters, ep_xq, ep_xq2, ep_xd, ep_xs, ep_a};
+    int st = ST_OK;
+    if (tma_dense(ggml_type, n_jobs, w, n_out, y, n_in, xq, xq2, xd, xs, nullptr, 0, nullptr, nullptr,
+                  static_cast<cudaStream_t>(stream), &st, nullptr, &ep))
+        return st;
+    return ST_BAD_SHAPE;        // the shape needs another kernel: qmv_mv_multi, then qmv_quant_q8 / qmv_act_q8
 }
 
 int qmv_mv_norm(int ggml_type, int n_jobs, const uint8_t* const* w, const int* n_out, float* const* y, int n_in,

@@ -75,6 +75,14 @@ __device__ __forceinline__ void quantize_group8(const float (&v)[4], long long i
     }
 }
 
+// the gated activation of act_q8 (ggufengine/mmvq.py:120-131): SiLU, or GELU in its tanh form, of x,
+// times u (has_u); one definition for the producer kernel and the staged matvec's epilogue
+__device__ __forceinline__ float act_value(float x, float u, bool has_u, int gelu) {
+    float v = gelu ? 0.5f * x * (1.f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x))) : x / (1.f + expf(-x));
+    if (has_u) v *= u;
+    return v;
+}
+
 static __global__ void __launch_bounds__(256) quant_q8_kernel(const void* __restrict__ x, int x_f32,
                                                        int8_t* __restrict__ xq, int8_t* __restrict__ xq2,
                                                        float* __restrict__ xd, float* __restrict__ xs,

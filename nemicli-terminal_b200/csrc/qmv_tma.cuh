@@ -52,7 +52,49 @@ struct TmaParams {
     const float* nw;
     float* nh;
     float nrs, neps;
+    // epilogue producer (dense jobs, teams wider than a warp): the next matvec's activation input from
+    // this launch's outputs.  A counter per 32-row group (ep_cnt, zero before the call, zero again after
+    // it) counts the group's rows as CTAs write them; the CTA that completes a group forms its input:
+    //   ep_kind 1: job ep_j0's outputs quantised (quant_q8's arithmetic)
+    //   ep_kind 2: a = SiLU(job ep_j0) * job ep_j1 (act_q8's arithmetic, written to ep_a), quantised
+    int ep_kind, ep_j0, ep_j1;
+    int* ep_cnt;
+    int8_t* ep_xq;
+    int8_t* ep_xq2;
+    float* ep_xd;
+    float* ep_xs;
+    float* ep_a;
 };
+
+// warp w of nw, after the rows [row0, row0 + rows) of job `job` are in y (all of this CTA's consumer
+// threads' stores ordered before by a barrier): count them per 32-row group (the warps take the
+// groups in turn, so their counter round trips overlap); for each group this completes, form its part
+// of the next input (see TmaParams ep_*)
+__device__ __forceinline__ void ep_groups(const TmaParams& P, int job, int row0, int rows, int w, int nw) {
+    if (P.ep_kind == 0 || rows <= 0 || (job != P.ep_j0 && job != P.ep_j1)) return;
+    const int lane = threadIdx.x & 31;
+    const int need = P.ep_kind == 2 ? 64 : 32;
+    for (int g = (row0 >> 5) + w; g <= (row0 + rows - 1) >> 5; g += nw) {
+        const int a = max(row0, 32 * g), b = min(row0 + rows, 32 * g + 32);
+        int last = 0;
+        if (lane == 0) {
+            int old;
+            asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(P.ep_cnt + g), "r"(b - a) : "memory");
+            last = old + (b - a) == need;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        __syncwarp();                                    // lane 0's acquire before every lane's loads
+        if (!last) continue;
+        const int i = 32 * g + lane;
+        float v = __ldcg(P.y[P.ep_j0] + i);
+        if (P.ep_kind == 2) {
+            v = act_value(v, __ldcg(P.y[P.ep_j1] + i), true, 0);
+            P.ep_a[i] = v;
+        }
+        quantize_group(v, i, P.ep_xq, P.ep_xq2, P.ep_xd, P.ep_xs);
+        if (lane == 0) P.ep_cnt[g] = 0;                  // ready for the next call
+    }
+}
 
 // ---- shared-memory access -----------------------------------------------------------------------
 
@@ -994,6 +1036,7 @@ __global__ void __launch_bounds__(32 * (NCW + 1), NCW <= 8 ? 2 : 1) mv_tma_kerne
             }
         }
         named_sync(kConsumerBarrier, 32 * NCW);
+        if (!dead && P.ids == nullptr) ep_groups(P, w_job, w_row0, w_rows, warp, NCW);
         w_rows = 0;
     };
     const long long hi = cta_row_begin(P, blockIdx.x + 1);

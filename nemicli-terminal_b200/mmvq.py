@@ -11,7 +11,8 @@ meaning and return shapes, computed by this package's sm_100a kernels through th
 * `norm_q8`, `akt_q8` — the fused one-token producers of an Eingang (mmvq.py:946-966): RMS norm with the
   residual add, and the gated activation, each one launch that also quantises its output.
 * `mv_geteilt`, `mv_norm` (new) — up to four matrices on one single-token input in one launch;
-  `mv_norm` forms norm_q8's RMS norm inside that launch (bit-identical to the two calls).
+  `mv_norm` forms norm_q8's RMS norm inside that launch (bit-identical to the two calls); with a
+  `NextInput` the launch also forms the next matvec's input (quantised outputs, or SiLU·mul of two).
 * `rope_kv`, `attention1`, `schritt_moeglich` — the attention steps of the reference's fused one-token
   layer (mmvq.py:969-1014) are not part of this package (the matvec path ends where attention begins).
   They are forwarded to an attention provider registered with `set_attention` (the reference's own
@@ -185,17 +186,52 @@ def mv(fmt: str, raw: torch.Tensor, x, n_out: int, n_in: int, out: Optional[torc
     return y[0] if vektor else y
 
 
-def mv_geteilt(fmt: str, mats, x, n_in: int) -> list:
+class NextInput:
+    """The activation input of the next matvec, formed from a matvec's own outputs by the CTAs that
+    write them (qmv_mv_multi_ep), so no producer launch follows the matvec: kind "quant" (one matrix's
+    outputs quantised, as Eingang(y) would) or "silu_mul" (SiLU of one matrix's outputs times
+    another's, as akt_q8(g, u, False) would; the fp32 product in `a`).  n: the values of the input.
+    Holds the Eingang, `a` and one counter per 32 values (zero between calls).  Calls that share one
+    object must not overlap on the GPU.  New entry point."""
+
+    def __init__(self, n: int, kind: str, device):
+        if kind not in ("quant", "silu_mul") or n % 32:
+            raise ValueError(f"NextInput: kind quant or silu_mul and a multiple of 32 values (got {kind}, {n})")
+        self.n, self.kind = n, kind
+        self.eingang = Eingang(n=n, device=device)
+        self.a = torch.empty(n, dtype=torch.float32, device=device) if kind == "silu_mul" else None
+        self.counters = torch.zeros(n // 32, dtype=torch.int32, device=device)
+
+
+def _produce(nxt: "NextInput", ys: list, src) -> None:
+    """The producer launch that qmv_mv_multi_ep saves (the shapes it does not take)."""
+    lib, e = _lib.load(), nxt.eingang
+    y0 = ys[src[0]].reshape(-1)
+    if nxt.kind == "quant":
+        _lib.check(lib.qmv_quant_q8(_lib.ptr(y0), 1, *e.zeiger(), nxt.n, _lib.stream_ptr(y0.device)), "qmv_quant_q8")
+    else:
+        y1 = ys[src[1]].reshape(-1)
+        _lib.check(lib.qmv_act_q8(_lib.ptr(y0), _lib.ptr(y1), 0, _lib.ptr(nxt.a), *e.zeiger(), nxt.n,
+                                  _lib.stream_ptr(y0.device)), "qmv_act_q8")
+
+
+def mv_geteilt(fmt: str, mats, x, n_in: int, next_input: Optional["NextInput"] = None, src=(0,)) -> list:
     """Several matrices that read the same input (q/k/v, gate/up) in one launch: mats = [(raw, n_out),
     ...] (at most 4); x one token ((n_in,) tensor or Eingang) -> [y (n_out,) float32, ...], or M tokens
     ((M, n_in) tensor or Eingang of M rows) -> [y (M, n_out), ...].  Each weight byte is read once per
     group of up to 8 tokens (Q4_K / Q8_0 several tokens: one tensor-core launch for all matrices); the
-    input is quantised once.  New entry point (the reference launches each matrix on its own)."""
+    input is quantised once.  next_input (one token): also form the next matvec's input from the
+    outputs of matrices src (NextInput; in the same launch where the staged kernel takes it, else by
+    the producer launch after it).  New entry point (the reference launches each matrix on its own)."""
     if not 1 <= len(mats) <= 4:
         raise RuntimeError("mv_geteilt: 1 to 4 matrices")
     for raw, n_out in mats:
         _check_raw(fmt, raw, n_out, n_in)
-    if not _ist_eingang(x) and x.numel() == n_in:
+    if next_input is not None:
+        need = 2 if next_input.kind == "silu_mul" else 1
+        if len(src) != need or any(not 0 <= j < len(mats) or mats[j][1] != next_input.n for j in src):
+            raise RuntimeError(f"mv_geteilt: next_input {next_input.kind} takes {need} matrices of {next_input.n} rows")
+    if not _ist_eingang(x) and x.numel() == n_in and next_input is None:
         ys = _fused(fmt, mats, x, n_in)
         if ys is not None:
             return ys
@@ -209,19 +245,32 @@ def mv_geteilt(fmt: str, mats, x, n_in: int) -> list:
     w_arr = (ctypes.c_void_p * n)(*[raw.data_ptr() for raw, _ in mats])
     n_arr = (ctypes.c_int * n)(*[n_out for _, n_out in mats])
     y_arr = (ctypes.c_void_p * n)(*[y.data_ptr() for y in ys])
+    if next_input is not None:
+        if M != 1:
+            raise RuntimeError("mv_geteilt: next_input takes one token")
+        nx = next_input
+        st = _lib.load().qmv_mv_multi_ep(TYPE_ID[fmt], n, w_arr, n_arr, y_arr, n_in, *e.zeiger(),
+                                         1 if nx.kind == "quant" else 2, src[0], src[-1], _lib.ptr(nx.counters),
+                                         *nx.eingang.zeiger(), _lib.ptr(nx.a), _lib.stream_ptr(dev))
+        if st != 2:
+            _lib.check(st, f"qmv_mv_multi_ep {fmt}")
+            return ys
     _lib.check(_lib.load().qmv_mv_multi_tok(TYPE_ID[fmt], n, w_arr, n_arr, y_arr, n_in, *e.zeiger(), M,
                                             _lib.stream_ptr(dev)), f"qmv_mv_multi_tok {fmt}")
+    if next_input is not None:
+        _produce(next_input, ys, src)
     return ys
 
 
 def mv_norm(fmt: str, mats, h: torch.Tensor, w: torch.Tensor, eps: float, rest: Optional[torch.Tensor] = None,
-            rs: float = 1.0, force: bool = False):
+            rs: float = 1.0, force: bool = False, next_input: Optional["NextInput"] = None, src=(0,)):
     """norm_q8(h, w, eps, rest, rs) followed by mv_geteilt on its input, in one launch: every CTA of the
     matvec forms the RMS norm (the norm kernel's sum order, so the quantised input and the outputs are
     bit-identical to the two calls).  mats = [(raw, n_out), ...] (1 to 4, one token) -> ([y (n_out,)
     float32, ...], new h) where new h = h + rs * rest (h itself without rest).  With PDL on (the two
     launches are faster then), for rows longer than FUSED_MAX_IN and for shapes the staged kernel does
     not take it is the two calls; force takes the one launch wherever the kernel takes the shape.
+    next_input / src: as mv_geteilt (then always the two calls, the matvec forming the next input).
     New entry point (the reference's one-token step calls norm_q8 and then mv per matrix,
     models/baukasten.py:205-240)."""
     if not 1 <= len(mats) <= 4:
@@ -234,7 +283,7 @@ def mv_norm(fmt: str, mats, h: torch.Tensor, w: torch.Tensor, eps: float, rest: 
         raise RuntimeError(f"mv_norm: h, w and rest must have the same length ({n_in})")
     for raw, n_out in mats:
         _check_raw(fmt, raw, n_out, n_in)
-    if force or _fused_ok(n_in):
+    if next_input is None and (force or _fused_ok(n_in)):
         dev = mats[0][0].device
         ys = [torch.empty(n_out, dtype=torch.float32, device=dev) for _, n_out in mats]
         hn = None if rest is None else torch.empty(n_in, dtype=torch.float32, device=dev)
@@ -249,7 +298,7 @@ def mv_norm(fmt: str, mats, h: torch.Tensor, w: torch.Tensor, eps: float, rest: 
             _lib.check(st, f"qmv_mv_norm {fmt}")
             return ys, (h if hn is None else hn)
     _, e, h_new = norm_q8(h, w, eps, rest, rs)
-    return mv_geteilt(fmt, mats, e, n_in), h_new
+    return mv_geteilt(fmt, mats, e, n_in, next_input, src), h_new
 
 
 _TEILEN = threading.local()

@@ -184,3 +184,50 @@ def test_mv_norm_refusals(cuda):
     assert st(1, wa, na, ya, 4096, _lib.ptr(h), _lib.ptr(h), one, None, _lib.ptr(w), eps, None) == 6   # r, no h_out
     assert st(5, wa, na, ya, 4096, _lib.ptr(h), None, one, None, _lib.ptr(w), eps, None) == 4    # > 4 matrices
     assert st(1, wa, na, ya, 4000, _lib.ptr(h), None, one, None, _lib.ptr(w), eps, None) == 2    # row length
+
+
+def _eingang_equal(a, b):
+    return all(torch.equal(getattr(a, f), getattr(b, f)) for f in ("xq", "xq2", "xd", "xs"))
+
+
+@pytest.mark.parametrize("fmt,n_in,rows,kind", [
+    ("Q4_K", 4096, (4096, 1024, 1024), "quant"),       # q/k/v: o's input from q
+    ("Q4_K", 4096, (14336, 14336), "silu_mul"),         # gate/up: down's input
+    ("Q8_0", 4096, (512, 256), "quant"),
+    ("Q6_K", 14336, (2048, 2048), "silu_mul"),
+    ("Q4_K", 1024, (512, 512), "silu_mul"),             # narrow teams: the producer launch instead
+])
+@pytest.mark.parametrize("pdl", [False, True])
+def test_next_input_equals_producers(cuda, fmt, n_in, rows, kind, pdl):
+    """mv_geteilt with a NextInput: the outputs are those of the plain call, and the next input formed
+    by the CTAs that finish each 32-row group equals, bit for bit, Eingang(y) ("quant") or akt_q8(g, u)
+    ("silu_mul"), on two calls in a row with different inputs (the group counters reset themselves)."""
+    old = mmvq.pdl(pdl)
+    try:
+        mats = [(synth.blocks(fmt, n, n_in, seed=31 + j, device=cuda), n) for j, n in enumerate(rows)]
+        src = (0,) if kind == "quant" else (0, 1)
+        nxt = mmvq.NextInput(rows[0], kind, cuda)
+        for call in range(2):
+            e = mmvq.Eingang(synth.activations(1, n_in, seed=40 + call, device=cuda)[0].contiguous())
+            ys = mmvq.mv_geteilt(fmt, mats, e, n_in, next_input=nxt, src=src)
+            ref = mmvq.mv_geteilt(fmt, mats, e, n_in)
+            assert all(torch.equal(a, b) for a, b in zip(ys, ref))
+            if kind == "quant":
+                assert _eingang_equal(nxt.eingang, mmvq.Eingang(ys[0]))
+            else:
+                a, e2 = mmvq.akt_q8(ys[0], ys[1], False)
+                assert torch.equal(nxt.a, a) and _eingang_equal(nxt.eingang, e2)
+            assert int(nxt.counters.abs().sum()) == 0
+    finally:
+        mmvq.pdl(old)
+
+
+def test_next_input_refusals(cuda):
+    e = mmvq.Eingang(synth.activations(1, 4096, seed=1, device=cuda)[0].contiguous())
+    mats = [(synth.blocks("Q4_K", 512, 4096, seed=2, device=cuda), 512)]
+    with pytest.raises(RuntimeError):                                     # silu_mul needs two matrices
+        mmvq.mv_geteilt("Q4_K", mats, e, 4096, next_input=mmvq.NextInput(512, "silu_mul", cuda), src=(0,))
+    with pytest.raises(RuntimeError):                                     # rows differ from the input's size
+        mmvq.mv_geteilt("Q4_K", mats, e, 4096, next_input=mmvq.NextInput(1024, "quant", cuda), src=(0,))
+    with pytest.raises(ValueError):
+        mmvq.NextInput(100, "quant", cuda)
