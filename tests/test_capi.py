@@ -106,3 +106,32 @@ def test_moe_argument_checks():
     assert call(ws=ctypes.c_void_p(4096 + 128)) == 3
     assert L.qmv_moe_workspace_bytes(4, 2, 256, 256) > 0
     assert L.qmv_moe_workspace_bytes(4, 2, 250, 256) == 0
+
+
+def test_multi_matrix_entry_checks():
+    """qmv_mv_multi_tok and qmv_mv_multi_ep refuse before any launch: null pointers, job counts, token
+    counts, the epilogue's kind, jobs and 32-row groups, misaligned buffers."""
+    L = _lib.load()
+    a = ctypes.c_void_p(4096)
+    Q4K = TYPE_ID["Q4_K"]
+    w2 = (ctypes.c_void_p * 2)(4096, 8192)
+    y2 = (ctypes.c_void_p * 2)(4096, 8192)
+    n2 = (ctypes.c_int * 2)(512, 512)
+    n_odd = (ctypes.c_int * 2)(500, 512)
+    n_diff = (ctypes.c_int * 2)(512, 256)
+    assert L.qmv_mv_multi_tok(Q4K, 2, None, n2, y2, 4096, a, a, a, a, 4, None) == 6
+    assert L.qmv_mv_multi_tok(Q4K, 5, w2, n2, y2, 4096, a, a, a, a, 4, None) == 4   # > 4 matrices
+    assert L.qmv_mv_multi_tok(Q4K, 2, w2, n2, y2, 4096, a, a, a, a, 0, None) == 4   # tokens
+    assert L.qmv_mv_multi_tok(Q4K, 2, w2, n2, y2, 4000, a, a, a, a, 4, None) == 2   # row length
+
+    def ep(kind=1, j0=0, j1=1, n=n2, cnt=a, xq=a, ea=a, n_in=4096):
+        return L.qmv_mv_multi_ep(Q4K, 2, w2, n, y2, n_in, a, a, a, a, kind, j0, j1, cnt, xq, a, a, a, ea, None)
+    assert ep(cnt=None) == 6
+    assert ep(kind=3) == 2
+    assert ep(j0=2) == 2
+    assert ep(kind=2, j1=0) == 2                                # the same matrix twice
+    assert ep(kind=2, ea=None) == 6                             # silu_mul needs its fp32 output
+    assert ep(n=n_odd) == 2                                     # not whole 32-row groups
+    assert ep(kind=2, n=n_diff) == 2                            # gate and up of different sizes
+    assert ep(xq=ctypes.c_void_p(4097)) == 3
+    assert ep(n_in=4000) == 2
