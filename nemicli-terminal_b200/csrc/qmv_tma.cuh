@@ -1066,8 +1066,11 @@ __global__ void __launch_bounds__(32 * (NCW + 1), NCW <= 8 ? 2 : 1) mv_tma_kerne
         float acc[NPER];
 #pragma unroll
         for (int i = 0; i < NPER; ++i) acc[i] = 0.f;
-        if (work && ti.nrows == NPER * TEAMS && R == NPER * TEAMS && !SUMS) {
-            // full tile: NPER independent rows per lane, no per-row guards (the compiler interleaves them)
+        if (work && 4 * ti.nrows >= 3 * R && R == NPER * TEAMS && !SUMS) {
+            // a full tile, or one at least 3/4 full (a 4096-row matrix's 27-28 rows a CTA): NPER
+            // independent rows per lane, no per-row guards (the compiler interleaves them); a short
+            // tile's rows past nrows compute on what the stage holds there (inside the stage; the
+            // stores below are guarded)
 #pragma unroll
             for (int k = 0; k < UPL; ++k) {
                 const int u = li + G * k;
